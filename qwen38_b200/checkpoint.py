@@ -1,0 +1,256 @@
+"""HF-layout checkpoints: random-init generation, safetensors save/load, lazy tensor sources.
+
+Target tensor names follow HF ``Qwen3_5ForCausalLM`` (``model.layers.N.linear_attn.in_proj_qkv``,
+``...self_attn.q_proj`` with per-head ``[query | gate]`` rows, ``model.norm``, ``lm_head``), the
+layout the reference loads in ``docker/qwen-c2-graft/graft/model_config.py:366-403``.  Drafter
+names follow the DSpark inventory in ``scripts/ci/dspark_intake.py:27-57`` (``fc``,
+``hidden_norm``, ``layers.N.*``, ``norm``, ``markov_head.markov_w{1,2}``).
+
+A ``TensorSource`` hands out one tensor at a time so the runtime can pack and shard layer by
+layer without materialising a second full copy of a 27B model; ``RandomSource`` derives every
+tensor from ``(seed, name)`` so all TP ranks see identical full tensors.
+"""
+from __future__ import annotations
+
+import json
+import math
+import os
+import zlib
+from typing import Callable, Iterable
+
+import torch
+
+from .config import FULL, LINEAR, DrafterConfig, ModelConfig
+
+
+def target_shapes(cfg: ModelConfig) -> dict:
+    h, it = cfg.hidden_size, cfg.intermediate_size
+    out = {"model.embed_tokens.weight": (cfg.vocab_size, h), "model.norm.weight": (h,)}
+    if not cfg.tie_word_embeddings:
+        out["lm_head.weight"] = (cfg.vocab_size, h)
+    for i, t in enumerate(cfg.layer_types):
+        p = f"model.layers.{i}."
+        out[p + "input_layernorm.weight"] = (h,)
+        out[p + "post_attention_layernorm.weight"] = (h,)
+        out[p + "mlp.gate_proj.weight"] = (it, h)
+        out[p + "mlp.up_proj.weight"] = (it, h)
+        out[p + "mlp.down_proj.weight"] = (h, it)
+        if t == LINEAR:
+            q = p + "linear_attn."
+            nv = cfg.linear_num_value_heads
+            out[q + "in_proj_qkv.weight"] = (cfg.gdn_conv_dim, h)
+            out[q + "in_proj_z.weight"] = (cfg.gdn_value_dim, h)
+            out[q + "in_proj_b.weight"] = (nv, h)
+            out[q + "in_proj_a.weight"] = (nv, h)
+            out[q + "conv1d.weight"] = (cfg.gdn_conv_dim, 1, cfg.linear_conv_kernel_dim)
+            out[q + "dt_bias"] = (nv,)
+            out[q + "A_log"] = (nv,)
+            out[q + "norm.weight"] = (cfg.linear_value_head_dim,)
+            out[q + "out_proj.weight"] = (h, cfg.gdn_value_dim)
+        else:
+            q = p + "self_attn."
+            d = cfg.head_dim
+            out[q + "q_proj.weight"] = (2 * cfg.num_attention_heads * d, h)
+            out[q + "k_proj.weight"] = (cfg.num_key_value_heads * d, h)
+            out[q + "v_proj.weight"] = (cfg.num_key_value_heads * d, h)
+            out[q + "o_proj.weight"] = (h, cfg.num_attention_heads * d)
+            out[q + "q_norm.weight"] = (d,)
+            out[q + "k_norm.weight"] = (d,)
+    return out
+
+
+def drafter_shapes(d: DrafterConfig, vocab: int) -> dict:
+    h = d.hidden_size
+    out = {
+        "fc.weight": (h, len(d.taps) * h),
+        "hidden_norm.weight": (h,),
+        "norm.weight": (h,),
+        "markov_head.markov_w1.weight": (vocab, d.markov_rank),
+        "markov_head.markov_w2.weight": (vocab, d.markov_rank),
+    }
+    for l in range(d.num_hidden_layers):
+        p = f"layers.{l}."
+        out[p + "input_layernorm.weight"] = (h,)
+        out[p + "post_attention_layernorm.weight"] = (h,)
+        out[p + "mlp.gate_proj.weight"] = (d.intermediate_size, h)
+        out[p + "mlp.up_proj.weight"] = (d.intermediate_size, h)
+        out[p + "mlp.down_proj.weight"] = (h, d.intermediate_size)
+        out[p + "self_attn.q_proj.weight"] = (d.num_attention_heads * d.head_dim, h)
+        out[p + "self_attn.k_proj.weight"] = (d.num_key_value_heads * d.head_dim, h)
+        out[p + "self_attn.v_proj.weight"] = (d.num_key_value_heads * d.head_dim, h)
+        out[p + "self_attn.o_proj.weight"] = (h, d.num_attention_heads * d.head_dim)
+        out[p + "self_attn.q_norm.weight"] = (d.head_dim,)
+        out[p + "self_attn.k_norm.weight"] = (d.head_dim,)
+    return out
+
+
+def _init_kind(name: str) -> str:
+    if name.endswith("A_log"):
+        return "alog"
+    if name.endswith("dt_bias"):
+        return "dt"
+    if name.endswith("conv1d.weight"):
+        return "conv"
+    if name.endswith("linear_attn.norm.weight"):
+        return "one"
+    if name.endswith("norm.weight") or name.endswith("layernorm.weight"):
+        return "zc"      # zero-centred (1+w) norm weight
+    return "normal"
+
+
+class TensorSource:
+    """Hands out tensors by HF name."""
+
+    def get(self, name: str, device=None, dtype=None) -> torch.Tensor:
+        raise NotImplementedError
+
+    def names(self) -> Iterable[str]:
+        raise NotImplementedError
+
+
+class RandomSource(TensorSource):
+    """Seeded random init of the named shapes; a tensor depends only on (seed, name)."""
+
+    def __init__(self, shapes: dict, seed: int = 0, std: float = 0.02, direct_norms: bool = False):
+        self.shapes, self.seed, self.std = shapes, seed, std
+        self.direct_norms = direct_norms     # drafter norms multiply by w directly (w near 1)
+
+    def names(self):
+        return list(self.shapes)
+
+    def get(self, name, device=None, dtype=None):
+        shape = self.shapes[name]
+        device = torch.device(device or "cpu")
+        gen = torch.Generator(device=device)
+        gen.manual_seed((self.seed * 1000003 + zlib.crc32(name.encode())) & 0x7FFFFFFFFFFF)
+        kind = _init_kind(name)
+        f32 = dict(device=device, dtype=torch.float32)
+        if kind == "normal":
+            t = torch.randn(shape, generator=gen, **f32) * self.std
+        elif kind == "zc":
+            t = (torch.rand(shape, generator=gen, **f32) - 0.5) * 0.2
+            if self.direct_norms:
+                t = t + 1.0
+        elif kind == "one":
+            t = 1.0 + (torch.rand(shape, generator=gen, **f32) - 0.5) * 0.2
+        elif kind == "conv":
+            k = shape[-1]
+            t = (torch.rand(shape, generator=gen, **f32) * 2 - 1) / math.sqrt(k)
+        elif kind == "alog":
+            t = torch.log(1 + 15 * torch.rand(shape, generator=gen, **f32))
+        elif kind == "dt":
+            t = 1.0 + 0.1 * torch.randn(shape, generator=gen, **f32)
+        else:
+            raise AssertionError(kind)
+        if dtype is not None and kind in ("normal", "zc", "one", "conv"):
+            t = t.to(dtype)
+        return t
+
+
+class DictSource(TensorSource):
+    def __init__(self, sd: dict):
+        self.sd = sd
+
+    def names(self):
+        return list(self.sd)
+
+    def get(self, name, device=None, dtype=None):
+        t = self.sd[name]
+        if device is not None:
+            t = t.to(device)
+        if dtype is not None and t.is_floating_point() and not name.endswith(("A_log", "dt_bias")):
+            t = t.to(dtype)
+        return t
+
+
+class SafetensorsSource(TensorSource):
+    """Reads tensors lazily from a (possibly sharded) safetensors checkpoint directory."""
+
+    def __init__(self, path: str, prefix: str = ""):
+        from safetensors import safe_open
+        self.path, self.prefix = path, prefix
+        index = os.path.join(path, "model.safetensors.index.json")
+        if os.path.exists(index):
+            with open(index) as f:
+                wm = json.load(f)["weight_map"]
+            files = sorted(set(wm.values()))
+        else:
+            files = [f for f in sorted(os.listdir(path)) if f.endswith(".safetensors")]
+            wm = None
+        self._handles = {f: safe_open(os.path.join(path, f), framework="pt") for f in files}
+        self._where = {}
+        for f, h in self._handles.items():
+            for k in h.keys():
+                self._where[k] = f
+        if wm is not None:
+            self._where.update(wm)
+
+    def names(self):
+        return [k[len(self.prefix):] for k in self._where if k.startswith(self.prefix)]
+
+    def get(self, name, device=None, dtype=None):
+        key = self.prefix + name
+        t = self._handles[self._where[key]].get_tensor(key)
+        if device is not None:
+            t = t.to(device)
+        if dtype is not None and t.is_floating_point() and not name.endswith(("A_log", "dt_bias")):
+            t = t.to(dtype)
+        return t
+
+
+def random_target_source(cfg: ModelConfig, seed: int = 0) -> RandomSource:
+    return RandomSource(target_shapes(cfg), seed=seed)
+
+
+def random_drafter_source(d: DrafterConfig, vocab: int, seed: int = 1) -> RandomSource:
+    return RandomSource(drafter_shapes(d, vocab), seed=seed, direct_norms=True)
+
+
+def materialize(src: TensorSource, device="cpu", dtype=torch.float32) -> dict:
+    return {n: src.get(n, device=device, dtype=dtype) for n in src.names()}
+
+
+def save_pretrained(path: str, cfg: ModelConfig, src: TensorSource, dtype=torch.bfloat16,
+                    shard_bytes: int = 4 << 30, drafter: tuple | None = None):
+    """Write ``config.json`` and (sharded) ``model.safetensors`` in HF layout.  ``drafter`` is an
+    optional ``(DrafterConfig, TensorSource)`` written under ``path/drafter``."""
+    from safetensors.torch import save_file
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump({"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"],
+                   "text_config": cfg.to_hf_text_config(), "tie_word_embeddings": cfg.tie_word_embeddings},
+                  f, indent=1)
+    shards, cur, size = [], {}, 0
+    for n in src.names():
+        t = src.get(n, dtype=dtype).contiguous()
+        if size + t.numel() * t.element_size() > shard_bytes and cur:
+            shards.append(cur)
+            cur, size = {}, 0
+        cur[n] = t
+        size += t.numel() * t.element_size()
+    if cur:
+        shards.append(cur)
+    wm = {}
+    for i, sh in enumerate(shards):
+        fn = f"model-{i + 1:05d}-of-{len(shards):05d}.safetensors"
+        save_file(sh, os.path.join(path, fn), metadata={"format": "pt"})
+        wm.update({k: fn for k in sh})
+    with open(os.path.join(path, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {}, "weight_map": wm}, f, indent=1)
+    if drafter is not None:
+        dcfg, dsrc = drafter
+        dpath = os.path.join(path, "drafter")
+        os.makedirs(dpath, exist_ok=True)
+        import dataclasses
+        with open(os.path.join(dpath, "config.json"), "w") as f:
+            json.dump(dict(dataclasses.asdict(dcfg), architectures=["DSparkDraftModel"]), f, indent=1)
+        save_file({n: dsrc.get(n, dtype=dtype).contiguous() for n in dsrc.names()},
+                  os.path.join(dpath, "model.safetensors"), metadata={"format": "pt"})
+
+
+def load_drafter_config(path: str) -> DrafterConfig:
+    import dataclasses
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    names = {f.name for f in dataclasses.fields(DrafterConfig)}
+    return DrafterConfig(**{k: v for k, v in raw.items() if k in names})

@@ -1,0 +1,176 @@
+"""Block drafter conditioned on target hidden states (DSpark family).
+
+Forward, as pinned by the reference's CPU backbone (``scripts/ci/dspark_backbone_reference.py:46-110``)
+and device drafter (``scripts/ci/dspark_device.py:34-103``):
+
+1. Context rows: ``hidden_norm(fc(concat(tap features)))`` for every committed target position;
+   each drafter layer projects them once into its K/V history (``k_norm`` + RoPE on K).
+2. Block rows: target embeddings of ``[anchor, MASK, ..., MASK]`` (``P = block_rows - 1`` rows)
+   at positions ``pos .. pos+P-1``; ``anchor`` is the committed seed at ``pos``.
+3. Each layer: RMSNorm, q/k/v projections (q/k per-head RMSNorm, YaRN RoPE), attention of every
+   block row over the whole history plus every block row (no causal mask inside the block),
+   ``o_proj`` residual, SwiGLU residual.  Norm weights multiply directly (no ``1+w``).
+4. Final norm, the target's (shared) LM head, then the sequential Markov selector: step i
+   scores ``logits[i] + pred[prev] . succ^T`` and takes the argmax (``scripts/ci/dspark_markov.py``).
+
+Publication (``scripts/ci/dflash_request_runtime.py:69-103``): after a commit, the accepted rows'
+tap features are projected and appended to the history (incremental, never re-projected).
+
+Tensor parallel like the target: heads split, KV heads replicated past their count, ``fc``
+row-parallel over its input features, ``o_proj``/``down`` row-parallel, vocab-parallel head and
+successor table with a cross-rank argmax per Markov step.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..config import DrafterConfig
+from ..ops import torch_ref as R
+from .target import GU_BLOCK, HybridTarget
+
+
+def _heads_split(n_heads, n_kv, tp, r):
+    hl = n_heads // tp
+    if tp > n_kv:
+        return hl, 1, [r * n_kv // tp]
+    kl = n_kv // tp
+    return hl, kl, list(range(r * kl, (r + 1) * kl))
+
+
+class BlockDrafter:
+    def __init__(self, dcfg: DrafterConfig, src, target: HybridTarget, *, max_context: int | None = None):
+        self.dcfg, self.target = dcfg, target
+        self.ops, self.comm = target.ops, target.comm
+        self.device, self.dtype = target.device, target.dtype
+        tp, r = target.tp, target.rank
+        self.tp = tp
+        H, Dh = dcfg.hidden_size, dcfg.head_dim
+        if H != target.cfg.hidden_size:
+            raise ValueError("drafter width must equal the target hidden size (shared embedding/head)")
+        if dcfg.num_attention_heads % tp or dcfg.intermediate_size % (tp * GU_BLOCK):
+            raise ValueError("drafter heads / intermediate do not divide by TP")
+        self.eps = dcfg.rms_norm_eps
+        self.P = dcfg.proposals
+        self.mask_id = dcfg.mask_id(target.cfg.vocab_size)
+        dev, dt = self.device, self.dtype
+        f32 = lambda n: src.get(n, device=dev, dtype=torch.float32).float().contiguous()
+        get = lambda n: src.get(n, device=dev, dtype=dt)
+        nt = len(dcfg.taps)
+        kin = nt * H
+        if kin % tp:
+            raise ValueError("fc input width must divide by TP")
+        kl = kin // tp
+        fc = get("fc.weight")
+        self.fc = fc[:, r * kl:(r + 1) * kl].contiguous()
+        self.fc_k = (r * kl, kl)
+        self.hidden_norm = f32("hidden_norm.weight")
+        self.norm = f32("norm.weight")
+        hl, kvl, kv_heads = _heads_split(dcfg.num_attention_heads, dcfg.num_key_value_heads, tp, r)
+        self.heads = (hl, kvl, Dh)
+        il = dcfg.intermediate_size // tp
+        self.layers = []
+        for l in range(dcfg.num_hidden_layers):
+            p = f"layers.{l}."
+            wq = get(p + "self_attn.q_proj.weight")[r * hl * Dh:(r + 1) * hl * Dh]
+            wk = get(p + "self_attn.k_proj.weight").view(dcfg.num_key_value_heads, Dh, H)[kv_heads].reshape(-1, H)
+            wv = get(p + "self_attn.v_proj.weight").view(dcfg.num_key_value_heads, Dh, H)[kv_heads].reshape(-1, H)
+            g = get(p + "mlp.gate_proj.weight")[r * il:(r + 1) * il]
+            u = get(p + "mlp.up_proj.weight")[r * il:(r + 1) * il]
+            gu = torch.stack([g.reshape(il // GU_BLOCK, GU_BLOCK, H), u.reshape(il // GU_BLOCK, GU_BLOCK, H)], 1)
+            self.layers.append(dict(
+                w_qkv=torch.cat([wq, wk, wv], 0).contiguous(),
+                w_kv=torch.cat([wk, wv], 0).contiguous(),
+                w_o=get(p + "self_attn.o_proj.weight")[:, r * hl * Dh:(r + 1) * hl * Dh].contiguous(),
+                qn=f32(p + "self_attn.q_norm.weight"), kn=f32(p + "self_attn.k_norm.weight"),
+                in_norm=f32(p + "input_layernorm.weight"), post_norm=f32(p + "post_attention_layernorm.weight"),
+                w_gu=gu.reshape(2 * il, H).contiguous(),
+                w_down=get(p + "mlp.down_proj.weight")[:, r * il:(r + 1) * il].contiguous(),
+            ))
+        vl = target.widths["vocab"]
+        self.pred = get("markov_head.markov_w1.weight").contiguous()                 # [V, R] replicated
+        self.succ = get("markov_head.markov_w2.weight")[r * vl:(r + 1) * vl].contiguous()  # [V_l, R]
+        inv, scale = R.yarn_inv_freq(Dh, dcfg.rope_theta, dcfg.yarn_factor, dcfg.yarn_beta_fast,
+                                     dcfg.yarn_beta_slow, dcfg.yarn_original_max_position)
+        self.inv_freq, self.rope_scale = inv.to(dev), scale
+        self.max_context = max_context or target.rt.max_context
+        cap = self.max_context + 2 * dcfg.block_rows
+        self.kctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
+        self.vctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
+        self.position = 0
+
+    # -------------------------------------------------------------------------------- helpers
+    def rope(self, positions):
+        return R.rope_cos_sin(positions, self.dcfg.head_dim, self.dcfg.rope_theta, self.inv_freq, self.rope_scale)
+
+    def _row_par(self, h, w):
+        part = self.ops.linear(h, w, out_dtype=torch.float32)
+        if self.tp > 1:
+            self.comm.all_reduce_(part)
+        return part
+
+    def _context_rows(self, feats):
+        """fc (row-parallel over tap features) then hidden_norm -> [S, H] in activation dtype."""
+        k0, kl = self.fc_k
+        part = self._row_par(feats[:, k0:k0 + kl].contiguous() if self.tp > 1 else feats, self.fc)
+        return self.ops.rms_norm(part, self.hidden_norm, self.eps, self.dtype)
+
+    # -------------------------------------------------------------------------------- history
+    def reset(self):
+        self.position = 0
+
+    @torch.no_grad()
+    def append(self, feats: torch.Tensor, pos: int):
+        """Project ``feats`` [n, taps*H] (target rows at positions pos..pos+n-1) into every layer's
+        K/V history."""
+        if pos != self.position:
+            raise ValueError(f"drafter history at {self.position}, publication at {pos}")
+        n = feats.shape[0]
+        if pos + n > self.max_context:
+            raise ValueError("drafter history capacity exceeded")
+        ctx = self._context_rows(feats)
+        cos, sin = self.rope(torch.arange(pos, pos + n, device=self.device))
+        hl, kvl, Dh = self.heads
+        for l, L in enumerate(self.layers):
+            kv = self.ops.linear(ctx, L["w_kv"])
+            k = kv[:, :kvl * Dh].reshape(n, kvl, Dh)
+            v = kv[:, kvl * Dh:].reshape(n, kvl, Dh)
+            k = R.apply_rope(self.ops.rms_norm(k, L["kn"], self.eps, torch.float32), cos, sin)
+            self.kctx[l, pos:pos + n] = k.to(self.dtype)
+            self.vctx[l, pos:pos + n] = v
+        self.position = pos + n
+
+    # -------------------------------------------------------------------------------- propose
+    @torch.no_grad()
+    def forward_block(self, anchor: torch.Tensor):
+        """Block forward at the current history frontier; returns local-vocab logits [P, V_l]."""
+        P, pos = self.P, self.position
+        hl, kvl, Dh = self.heads
+        ids = torch.full((P,), self.mask_id, dtype=torch.long, device=self.device)
+        ids[0] = anchor.reshape(())
+        h = self.ops.embedding(ids, self.target.embed).float()
+        cos, sin = self.rope(torch.arange(pos, pos + P, device=self.device))
+        for l, L in enumerate(self.layers):
+            hn = self.ops.rms_norm(h, L["in_norm"], self.eps, self.dtype)
+            qkv = self.ops.linear(hn, L["w_qkv"])
+            q = qkv[:, :hl * Dh].reshape(P, hl, Dh)
+            k = qkv[:, hl * Dh:(hl + kvl) * Dh].reshape(P, kvl, Dh)
+            v = qkv[:, (hl + kvl) * Dh:].reshape(P, kvl, Dh)
+            q = R.apply_rope(self.ops.rms_norm(q, L["qn"], self.eps, torch.float32), cos, sin).to(self.dtype)
+            k = R.apply_rope(self.ops.rms_norm(k, L["kn"], self.eps, torch.float32), cos, sin).to(self.dtype)
+            o = self.ops.draft_attention(q, self.kctx[l], self.vctx[l], pos, k, v, Dh ** -0.5, self.dtype)
+            h += self._row_par(o, L["w_o"])
+            hn = self.ops.rms_norm(h, L["post_norm"], self.eps, self.dtype)
+            gu = self.ops.linear_swiglu(hn, L["w_gu"], GU_BLOCK)
+            h += self._row_par(gu, L["w_down"])
+        hn = self.ops.rms_norm(h, self.norm, self.eps, self.dtype)
+        return self.ops.linear(hn, self.target.lm_head, out_dtype=torch.float32)
+
+    @torch.no_grad()
+    def propose(self, anchor: torch.Tensor) -> torch.Tensor:
+        """Returns P proposal ids (device int64) for the block after ``anchor``."""
+        logits = self.forward_block(anchor)
+        return self.ops.markov_select(logits, anchor, self.pred, self.succ, self.target.vocab_offset,
+                                      self.comm if self.tp > 1 else None)
+
+    def close(self):
+        self.position = 0
