@@ -1,0 +1,40 @@
+// Python bindings of the qwen38_b200 sm_100a kernels.
+#include <torch/extension.h>
+
+void q38_linear(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, torch::Tensor ws,
+                torch::Tensor counters, torch::Tensor err);
+void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, torch::Tensor out_val, torch::Tensor out_idx,
+                        int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
+                        torch::Tensor counters, torch::Tensor err);
+void q38_clear_map_cache();
+void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, torch::Tensor state,
+                       torch::Tensor conv_w, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
+                       c10::optional<torch::Tensor> out, int64_t rows, c10::optional<torch::Tensor> rows_dev,
+                       int64_t nk, int64_t nv, int64_t D, double eps);
+void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_off, int64_t nq, int64_t nkv,
+                   int64_t D, int64_t rd, torch::Tensor qn, torch::Tensor kn, torch::Tensor inv_freq,
+                   double rope_scale, double eps, torch::Tensor pos, c10::optional<torch::Tensor> q_out,
+                   torch::Tensor kcache, torch::Tensor vcache, c10::optional<torch::Tensor> block_table,
+                   int64_t block_size);
+void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                     c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
+                     int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
+                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
+void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
+void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
+                     torch::Tensor out, c10::optional<torch::Tensor> out_val, torch::Tensor part_val,
+                     torch::Tensor part_idx, int64_t vocab_offset, bool write_prev);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "qwen38_b200 sm_100a kernels";
+  m.def("linear", &q38_linear);
+  m.def("lm_head_argmax", &q38_lm_head_argmax);
+  m.def("clear_map_cache", &q38_clear_map_cache);
+  m.def("gdn_recurrent", &q38_gdn_recurrent);
+  m.def("attn_prep", &q38_attn_prep);
+  m.def("attn_decode", &q38_attn_decode);
+  m.def("rms_norm", &q38_rms_norm);
+  m.def("embedding", &q38_embedding);
+  m.def("markov_step", &q38_markov_step);
+}

@@ -99,9 +99,6 @@ class BlockDrafter:
         self.position = 0
 
     # -------------------------------------------------------------------------------- helpers
-    def rope(self, positions):
-        return R.rope_cos_sin(positions, self.dcfg.head_dim, self.dcfg.rope_theta, self.inv_freq, self.rope_scale)
-
     def _row_par(self, h, w):
         part = self.ops.linear(h, w, out_dtype=torch.float32)
         if self.tp > 1:
@@ -128,15 +125,12 @@ class BlockDrafter:
         if pos + n > self.max_context:
             raise ValueError("drafter history capacity exceeded")
         ctx = self._context_rows(feats)
-        cos, sin = self.rope(torch.arange(pos, pos + n, device=self.device))
+        positions = torch.arange(pos, pos + n, device=self.device, dtype=torch.int32)
         hl, kvl, Dh = self.heads
         for l, L in enumerate(self.layers):
             kv = self.ops.linear(ctx, L["w_kv"])
-            k = kv[:, :kvl * Dh].reshape(n, kvl, Dh)
-            v = kv[:, kvl * Dh:].reshape(n, kvl, Dh)
-            k = R.apply_rope(self.ops.rms_norm(k, L["kn"], self.eps, torch.float32), cos, sin)
-            self.kctx[l, pos:pos + n] = k.to(self.dtype)
-            self.vctx[l, pos:pos + n] = v
+            self.ops.kv_append(kv, L["kn"], self.inv_freq, self.rope_scale, Dh, kvl, Dh, self.eps, positions,
+                               self.kctx[l], self.vctx[l])
         self.position = pos + n
 
     # -------------------------------------------------------------------------------- propose
@@ -148,16 +142,12 @@ class BlockDrafter:
         ids = torch.full((P,), self.mask_id, dtype=torch.long, device=self.device)
         ids[0] = anchor.reshape(())
         h = self.ops.embedding(ids, self.target.embed).float()
-        cos, sin = self.rope(torch.arange(pos, pos + P, device=self.device))
+        positions = torch.arange(pos, pos + P, device=self.device, dtype=torch.int32)
         for l, L in enumerate(self.layers):
             hn = self.ops.rms_norm(h, L["in_norm"], self.eps, self.dtype)
             qkv = self.ops.linear(hn, L["w_qkv"])
-            q = qkv[:, :hl * Dh].reshape(P, hl, Dh)
-            k = qkv[:, hl * Dh:(hl + kvl) * Dh].reshape(P, kvl, Dh)
-            v = qkv[:, (hl + kvl) * Dh:].reshape(P, kvl, Dh)
-            q = R.apply_rope(self.ops.rms_norm(q, L["qn"], self.eps, torch.float32), cos, sin).to(self.dtype)
-            k = R.apply_rope(self.ops.rms_norm(k, L["kn"], self.eps, torch.float32), cos, sin).to(self.dtype)
-            o = self.ops.draft_attention(q, self.kctx[l], self.vctx[l], pos, k, v, Dh ** -0.5, self.dtype)
+            o = self.ops.draft_block_attention(qkv, L["qn"], L["kn"], self.inv_freq, self.rope_scale, self.heads,
+                                               self.eps, positions, self.kctx[l], self.vctx[l], self.dtype)
             h += self._row_par(o, L["w_o"])
             hn = self.ops.rms_norm(h, L["post_norm"], self.eps, self.dtype)
             gu = self.ops.linear_swiglu(hn, L["w_gu"], GU_BLOCK)

@@ -180,6 +180,14 @@ class HybridTarget:
             self.layers.append(L)
         self.gdn_index = {i: j for j, i in enumerate(cfg.linear_layers)}
         self.attn_index = {i: j for j, i in enumerate(cfg.full_layers)}
+        # per-layer GDN parameters stacked [Lg, ...] so one launch can commit every layer;
+        # each layer's dict entries become views into the stacks
+        if cfg.linear_layers:
+            for key in ("conv_w", "A_log", "dt_bias", "norm_w"):
+                stack = torch.stack([self.layers[i][key] for i in cfg.linear_layers]).contiguous()
+                setattr(self, "gdn_" + key, stack)
+                for j, i in enumerate(cfg.linear_layers):
+                    self.layers[i][key] = stack[j]
 
         # ---- RoPE inverse frequencies (partial rotary, half-split)
         rd = cfg.rope_dim
@@ -244,8 +252,8 @@ class HybridTarget:
             seq.block_table[len(seq.blocks) - len(new):len(seq.blocks)] = torch.tensor(
                 new, dtype=torch.int32, device=self.device)
 
-    def rope(self, positions):
-        return R.rope_cos_sin(positions, self.cfg.rope_dim, self.cfg.rope_theta, self.inv_freq)
+    def positions(self, start: int, n: int):
+        return torch.arange(start, start + n, device=self.device, dtype=torch.int32)
 
     # ------------------------------------------------------------------ blocks
     def _row_parallel(self, h, w, x):
@@ -287,7 +295,7 @@ class HybridTarget:
             tok = tokens[c0:c1]
             pos0 = seq.pos
             x = self.ops.embedding(tok, self.embed).float()
-            cos, sin = self.rope(torch.arange(pos0, pos0 + tok.shape[0], device=self.device))
+            positions = self.positions(pos0, tok.shape[0])
             for i, L in enumerate(self.layers):
                 h = self.ops.rms_norm(x, L["in_norm"], self.eps, self.dtype)
                 proj = self.ops.linear(h, L["w_in"])
@@ -298,10 +306,10 @@ class HybridTarget:
                                              self.rt.gdn_chunk, self.dtype)
                 else:
                     j = self.attn_index[i]
-                    q, gate = self.ops.attn_prep(proj, L["qn"], L["kn"], cos, sin, L["dims"], self.eps,
-                                                 self.kcache[j], self.vcache[j], seq.block_table, pos0,
-                                                 self.block_size)
-                    o = self.ops.attn_prefill(q, gate, self.kcache[j], self.vcache[j], seq.block_table, pos0,
+                    q, gate = self.ops.attn_prep(proj, L["qn"], L["kn"], self.inv_freq, 1.0, self.cfg.rope_dim,
+                                                 L["dims"], self.eps, positions, self.kcache[j], self.vcache[j],
+                                                 seq.block_table, self.block_size)
+                    o = self.ops.attn_prefill(q, gate, self.kcache[j], self.vcache[j], seq.block_table, positions,
                                               self.block_size, self.dtype)
                 self._row_parallel(o, L["w_out"], x)
                 self._mlp(L, x)
@@ -326,8 +334,8 @@ class HybridTarget:
             seq.verify_rows = (off, int(t.shape[0]))
             off += int(t.shape[0])
         tokens = torch.cat([t for _, t in batch]) if len(batch) > 1 else batch[0][1]
-        positions = torch.cat([torch.arange(s.pos, s.pos + t.shape[0], device=self.device) for s, t in batch])
-        cos, sin = self.rope(positions)
+        positions = torch.cat([self.positions(s.pos, t.shape[0]) for s, t in batch]) if len(batch) > 1 else \
+            self.positions(batch[0][0].pos, batch[0][1].shape[0])
         feats = self._tap_buffer(rows, taps)
         tap_pos = {t: j for j, t in enumerate(taps)}
         x = self.ops.embedding(tokens, self.embed).float()
@@ -347,11 +355,12 @@ class HybridTarget:
                 j = self.attn_index[i]
                 for seq, t in batch:
                     o0, n = seq.verify_rows
-                    q, gate = self.ops.attn_prep(proj[o0:o0 + n], L["qn"], L["kn"], cos[o0:o0 + n], sin[o0:o0 + n],
-                                                 L["dims"], self.eps, self.kcache[j], self.vcache[j],
-                                                 seq.block_table, seq.pos, self.block_size)
+                    pr = positions[o0:o0 + n]
+                    q, gate = self.ops.attn_prep(proj[o0:o0 + n], L["qn"], L["kn"], self.inv_freq, 1.0,
+                                                 self.cfg.rope_dim, L["dims"], self.eps, pr, self.kcache[j],
+                                                 self.vcache[j], seq.block_table, self.block_size)
                     outs.append(self.ops.attn_decode(q, gate, self.kcache[j], self.vcache[j], seq.block_table,
-                                                     seq.pos, self.block_size, self.dtype))
+                                                     pr, self.block_size, self.dtype))
             o = torch.cat(outs, 0) if len(outs) > 1 else outs[0]
             self._row_parallel(o, L["w_out"], x)
             self._mlp(L, x)
@@ -368,11 +377,10 @@ class HybridTarget:
         o0, rows = seq.verify_rows
         if not 0 <= n <= rows:
             raise ValueError(f"commit of {n} rows outside the verified block of {rows}")
-        for i, L in enumerate(self.layers):
-            if L["kind"] == LINEAR:
-                j = self.gdn_index[i]
-                self.ops.gdn_commit(self.gdn_stash[j, o0:o0 + rows], n, self.conv[seq.slot, j],
-                                    self.rec[seq.slot, j], L["conv_w"], L["A_log"], L["dt_bias"], L["dims"])
+        if self.cfg.linear_layers and n > 0:
+            dims = self.layers[self.cfg.linear_layers[0]]["dims"]
+            self.ops.gdn_commit_layers(self.gdn_stash[:, o0:o0 + rows], n, self.conv[seq.slot], self.rec[seq.slot],
+                                       self.gdn_conv_w, self.gdn_A_log, self.gdn_dt_bias, dims)
         seq.pos += n
         seq.verify_rows = None
 

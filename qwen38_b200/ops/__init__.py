@@ -97,49 +97,86 @@ class TorchOps:
         return R.gated_rms_norm(o, z, norm_w, eps).to(out_dtype).reshape(proj.shape[0], nv * dv)
 
     # ---- attention -------------------------------------------------------------------
-    def attn_prep(self, proj, qn_w, kn_w, cos, sin, dims, eps, kcache, vcache, block_table, pos0, block_size):
-        """Split [q | gate | k | v] rows, q/k (1+w) RMSNorm, partial RoPE, write K/V rows into
-        the paged cache at positions pos0..pos0+T-1.  Returns q [T, H, D], gate [T, H*D]."""
+    def attn_prep(self, proj, qn_w, kn_w, inv_freq, rope_scale, rd, dims, eps, positions, kcache, vcache,
+                  block_table, block_size):
+        """Split [q | gate | k | v] rows, q/k RMSNorm (multiplier weights), partial RoPE at
+        ``positions`` [T] (int32), write K/V rows into the cache (paged via ``block_table``, or
+        contiguous when it is None).  Returns q [T, H, D] and the gate columns [T, H*D]."""
         H, Hkv, D = dims
         T = proj.shape[0]
         q = proj[:, :H * D].reshape(T, H, D)
         gate = proj[:, H * D:2 * H * D]
         k = proj[:, 2 * H * D:2 * H * D + Hkv * D].reshape(T, Hkv, D)
         v = proj[:, 2 * H * D + Hkv * D:2 * H * D + 2 * Hkv * D].reshape(T, Hkv, D)
-        q = self.rms_norm(q, qn_w, eps, torch.float32)   # qn_w / kn_w hold 1+w
-        k = self.rms_norm(k, kn_w, eps, torch.float32)
-        q = R.apply_rope(q, cos, sin).to(proj.dtype)
-        k = R.apply_rope(k, cos, sin).to(kcache.dtype)
-        pos = torch.arange(pos0, pos0 + T, device=proj.device)
-        blk = block_table[(pos // block_size).long()].long()
-        off = pos % block_size
-        kcache[blk, off] = k
-        vcache[blk, off] = v.to(vcache.dtype)
+        cos, sin = R.rope_cos_sin(positions, rd, 1.0, inv_freq, rope_scale)
+        q = R.apply_rope(self.rms_norm(q, qn_w, eps, torch.float32), cos, sin).to(proj.dtype)
+        k = R.apply_rope(self.rms_norm(k, kn_w, eps, torch.float32), cos, sin).to(kcache.dtype)
+        self._write_kv(k, v, positions, kcache, vcache, block_table, block_size)
         return q, gate
 
-    def attn_decode(self, q, gate, kcache, vcache, block_table, pos0, block_size, out_dtype):
-        """Row t (position pos0+t) attends cache keys 0..pos0+t; output times sigmoid(gate)."""
+    def _write_kv(self, k, v, positions, kcache, vcache, block_table, block_size):
+        pos = positions.long()
+        if block_table is None:
+            kcache[pos] = k.to(kcache.dtype)
+            vcache[pos] = v.to(vcache.dtype)
+        else:
+            blk = block_table[pos // block_size].long()
+            kcache[blk, pos % block_size] = k.to(kcache.dtype)
+            vcache[blk, pos % block_size] = v.to(vcache.dtype)
+
+    def _gather_kv(self, kcache, vcache, block_table, block_size, n):
+        pos = torch.arange(n, device=kcache.device)
+        if block_table is None:
+            return kcache[:n], vcache[:n]
+        blk = block_table[pos // block_size].long()
+        return kcache[blk, pos % block_size], vcache[blk, pos % block_size]
+
+    def attn_decode(self, q, gate, kcache, vcache, block_table, positions, block_size, out_dtype, causal=True):
+        """Row t attends cache keys 0..positions[t] (causal) or 0..positions[-1] (full);
+        output times sigmoid(gate) when a gate is given."""
         T, H, D = q.shape
-        S = pos0 + T
-        pos = torch.arange(S, device=q.device)
-        blk = block_table[(pos // block_size).long()].long()
-        K = kcache[blk, pos % block_size]
-        V = vcache[blk, pos % block_size]
-        qpos = torch.arange(pos0, pos0 + T, device=q.device)
-        o = R.attention(q, K, V, qpos, pos, D ** -0.5, causal=True)
-        o = o.reshape(T, H * D) * torch.sigmoid(gate.float())
+        n = int(positions[-1]) + 1
+        K, V = self._gather_kv(kcache, vcache, block_table, block_size, n)
+        kpos = torch.arange(n, device=q.device)
+        o = R.attention(q, K, V, positions.long(), kpos, D ** -0.5, causal=causal)
+        o = o.reshape(T, H * D)
+        if gate is not None:
+            o = o * torch.sigmoid(gate.float())
         return o.to(out_dtype)
 
     attn_prefill = attn_decode
 
-    def draft_attention(self, q, kctx, vctx, n_ctx, k_blk, v_blk, scale, out_dtype):
-        """Every block row attends all ``n_ctx`` history rows plus every block row (no mask)."""
-        P, H, D = q.shape
-        K = torch.cat([kctx[:n_ctx], k_blk.to(kctx.dtype)], 0)
-        V = torch.cat([vctx[:n_ctx], v_blk.to(vctx.dtype)], 0)
-        pos = torch.zeros(K.shape[0], device=q.device)
-        o = R.attention(q, K, V, torch.zeros(P, device=q.device), pos, scale, causal=False)
-        return o.reshape(P, H * D).to(out_dtype)
+    def kv_append(self, kv, kn_w, inv_freq, rope_scale, rd, nkv, D, eps, positions, kcache, vcache):
+        """Drafter context rows: k = RoPE(RMSNorm(k)), v as is, written contiguously."""
+        T = kv.shape[0]
+        k = kv[:, :nkv * D].reshape(T, nkv, D)
+        v = kv[:, nkv * D:2 * nkv * D].reshape(T, nkv, D)
+        cos, sin = R.rope_cos_sin(positions, rd, 1.0, inv_freq, rope_scale)
+        k = R.apply_rope(self.rms_norm(k, kn_w, eps, torch.float32), cos, sin)
+        self._write_kv(k, v, positions, kcache, vcache, None, 0)
+
+    def draft_block_attention(self, qkv, qn_w, kn_w, inv_freq, rope_scale, dims, eps, positions, kcache, vcache,
+                              out_dtype):
+        """Drafter block rows [q | k | v]: norm + RoPE, block K/V written after the history at
+        ``positions``, then every block row attends the whole history and every block row."""
+        H, Hkv, D = dims
+        T = qkv.shape[0]
+        q = qkv[:, :H * D].reshape(T, H, D)
+        k = qkv[:, H * D:(H + Hkv) * D].reshape(T, Hkv, D)
+        v = qkv[:, (H + Hkv) * D:(H + 2 * Hkv) * D].reshape(T, Hkv, D)
+        cos, sin = R.rope_cos_sin(positions, D, 1.0, inv_freq, rope_scale)
+        q = R.apply_rope(self.rms_norm(q, qn_w, eps, torch.float32), cos, sin).to(qkv.dtype)
+        k = R.apply_rope(self.rms_norm(k, kn_w, eps, torch.float32), cos, sin)
+        self._write_kv(k, v, positions, kcache, vcache, None, 0)
+        return self.attn_decode(q, None, kcache, vcache, None, positions, 0, out_dtype, causal=False)
+
+    def gdn_commit_layers(self, stash, n, conv, rec, conv_w, A_log, dt_bias, dims):
+        """Commit the first ``n`` rows of every layer's kept projection rows (stacked [L, ...])."""
+        for j in range(stash.shape[0]):
+            self.gdn_commit(stash[j], n, conv[j], rec[j], conv_w[j], A_log[j], dt_bias[j], dims)
+
+    def check(self):
+        pass
 
     # ---- sampling --------------------------------------------------------------------
     def markov_select(self, logits, anchor, pred, succ, vocab_offset=0, comm=None):

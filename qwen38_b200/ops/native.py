@@ -1,0 +1,229 @@
+"""``NativeOps``: the runtime's op set on the hand-written sm_100a kernels.
+
+Requires CUDA tensors and the in-tree extension (``qwen38_b200/_build``); there is no fallback.
+Scratch buffers (split-K partials and counters, attention split partials, argmax partials, the
+device error word) are allocated once per device so every launch is graph-capturable.
+
+``launches`` counts the kernels this op set enqueued (bench ``gpu_launches``).
+"""
+from __future__ import annotations
+
+import torch
+
+from . import TorchOps
+from . import torch_ref as R
+from .build import load
+
+EPI_BF16, EPI_F32, EPI_ADD_F32, EPI_SWIGLU, EPI_ARGMAX = range(5)
+
+
+class KernelError(RuntimeError):
+    pass
+
+
+_ERR_NAMES = {1: "TMA/mbarrier wait timeout", 2: "accumulator wait timeout", 4: "split-K fix-up timeout",
+              8: "peer flag timeout", 16: "unsupported shape"}
+
+
+class NativeOps(TorchOps):
+    name = "native"
+
+    def __init__(self, device=None, max_keys: int = 1 << 17, ws_mb: int = 64):
+        self.C = load()
+        if not torch.cuda.is_available():
+            raise RuntimeError("NativeOps needs a CUDA device")
+        self.device = torch.device(device or f"cuda:{torch.cuda.current_device()}")
+        dev = self.device
+        self.ws = torch.zeros(ws_mb << 18, dtype=torch.float32, device=dev)          # ws_mb MiB
+        self.counters = torch.zeros(1 << 16, dtype=torch.int32, device=dev)
+        self.err = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.amax_val = torch.empty(1 << 20, dtype=torch.float32, device=dev)
+        self.amax_idx = torch.empty(1 << 20, dtype=torch.int32, device=dev)
+        self.max_keys = max_keys
+        self._attn_bufs = {}
+        self.rows_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.launches = 0
+
+    # ------------------------------------------------------------------ errors
+    def check(self):
+        e = int(self.err.item())
+        if e:
+            names = [n for b, n in _ERR_NAMES.items() if e & b]
+            self.err.zero_()
+            self.counters.zero_()
+            raise KernelError(f"device error word {e}: {', '.join(names)}")
+
+    # ------------------------------------------------------------------ GEMMs
+    def linear(self, x, w, out_dtype=None):
+        x = x.contiguous()
+        T, N = x.shape[0], w.shape[0]
+        if out_dtype == torch.float32:
+            out = torch.empty(T, N, dtype=torch.float32, device=x.device)
+            self.C.linear(x, w, out, EPI_F32, self.ws, self.counters, self.err)
+        else:
+            out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
+            self.C.linear(x, w, out, EPI_BF16, self.ws, self.counters, self.err)
+        self.launches += 1
+        return out
+
+    def linear_residual(self, x, w, residual):
+        self.C.linear(x.contiguous(), w, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
+        self.launches += 1
+        return residual
+
+    def linear_swiglu(self, x, w_gu, block):
+        if block != 64:
+            raise ValueError("the SwiGLU epilogue pairs 64-row gate/up blocks")
+        x = x.contiguous()
+        out = torch.empty(x.shape[0], w_gu.shape[0] // 2, dtype=torch.bfloat16, device=x.device)
+        self.C.linear(x, w_gu, out, EPI_SWIGLU, self.ws, self.counters, self.err)
+        self.launches += 1
+        return out
+
+    def lm_head_argmax(self, x, w, vocab_offset=0):
+        x = x.contiguous()
+        T = x.shape[0]
+        val = torch.empty(T, dtype=torch.float32, device=x.device)
+        idx = torch.empty(T, dtype=torch.int64, device=x.device)
+        self.C.lm_head_argmax(x, w, val, idx, int(vocab_offset), self.amax_val, self.amax_idx, self.ws,
+                              self.counters, self.err)
+        self.launches += 2
+        return val, idx
+
+    # ------------------------------------------------------------------ norms / embedding
+    def rms_norm(self, x, w_eff, eps, out_dtype):
+        if out_dtype != torch.bfloat16:
+            return super().rms_norm(x, w_eff, eps, out_dtype)
+        x2 = x.reshape(-1, x.shape[-1])
+        out = torch.empty(x2.shape, dtype=torch.bfloat16, device=x.device)
+        self.C.rms_norm(x2, w_eff, float(eps), out)
+        self.launches += 1
+        return out.reshape(x.shape)
+
+    def embedding(self, ids, table):
+        out = torch.empty(ids.numel(), table.shape[1], dtype=torch.float32, device=ids.device)
+        self.C.embedding(ids.reshape(-1).long(), table, out)
+        self.launches += 1
+        return out
+
+    # ------------------------------------------------------------------ GDN
+    def gdn_verify(self, proj, window, state, conv_w, A_log, dt_bias, norm_w, eps, dims, out_dtype):
+        nk, nv, dk, dv = dims
+        out = torch.empty(proj.shape[0], nv * dv, dtype=torch.bfloat16, device=proj.device)
+        self.C.gdn_recurrent(0, proj, window, state, conv_w, A_log, dt_bias, norm_w, out, proj.shape[0], None,
+                             nk, nv, dk, float(eps))
+        self.launches += 1
+        return out
+
+    def gdn_prefill(self, proj, window, state, conv_w, A_log, dt_bias, norm_w, eps, dims, chunk, out_dtype):
+        nk, nv, dk, dv = dims
+        out = torch.empty(proj.shape[0], nv * dv, dtype=torch.bfloat16, device=proj.device)
+        self.C.gdn_recurrent(2, proj, window, state, conv_w, A_log, dt_bias, norm_w, out, proj.shape[0], None,
+                             nk, nv, dk, float(eps))
+        self.launches += 2
+        return out
+
+    def gdn_commit(self, proj, n, window, state, conv_w, A_log, dt_bias, dims):
+        nk, nv, dk, dv = dims
+        self.rows_dev.fill_(int(n))
+        dummy_norm = torch.empty(dv, dtype=torch.float32, device=proj.device)
+        self.C.gdn_recurrent(1, proj, window, state, conv_w, A_log, dt_bias, dummy_norm, None, int(n),
+                             self.rows_dev, nk, nv, dk, 1e-6)
+        self.launches += 2
+
+    def gdn_commit_layers(self, stash, n, conv, rec, conv_w, A_log, dt_bias, dims):
+        nk, nv, dk, dv = dims
+        self.rows_dev.fill_(int(n))
+        norm_dummy = torch.empty(rec.shape[0], dv, dtype=torch.float32, device=rec.device)
+        self.C.gdn_recurrent(1, stash, conv, rec, conv_w, A_log, dt_bias, norm_dummy, None, int(n), self.rows_dev,
+                             nk, nv, dk, 1e-6)
+        self.launches += 2
+
+    # ------------------------------------------------------------------ attention
+    def _bufs(self, nkv, nqv, D):
+        key = (nkv, nqv, D)
+        b = self._attn_bufs.get(key)
+        if b is None:
+            splits = -(-self.max_keys // 256)
+            b = (torch.empty(nkv * splits * nqv * D, dtype=torch.float32, device=self.device),
+                 torch.empty(nkv * splits * nqv * 2, dtype=torch.float32, device=self.device))
+            self._attn_bufs[key] = b
+        return b
+
+    def attn_prep(self, proj, qn_w, kn_w, inv_freq, rope_scale, rd, dims, eps, positions, kcache, vcache,
+                  block_table, block_size):
+        H, Hkv, D = dims
+        T = proj.shape[0]
+        q = torch.empty(T, H, D, dtype=torch.bfloat16, device=proj.device)
+        self.C.attn_prep(proj, 0, 2 * H * D, 2 * H * D + Hkv * D, H, Hkv, D, rd, qn_w, kn_w, inv_freq,
+                         float(rope_scale), float(eps), positions, q, kcache, vcache, block_table, block_size)
+        self.launches += 1
+        return q, proj[:, H * D:2 * H * D]
+
+    def attn_decode(self, q, gate, kcache, vcache, block_table, positions, block_size, out_dtype, causal=True):
+        T, H, D = q.shape
+        if T > 32:
+            return self.attn_prefill(q, gate, kcache, vcache, block_table, positions, block_size, out_dtype)
+        nkv = kcache.shape[-2]
+        po, pml = self._bufs(nkv, H // nkv * T, D)
+        out = torch.empty(T, H * D, dtype=torch.bfloat16, device=q.device)
+        g = gate
+        self.C.attn_decode(q, kcache, vcache, block_table, block_size, positions, D ** -0.5, int(causal), g,
+                           0, out, po, pml, self.max_keys)
+        self.launches += 2
+        return out
+
+    def attn_prefill(self, q, gate, kcache, vcache, block_table, positions, block_size, out_dtype):
+        """Causal prefill attention of a chunk over the paged cache.  Library flash-attention
+        (torch SDPA) on gathered K/V: the baseline path for this op."""
+        import torch.nn.functional as F
+        from torch.nn.attention.bias import causal_lower_right
+        T, H, D = q.shape
+        n = int(positions[-1].item()) + 1
+        K, V = self._gather_kv(kcache, vcache, block_table, block_size, n)
+        qh = q.transpose(0, 1)[None]                     # [1, H, T, D]
+        kh = K.transpose(0, 1)[None]
+        vh = V.transpose(0, 1)[None]
+        rep = H // kh.shape[1]
+        if rep > 1:
+            kh = kh.repeat_interleave(rep, 1)
+            vh = vh.repeat_interleave(rep, 1)
+        o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=causal_lower_right(T, n))
+        o = o[0].transpose(0, 1).reshape(T, H * D)
+        o = o * torch.sigmoid(gate.float()).to(o.dtype)
+        return o.to(out_dtype)
+
+    def kv_append(self, kv, kn_w, inv_freq, rope_scale, rd, nkv, D, eps, positions, kcache, vcache):
+        self.C.attn_prep(kv, -1, 0, nkv * D, 0, nkv, D, rd, kn_w, kn_w, inv_freq, float(rope_scale), float(eps),
+                         positions, None, kcache, vcache, None, 0)
+        self.launches += 1
+
+    def draft_block_attention(self, qkv, qn_w, kn_w, inv_freq, rope_scale, dims, eps, positions, kcache, vcache,
+                              out_dtype):
+        H, Hkv, D = dims
+        T = qkv.shape[0]
+        q = torch.empty(T, H, D, dtype=torch.bfloat16, device=qkv.device)
+        self.C.attn_prep(qkv, 0, H * D, (H + Hkv) * D, H, Hkv, D, D, qn_w, kn_w, inv_freq, float(rope_scale),
+                         float(eps), positions, q, kcache, vcache, None, 0)
+        po, pml = self._bufs(Hkv, H // Hkv * T, D)
+        out = torch.empty(T, H * D, dtype=torch.bfloat16, device=qkv.device)
+        self.C.attn_decode(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
+                           self.max_keys)
+        self.launches += 3
+        return out
+
+    # ------------------------------------------------------------------ sampling
+    def markov_select(self, logits, anchor, pred, succ, vocab_offset=0, comm=None):
+        P = logits.shape[0]
+        prev = anchor.reshape(1).clone().long()
+        out = torch.empty(P, dtype=torch.int64, device=logits.device)
+        val = torch.empty(1, dtype=torch.float32, device=logits.device)
+        for i in range(P):
+            self.C.markov_step(logits[i].contiguous(), pred, succ, prev, out[i:i + 1], val, self.amax_val,
+                               self.amax_idx, int(vocab_offset), comm is None)
+            self.launches += 2
+            if comm is not None:
+                g = comm.argmax_reduce(val, out[i:i + 1])
+                out[i:i + 1].copy_(g)
+                prev.copy_(g)
+        return out

@@ -1,0 +1,194 @@
+"""Numerics of the sm_100a kernels against the plain-PyTorch fp32 definitions of the same ops,
+plus the batch-invariance property the speculative runtime relies on (a verify row is
+bit-identical to the same row run alone)."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+from qwen38_b200.ops import TorchOps, torch_ref as R  # noqa: E402
+from qwen38_b200.ops.native import NativeOps  # noqa: E402
+
+DEV = "cuda"
+
+
+@pytest.fixture(scope="module")
+def nops():
+    return NativeOps()
+
+
+def _rel(a, b):
+    return ((a.float() - b.float()).norm() / (b.float().norm() + 1e-12)).item()
+
+
+def _bf(*shape, scale=1.0, seed=0):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    return (torch.randn(*shape, generator=g, device=DEV) * scale).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("T", [1, 3, 16, 32, 77, 300])
+@pytest.mark.parametrize("N,K", [(1000, 640), (5120, 6144), (384, 17408)])
+def test_linear_matches_fp32(nops, T, N, K):
+    x, w = _bf(T, K, seed=1), _bf(N, K, scale=0.02, seed=2)
+    ref = x.float() @ w.float().t()
+    y = nops.linear(x, w)
+    assert _rel(y, ref) < 8e-3
+    y32 = nops.linear(x, w, out_dtype=torch.float32)
+    assert _rel(y32, ref) < 1e-4
+    nops.check()
+
+
+@pytest.mark.parametrize("T", [1, 16, 200])
+def test_linear_residual_and_swiglu(nops, T):
+    K, I = 1024, 768
+    x, wd = _bf(T, K, seed=3), _bf(512, K, scale=0.02, seed=4)
+    res = torch.randn(T, 512, device=DEV)
+    ref = res + x.float() @ wd.float().t()
+    nops.linear_residual(x, wd, res)
+    assert _rel(res, ref) < 1e-4
+    wgu = _bf(2 * I, K, scale=0.02, seed=5)
+    y = nops.linear_swiglu(x, wgu, 64)
+    r = (x.float() @ wgu.float().t()).view(T, -1, 2, 64)
+    ref = (torch.nn.functional.silu(r[:, :, 0]) * r[:, :, 1]).reshape(T, -1)
+    assert _rel(y, ref) < 8e-3
+    nops.check()
+
+
+def test_batch_invariance_of_skinny_gemm(nops):
+    K, N = 5120, 17408
+    x, w = _bf(16, K, seed=6), _bf(N, K, scale=0.02, seed=7)
+    full = nops.linear(x, w, out_dtype=torch.float32)
+    for t in (0, 5, 15):
+        one = nops.linear(x[t:t + 1], w, out_dtype=torch.float32)
+        assert torch.equal(one[0], full[t])
+    nops.check()
+
+
+@pytest.mark.parametrize("T", [1, 16])
+def test_lm_head_argmax(nops, T):
+    V, K = 50000, 1024
+    x, w = _bf(T, K, seed=8), _bf(V, K, scale=0.05, seed=9)
+    val, idx = nops.lm_head_argmax(x, w, 100)
+    logits = x.float() @ w.float().t()
+    ref_v, ref_i = logits.max(-1)
+    assert torch.allclose(val, ref_v, rtol=1e-3, atol=1e-3)
+    # ties/near-ties aside, the chosen logit must be the max up to accumulation error
+    chosen = logits.gather(1, (idx - 100)[:, None])[:, 0]
+    assert torch.all(chosen >= ref_v - 1e-2)
+    nops.check()
+
+
+def test_rms_norm_and_embedding(nops):
+    x = torch.randn(7, 5120, device=DEV)
+    w = torch.rand(5120, device=DEV) + 0.5
+    y = nops.rms_norm(x, w, 1e-6, torch.bfloat16)
+    assert _rel(y, TorchOps().rms_norm(x, w, 1e-6, torch.float32)) < 5e-3
+    table = _bf(1000, 256, seed=10)
+    ids = torch.tensor([3, 999, 0, 3], device=DEV)
+    assert torch.equal(nops.embedding(ids, table), table[ids].float())
+
+
+def _gdn_case(T, nk=4, nv=12, D=128, seed=11):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    C = 2 * nk * D + nv * D
+    width = C + nv * D + 2 * nv
+    proj = (torch.randn(T, width, generator=g, device=DEV)).to(torch.bfloat16)
+    window = (torch.randn(3, C, generator=g, device=DEV)).to(torch.bfloat16)
+    state = torch.randn(nv, D, D, generator=g, device=DEV) * 0.1
+    conv_w = torch.rand(C, 4, generator=g, device=DEV) - 0.5
+    A_log = torch.log(1 + 15 * torch.rand(nv, generator=g, device=DEV))
+    dt = 1 + 0.1 * torch.randn(nv, generator=g, device=DEV)
+    norm_w = 1 + 0.1 * torch.randn(D, generator=g, device=DEV)
+    return proj, window, state, conv_w, A_log, dt, norm_w, (nk, nv, D, D)
+
+
+@pytest.mark.parametrize("T", [1, 4, 16, 40])
+def test_gdn_verify_matches_reference(nops, T):
+    proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T)
+    ref = TorchOps().gdn_verify(proj.float(), window.float(), state, conv_w, A_log, dt, norm_w, 1e-6, dims,
+                                torch.float32)
+    out = nops.gdn_verify(proj, window, state, conv_w, A_log, dt, norm_w, 1e-6, dims, torch.bfloat16)
+    assert _rel(out, ref) < 1e-2
+    nops.check()
+
+
+def test_gdn_verify_rows_equal_sequential_commit_decode(nops):
+    """Row t of a verify == decode after committing rows < t (bitwise), and commit == replay."""
+    T = 8
+    proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T, seed=12)
+    out = nops.gdn_verify(proj, window, state, conv_w, A_log, dt, norm_w, 1e-6, dims, torch.bfloat16)
+    st, win = state.clone(), window.clone()
+    for t in range(T):
+        one = nops.gdn_verify(proj[t:t + 1], win, st, conv_w, A_log, dt, norm_w, 1e-6, dims, torch.bfloat16)
+        assert torch.equal(one[0], out[t])
+        nops.gdn_commit(proj[t:t + 1], 1, win, st, conv_w, A_log, dt, dims)
+    st2, win2 = state.clone(), window.clone()
+    nops.gdn_commit(proj, T, win2, st2, conv_w, A_log, dt, dims)
+    assert torch.equal(st, st2) and torch.equal(win, win2)
+    ref_st, ref_win = state.clone(), window.float().clone()
+    TorchOps().gdn_commit(proj.float(), T, ref_win, ref_st, conv_w, A_log, dt, dims)
+    assert _rel(st2, ref_st) < 1e-3
+    nops.check()
+
+
+def test_gdn_prefill_matches_chunked_reference(nops):
+    T = 300
+    proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T, seed=13)
+    ref_st, ref_win = state.clone(), window.float().clone()
+    ref = TorchOps().gdn_prefill(proj.float(), ref_win, ref_st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64,
+                                 torch.float32)
+    st, win = state.clone(), window.clone()
+    out = nops.gdn_prefill(proj, win, st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
+    assert _rel(out, ref) < 1e-2
+    assert _rel(st, ref_st) < 1e-3
+    assert torch.equal(win, ref_win.to(torch.bfloat16))
+    nops.check()
+
+
+def _attn_case(T, pos0, H=6, Hkv=1, D=256, bs=16, seed=14):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    nblocks = (pos0 + T + bs - 1) // bs + 4
+    kc = (torch.randn(nblocks, bs, Hkv, D, generator=g, device=DEV) * 0.5).to(torch.bfloat16)
+    vc = torch.randn(nblocks, bs, Hkv, D, generator=g, device=DEV).to(torch.bfloat16)
+    bt = torch.randperm(nblocks, generator=torch.Generator().manual_seed(seed)).to(torch.int32).to(DEV)
+    proj = torch.randn(T, 2 * H * D + 2 * Hkv * D, generator=g, device=DEV).to(torch.bfloat16)
+    qn = 1 + 0.1 * torch.randn(D, generator=g, device=DEV)
+    kn = 1 + 0.1 * torch.randn(D, generator=g, device=DEV)
+    rd = 64
+    inv = 1.0 / (1e7 ** (torch.arange(0, rd, 2, dtype=torch.float32, device=DEV) / rd))
+    pos = torch.arange(pos0, pos0 + T, device=DEV, dtype=torch.int32)
+    return proj, qn, kn, inv, rd, (H, Hkv, D), pos, kc, vc, bt, bs
+
+
+@pytest.mark.parametrize("T,pos0", [(1, 0), (16, 100), (16, 4000), (5, 700)])
+def test_attention_prep_and_decode(nops, T, pos0):
+    proj, qn, kn, inv, rd, dims, pos, kc, vc, bt, bs = _attn_case(T, pos0)
+    kc2, vc2 = kc.clone(), vc.clone()
+    tops = TorchOps()
+    q_ref, gate = tops.attn_prep(proj.float(), qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc2, vc2, bt, bs)
+    q, gate_n = nops.attn_prep(proj, qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc, vc, bt, bs)
+    assert _rel(q, q_ref) < 1e-2
+    assert _rel(kc.float(), kc2.float()) < 1e-2
+    ref = tops.attn_decode(q_ref.float(), gate.float(), kc2.float(), vc2.float(), bt, pos, bs, torch.float32)
+    out = nops.attn_decode(q, gate_n, kc, vc, bt, pos, bs, torch.bfloat16)
+    assert _rel(out, ref) < 2e-2
+    # batch invariance: row t alone == row t of the block
+    for t in (0, T - 1):
+        one = nops.attn_decode(q[t:t + 1], gate_n[t:t + 1], kc, vc, bt, pos[t:t + 1], bs, torch.bfloat16)
+        assert torch.equal(one[0], out[t])
+    nops.check()
+
+
+def test_markov_select(nops):
+    P, V, Rk = 5, 3000, 64
+    g = torch.Generator(device=DEV).manual_seed(15)
+    logits = torch.randn(P, V, generator=g, device=DEV)
+    pred = (torch.randn(V, Rk, generator=g, device=DEV) * 0.3).to(torch.bfloat16)
+    succ = (torch.randn(V, Rk, generator=g, device=DEV) * 0.3).to(torch.bfloat16)
+    anchor = torch.tensor([17], device=DEV)
+    out = nops.markov_select(logits, anchor, pred, succ).tolist()
+    ref = R.markov_select(logits.cpu(), 17, pred.cpu(), succ.cpu())
+    assert out == ref
