@@ -91,9 +91,8 @@ __global__ void attn_prep_kernel(PrepArgs a) {
 }
 
 // ------------------------------------------------------------------------------- decode
-constexpr int CH = 256;      // keys per split
-constexpr int SUBK = 32;     // keys per staged sub-tile
-constexpr int MAXQ = 96;     // query vectors per pass (8 warps x 12)
+constexpr int CH = 128;      // keys per split (fixed absolute chunks)
+constexpr int MAXW = 8;      // warps per CTA: one 16-row query tile each
 
 struct DecodeArgs {
   const __nv_bfloat16* q;      // [T, nq, D]
@@ -105,128 +104,187 @@ struct DecodeArgs {
   int T, nq, nkv, D;
   float scale;
   int causal;
-  float* part_o;               // [nkv, splits, nq/nkv*T, D]
-  float* part_ml;              // [nkv, splits, nq/nkv*T, 2]
+  float* part_o;               // [nkv, splits, nqv, D]
+  float* part_ml;              // [nkv, splits, nqv, 2]
   int max_splits;
 };
 
-template <int D, int QPW>
-__global__ void __launch_bounds__(256)
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x2_t(uint32_t addr, uint32_t& r0, uint32_t& r1) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                               uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// One CTA per (KV head g, 128-key chunk s).  All query vectors of the GQA group (rep heads x T
+// rows) are processed against the chunk staged once in shared memory: warp w owns query rows
+// 16w..16w+15 of the current group of up to 128 rows.  S = Q K^T and O = P V on tensor cores
+// (m16n8k16, fp32 accumulate); the softmax of a row is computed inside the chunk only, and the
+// (max, sum, unnormalised O) partial is merged across chunks in chunk order by the combine kernel.
+template <int D>
+__global__ void __launch_bounds__(256, 1)
 attn_decode_kernel(DecodeArgs a) {
-  constexpr int DP = D + 8;                 // padded row (bf16) -> conflict-free 16-B reads
-  constexpr int DPL = D / 32;               // dims per lane in PV
+  constexpr int DP = D + 8;                 // padded row: conflict-free ldmatrix
+  constexpr int NT_K = CH / 8;              // key n-tiles per chunk
+  constexpr int NT_D = D / 8;               // output n-tiles
   const int g = blockIdx.x, s = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.nq / a.nkv;
-  const int nqv = rep * a.T;                // query vectors of this KV head
-  const int n_keys = a.qpos[a.T - 1] + 1;   // rows are consecutive positions; last sees most
+  const int nqv = rep * a.T;
+  const int n_keys = a.qpos[a.T - 1] + 1;
   const int k0 = s * CH;
   if (k0 >= n_keys) return;
   const int k1 = min(n_keys, k0 + CH);
 
   extern __shared__ __align__(16) uint8_t smem[];
   __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* Vs = Ks + SUBK * DP;
-  __nv_bfloat16* Qs = Vs + SUBK * DP;       // [MAXQ][DP]
+  __nv_bfloat16* Vs = Ks + CH * DP;
+  __nv_bfloat16* Qs = Vs + CH * DP;          // [MAXW*16][DP]
 
-  for (int qb = 0; qb < nqv; qb += MAXQ) {
-    const int nqb = min(MAXQ, nqv - qb);
-    // stage queries (query vector qi -> head g*rep + qi / T, row qi % T)
-    for (int idx = threadIdx.x; idx < nqb * (D / 8); idx += blockDim.x) {
+  // ---- stage the K/V chunk (zeros past the visible keys)
+  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
+    const int j = idx / (D / 8), ch = idx % (D / 8);
+    const int kp = k0 + j;
+    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
+    if (kp < k1) {
+      size_t base;
+      if (a.block_table) {
+        const int blk = a.block_table[kp / a.block_size];
+        base = ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
+      } else {
+        base = (size_t)kp * a.nkv + g;
+      }
+      kv = reinterpret_cast<const uint4*>(a.kcache + base * D)[ch];
+      vv = reinterpret_cast<const uint4*>(a.vcache + base * D)[ch];
+    }
+    reinterpret_cast<uint4*>(Ks + j * DP)[ch] = kv;
+    reinterpret_cast<uint4*>(Vs + j * DP)[ch] = vv;
+  }
+
+  const int nwarps = blockDim.x >> 5;
+  for (int qb = 0; qb < nqv; qb += nwarps * 16) {
+    __syncthreads();
+    // ---- stage this group's query rows (zeros for padding rows)
+    for (int idx = threadIdx.x; idx < nwarps * 16 * (D / 8); idx += blockDim.x) {
       const int qi = idx / (D / 8), ch = idx % (D / 8);
       const int gq = qb + qi;
-      const int hq = g * rep + gq / a.T, t = gq % a.T;
-      reinterpret_cast<uint4*>(Qs + qi * DP)[ch] =
-          reinterpret_cast<const uint4*>(a.q + ((size_t)t * a.nq + hq) * D)[ch];
-    }
-    float m[QPW], lsum[QPW], o[QPW][DPL];
-    int myq[QPW], mypos[QPW];
-#pragma unroll
-    for (int i = 0; i < QPW; ++i) {
-      m[i] = -INFINITY;
-      lsum[i] = 0.f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) o[i][d] = 0.f;
-      const int qi = warp * QPW + i;
-      myq[i] = qi;
-      mypos[i] = qi < nqb ? a.qpos[(qb + qi) % a.T] : -1;
-    }
-    for (int kb = k0; kb < k1; kb += SUBK) {
-      __syncthreads();
-      // stage K/V sub-tile
-      for (int idx = threadIdx.x; idx < SUBK * (D / 8); idx += blockDim.x) {
-        const int j = idx / (D / 8), ch = idx % (D / 8);
-        const int kp = kb + j;
-        uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-        if (kp < k1) {
-          size_t base;
-          if (a.block_table) {
-            const int blk = a.block_table[kp / a.block_size];
-            base = ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
-          } else {
-            base = (size_t)kp * a.nkv + g;
-          }
-          kv = reinterpret_cast<const uint4*>(a.kcache + base * D)[ch];
-          vv = reinterpret_cast<const uint4*>(a.vcache + base * D)[ch];
-        }
-        reinterpret_cast<uint4*>(Ks + j * DP)[ch] = kv;
-        reinterpret_cast<uint4*>(Vs + j * DP)[ch] = vv;
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (gq < nqv) {
+        const int hq = g * rep + gq / a.T, t = gq % a.T;
+        v = reinterpret_cast<const uint4*>(a.q + ((size_t)t * a.nq + hq) * D)[ch];
       }
-      __syncthreads();
-      const int kp = kb + lane;
+      reinterpret_cast<uint4*>(Qs + qi * DP)[ch] = v;
+    }
+    __syncthreads();
+    const int row0 = qb + warp * 16;
+    if (row0 >= nqv) continue;
+
+    // ---- S = Q K^T  (16 rows x CH keys per warp)
+    float S[NT_K][4];
 #pragma unroll
-      for (int i = 0; i < QPW; ++i) {
-        if (myq[i] >= nqb) continue;
-        // score of key `lane` for query i
-        float sc = 0.f;
-        const uint4* qrow = reinterpret_cast<const uint4*>(Qs + myq[i] * DP);
-        const uint4* krow = reinterpret_cast<const uint4*>(Ks + lane * DP);
-#pragma unroll 4
-        for (int ch = 0; ch < D / 8; ++ch) {
-          const uint4 qa = qrow[ch], kk = krow[ch];
-          const __nv_bfloat162* q2 = reinterpret_cast<const __nv_bfloat162*>(&qa);
-          const __nv_bfloat162* k2 = reinterpret_cast<const __nv_bfloat162*>(&kk);
+    for (int n = 0; n < NT_K; ++n) S[n][0] = S[n][1] = S[n][2] = S[n][3] = 0.f;
+    const uint32_t qbase = smem_u32(Qs + (warp * 16) * DP);
+    const uint32_t kbase = smem_u32(Ks);
 #pragma unroll
-          for (int u = 0; u < 4; ++u) {
-            const float2 qf = __bfloat1622float2(q2[u]), kf = __bfloat1622float2(k2[u]);
-            sc = fmaf(qf.x, kf.x, sc);
-            sc = fmaf(qf.y, kf.y, sc);
-          }
-        }
-        sc *= a.scale;
-        const bool valid = kp < k1 && (!a.causal || kp <= mypos[i]);
-        if (!valid) sc = -INFINITY;
-        const float mt = warp_max(sc);
-        const float mn = fmaxf(m[i], mt);
-        if (mn == -INFINITY) continue;     // nothing visible yet for this query
-        const float pj = valid ? __expf(sc - mn) : 0.f;
-        const float corr = __expf(m[i] - mn);
-        lsum[i] = lsum[i] * corr + warp_sum(pj);
-        m[i] = mn;
+    for (int kk = 0; kk < D / 16; ++kk) {
+      uint32_t a0, a1, a2, a3;
+      // A fragment rows 0-15, cols kk*16 .. +15
+      ldsm_x4(qbase + (uint32_t)(((lane & 15) * DP + kk * 16 + (lane >> 4) * 8) * 2), a0, a1, a2, a3);
 #pragma unroll
-        for (int d = 0; d < DPL; ++d) o[i][d] *= corr;
-        for (int j = 0; j < SUBK; ++j) {
-          const float pb = __shfl_sync(0xffffffffu, pj, j);
-          if (pb == 0.f) continue;
-          const __nv_bfloat16* vrow = Vs + j * DP + lane * DPL;
-#pragma unroll
-          for (int d = 0; d < DPL; ++d) o[i][d] = fmaf(pb, __bfloat162float(vrow[d]), o[i][d]);
-        }
+      for (int n = 0; n < NT_K; ++n) {
+        uint32_t b0, b1;
+        // B fragment (col-major 16x8): key rows n*8..n*8+7, d cols kk*16 .. +15
+        ldsm_x2(kbase + (uint32_t)(((n * 8 + (lane & 7)) * DP + kk * 16 + ((lane >> 3) & 1) * 8) * 2), b0, b1);
+        mma_bf16_16816(S[n], a0, a1, a2, a3, b0, b1);
       }
     }
-    // write partials
+    // ---- mask + row max / sum (rows r_lo = lane/4, r_hi = lane/4 + 8)
+    const int r_lo = row0 + (lane >> 2), r_hi = r_lo + 8;
+    const int p_lo = r_lo < nqv ? a.qpos[r_lo % a.T] : -1;
+    const int p_hi = r_hi < nqv ? a.qpos[r_hi % a.T] : -1;
+    float m_lo = -INFINITY, m_hi = -INFINITY;
 #pragma unroll
-    for (int i = 0; i < QPW; ++i) {
-      if (myq[i] >= nqb) continue;
-      const size_t qv = (size_t)(qb + myq[i]);
-      const size_t pidx = ((size_t)g * a.max_splits + s) * nqv + qv;
-      float* po = a.part_o + pidx * D + lane * DPL;
+    for (int n = 0; n < NT_K; ++n) {
 #pragma unroll
-      for (int d = 0; d < DPL; ++d) po[d] = o[i][d];
-      if (lane == 0) {
-        a.part_ml[pidx * 2] = m[i];
-        a.part_ml[pidx * 2 + 1] = lsum[i];
+      for (int e = 0; e < 2; ++e) {
+        const int kp = k0 + n * 8 + (lane & 3) * 2 + e;
+        const bool ok_lo = kp < k1 && (!a.causal || kp <= p_lo);
+        const bool ok_hi = kp < k1 && (!a.causal || kp <= p_hi);
+        S[n][e] = ok_lo ? S[n][e] * a.scale : -INFINITY;
+        S[n][2 + e] = ok_hi ? S[n][2 + e] * a.scale : -INFINITY;
+        m_lo = fmaxf(m_lo, S[n][e]);
+        m_hi = fmaxf(m_hi, S[n][2 + e]);
       }
+    }
+    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, 1));
+    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, 2));
+    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, 1));
+    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, 2));
+    const float mz_lo = m_lo == -INFINITY ? 0.f : m_lo;
+    const float mz_hi = m_hi == -INFINITY ? 0.f : m_hi;
+    float l_lo = 0.f, l_hi = 0.f;
+#pragma unroll
+    for (int n = 0; n < NT_K; ++n) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        S[n][e] = __expf(S[n][e] - mz_lo);
+        S[n][2 + e] = __expf(S[n][2 + e] - mz_hi);
+        l_lo += S[n][e];
+        l_hi += S[n][2 + e];
+      }
+    }
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+    l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+    l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+
+    // ---- O = P V  (P re-used from the S accumulators as bf16 A fragments)
+    float O[NT_D][4];
+#pragma unroll
+    for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;
+    const uint32_t vbase = smem_u32(Vs);
+#pragma unroll
+    for (int j = 0; j < CH / 16; ++j) {
+      const uint32_t a0 = pack_bf16(S[2 * j][0], S[2 * j][1]);
+      const uint32_t a1 = pack_bf16(S[2 * j][2], S[2 * j][3]);
+      const uint32_t a2 = pack_bf16(S[2 * j + 1][0], S[2 * j + 1][1]);
+      const uint32_t a3 = pack_bf16(S[2 * j + 1][2], S[2 * j + 1][3]);
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) {
+        uint32_t b0, b1;
+        // B (16 keys x 8 d) from row-major V via transposed ldmatrix
+        ldsm_x2_t(vbase + (uint32_t)(((j * 16 + (lane & 15)) * DP + n * 8) * 2), b0, b1);
+        mma_bf16_16816(O[n], a0, a1, a2, a3, b0, b1);
+      }
+    }
+    // ---- write partials
+    const size_t plo = ((size_t)g * a.max_splits + s) * nqv + r_lo;
+    const size_t phi = ((size_t)g * a.max_splits + s) * nqv + r_hi;
+#pragma unroll
+    for (int n = 0; n < NT_D; ++n) {
+      const int d = n * 8 + (lane & 3) * 2;
+      if (r_lo < nqv) *reinterpret_cast<float2*>(a.part_o + plo * D + d) = make_float2(O[n][0], O[n][1]);
+      if (r_hi < nqv) *reinterpret_cast<float2*>(a.part_o + phi * D + d) = make_float2(O[n][2], O[n][3]);
+    }
+    if ((lane & 3) == 0) {
+      if (r_lo < nqv) { a.part_ml[plo * 2] = m_lo; a.part_ml[plo * 2 + 1] = l_lo; }
+      if (r_hi < nqv) { a.part_ml[phi * 2] = m_hi; a.part_ml[phi * 2 + 1] = l_hi; }
     }
   }
 }
@@ -322,24 +380,19 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
   a.part_o = part_o.data_ptr<float>();
   a.part_ml = part_ml.data_ptr<float>();
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int qpw = (std::min(nqv, q38::MAXQ) + 7) / 8;
-  const size_t smem = (size_t)(2 * q38::SUBK + q38::MAXQ) * (D + 8) * 2;
+  const int warps = std::min(q38::MAXW, (nqv + 15) / 16);
+  const size_t smem = (size_t)(2 * q38::CH + warps * 16) * (D + 8) * 2;
   dim3 grid(nkv, a.max_splits);
-#define Q38_DEC(DD, QQ)                                                                                     \
+#define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
-    auto k = q38::attn_decode_kernel<DD, QQ>;                                                               \
+    auto k = q38::attn_decode_kernel<DD>;                                                                   \
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                        \
-    k<<<grid, 256, smem, st>>>(a);                                                                          \
+    k<<<grid, warps * 32, smem, st>>>(a);                                                                   \
   }
-#define Q38_DEC_D(DD)                                                   \
-  if (qpw <= 1) Q38_DEC(DD, 1) else if (qpw <= 2) Q38_DEC(DD, 2)        \
-  else if (qpw <= 4) Q38_DEC(DD, 4) else if (qpw <= 8) Q38_DEC(DD, 8)   \
-  else Q38_DEC(DD, 12)
-  if (D == 256) { Q38_DEC_D(256) }
-  else if (D == 128) { Q38_DEC_D(128) }
-  else if (D == 64) { Q38_DEC_D(64) }
+  if (D == 256) Q38_DEC(256)
+  else if (D == 128) Q38_DEC(128)
+  else if (D == 64) Q38_DEC(64)
   else TORCH_CHECK(false, "head dim 64/128/256 supported");
-#undef Q38_DEC_D
 #undef Q38_DEC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const __nv_bfloat16* gp = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;

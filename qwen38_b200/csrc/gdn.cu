@@ -72,7 +72,11 @@ gdn_recurrent_kernel(GdnArgs a) {
   const int cq = kh * D, ck = a.nk * D + kh * D, cv = 2 * a.nk * D + h * D;
   const int cz = a.C + h * D, cb = a.C + a.nv * D + h, ca = a.C + a.nv * D + a.nv + h;
 
-  __shared__ float q_s[SUB][D], k_s[SUB][D], v_s[SUB][D];
+  // q/k rows are read by the 4 threads of a column at quarter offsets: pad each quarter by 4 floats
+  // so the quarters fall in different banks.
+  constexpr int QP = RPT + 4;
+  __shared__ __align__(16) float q_s[SUB][4 * QP], k_s[SUB][4 * QP];
+  __shared__ float v_s[SUB][D];
   __shared__ float g_s[SUB], b_s[SUB];
   __shared__ float o_s[SUB][D];
   __shared__ float red_s[SUB][2][NT / 32];
@@ -96,21 +100,29 @@ gdn_recurrent_kernel(GdnArgs a) {
     return __bfloat162float(proj[(size_t)r * a.proj_ld + ch]);
   };
 
+  const int qidx = (col / RPT) * QP + (col % RPT);   // padded slot of channel `col`
   for (int r0 = 0; r0 < rows; r0 += SUB) {
     const int nsub = min(SUB, rows - r0);
     // ---- prologue: conv + silu for q/k/v channel `col`, split rows over the 4 parts
     for (int t = part; t < nsub; t += 4) {
       const int r = r0 + t;
+      float xq[KC], xk[KC], xv[KC];
+#pragma unroll
+      for (int j = 0; j < KC; ++j) {          // issue all loads before the arithmetic
+        const int rr = r - (KC - 1) + j;
+        xq[j] = x_at(rr, cq + col);
+        xk[j] = x_at(rr, ck + col);
+        xv[j] = x_at(rr, cv + col);
+      }
       float sq = 0.f, sk = 0.f, sv = 0.f;
 #pragma unroll
       for (int j = 0; j < KC; ++j) {
-        const int rr = r - (KC - 1) + j;
-        sq += wq[j] * x_at(rr, cq + col);
-        sk += wk[j] * x_at(rr, ck + col);
-        sv += wv[j] * x_at(rr, cv + col);
+        sq += wq[j] * xq[j];
+        sk += wk[j] * xk[j];
+        sv += wv[j] * xv[j];
       }
-      q_s[t][col] = silu_f(sq);
-      k_s[t][col] = silu_f(sk);
+      q_s[t][qidx] = silu_f(sq);
+      k_s[t][qidx] = silu_f(sk);
       v_s[t][col] = silu_f(sv);
     }
     if (tid < nsub) {
@@ -127,7 +139,11 @@ gdn_recurrent_kernel(GdnArgs a) {
       const int warp = tid >> 5, lane = tid & 31;
       for (int t = 0; t < nsub; ++t) {
         float pq = 0.f, pk = 0.f;
-        for (int c = tid; c < D; c += NT) { pq += q_s[t][c] * q_s[t][c]; pk += k_s[t][c] * k_s[t][c]; }
+        for (int c = tid; c < D; c += NT) {
+          const int ci = (c / RPT) * QP + (c % RPT);
+          pq += q_s[t][ci] * q_s[t][ci];
+          pk += k_s[t][ci] * k_s[t][ci];
+        }
         pq = warp_sum(pq);
         pk = warp_sum(pk);
         if (lane == 0) { red_s[t][0][warp] = pq; red_s[t][1][warp] = pk; }
@@ -142,8 +158,9 @@ gdn_recurrent_kernel(GdnArgs a) {
       __syncthreads();
       for (int t = 0; t < nsub; ++t) {
         for (int c = tid; c < D; c += NT) {
-          q_s[t][c] *= red_s[t][0][0];
-          k_s[t][c] *= red_s[t][1][0];
+          const int ci = (c / RPT) * QP + (c % RPT);
+          q_s[t][ci] *= red_s[t][0][0];
+          k_s[t][ci] *= red_s[t][1][0];
         }
       }
       __syncthreads();
@@ -155,7 +172,7 @@ gdn_recurrent_kernel(GdnArgs a) {
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
         S[i] *= decay;
-        kv += S[i] * k_s[t][part * RPT + i];
+        kv += S[i] * k_s[t][part * QP + i];
       }
       kv += __shfl_xor_sync(0xffffffffu, kv, 1);
       kv += __shfl_xor_sync(0xffffffffu, kv, 2);
@@ -163,8 +180,8 @@ gdn_recurrent_kernel(GdnArgs a) {
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
-        S[i] += k_s[t][part * RPT + i] * delta;
-        o += S[i] * q_s[t][part * RPT + i];
+        S[i] += k_s[t][part * QP + i] * delta;
+        o += S[i] * q_s[t][part * QP + i];
       }
       if constexpr (WRITE_OUT) {
         o += __shfl_xor_sync(0xffffffffu, o, 1);

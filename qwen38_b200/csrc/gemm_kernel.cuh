@@ -1,0 +1,340 @@
+// tcgen05 GEMM family for the hybrid target: D[m, n] = sum_k A[m, k] * B[n, k]  (both K-major bf16).
+//
+// One warp-specialised kernel, two roles:
+//  * swap-AB streaming (decode / verify, <= 32 token rows): A = weight [N_out, K] (the 128-row
+//    UMMA M side), B = token rows [T, K] (N = 32).  Weight tiles stream through a TMA ring at HBM
+//    rate; split-K over K blocks is reduced by the last-arriving CTA of each tile in a fixed order,
+//    so a token row's result never depends on how many rows ran with it (verify rows are bit-
+//    identical to single-row decode).
+//  * prefill tiles (> 32 rows): A = tokens [T, K], B = weight [N_out, K], 128 x 256 tiles.
+// Roles inside a 128-thread CTA: thread 0 issues TMA loads, thread 32 issues tcgen05.mma (one
+// elected thread), all four warps drain TMEM with tcgen05.ld in the epilogue.  Epilogues: bf16
+// store, fp32 store, fp32 accumulate into the residual stream, SwiGLU over [gate 64 | up 64] row
+// blocks, per-tile argmax (LM head).
+#pragma once
+#include <torch/extension.h>
+#include <ATen/cuda/CUDAContext.h>
+
+#include "common.cuh"
+
+namespace q38 {
+
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+
+struct GemmArgs {
+  int M, N, K;
+  int kblocks, kps;           // total 64-wide K blocks, K blocks per split
+  int splits;
+  void* out;
+  long long ldo;
+  float* ws;                  // split-K partials
+  int* counters;              // split-K arrival counters (left at zero)
+  int* err;
+  float* amax_val;            // EPI_ARGMAX partials [m_tiles, N]
+  int* amax_idx;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+};
+
+template <int BN, int STAGES, int EPI, bool SWAP>
+__global__ void __launch_bounds__(128, 1)
+gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs g) {
+  using S = Smem<BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
+  uint64_t* empty_bar = full_bar + STAGES;
+  uint64_t* acc_bar = empty_bar + STAGES;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
+  const int m0 = m_tile * BM, n0 = n_tile * BN;
+  const int kb0 = split * g.kps;
+  const int kb1 = min(g.kblocks, kb0 + g.kps);
+  const int nk = kb1 - kb0;
+  constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
+
+  if (tid == 0) {
+    tma_prefetch_desc(&map_a);
+    tma_prefetch_desc(&map_b);
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(acc_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (tid == 0) {
+    // ---------------- TMA producer
+    const uint64_t pol_a = SWAP ? policy_evict_first() : policy_evict_last();
+    const uint64_t pol_b = SWAP ? policy_evict_last() : policy_evict_first();
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      if (i >= STAGES) {
+        if (!mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      }
+      uint8_t* sa = smem + s * S::STAGE_BYTES;
+      uint8_t* sb = sa + S::A_BYTES;
+      mbar_expect_tx(&full_bar[s], S::STAGE_BYTES);
+      const int kx = (kb0 + i) * BK;
+      tma_load_2d_hint(sa, &map_a, &full_bar[s], kx, m0, pol_a);
+      tma_load_2d_hint(sb, &map_b, &full_bar[s], kx, n0, pol_b);
+    }
+  } else if (tid == 32) {
+    // ---------------- MMA issuer (single thread)
+    constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    for (int i = 0; i < nk; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(&full_bar[s], (i / STAGES) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      tc_fence_after();
+      const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
+      const uint32_t sb = sa + S::A_BYTES;
+      const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
+#pragma unroll
+      for (int k = 0; k < BK / 16; ++k) {
+        // advance 16 bf16 (32 B) along K inside the 128-B swizzle atom
+        umma_bf16(tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (i > 0 || k > 0) ? 1u : 0u);
+      }
+      umma_commit(&empty_bar[s]);
+    }
+    umma_commit(acc_bar);
+  }
+
+  // ---------------- epilogue: all warps
+  __syncwarp();
+  mbar_wait(acc_bar, 0, g.err, kErrMmaWait, abort_flag);
+  tc_fence_after();
+  __syncthreads();
+  const bool ok = (*abort_flag == 0);   // CTA-uniform after the barrier
+
+  const int row = warp * 32 + lane;   // TMEM lane == tile row m
+  const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
+
+  if (ok && nk > 0) {
+    if constexpr (SWAP) {
+      // Each thread owns output feature m0+row, tokens n0 .. n0+BN-1 (BN == 32).
+      static_assert(BN == 32, "swap mode uses 32 token columns");
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(trow, r);
+      tmem_ld_wait();
+      float acc[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
+
+      bool do_epi = true;
+      if (g.splits > 1) {
+        const int tile = m_tile;  // single n tile in swap mode
+        float* part = g.ws + ((size_t)tile * g.splits + split) * (BM * BN);
+#pragma unroll
+        for (int j = 0; j < 32; ++j) part[j * BM + row] = acc[j];
+        __threadfence();
+        __syncthreads();
+        if (tid == 0) {
+          const int prev = atomicAdd(&g.counters[tile], 1);
+          *last_flag = (prev == g.splits - 1);
+        }
+        __syncthreads();
+        do_epi = *last_flag != 0;
+        if (do_epi) {
+          __threadfence();
+          const float* base = g.ws + (size_t)tile * g.splits * (BM * BN);
+#pragma unroll
+          for (int j = 0; j < 32; ++j) acc[j] = 0.f;
+          for (int s = 0; s < g.splits; ++s) {
+            const volatile float* p = base + (size_t)s * (BM * BN);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] += p[j * BM + row];
+          }
+          if (tid == 0) g.counters[tile] = 0;
+        }
+      }
+      if (do_epi) {
+        const int m = m0 + row;
+        const int nvalid = min(32, g.N - n0);
+        if constexpr (EPI == EPI_SWIGLU) {
+          // rows [0,64) gate, [64,128) up of feature block m_tile; exchange up through smem
+          float* up_s = reinterpret_cast<float*>(smem);   // ring is idle now
+          if (row >= 64) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) up_s[j * 64 + (row - 64)] = acc[j];
+          }
+          __syncthreads();
+          if (row < 64) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out);
+            const int f = m_tile * 64 + row;
+            for (int j = 0; j < nvalid; ++j) {
+              const float u = up_s[j * 64 + row];
+              o[(size_t)(n0 + j) * g.ldo + f] = __float2bfloat16(silu_f(acc[j]) * u);
+            }
+          }
+        } else if constexpr (EPI == EPI_ARGMAX) {
+          // per token column: max over the 128 rows of this tile, ties -> lowest row
+          float* sv = reinterpret_cast<float*>(smem);
+          int* si = reinterpret_cast<int*>(smem + 4 * 32 * 4);
+          for (int j = 0; j < nvalid; ++j) {
+            float v = (m < g.M) ? acc[j] : -INFINITY;
+            int idx = m;
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) {
+              const float v2 = __shfl_xor_sync(0xffffffffu, v, o);
+              const int i2 = __shfl_xor_sync(0xffffffffu, idx, o);
+              if (v2 > v || (v2 == v && i2 < idx)) { v = v2; idx = i2; }
+            }
+            if (lane == 0) { sv[warp * 32 + j] = v; si[warp * 32 + j] = idx; }
+          }
+          __syncthreads();
+          if (tid < nvalid) {
+            float v = sv[tid];
+            int idx = si[tid];
+#pragma unroll
+            for (int w = 1; w < 4; ++w) {
+              const float v2 = sv[w * 32 + tid];
+              const int i2 = si[w * 32 + tid];
+              if (v2 > v || (v2 == v && i2 < idx)) { v = v2; idx = i2; }
+            }
+            g.amax_val[(size_t)m_tile * g.N + n0 + tid] = v;
+            g.amax_idx[(size_t)m_tile * g.N + n0 + tid] = idx;
+          }
+        } else {
+          if (m < g.M) {
+            for (int j = 0; j < nvalid; ++j) {
+              const size_t off = (size_t)(n0 + j) * g.ldo + m;
+              if constexpr (EPI == EPI_BF16) {
+                reinterpret_cast<__nv_bfloat16*>(g.out)[off] = __float2bfloat16(acc[j]);
+              } else if constexpr (EPI == EPI_F32) {
+                reinterpret_cast<float*>(g.out)[off] = acc[j];
+              } else {
+                reinterpret_cast<float*>(g.out)[off] += acc[j];
+              }
+            }
+          }
+        }
+      }
+    } else {
+      // Non-swap: thread owns token row m0+row, features n0 .. n0+BN-1.
+      const int m = m0 + row;
+      const bool rv = m < g.M;
+      if constexpr (EPI == EPI_SWIGLU) {
+        // BN = 256 columns = two [gate 64 | up 64] blocks -> 128 output features
+        __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ldo;
+#pragma unroll 1
+        for (int blk = 0; blk < BN / 128; ++blk) {
+#pragma unroll 1
+          for (int half = 0; half < 2; ++half) {
+            uint32_t rg[32], ru[32];
+            tmem_ld_32x32b_x32(trow + blk * 128 + half * 32, rg);
+            tmem_ld_32x32b_x32(trow + blk * 128 + 64 + half * 32, ru);
+            tmem_ld_wait();
+            const int f0 = (n0 / 2) + blk * 64 + half * 32;
+            if (rv && f0 < g.N / 2) {
+              __align__(16) __nv_bfloat16 vals[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                vals[j] = __float2bfloat16(silu_f(__uint_as_float(rg[j])) * __uint_as_float(ru[j]));
+#pragma unroll
+              for (int q = 0; q < 4; ++q)
+                reinterpret_cast<uint4*>(o + f0)[q] = reinterpret_cast<const uint4*>(vals)[q];
+            }
+          }
+        }
+      } else {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(trow + c * 32, r);
+          tmem_ld_wait();
+          const int nb = n0 + c * 32;
+          if (!rv || nb >= g.N) continue;
+          const bool full = nb + 32 <= g.N;
+          if constexpr (EPI == EPI_BF16) {
+            __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out) + (size_t)m * g.ldo + nb;
+            if (full) {
+              __align__(16) __nv_bfloat16 vals[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j) vals[j] = __float2bfloat16(__uint_as_float(r[j]));
+#pragma unroll
+              for (int q = 0; q < 4; ++q) reinterpret_cast<uint4*>(o)[q] = reinterpret_cast<const uint4*>(vals)[q];
+            } else {
+              for (int j = 0; j < g.N - nb; ++j) o[j] = __float2bfloat16(__uint_as_float(r[j]));
+            }
+          } else {
+            float* o = reinterpret_cast<float*>(g.out) + (size_t)m * g.ldo + nb;
+            if (full) {
+#pragma unroll
+              for (int q = 0; q < 8; ++q) {
+                float4 v = make_float4(__uint_as_float(r[4 * q]), __uint_as_float(r[4 * q + 1]),
+                                       __uint_as_float(r[4 * q + 2]), __uint_as_float(r[4 * q + 3]));
+                if constexpr (EPI == EPI_ADD_F32) {
+                  const float4 p = reinterpret_cast<float4*>(o)[q];
+                  v.x += p.x; v.y += p.y; v.z += p.z; v.w += p.w;
+                }
+                reinterpret_cast<float4*>(o)[q] = v;
+              }
+            } else {
+              for (int j = 0; j < g.N - nb; ++j) {
+                if constexpr (EPI == EPI_ADD_F32) o[j] += __uint_as_float(r[j]);
+                else o[j] = __uint_as_float(r[j]);
+              }
+            }
+          }
+        }
+      }
+    }
+  }
+
+  // ---------------- teardown
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 0) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+template <int BN, int STAGES, int EPI, bool SWAP>
+void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st) {
+  auto kern = gemm_tn_kernel<BN, STAGES, EPI, SWAP>;
+  constexpr int smem = Smem<BN, STAGES>::TOTAL;
+  static bool configured = false;
+  if (!configured) {
+    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess,
+                "cudaFuncSetAttribute failed");
+    configured = true;
+  }
+  kern<<<grid, 128, smem, st>>>(ma, mb, g);
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+constexpr int SKINNY_STAGES = 5;   // 5 x 20 KB ring: two CTAs per SM
+constexpr int PREFILL_BN = 256;
+constexpr int PREFILL_STAGES = 4;  // 4 x 48 KB ring
+
+// epilogue-dispatched launchers, one translation unit each
+void launch_swap(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st);
+void launch_prefill(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid,
+                    cudaStream_t st);
+
+}  // namespace q38

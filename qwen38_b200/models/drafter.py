@@ -97,6 +97,11 @@ class BlockDrafter:
         self.kctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
         self.vctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
         self.position = 0
+        self.use_graphs = target.use_graphs
+        self._graph = None
+        self._anchor_buf = torch.zeros(1, dtype=torch.long, device=dev)
+        self._pos_buf = torch.zeros(self.P, dtype=torch.int32, device=dev)
+        self._pos_host = torch.zeros(self.P, dtype=torch.int32).pin_memory() if dev.type == "cuda" else None
 
     # -------------------------------------------------------------------------------- helpers
     def _row_par(self, h, w):
@@ -135,14 +140,15 @@ class BlockDrafter:
 
     # -------------------------------------------------------------------------------- propose
     @torch.no_grad()
-    def forward_block(self, anchor: torch.Tensor):
+    def forward_block(self, anchor: torch.Tensor, positions: torch.Tensor | None = None):
         """Block forward at the current history frontier; returns local-vocab logits [P, V_l]."""
         P, pos = self.P, self.position
         hl, kvl, Dh = self.heads
         ids = torch.full((P,), self.mask_id, dtype=torch.long, device=self.device)
-        ids[0] = anchor.reshape(())
+        ids[:1] = anchor.reshape(1)
         h = self.ops.embedding(ids, self.target.embed).float()
-        positions = torch.arange(pos, pos + P, device=self.device, dtype=torch.int32)
+        if positions is None:
+            positions = torch.arange(pos, pos + P, device=self.device, dtype=torch.int32)
         for l, L in enumerate(self.layers):
             hn = self.ops.rms_norm(h, L["in_norm"], self.eps, self.dtype)
             qkv = self.ops.linear(hn, L["w_qkv"])
@@ -155,12 +161,35 @@ class BlockDrafter:
         hn = self.ops.rms_norm(h, self.norm, self.eps, self.dtype)
         return self.ops.linear(hn, self.target.lm_head, out_dtype=torch.float32)
 
-    @torch.no_grad()
-    def propose(self, anchor: torch.Tensor) -> torch.Tensor:
-        """Returns P proposal ids (device int64) for the block after ``anchor``."""
-        logits = self.forward_block(anchor)
+    def _propose_eager(self, anchor, positions=None):
+        logits = self.forward_block(anchor, positions)
         return self.ops.markov_select(logits, anchor, self.pred, self.succ, self.target.vocab_offset,
                                       self.comm if self.tp > 1 else None)
+
+    @torch.no_grad()
+    def propose(self, anchor: torch.Tensor) -> torch.Tensor:
+        """Returns P proposal ids (device int64) for the block after ``anchor`` (CUDA-graph replay
+        with static anchor/position buffers when graphs are enabled)."""
+        if not self.use_graphs:
+            return self._propose_eager(anchor)
+        if self.position + self.P > self.kctx.shape[1]:
+            raise ValueError("drafter history capacity exceeded")
+        self._anchor_buf.copy_(anchor.reshape(1))
+        self._pos_host.copy_(torch.arange(self.position, self.position + self.P, dtype=torch.int32))
+        self._pos_buf.copy_(self._pos_host, non_blocking=True)
+        if self._graph is None:
+            self._propose_eager(self._anchor_buf, self._pos_buf)          # warm-up
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            l0 = getattr(self.ops, "launches", 0)
+            with torch.cuda.graph(g):
+                out = self._propose_eager(self._anchor_buf, self._pos_buf)
+            self._graph = (g, out, getattr(self.ops, "launches", 0) - l0)
+        g, out, n = self._graph
+        g.replay()
+        if hasattr(self.ops, "launches"):
+            self.ops.launches += n
+        return out
 
     def close(self):
         self.position = 0

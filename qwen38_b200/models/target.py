@@ -114,20 +114,36 @@ def pack_mlp(src, i, cfg: ModelConfig, tp, r, device, dtype):
 
 # ------------------------------------------------------------------------------------ state
 class BlockAllocator:
-    """Free-list allocator of fixed-size KV blocks (the native C++ allocator in
-    ``qwen38_b200.runtime`` mirrors this when built)."""
+    """Reference-counted free-list allocator of fixed-size KV blocks.  A block is shared by every
+    sequence and prefix checkpoint that holds it and returns to the free list when the last holder
+    releases it."""
 
     def __init__(self, num_blocks: int):
         self.free = list(range(num_blocks - 1, -1, -1))
+        self.refs = [0] * num_blocks
         self.num_blocks = num_blocks
 
     def alloc(self, n: int) -> list:
         if n > len(self.free):
             raise MemoryError(f"KV pool exhausted: need {n} blocks, {len(self.free)} free")
-        return [self.free.pop() for _ in range(n)]
+        out = [self.free.pop() for _ in range(n)]
+        for b in out:
+            self.refs[b] = 1
+        return out
+
+    def incref(self, blocks):
+        for b in blocks:
+            if self.refs[b] <= 0:
+                raise ValueError(f"block {b} is not allocated")
+            self.refs[b] += 1
 
     def release(self, blocks):
-        self.free.extend(reversed(list(blocks)))
+        for b in reversed(list(blocks)):
+            if self.refs[b] <= 0:
+                raise ValueError(f"double release of block {b}")
+            self.refs[b] -= 1
+            if self.refs[b] == 0:
+                self.free.append(b)
 
     @property
     def num_free(self):
@@ -221,6 +237,11 @@ class HybridTarget:
         self.kcache = torch.zeros(max(La, 1), kv_blocks, bs, hkv, D, device=self.device, dtype=kvd)
         self.vcache = torch.zeros(max(La, 1), kv_blocks, bs, hkv, D, device=self.device, dtype=kvd)
         self.allocator = BlockAllocator(kv_blocks)
+        # per-slot block tables at fixed addresses (captured graphs reference them)
+        self.block_tables = torch.zeros(max_slots, self.max_blocks_per_seq, dtype=torch.int32, device=self.device)
+        self.use_graphs = bool(self.rt.use_cuda_graphs) and self.device.type == "cuda"
+        self._graphs = {}
+        self._graph_pool = None
 
     # ------------------------------------------------------------------ sequences
     def new_sequence(self) -> SeqState:
@@ -230,7 +251,8 @@ class HybridTarget:
         if hasattr(self, "rec"):
             self.rec[slot].zero_()
             self.conv[slot].zero_()
-        bt = torch.zeros(self.max_blocks_per_seq, dtype=torch.int32, device=self.device)
+        bt = self.block_tables[slot]
+        bt.zero_()
         return SeqState(slot=slot, block_table=bt)
 
     def release(self, seq: SeqState):
@@ -323,6 +345,54 @@ class HybridTarget:
     # ------------------------------------------------------------------ verify / commit
     @torch.no_grad()
     def verify(self, batch, taps=()):
+        """Uncommitted forward (CUDA-graph replay for a single sequence when enabled)."""
+        if self.use_graphs and len(batch) == 1:
+            return self._verify_graphed(batch[0][0], batch[0][1], tuple(taps))
+        return self._verify_eager(batch, taps)
+
+    def _verify_graphed(self, seq: SeqState, tokens: torch.Tensor, taps: tuple):
+        T = int(tokens.shape[0])
+        if T > self.max_verify_rows:
+            raise ValueError(f"{T} verify rows exceed max_verify_rows={self.max_verify_rows}")
+        self.reserve(seq, seq.pos + T)
+        key = (seq.slot, T, taps)
+        g = self._graphs.get(key)
+        if g is None:
+            g = self._capture_verify(seq, T, taps)
+            self._graphs[key] = g
+        g["tokens"].copy_(tokens, non_blocking=True)
+        g["pos_host"].copy_(torch.arange(seq.pos, seq.pos + T, dtype=torch.int32))
+        g["positions"].copy_(g["pos_host"], non_blocking=True)
+        seq.verify_rows = (0, T)
+        g["graph"].replay()
+        if hasattr(self.ops, "launches"):
+            self.ops.launches += g["launches"]
+        return g["pred"], g["feats"]
+
+    def _capture_verify(self, seq: SeqState, T: int, taps: tuple):
+        dev = self.device
+        tokens = torch.zeros(T, dtype=torch.long, device=dev)
+        positions = torch.arange(seq.pos, seq.pos + T, dtype=torch.int32, device=dev)
+        pos_host = torch.zeros(T, dtype=torch.int32).pin_memory()
+        saved = seq.pos, seq.verify_rows
+        # eager warm-up on the static buffers (kernel attributes, tensor-map caches)
+        self._verify_eager([(seq, tokens)], taps, positions=positions)
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        l0 = getattr(self.ops, "launches", 0)
+        with torch.cuda.graph(graph):
+            pred, feats = self._verify_eager([(seq, tokens)], taps, positions=positions)
+        launches = getattr(self.ops, "launches", 0) - l0
+        seq.pos, seq.verify_rows = saved
+        return dict(graph=graph, tokens=tokens, positions=positions, pos_host=pos_host, pred=pred, feats=feats,
+                    launches=launches)
+
+    def _pool(self):
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        return self._graph_pool
+
+    def _verify_eager(self, batch, taps=(), positions=None):
         """Uncommitted forward.  ``batch``: list of (SeqState, tokens [T_s]) with the tokens at
         positions ``seq.pos ..``.  Returns (argmax [sum T_s] int64, taps [sum T_s, n*H] or None)."""
         rows = sum(int(t.shape[0]) for _, t in batch)
@@ -334,8 +404,9 @@ class HybridTarget:
             seq.verify_rows = (off, int(t.shape[0]))
             off += int(t.shape[0])
         tokens = torch.cat([t for _, t in batch]) if len(batch) > 1 else batch[0][1]
-        positions = torch.cat([self.positions(s.pos, t.shape[0]) for s, t in batch]) if len(batch) > 1 else \
-            self.positions(batch[0][0].pos, batch[0][1].shape[0])
+        if positions is None:
+            positions = torch.cat([self.positions(s.pos, t.shape[0]) for s, t in batch]) if len(batch) > 1 else \
+                self.positions(batch[0][0].pos, batch[0][1].shape[0])
         feats = self._tap_buffer(rows, taps)
         tap_pos = {t: j for j, t in enumerate(taps)}
         x = self.ops.embedding(tokens, self.embed).float()
@@ -404,6 +475,35 @@ class HybridTarget:
             snap["rec"] = self.rec[seq.slot].clone()
             snap["conv"] = self.conv[seq.slot].clone()
         return snap
+
+    def prefix_snapshot(self, seq: SeqState, pos: int) -> dict:
+        """Checkpoint of the first ``pos`` committed tokens: GDN state + conv window (copies) and
+        the KV blocks below ``pos`` (shared, reference-counted).  ``pos`` must equal the committed
+        length and sit on a KV block boundary."""
+        if pos != seq.pos or pos % self.block_size:
+            raise ValueError("prefix snapshots are taken at the committed frontier on a block boundary")
+        blocks = list(seq.blocks[:pos // self.block_size])
+        self.allocator.incref(blocks)
+        snap = self.snapshot(seq)
+        snap["blocks"] = blocks
+        snap["nbytes"] = sum(t.numel() * t.element_size() for k, t in snap.items() if torch.is_tensor(t))
+        return snap
+
+    def release_prefix(self, snap: dict):
+        self.allocator.release(snap.get("blocks", []))
+        snap["blocks"] = []
+
+    def sequence_from_prefix(self, snap: dict) -> SeqState:
+        """New sequence whose first ``snap['pos']`` tokens reuse the checkpoint's KV blocks and
+        state; later positions get blocks of their own."""
+        seq = self.new_sequence()
+        blocks = list(snap["blocks"])
+        self.allocator.incref(blocks)
+        seq.blocks = blocks
+        if blocks:
+            seq.block_table[:len(blocks)] = torch.tensor(blocks, dtype=torch.int32, device=self.device)
+        self.restore(seq, snap)
+        return seq
 
     def restore(self, seq: SeqState, snap: dict):
         if hasattr(self, "rec"):

@@ -144,7 +144,7 @@ class NativeOps(TorchOps):
         key = (nkv, nqv, D)
         b = self._attn_bufs.get(key)
         if b is None:
-            splits = -(-self.max_keys // 256)
+            splits = -(-self.max_keys // 128)   # 128-key chunks (csrc/attention.cu CH)
             b = (torch.empty(nkv * splits * nqv * D, dtype=torch.float32, device=self.device),
                  torch.empty(nkv * splits * nqv * 2, dtype=torch.float32, device=self.device))
             self._attn_bufs[key] = b

@@ -68,8 +68,9 @@ class NeuralAdapter:
 
 
 class SpecRuntime:
-    def __init__(self, target, drafter=None, *, verifier_rows: int = 16, lookup: bool = False):
+    def __init__(self, target, drafter=None, *, verifier_rows: int = 16, lookup: bool = False, prefix=None):
         self.target, self.drafter = target, drafter
+        self.prefix = prefix                       # optional PrefixRegistry
         self.verifier_rows = verifier_rows
         self.lookup = lookup
         self.taps = tuple(drafter.dcfg.taps) if drafter is not None else ()
@@ -105,15 +106,13 @@ class SpecRuntime:
                                           dtype=torch.long)
             if tgt.device.type == "cuda":
                 prompt_host = prompt_host.pin_memory()
-        seq = tgt.new_sequence()
+        seq = None
+        ck = None
         try:
             t0 = self._event()
             prompt_dev = prompt_host.to(tgt.device, non_blocking=True)
             self.h2d_bytes += prompt_host.numel() * 8
-            nxt, feats = tgt.prefill(seq, prompt_dev, taps=self.taps)
-            if self.drafter is not None:
-                self.drafter.reset()
-                self.drafter.append(feats, 0)
+            seq, nxt, ck = self._prefill(prompt_host, prompt_dev)
             seed = int(nxt.item())
             self.d2h_bytes += 8
             t1 = self._event()
@@ -159,10 +158,52 @@ class SpecRuntime:
                 pp_tok_s=prompt_host.numel() / (pp_ms / 1e3), committed=committed,
                 tg_tok_s=committed / (tg_ms / 1e3) if tg_ms > 0 else float("nan"), blocks=len(blocks),
                 mean_accepted=sum(b[1] for b in blocks) / max(1, len(blocks)),
-                tokens_per_block=committed / max(1, len(blocks)))
+                tokens_per_block=committed / max(1, len(blocks)), reused_prefix=ck.pos if ck else 0)
         finally:
-            tgt.release(seq)
+            if ck is not None:
+                self.prefix.unpin(ck)
+            if seq is not None:
+                tgt.release(seq)
             self.session = None
+
+    def _prefill(self, prompt_host, prompt_dev):
+        """Prefill through the prefix registry when attached: restore the longest exact checkpoint,
+        prefill the rest in boundary-aligned segments and capture a checkpoint at each boundary."""
+        tgt, dr = self.target, self.drafter
+        n = int(prompt_host.numel())
+        toks = None
+        ck = None
+        if self.prefix is not None:
+            toks = prompt_host.tolist()
+            ck = self.prefix.lookup(toks)
+        if ck is not None:
+            self.prefix.pin(ck)
+            seq = self.prefix.restore(ck, dr)
+            start = ck.pos
+        else:
+            seq = tgt.new_sequence()
+            start = 0
+            if dr is not None:
+                dr.reset()
+        try:
+            cuts = [n]
+            if self.prefix is not None:
+                b = self.prefix.boundary
+                cuts = [p for p in range((start // b + 1) * b, n, b)] + [n]
+            nxt, cur = None, start
+            for end in cuts:
+                nxt, feats = tgt.prefill(seq, prompt_dev[cur:end], taps=self.taps)
+                if dr is not None:
+                    dr.append(feats, cur)
+                if self.prefix is not None and end < n:
+                    self.prefix.capture(seq, toks, dr)
+                cur = end
+            return seq, nxt, ck
+        except BaseException:
+            if ck is not None:
+                self.prefix.unpin(ck)
+            tgt.release(seq)
+            raise
 
 
 def greedy_reference(target, prompt, max_new_tokens, eos=None):

@@ -1,0 +1,152 @@
+"""Kernel micro-benchmarks with roofline fractions.
+
+Times one native kernel in isolation with CUDA events on the launching stream (warm-up, an L2
+flush of 256 MB between timed iterations, synchronise on both sides) and reports the achieved
+bandwidth / throughput against the measured peaks (``MEASURED_PEAKS.json`` at the repo root;
+6.65 TB/s and 1.59 PFLOP/s as fallback).
+
+    python -m qwen38_b200.utils.kbench gemm --T 16 --N 5120 --K 17408
+    python -m qwen38_b200.utils.kbench gemm --T 4096 --N 34816 --K 5120 --epi swiglu
+    python -m qwen38_b200.utils.kbench gdn --T 16 --nv 48
+    python -m qwen38_b200.utils.kbench attn --T 16 --ctx 4096
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def time_kernel(fn, iters=20, warmup=3, flush=True):
+    flush_buf = torch.empty(64 << 20, dtype=torch.float32, device="cuda") if flush else None
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(iters):
+        if flush_buf is not None:
+            flush_buf.zero_()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    times.sort()
+    return times[len(times) // 2]
+
+
+def bench_gemm(a):
+    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU, NativeOps
+    ops = NativeOps()
+    x = torch.randn(a.T, a.K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(a.N, a.K, device="cuda") * 0.02).to(torch.bfloat16)
+    if a.epi == "swiglu":
+        fn = lambda: ops.linear_swiglu(x, w, 64)
+    elif a.epi == "add":
+        res = torch.zeros(a.T, a.N, device="cuda")
+        fn = lambda: ops.linear_residual(x, w, res)
+    else:
+        fn = lambda: ops.linear(x, w)
+    if a.iters == 0:            # single launch (profiler captures)
+        fn()
+        torch.cuda.synchronize()
+        ops.check()
+        return {}
+    ms = time_kernel(fn, a.iters)
+    ops.check()
+    hbm, tf, src = peaks()
+    flops = 2.0 * a.T * a.N * a.K
+    bytes_ = a.N * a.K * 2 + a.T * a.K * 2 + a.T * a.N * (2 if a.epi != "add" else 8)
+    out = {"kernel": "gemm", "T": a.T, "N": a.N, "K": a.K, "epi": a.epi, "ms": round(ms, 4),
+           "tflops": round(flops / ms / 1e9, 1), "gbs": round(bytes_ / ms / 1e6, 1)}
+    out[f"frac_bw_of_{src}"] = round(bytes_ / ms / 1e6 / hbm, 3)
+    out[f"frac_tc_of_{src}"] = round(flops / ms / 1e9 / tf, 3)
+    if a.compare:
+        ref = lambda: x @ w.t()
+        out["cublas_ms"] = round(time_kernel(ref, a.iters), 4)
+    return out
+
+
+def bench_gdn(a):
+    from ..ops.native import NativeOps
+    ops = NativeOps()
+    nk, nv, D = a.nv // 3, a.nv, 128
+    C = 2 * nk * D + nv * D
+    proj = torch.randn(a.T, C + nv * D + 2 * nv, device="cuda").to(torch.bfloat16)
+    window = torch.randn(3, C, device="cuda").to(torch.bfloat16)
+    state = torch.randn(nv, D, D, device="cuda") * 0.1
+    conv_w = torch.rand(C, 4, device="cuda") - 0.5
+    A_log = torch.rand(nv, device="cuda")
+    dt = torch.ones(nv, device="cuda")
+    nw = torch.ones(D, device="cuda")
+    fn = lambda: ops.gdn_verify(proj, window, state, conv_w, A_log, dt, nw, 1e-6, (nk, nv, D, D), torch.bfloat16)
+    if a.iters == 0:
+        fn()
+        torch.cuda.synchronize()
+        return {}
+    ms = time_kernel(fn, a.iters)
+    bytes_ = state.numel() * 4 + proj.numel() * 2
+    hbm, tf, src = peaks()
+    return {"kernel": "gdn_verify", "T": a.T, "nv": nv, "ms": round(ms, 4), "gbs": round(bytes_ / ms / 1e6, 1),
+            f"frac_bw_of_{src}": round(bytes_ / ms / 1e6 / hbm, 3)}
+
+
+def bench_attn(a):
+    from ..ops.native import NativeOps
+    ops = NativeOps(max_keys=a.ctx + 64)
+    H, Hkv, D, bs = a.heads, a.kv_heads, 256, 16
+    nb = (a.ctx + a.T) // bs + 2
+    kc = torch.randn(nb, bs, Hkv, D, device="cuda").to(torch.bfloat16)
+    vc = torch.randn(nb, bs, Hkv, D, device="cuda").to(torch.bfloat16)
+    bt = torch.arange(nb, dtype=torch.int32, device="cuda")
+    q = torch.randn(a.T, H, D, device="cuda").to(torch.bfloat16)
+    gate = torch.randn(a.T, H * D, device="cuda").to(torch.bfloat16)
+    pos = torch.arange(a.ctx, a.ctx + a.T, dtype=torch.int32, device="cuda")
+    fn = lambda: ops.attn_decode(q, gate, kc, vc, bt, pos, bs, torch.bfloat16)
+    if a.iters == 0:
+        fn()
+        torch.cuda.synchronize()
+        return {}
+    ms = time_kernel(fn, a.iters)
+    bytes_ = 2 * (a.ctx + a.T) * Hkv * D * 2
+    flops = 4.0 * a.T * H * (a.ctx + a.T) * D
+    hbm, tf, src = peaks()
+    return {"kernel": "attn_decode", "T": a.T, "ctx": a.ctx, "ms": round(ms, 4), "gbs": round(bytes_ / ms / 1e6, 1),
+            "tflops": round(flops / ms / 1e9, 2), f"frac_bw_of_{src}": round(bytes_ / ms / 1e6 / hbm, 3)}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("kind", choices=["gemm", "gdn", "attn"])
+    ap.add_argument("--T", type=int, default=16)
+    ap.add_argument("--N", type=int, default=5120)
+    ap.add_argument("--K", type=int, default=17408)
+    ap.add_argument("--epi", default="bf16", choices=["bf16", "add", "swiglu"])
+    ap.add_argument("--nv", type=int, default=48)
+    ap.add_argument("--ctx", type=int, default=4096)
+    ap.add_argument("--heads", type=int, default=24)
+    ap.add_argument("--kv-heads", type=int, default=4)
+    ap.add_argument("--iters", type=int, default=20)
+    ap.add_argument("--compare", action="store_true", help="also time torch/cuBLAS for the same GEMM")
+    a = ap.parse_args()
+    out = {"gemm": bench_gemm, "gdn": bench_gdn, "attn": bench_attn}[a.kind](a)
+    if out:
+        print(json.dumps(out))
+
+
+if __name__ == "__main__":
+    main()

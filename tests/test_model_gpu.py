@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():
     pytest.skip("needs a CUDA device", allow_module_level=True)
 
-from qwen38_b200.checkpoint import materialize, random_drafter_source, random_target_source  # noqa: E402
+from qwen38_b200.checkpoint import DictSource, materialize, random_drafter_source, random_target_source  # noqa: E402
 from qwen38_b200.config import (FULL, LINEAR, DrafterConfig, ModelConfig, RuntimeConfig,  # noqa: E402
                                 tiny_drafter_config, tiny_model_config)
 from qwen38_b200.models.drafter import BlockDrafter  # noqa: E402
@@ -43,9 +43,11 @@ def test_tiny_native_speculative_equals_greedy(nops):
 
 
 def test_tiny_native_prefill_close_to_reference(nops):
-    tgt = _tiny_target(nops)
-    cfg = tgt.cfg
-    ref = ReferenceModel(cfg, materialize(random_target_source(cfg, 0)))
+    cfg = tiny_model_config()
+    sd = materialize(random_target_source(cfg, 0))          # generated on the CPU, shared by both
+    rt = RuntimeConfig(max_context=1024, prefill_chunk=64, gdn_chunk=16)
+    tgt = HybridTarget(cfg, DictSource(sd), rt, device="cuda", dtype=torch.bfloat16, ops=nops)
+    ref = ReferenceModel(cfg, sd)
     toks = torch.randint(0, cfg.vocab_size, (150,), generator=torch.Generator().manual_seed(1))
     logits, taps, hn = ref.step(toks, ref.new_state(), taps=(3,))
     seq = tgt.new_sequence()

@@ -1,0 +1,76 @@
+"""Prefix reuse (BASELINE config 4 on the tiny shape): a request whose prefix matches an earlier
+one restores KV blocks + GDN state + drafter history at the boundary and prefills only the
+suffix; output, GDN state and logits equal a cold full prefill exactly."""
+import pytest
+import torch
+
+from qwen38_b200.config import RuntimeConfig
+from qwen38_b200.models.drafter import BlockDrafter
+from qwen38_b200.models.target import HybridTarget
+from qwen38_b200.prefix.registry import KillSwitch, PrefixRegistry
+from qwen38_b200.spec.engine import SpecRuntime, greedy_reference
+
+RT = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
+
+
+def _prompts(tiny):
+    g = torch.Generator().manual_seed(7)
+    prefix = torch.randint(0, 4096, (128,), generator=g).tolist()
+    a = prefix + torch.randint(0, 4096, (100,), generator=g).tolist()
+    b = prefix + torch.randint(0, 4096, (90,), generator=g).tolist()
+    return a, b
+
+
+def test_prefix_reuse_is_exact(tiny):
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RT, max_slots=2)
+    dr = BlockDrafter(tiny["dcfg"], tiny["dsrc"], tgt)
+    a, b = _prompts(tiny)
+    gold_b = greedy_reference(tgt, b, 24)
+    # cold reference state after prefill of b
+    seq = tgt.new_sequence()
+    cold_next, _ = tgt.prefill(seq, torch.tensor(b))
+    cold_rec = tgt.rec[seq.slot].clone()
+    tgt.release(seq)
+
+    reg = PrefixRegistry(tgt, budget_bytes=1 << 30, boundary=64)
+    sr = SpecRuntime(tgt, dr, verifier_rows=4, prefix=reg)
+    ra = sr.generate(a, 24)
+    assert ra["reused_prefix"] == 0 and reg.stats["captures"] == 3        # boundaries 64, 128, 192
+    rb = sr.generate(b, 24, gold_check=gold_b)
+    assert rb["reused_prefix"] == 128 and rb["tokens"] == gold_b
+    assert reg.stats["hits"] == 1
+
+    # restored + suffix prefill reproduces the cold state bit for bit
+    ck = reg.lookup(b)
+    seq = reg.restore(ck, dr)
+    warm_next, _ = tgt.prefill(seq, torch.tensor(b[128:]))
+    assert int(warm_next) == int(cold_next)
+    assert torch.equal(tgt.rec[seq.slot], cold_rec)
+    tgt.release(seq)
+
+
+def test_registry_budget_pins_and_kill_switch(tiny, tmp_path):
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RT, max_slots=2)
+    a, b = _prompts(tiny)
+    reg = PrefixRegistry(tgt, budget_bytes=1 << 30, boundary=64)
+    seq = tgt.new_sequence()
+    tgt.prefill(seq, torch.tensor(a[:64]))
+    ck1 = reg.capture(seq, a)
+    tgt.prefill(seq, torch.tensor(a[64:128]))
+    ck2 = reg.capture(seq, a)
+    assert reg.lookup(b).pos == 128
+    free_before = tgt.allocator.num_free
+    tgt.release(seq)
+    assert tgt.allocator.num_free == free_before          # blocks still held by the checkpoints
+    reg.budget = ck2.nbytes                                 # room for one: the LRU entry goes
+    reg.pin(ck2)
+    reg._enforce_budget()
+    assert ck1.key not in reg.entries and ck2.key in reg.entries
+    reg.unpin(ck2)
+    flag = tmp_path / "off"
+    reg.kill = KillSwitch(str(flag), poll_s=0.0)
+    assert reg.lookup(b) is not None
+    flag.write_text("1")
+    assert reg.lookup(b) is None and reg.export_stats()["disabled"]
+    reg.clear()
+    assert tgt.allocator.num_free == tgt.allocator.num_blocks
