@@ -37,6 +37,8 @@ struct PrepArgs {
 };
 
 __global__ void attn_prep_kernel(PrepArgs a) {
+  pdl_wait();
+  pdl_trigger();
   const int t = blockIdx.x;
   const int hh = blockIdx.y;        // [0, nq) q heads, [nq, nq+nkv) kv heads
   const int c = threadIdx.x;        // channel
@@ -143,6 +145,8 @@ attn_decode_kernel(DecodeArgs a) {
   constexpr int DP = D + 8;                 // padded row: conflict-free ldmatrix
   constexpr int NT_K = CH / 8;              // key n-tiles per chunk
   constexpr int NT_D = D / 8;               // output n-tiles
+  pdl_wait();
+  pdl_trigger();
   const int g = blockIdx.x, s = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rep = a.nq / a.nkv;
@@ -291,6 +295,8 @@ attn_decode_kernel(DecodeArgs a) {
 
 __global__ void attn_combine_kernel(DecodeArgs a, const __nv_bfloat16* gate, long long gate_ld, int gate_off,
                                     __nv_bfloat16* out, long long out_ld) {
+  pdl_wait();
+  pdl_trigger();
   const int hq = blockIdx.x, t = blockIdx.y;
   const int D = a.D;
   const int rep = a.nq / a.nkv;
@@ -350,7 +356,7 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
   a.block_size = (int)block_size;
   const int T = (int)proj.size(0);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  q38::attn_prep_kernel<<<dim3(T, (unsigned)(nq + nkv)), (unsigned)D, D * sizeof(float), st>>>(a);
+  q38::launch_pdl(q38::attn_prep_kernel, dim3(T, (unsigned)(nq + nkv)), dim3((unsigned)D), D * sizeof(float), st, a);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -380,14 +386,14 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
   a.part_o = part_o.data_ptr<float>();
   a.part_ml = part_ml.data_ptr<float>();
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int warps = std::min(q38::MAXW, (nqv + 15) / 16);
+  const int warps = std::max(4, std::min(q38::MAXW, (nqv + 15) / 16));   // >= 4 warps to stage K/V
   const size_t smem = (size_t)(2 * q38::CH + warps * 16) * (D + 8) * 2;
   dim3 grid(nkv, a.max_splits);
 #define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
     auto k = q38::attn_decode_kernel<DD>;                                                                   \
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                        \
-    k<<<grid, warps * 32, smem, st>>>(a);                                                                   \
+    q38::launch_pdl(k, grid, dim3(warps * 32), smem, st, a);                                               \
   }
   if (D == 256) Q38_DEC(256)
   else if (D == 128) Q38_DEC(128)
@@ -396,8 +402,8 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
 #undef Q38_DEC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const __nv_bfloat16* gp = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
-  q38::attn_combine_kernel<<<dim3(nq, T), std::min(D, 256), 0, st>>>(
-      a, gp, gate ? gate->stride(0) : 0, (int)gate_off, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-      out.stride(0));
+  q38::launch_pdl(q38::attn_combine_kernel, dim3(nq, T), dim3(std::min(D, 256)), 0, st, a, gp,
+                  (long long)(gate ? gate->stride(0) : 0), (int)gate_off,
+                  reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

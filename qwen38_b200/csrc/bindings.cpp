@@ -1,9 +1,9 @@
 // Python bindings of the qwen38_b200 sm_100a kernels.
 #include <torch/extension.h>
 
-void q38_linear(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, torch::Tensor ws,
+void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi, torch::Tensor ws,
                 torch::Tensor counters, torch::Tensor err);
-void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, torch::Tensor out_val, torch::Tensor out_idx,
+void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
                         torch::Tensor counters, torch::Tensor err);
 void q38_clear_map_cache();
@@ -20,6 +20,10 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
                      torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+void q38_gdn_chunk_prefill(torch::Tensor proj, torch::Tensor window, torch::Tensor state, torch::Tensor conv_w,
+                           torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor out,
+                           torch::Tensor work, int64_t nk, int64_t nv, double eps);
+size_t q38_gdn_chunk_workspace_bytes(int64_t S, int64_t nv);
 void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
 void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
@@ -32,6 +36,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("lm_head_argmax", &q38_lm_head_argmax);
   m.def("clear_map_cache", &q38_clear_map_cache);
   m.def("gdn_recurrent", &q38_gdn_recurrent);
+  m.def("gdn_chunk_prefill", &q38_gdn_chunk_prefill);
+  m.def("gdn_chunk_workspace_bytes", &q38_gdn_chunk_workspace_bytes);
   m.def("attn_prep", &q38_attn_prep);
   m.def("attn_decode", &q38_attn_decode);
   m.def("rms_norm", &q38_rms_norm);

@@ -59,14 +59,14 @@ gdn_recurrent_kernel(GdnArgs a) {
   const int rep = a.nv / a.nk;
   const int kh = h / rep;
 
-  const __nv_bfloat16* proj = a.proj + layer * a.proj_layer_stride;
-  const __nv_bfloat16* window = a.window + layer * a.win_layer_stride;
-  float* state = a.state + layer * a.state_layer_stride + (size_t)h * D * D;
-  const float* conv_w = a.conv_w + layer * a.convw_layer_stride;
+  const __nv_bfloat16* __restrict__ proj = a.proj + layer * a.proj_layer_stride;
+  const __nv_bfloat16* __restrict__ window = a.window + layer * a.win_layer_stride;
+  float* __restrict__ state = a.state + layer * a.state_layer_stride + (size_t)h * D * D;
+  const float* __restrict__ conv_w = a.conv_w + layer * a.convw_layer_stride;
+  __nv_bfloat16* __restrict__ outp = a.out;
   const float A = -__expf(a.A_log[layer * a.nv + h]);
   const float dtb = a.dt_bias[layer * a.nv + h];
   const float* norm_w = a.norm_w + layer * D;
-  const int rows = a.rows_dev ? *a.rows_dev : a.rows;
 
   // channel offsets of this head inside [q | k | v | z | b | a]
   const int cq = kh * D, ck = a.nk * D + kh * D, cv = 2 * a.nk * D + h * D;
@@ -81,12 +81,7 @@ gdn_recurrent_kernel(GdnArgs a) {
   __shared__ float o_s[SUB][D];
   __shared__ float red_s[SUB][2][NT / 32];
 
-  // state registers
-  float S[RPT];
-#pragma unroll
-  for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + col];
-
-  // conv taps for the three channels this thread may evaluate (q/k/v channel `col`)
+  // conv taps are static; everything else may come from the previous kernel
   float wq[KC], wk[KC], wv[KC];
 #pragma unroll
   for (int j = 0; j < KC; ++j) {
@@ -94,6 +89,15 @@ gdn_recurrent_kernel(GdnArgs a) {
     wk[j] = conv_w[(size_t)(ck + col) * KC + j];
     wv[j] = conv_w[(size_t)(cv + col) * KC + j];
   }
+  pdl_wait();
+  pdl_trigger();
+  const int rows = a.rows_dev ? *a.rows_dev : a.rows;
+
+  // state registers
+  float S[RPT];
+#pragma unroll
+  for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + col];
+
 
   auto x_at = [&](int r, int ch) -> float {   // r in [-(K-1), rows)
     if (r < 0) return __bfloat162float(window[(size_t)(r + KC - 1) * a.C + ch]);
@@ -104,7 +108,10 @@ gdn_recurrent_kernel(GdnArgs a) {
   for (int r0 = 0; r0 < rows; r0 += SUB) {
     const int nsub = min(SUB, rows - r0);
     // ---- prologue: conv + silu for q/k/v channel `col`, split rows over the 4 parts
-    for (int t = part; t < nsub; t += 4) {
+#pragma unroll
+    for (int tt = 0; tt < SUB / 4; ++tt) {
+      const int t = part + 4 * tt;
+      if (t >= nsub) break;
       const int r = r0 + t;
       float xq[KC], xk[KC], xv[KC];
 #pragma unroll
@@ -206,12 +213,22 @@ gdn_recurrent_kernel(GdnArgs a) {
         red_s[tid][1][0] = rsqrtf(s / D + a.eps);
       }
       __syncthreads();
-      for (int idx = tid; idx < nsub * D; idx += NT) {
+      constexpr int PER = (SUB * D + NT - 1) / NT;
+      float zv[PER];
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {            // issue every z load before any store
+        const int idx = tid + u * NT;
         const int t = idx / D, c = idx % D;
-        const int r = r0 + t;
-        const float z = __bfloat162float(proj[(size_t)r * a.proj_ld + cz + c]);
-        const float y = o_s[t][c] * red_s[t][1][0] * norm_w[c] * silu_f(z);
-        a.out[(size_t)r * a.out_ld + (size_t)h * D + c] = __float2bfloat16(y);
+        zv[u] = (t < nsub) ? __bfloat162float(proj[(size_t)(r0 + t) * a.proj_ld + cz + c]) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < PER; ++u) {
+        const int idx = tid + u * NT;
+        const int t = idx / D, c = idx % D;
+        if (t < nsub) {
+          const float y = o_s[t][c] * red_s[t][1][0] * norm_w[c] * silu_f(zv[u]);
+          outp[(size_t)(r0 + t) * a.out_ld + (size_t)h * D + c] = __float2bfloat16(y);
+        }
       }
     }
     __syncthreads();
@@ -229,6 +246,8 @@ __global__ void gdn_window_kernel(const __nv_bfloat16* __restrict__ proj, long l
                                   int C, int rows, const int* rows_dev) {
   const int layer = blockIdx.y;
   const int ch = blockIdx.x * blockDim.x + threadIdx.x;
+  pdl_wait();
+  pdl_trigger();
   if (ch >= C) return;
   const int n = rows_dev ? *rows_dev : rows;
   if (n <= 0) return;
@@ -287,9 +306,9 @@ void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, t
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   dim3 grid((unsigned)nv, (unsigned)layers);
 #define Q38_GDN_LAUNCH(DD)                                                                              \
-  if (mode == 0) q38::gdn_recurrent_kernel<DD, 4, 16, true, false><<<grid, 4 * DD, 0, st>>>(a);          \
-  else if (mode == 1) q38::gdn_recurrent_kernel<DD, 4, 16, false, true><<<grid, 4 * DD, 0, st>>>(a);     \
-  else q38::gdn_recurrent_kernel<DD, 4, 16, true, true><<<grid, 4 * DD, 0, st>>>(a);
+  if (mode == 0) q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, true, false>, grid, dim3(4 * DD), 0, st, a); \
+  else if (mode == 1) q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, false, true>, grid, dim3(4 * DD), 0, st, a); \
+  else q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, true, true>, grid, dim3(4 * DD), 0, st, a);
   if (D == 128) { Q38_GDN_LAUNCH(128) }
   else if (D == 32) { Q38_GDN_LAUNCH(32) }
   else TORCH_CHECK(false, "GDN head dim 32 or 128 supported");
@@ -297,9 +316,9 @@ void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, t
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   if (mode != 0) {
     dim3 g2((unsigned)((C + 255) / 256), (unsigned)layers);
-    q38::gdn_window_kernel<4><<<g2, 256, 0, st>>>(a.proj, a.proj_ld, a.proj_layer_stride,
-                                                  reinterpret_cast<__nv_bfloat16*>(window.data_ptr()),
-                                                  a.win_layer_stride, C, (int)rows, a.rows_dev);
+    q38::launch_pdl(q38::gdn_window_kernel<4>, g2, dim3(256), 0, st, a.proj, a.proj_ld, a.proj_layer_stride,
+                    reinterpret_cast<__nv_bfloat16*>(window.data_ptr()), a.win_layer_stride, C, (int)rows,
+                    a.rows_dev);
     C10_CUDA_KERNEL_LAUNCH_CHECK();
   }
 }

@@ -8,10 +8,21 @@
 
 namespace q38 {
 
+bool pdl_enabled() {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = getenv("Q38_PDL");      // opt-in: measured slower on the verify chain
+    on = (e && e[0] == '1') ? 1 : 0;
+  }
+  return on == 1;
+}
+
 // Final reduction of per-tile argmax partials: out_idx[n] = argmax over tiles (ties -> lower index)
 __global__ void argmax_finalize_kernel(const float* __restrict__ val, const int* __restrict__ idx, int tiles, int N,
                                        long long vocab_offset, float* __restrict__ out_val,
                                        int64_t* __restrict__ out_idx) {
+  pdl_wait();
+  pdl_trigger();
   const int n = blockIdx.x;
   float best = -INFINITY;
   int bi = 0x7fffffff;
@@ -127,13 +138,16 @@ static int num_sms() {
 }
 
 // out (m, n) layout: swap -> out[n * ldo + m]; prefill -> out[m * ldo + n]
-void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor& out, int epi, const Scratch& sc,
-                   float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr) {
+// `w` is a tile-contiguous weight ([ceil(N/128) * ceil(K/64) * 128, 64], see tile_weight in
+// qwen38_b200/ops/native.py) of logical shape [N, K].
+void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
+                   const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
-  TORCH_CHECK(x.dim() == 2 && w.dim() == 2 && x.size(1) == w.size(1), "x [T,K], w [N,K] required");
-  TORCH_CHECK(x.stride(1) == 1 && w.stride(1) == 1, "K-contiguous operands required");
-  const int T = (int)x.size(0), K = (int)x.size(1), N = (int)w.size(0);
+  TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
+  const int T = (int)x.size(0), K = (int)x.size(1);
+  TORCH_CHECK(w.dim() == 2 && w.size(1) == BK && w.is_contiguous(), "tile-contiguous weight [rows, 64] required");
+  TORCH_CHECK(w.size(0) == (int64_t)((N + BM - 1) / BM) * ((K + BK - 1) / BK) * BM, "weight tiling mismatch");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   GemmArgs g{};
   g.K = K;
@@ -163,7 +177,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
       g.amax_idx = amax_idx;
       *amax_tiles = m_tiles;
     }
-    CUtensorMap ma = cached_map(w, BM, true);
+    CUtensorMap ma = cached_map(w, BM, true);      // one 16 KB weight tile per box
     CUtensorMap mb = cached_map(x, 32, false);
     dim3 grid(m_tiles, 1, splits);
     launch_swap(epi, ma, mb, g, grid, st);
@@ -175,7 +189,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
     g.kps = g.kblocks;
     if (epi == EPI_SWIGLU) TORCH_CHECK(N % PREFILL_BN == 0, "SwiGLU prefill needs N % 256 == 0");
     CUtensorMap ma = cached_map(x, BM, false);
-    CUtensorMap mb = cached_map(w, PREFILL_BN, true);
+    CUtensorMap mb = cached_map(w, BM, true);      // two 16 KB weight tiles per 256-row stage
     dim3 grid((T + BM - 1) / BM, (N + PREFILL_BN - 1) / PREFILL_BN, 1);
     launch_prefill(epi, ma, mb, g, grid, st);
   }
@@ -184,7 +198,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, torch::Tensor
 }  // namespace q38
 
 // ----------------------------------------------------------------------------- bindings
-void q38_linear(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi, torch::Tensor ws,
+void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi, torch::Tensor ws,
                 torch::Tensor counters, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(x.device());
   auto sc = q38::scratch_of(ws, counters, err);
@@ -194,25 +208,27 @@ void q38_linear(torch::Tensor x, torch::Tensor w, torch::Tensor out, int64_t epi
     TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 output required");
   }
   TORCH_CHECK(out.stride(1) == 1, "row-contiguous output required");
-  q38::gemm_dispatch(x, w, out, (int)epi, sc);
+  q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc);
 }
 
-void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, torch::Tensor out_val, torch::Tensor out_idx,
+void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
                         torch::Tensor counters, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(x.device());
   auto sc = q38::scratch_of(ws, counters, err);
   const int T = (int)x.size(0);
   TORCH_CHECK(T <= 32, "LM-head argmax serves <= 32 rows");
-  const int tiles_needed = (int)((w.size(0) + 127) / 128);
+  const int tiles_needed = (int)((N + 127) / 128);
   TORCH_CHECK(part_val.numel() >= (int64_t)tiles_needed * T && part_idx.numel() >= (int64_t)tiles_needed * T,
               "argmax partial buffers too small");
   int tiles = 0;
   torch::Tensor dummy = out_val;  // not written by the argmax epilogue
-  q38::gemm_dispatch(x, w, dummy, q38::EPI_ARGMAX, sc, part_val.data_ptr<float>(), part_idx.data_ptr<int>(), &tiles);
+  q38::gemm_dispatch(x, w, (int)N, dummy, q38::EPI_ARGMAX, sc, part_val.data_ptr<float>(), part_idx.data_ptr<int>(),
+                     &tiles);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  q38::argmax_finalize_kernel<<<T, 256, 0, st>>>(part_val.data_ptr<float>(), part_idx.data_ptr<int>(), tiles, T,
-                                                 vocab_offset, out_val.data_ptr<float>(), out_idx.data_ptr<int64_t>());
+  q38::launch_pdl(q38::argmax_finalize_kernel, dim3(T), dim3(256), 0, st, (const float*)part_val.data_ptr<float>(),
+                  (const int*)part_idx.data_ptr<int>(), tiles, T, (long long)vocab_offset, out_val.data_ptr<float>(),
+                  out_idx.data_ptr<int64_t>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -86,24 +86,51 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (tid == 0) pdl_trigger();
 
   if (tid == 0) {
     // ---------------- TMA producer
-    const uint64_t pol_a = SWAP ? policy_evict_first() : policy_evict_last();
-    const uint64_t pol_b = SWAP ? policy_evict_last() : policy_evict_first();
-    for (int i = 0; i < nk; ++i) {
-      const int s = i % STAGES;
-      if (i >= STAGES) {
-        if (!mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
+    // Weights are stored tile-contiguous (wtile row (t * kblocks + kb) * 128 + r holds weight row
+    // 128 t + r, columns 64 kb ..): every weight tile is one contiguous 16 KB block.  The weight
+    // operand (A in swap mode, B otherwise) is static, so its first STAGES tiles are requested
+    // before waiting for the previous kernel; activation tiles after.
+    const uint64_t pol_w = policy_evict_first();
+    const uint64_t pol_x = policy_evict_last();
+    auto load_w = [&](int stage, int kb) {
+      uint8_t* sa = smem + stage * S::STAGE_BYTES;
+      if constexpr (SWAP) {
+        tma_load_2d_hint(sa, &map_a, &full_bar[stage], 0, (m_tile * g.kblocks + kb) * BM, pol_w);
+      } else {
+        uint8_t* sb = sa + S::A_BYTES;
+#pragma unroll
+        for (int j = 0; j < BN / BM; ++j)
+          tma_load_2d_hint(sb + j * (BM * BK * 2), &map_b, &full_bar[stage], 0,
+                           ((n_tile * (BN / BM) + j) * g.kblocks + kb) * BM, pol_w);
       }
-      uint8_t* sa = smem + s * S::STAGE_BYTES;
-      uint8_t* sb = sa + S::A_BYTES;
-      mbar_expect_tx(&full_bar[s], S::STAGE_BYTES);
-      const int kx = (kb0 + i) * BK;
-      tma_load_2d_hint(sa, &map_a, &full_bar[s], kx, m0, pol_a);
-      tma_load_2d_hint(sb, &map_b, &full_bar[s], kx, n0, pol_b);
+    };
+    auto load_x = [&](int stage, int kb) {
+      uint8_t* sa = smem + stage * S::STAGE_BYTES;
+      if constexpr (SWAP) tma_load_2d_hint(sa + S::A_BYTES, &map_b, &full_bar[stage], kb * BK, n0, pol_x);
+      else tma_load_2d_hint(sa, &map_a, &full_bar[stage], kb * BK, m0, pol_x);
+    };
+    const int pre = nk < STAGES ? nk : STAGES;
+    for (int i = 0; i < pre; ++i) {
+      mbar_expect_tx(&full_bar[i], S::STAGE_BYTES);
+      load_w(i, kb0 + i);
     }
-  } else if (tid == 32) {
+    pdl_wait();
+    for (int i = 0; i < pre; ++i) load_x(i, kb0 + i);
+    for (int i = pre; i < nk; ++i) {
+      const int s = i % STAGES;
+      if (!mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      mbar_expect_tx(&full_bar[s], S::STAGE_BYTES);
+      load_w(s, kb0 + i);
+      load_x(s, kb0 + i);
+    }
+  } else {
+    pdl_wait();     // nothing upstream is read or written before this point
+  }
+  if (tid == 32) {
     // ---------------- MMA issuer (single thread)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     for (int i = 0; i < nk; ++i) {
@@ -324,8 +351,7 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g
                 "cudaFuncSetAttribute failed");
     configured = true;
   }
-  kern<<<grid, 128, smem, st>>>(ma, mb, g);
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
+  TORCH_CHECK(launch_pdl(kern, grid, dim3(128), (size_t)smem, st, ma, mb, g) == cudaSuccess, "GEMM launch failed");
 }
 
 constexpr int SKINNY_STAGES = 5;   // 5 x 20 KB ring: two CTAs per SM

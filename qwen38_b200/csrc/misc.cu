@@ -13,41 +13,52 @@
 
 namespace q38 {
 
-template <typename TIn>
-__global__ void rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restrict__ w, int H,
-                                float eps, __nv_bfloat16* __restrict__ out, long long ldo) {
+// One CTA per row; the row stays in registers between the sum of squares and the scaling.
+template <typename TIn, int VPT>
+__global__ void __launch_bounds__(256)
+rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restrict__ w, int H, float eps,
+                __nv_bfloat16* __restrict__ out, long long ldo) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const TIn* xr = x + (size_t)r * ldx;
   __shared__ float red[32];
+  float v[VPT];
   float ss = 0.f;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v;
-    if constexpr (std::is_same<TIn, float>::value) v = xr[i];
-    else v = __bfloat162float(xr[i]);
-    ss += v * v;
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = threadIdx.x + u * blockDim.x;
+    float f = 0.f;
+    if (i < H) {
+      if constexpr (std::is_same<TIn, float>::value) f = xr[i];
+      else f = __bfloat162float(xr[i]);
+    }
+    v[u] = f;
+    ss += f * f;
   }
   ss = warp_sum(ss);
   const int w_ = threadIdx.x >> 5, l = threadIdx.x & 31;
   if (l == 0) red[w_] = ss;
   __syncthreads();
-  if (threadIdx.x == 0) {
-    float s = 0.f;
-    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) s += red[i];
-    red[31] = rsqrtf(s / H + eps);
+  if (threadIdx.x < 32) {
+    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+    t = warp_sum(t);
+    if (threadIdx.x == 0) red[31] = rsqrtf(t / H + eps);
   }
   __syncthreads();
   const float inv = red[31];
   __nv_bfloat16* o = out + (size_t)r * ldo;
-  for (int i = threadIdx.x; i < H; i += blockDim.x) {
-    float v;
-    if constexpr (std::is_same<TIn, float>::value) v = xr[i];
-    else v = __bfloat162float(xr[i]);
-    o[i] = __float2bfloat16(v * inv * w[i]);
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = threadIdx.x + u * blockDim.x;
+    if (i < H) o[i] = __float2bfloat16(v[u] * inv * w[i]);
   }
 }
 
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int H,
                              float* __restrict__ out) {
+  pdl_wait();
+  pdl_trigger();
   const int r = blockIdx.x;
   const int64_t id = ids[r];
   const __nv_bfloat16* src = table + (size_t)id * H;
@@ -72,6 +83,8 @@ markov_step_kernel(const float* __restrict__ logits, const __nv_bfloat16* __rest
   extern __shared__ float pp[];   // [R]
   __shared__ float sv[8];
   __shared__ int si[8];
+  pdl_wait();
+  pdl_trigger();
   const int64_t pv = *prev;
   for (int i = threadIdx.x; i < R; i += blockDim.x) pp[i] = __bfloat162float(pred[(size_t)pv * R + i]);
   __syncthreads();
@@ -112,6 +125,8 @@ markov_step_kernel(const float* __restrict__ logits, const __nv_bfloat16* __rest
 __global__ void markov_finalize_kernel(const float* __restrict__ part_val, const int* __restrict__ part_idx,
                                        int tiles, long long vocab_offset, int64_t* __restrict__ prev,
                                        int64_t* __restrict__ out, float* __restrict__ out_val) {
+  pdl_wait();
+  pdl_trigger();
   float best = -INFINITY;
   int bi = 0x7fffffff;
   for (int t = threadIdx.x; t < tiles; t += blockDim.x) {
@@ -148,15 +163,24 @@ void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor ou
   const int R = (int)x.size(0), H = (int)x.size(1);
   if (R == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  const int threads = H >= 2048 ? 512 : 256;
-  if (x.scalar_type() == at::kFloat)
-    q38::rms_norm_kernel<float><<<R, threads, 0, st>>>(x.data_ptr<float>(), x.stride(0), w.data_ptr<float>(), H,
-                                                        (float)eps, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
-                                                        out.stride(0));
-  else
-    q38::rms_norm_kernel<__nv_bfloat16><<<R, threads, 0, st>>>(
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), x.stride(0), w.data_ptr<float>(), H, (float)eps,
-        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), out.stride(0));
+  TORCH_CHECK(H <= 256 * 32, "rms_norm: hidden too large");
+  const int vpt = (H + 255) / 256;
+#define Q38_NORM(VV)                                                                                        \
+  if (x.scalar_type() == at::kFloat)                                                                        \
+    q38::launch_pdl(q38::rms_norm_kernel<float, VV>, dim3(R), dim3(256), 0, st, (const float*)x.data_ptr<float>(), \
+        (long long)x.stride(0), (const float*)w.data_ptr<float>(), H, (float)eps,                          \
+        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));                        \
+  else                                                                                                      \
+    q38::launch_pdl(q38::rms_norm_kernel<__nv_bfloat16, VV>, dim3(R), dim3(256), 0, st,                     \
+        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0),                       \
+        (const float*)w.data_ptr<float>(), H, (float)eps, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),  \
+        (long long)out.stride(0));
+  if (vpt <= 1) { Q38_NORM(1) }
+  else if (vpt <= 4) { Q38_NORM(4) }
+  else if (vpt <= 8) { Q38_NORM(8) }
+  else if (vpt <= 20) { Q38_NORM(20) }
+  else { Q38_NORM(32) }
+#undef Q38_NORM
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -167,8 +191,9 @@ void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out) {
   const int R = (int)ids.numel(), H = (int)table.size(1);
   TORCH_CHECK(H % 8 == 0, "hidden must be a multiple of 8");
   if (R == 0) return;
-  q38::embed_kernel<<<R, 256, 0, at::cuda::getCurrentCUDAStream()>>>(
-      ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()), H, out.data_ptr<float>());
+  q38::launch_pdl(q38::embed_kernel, dim3(R), dim3(256), 0, at::cuda::getCurrentCUDAStream(),
+                  (const int64_t*)ids.data_ptr<int64_t>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+                  H, out.data_ptr<float>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
@@ -182,14 +207,14 @@ void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor
   const int tiles = (V + 255) / 256;
   TORCH_CHECK(part_val.numel() >= tiles, "partial buffer too small");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  q38::markov_step_kernel<<<tiles, 256, R * sizeof(float), st>>>(
-      logits_row.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(pred.data_ptr()),
-      reinterpret_cast<const __nv_bfloat16*>(succ.data_ptr()), V, R, prev.data_ptr<int64_t>(),
+  q38::launch_pdl(q38::markov_step_kernel, dim3(tiles), dim3(256), R * sizeof(float), st,
+      (const float*)logits_row.data_ptr<float>(), reinterpret_cast<const __nv_bfloat16*>(pred.data_ptr()),
+      reinterpret_cast<const __nv_bfloat16*>(succ.data_ptr()), V, R, (const int64_t*)prev.data_ptr<int64_t>(),
       part_val.data_ptr<float>(), part_idx.data_ptr<int>());
   C10_CUDA_KERNEL_LAUNCH_CHECK();
-  q38::markov_finalize_kernel<<<1, 256, 0, st>>>(part_val.data_ptr<float>(), part_idx.data_ptr<int>(), tiles,
-                                                 vocab_offset, write_prev ? prev.data_ptr<int64_t>() : nullptr,
-                                                 out.data_ptr<int64_t>(),
-                                                 out_val ? out_val->data_ptr<float>() : nullptr);
+  q38::launch_pdl(q38::markov_finalize_kernel, dim3(1), dim3(256), 0, st, (const float*)part_val.data_ptr<float>(),
+                  (const int*)part_idx.data_ptr<int>(), tiles, (long long)vocab_offset,
+                  write_prev ? prev.data_ptr<int64_t>() : (int64_t*)nullptr, out.data_ptr<int64_t>(),
+                  out_val ? out_val->data_ptr<float>() : (float*)nullptr);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

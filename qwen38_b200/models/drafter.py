@@ -38,7 +38,8 @@ def _heads_split(n_heads, n_kv, tp, r):
 
 
 class BlockDrafter:
-    def __init__(self, dcfg: DrafterConfig, src, target: HybridTarget, *, max_context: int | None = None):
+    def __init__(self, dcfg: DrafterConfig, src, target: HybridTarget, *, max_context: int | None = None,
+                 slots: int = 1):
         self.dcfg, self.target = dcfg, target
         self.ops, self.comm = target.ops, target.comm
         self.device, self.dtype = target.device, target.dtype
@@ -61,7 +62,8 @@ class BlockDrafter:
             raise ValueError("fc input width must divide by TP")
         kl = kin // tp
         fc = get("fc.weight")
-        self.fc = fc[:, r * kl:(r + 1) * kl].contiguous()
+        self.fc = self.ops.prepare_weight(fc[:, r * kl:(r + 1) * kl].contiguous())
+        del fc
         self.fc_k = (r * kl, kl)
         self.hidden_norm = f32("hidden_norm.weight")
         self.norm = f32("norm.weight")
@@ -77,14 +79,15 @@ class BlockDrafter:
             g = get(p + "mlp.gate_proj.weight")[r * il:(r + 1) * il]
             u = get(p + "mlp.up_proj.weight")[r * il:(r + 1) * il]
             gu = torch.stack([g.reshape(il // GU_BLOCK, GU_BLOCK, H), u.reshape(il // GU_BLOCK, GU_BLOCK, H)], 1)
+            pw = self.ops.prepare_weight
             self.layers.append(dict(
-                w_qkv=torch.cat([wq, wk, wv], 0).contiguous(),
-                w_kv=torch.cat([wk, wv], 0).contiguous(),
-                w_o=get(p + "self_attn.o_proj.weight")[:, r * hl * Dh:(r + 1) * hl * Dh].contiguous(),
+                w_qkv=pw(torch.cat([wq, wk, wv], 0).contiguous()),
+                w_kv=pw(torch.cat([wk, wv], 0).contiguous()),
+                w_o=pw(get(p + "self_attn.o_proj.weight")[:, r * hl * Dh:(r + 1) * hl * Dh].contiguous()),
                 qn=f32(p + "self_attn.q_norm.weight"), kn=f32(p + "self_attn.k_norm.weight"),
                 in_norm=f32(p + "input_layernorm.weight"), post_norm=f32(p + "post_attention_layernorm.weight"),
-                w_gu=gu.reshape(2 * il, H).contiguous(),
-                w_down=get(p + "mlp.down_proj.weight")[:, r * il:(r + 1) * il].contiguous(),
+                w_gu=pw(gu.reshape(2 * il, H).contiguous()),
+                w_down=pw(get(p + "mlp.down_proj.weight")[:, r * il:(r + 1) * il].contiguous()),
             ))
         vl = target.widths["vocab"]
         self.pred = get("markov_head.markov_w1.weight").contiguous()                 # [V, R] replicated
@@ -94,14 +97,33 @@ class BlockDrafter:
         self.inv_freq, self.rope_scale = inv.to(dev), scale
         self.max_context = max_context or target.rt.max_context
         cap = self.max_context + 2 * dcfg.block_rows
-        self.kctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
-        self.vctx = torch.zeros(dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
-        self.position = 0
+        # one projected K/V history per slot (a request being served owns one slot)
+        self.slots = slots
+        self.kctx_all = torch.zeros(slots, dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
+        self.vctx_all = torch.zeros(slots, dcfg.num_hidden_layers, cap, kvl, Dh, device=dev, dtype=dt)
+        self.positions = [0] * slots
         self.use_graphs = target.use_graphs
-        self._graph = None
-        self._anchor_buf = torch.zeros(1, dtype=torch.long, device=dev)
-        self._pos_buf = torch.zeros(self.P, dtype=torch.int32, device=dev)
+        self._graphs = {}
+        self._anchor_buf = torch.zeros(slots, 1, dtype=torch.long, device=dev)
+        self._pos_buf = torch.zeros(slots, self.P, dtype=torch.int32, device=dev)
         self._pos_host = torch.zeros(self.P, dtype=torch.int32).pin_memory() if dev.type == "cuda" else None
+
+    # slot-0 views (single-stream API)
+    @property
+    def kctx(self):
+        return self.kctx_all[0]
+
+    @property
+    def vctx(self):
+        return self.vctx_all[0]
+
+    @property
+    def position(self):
+        return self.positions[0]
+
+    @position.setter
+    def position(self, v):
+        self.positions[0] = v
 
     # -------------------------------------------------------------------------------- helpers
     def _row_par(self, h, w):
@@ -117,15 +139,15 @@ class BlockDrafter:
         return self.ops.rms_norm(part, self.hidden_norm, self.eps, self.dtype)
 
     # -------------------------------------------------------------------------------- history
-    def reset(self):
-        self.position = 0
+    def reset(self, slot: int = 0):
+        self.positions[slot] = 0
 
     @torch.no_grad()
-    def append(self, feats: torch.Tensor, pos: int):
+    def append(self, feats: torch.Tensor, pos: int, slot: int = 0):
         """Project ``feats`` [n, taps*H] (target rows at positions pos..pos+n-1) into every layer's
-        K/V history."""
-        if pos != self.position:
-            raise ValueError(f"drafter history at {self.position}, publication at {pos}")
+        K/V history of ``slot``."""
+        if pos != self.positions[slot]:
+            raise ValueError(f"drafter history at {self.positions[slot]}, publication at {pos}")
         n = feats.shape[0]
         if pos + n > self.max_context:
             raise ValueError("drafter history capacity exceeded")
@@ -135,14 +157,14 @@ class BlockDrafter:
         for l, L in enumerate(self.layers):
             kv = self.ops.linear(ctx, L["w_kv"])
             self.ops.kv_append(kv, L["kn"], self.inv_freq, self.rope_scale, Dh, kvl, Dh, self.eps, positions,
-                               self.kctx[l], self.vctx[l])
-        self.position = pos + n
+                               self.kctx_all[slot, l], self.vctx_all[slot, l])
+        self.positions[slot] = pos + n
 
     # -------------------------------------------------------------------------------- propose
     @torch.no_grad()
-    def forward_block(self, anchor: torch.Tensor, positions: torch.Tensor | None = None):
+    def forward_block(self, anchor: torch.Tensor, positions: torch.Tensor | None = None, slot: int = 0):
         """Block forward at the current history frontier; returns local-vocab logits [P, V_l]."""
-        P, pos = self.P, self.position
+        P, pos = self.P, self.positions[slot]
         hl, kvl, Dh = self.heads
         ids = torch.full((P,), self.mask_id, dtype=torch.long, device=self.device)
         ids[:1] = anchor.reshape(1)
@@ -153,7 +175,8 @@ class BlockDrafter:
             hn = self.ops.rms_norm(h, L["in_norm"], self.eps, self.dtype)
             qkv = self.ops.linear(hn, L["w_qkv"])
             o = self.ops.draft_block_attention(qkv, L["qn"], L["kn"], self.inv_freq, self.rope_scale, self.heads,
-                                               self.eps, positions, self.kctx[l], self.vctx[l], self.dtype)
+                                               self.eps, positions, self.kctx_all[slot, l],
+                                               self.vctx_all[slot, l], self.dtype)
             h += self._row_par(o, L["w_o"])
             hn = self.ops.rms_norm(h, L["post_norm"], self.eps, self.dtype)
             gu = self.ops.linear_swiglu(hn, L["w_gu"], GU_BLOCK)
@@ -161,35 +184,37 @@ class BlockDrafter:
         hn = self.ops.rms_norm(h, self.norm, self.eps, self.dtype)
         return self.ops.linear(hn, self.target.lm_head, out_dtype=torch.float32)
 
-    def _propose_eager(self, anchor, positions=None):
-        logits = self.forward_block(anchor, positions)
+    def _propose_eager(self, anchor, positions=None, slot: int = 0):
+        logits = self.forward_block(anchor, positions, slot)
         return self.ops.markov_select(logits, anchor, self.pred, self.succ, self.target.vocab_offset,
                                       self.comm if self.tp > 1 else None)
 
     @torch.no_grad()
-    def propose(self, anchor: torch.Tensor) -> torch.Tensor:
+    def propose(self, anchor: torch.Tensor, slot: int = 0) -> torch.Tensor:
         """Returns P proposal ids (device int64) for the block after ``anchor`` (CUDA-graph replay
         with static anchor/position buffers when graphs are enabled)."""
         if not self.use_graphs:
-            return self._propose_eager(anchor)
-        if self.position + self.P > self.kctx.shape[1]:
+            return self._propose_eager(anchor, None, slot)
+        pos = self.positions[slot]
+        if pos + self.P > self.kctx_all.shape[2]:
             raise ValueError("drafter history capacity exceeded")
-        self._anchor_buf.copy_(anchor.reshape(1))
-        self._pos_host.copy_(torch.arange(self.position, self.position + self.P, dtype=torch.int32))
-        self._pos_buf.copy_(self._pos_host, non_blocking=True)
-        if self._graph is None:
-            self._propose_eager(self._anchor_buf, self._pos_buf)          # warm-up
+        ab, pb = self._anchor_buf[slot], self._pos_buf[slot]
+        ab.copy_(anchor.reshape(1))
+        self._pos_host.copy_(torch.arange(pos, pos + self.P, dtype=torch.int32))
+        pb.copy_(self._pos_host, non_blocking=True)
+        if slot not in self._graphs:
+            self._propose_eager(ab, pb, slot)          # warm-up
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             l0 = getattr(self.ops, "launches", 0)
             with torch.cuda.graph(g):
-                out = self._propose_eager(self._anchor_buf, self._pos_buf)
-            self._graph = (g, out, getattr(self.ops, "launches", 0) - l0)
-        g, out, n = self._graph
+                out = self._propose_eager(ab, pb, slot)
+            self._graphs[slot] = (g, out, getattr(self.ops, "launches", 0) - l0)
+        g, out, n = self._graphs[slot]
         g.replay()
         if hasattr(self.ops, "launches"):
             self.ops.launches += n
         return out
 
-    def close(self):
-        self.position = 0
+    def close(self, slot: int = 0):
+        self.positions[slot] = 0

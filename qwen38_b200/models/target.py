@@ -183,7 +183,8 @@ class HybridTarget:
         head = self.embed if cfg.tie_word_embeddings else src.get("lm_head.weight", device=self.device, dtype=dtype)
         vl = self.widths["vocab"]
         self.vocab_offset = r * vl
-        self.lm_head = head[r * vl:(r + 1) * vl].contiguous()
+        self.lm_head = self.ops.prepare_weight(head[r * vl:(r + 1) * vl].contiguous())
+        del head
         self.final_norm = (1.0 + src.get("model.norm.weight", **f32).float()).contiguous()
         self.layers = []
         for i, t in enumerate(cfg.layer_types):
@@ -193,6 +194,8 @@ class HybridTarget:
             L.update(pack_mlp(src, i, cfg, tp, r, self.device, dtype))
             L["in_norm"] = (1.0 + src.get(pfx + "input_layernorm.weight", **f32).float()).contiguous()
             L["post_norm"] = (1.0 + src.get(pfx + "post_attention_layernorm.weight", **f32).float()).contiguous()
+            for key in ("w_in", "w_out", "w_gu", "w_down"):
+                L[key] = self.ops.prepare_weight(L[key])
             self.layers.append(L)
         self.gdn_index = {i: j for j, i in enumerate(cfg.linear_layers)}
         self.attn_index = {i: j for j, i in enumerate(cfg.full_layers)}

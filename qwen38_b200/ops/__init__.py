@@ -17,6 +17,10 @@ class TorchOps:
     name = "torch"
 
     # ---- GEMM family: y = x @ w^T ------------------------------------------------
+    def prepare_weight(self, w):
+        """Storage layout of a GEMM weight for this op set (identity here)."""
+        return w
+
     def linear(self, x, w, out_dtype=None):
         y = x @ w.t()
         return y if out_dtype is None else y.to(out_dtype)

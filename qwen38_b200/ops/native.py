@@ -21,6 +21,37 @@ class KernelError(RuntimeError):
     pass
 
 
+class TiledWeight:
+    """A GEMM weight of logical shape [N, K] stored tile-contiguous for the tcgen05 kernels:
+    tile (n // 128, k // 64) is one contiguous 16 KB block, so every TMA load of a weight tile is
+    a single contiguous stream.  Rows / columns are zero-padded to multiples of 128 / 64."""
+    __slots__ = ("t", "N", "K")
+
+    def __init__(self, t, N, K):
+        self.t, self.N, self.K = t, N, K
+
+    @property
+    def shape(self):
+        return (self.N, self.K)
+
+
+def tile_weight(w: torch.Tensor) -> TiledWeight:
+    N, K = w.shape
+    NT, KB = -(-N // 128), -(-K // 64)
+    if N % 128 or K % 64:
+        wp = torch.zeros(NT * 128, KB * 64, dtype=w.dtype, device=w.device)
+        wp[:N, :K] = w
+    else:
+        wp = w
+    t = wp.reshape(NT, 128, KB, 64).permute(0, 2, 1, 3).contiguous().view(NT * KB * 128, 64)
+    return TiledWeight(t, N, K)
+
+
+def untile_weight(tw: TiledWeight) -> torch.Tensor:
+    NT, KB = -(-tw.N // 128), -(-tw.K // 64)
+    return tw.t.view(NT, KB, 128, 64).permute(0, 2, 1, 3).reshape(NT * 128, KB * 64)[:tw.N, :tw.K]
+
+
 _ERR_NAMES = {1: "TMA/mbarrier wait timeout", 2: "accumulator wait timeout", 4: "split-K fix-up timeout",
               8: "peer flag timeout", 16: "unsupported shape"}
 
@@ -43,6 +74,8 @@ class NativeOps(TorchOps):
         self._attn_bufs = {}
         self.rows_dev = torch.zeros(1, dtype=torch.int32, device=dev)
         self.launches = 0
+        self.chunked_prefill = True
+        self._gdn_work = None
 
     # ------------------------------------------------------------------ errors
     def check(self):
@@ -54,38 +87,45 @@ class NativeOps(TorchOps):
             raise KernelError(f"device error word {e}: {', '.join(names)}")
 
     # ------------------------------------------------------------------ GEMMs
+    def prepare_weight(self, w):
+        return w if isinstance(w, TiledWeight) else tile_weight(w.to(torch.bfloat16).contiguous())
+
     def linear(self, x, w, out_dtype=None):
+        w = self.prepare_weight(w)
         x = x.contiguous()
-        T, N = x.shape[0], w.shape[0]
+        T, N = x.shape[0], w.N
         if out_dtype == torch.float32:
             out = torch.empty(T, N, dtype=torch.float32, device=x.device)
-            self.C.linear(x, w, out, EPI_F32, self.ws, self.counters, self.err)
+            self.C.linear(x, w.t, N, out, EPI_F32, self.ws, self.counters, self.err)
         else:
             out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
-            self.C.linear(x, w, out, EPI_BF16, self.ws, self.counters, self.err)
+            self.C.linear(x, w.t, N, out, EPI_BF16, self.ws, self.counters, self.err)
         self.launches += 1
         return out
 
     def linear_residual(self, x, w, residual):
-        self.C.linear(x.contiguous(), w, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
+        w = self.prepare_weight(w)
+        self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
         self.launches += 1
         return residual
 
     def linear_swiglu(self, x, w_gu, block):
         if block != 64:
             raise ValueError("the SwiGLU epilogue pairs 64-row gate/up blocks")
+        w_gu = self.prepare_weight(w_gu)
         x = x.contiguous()
-        out = torch.empty(x.shape[0], w_gu.shape[0] // 2, dtype=torch.bfloat16, device=x.device)
-        self.C.linear(x, w_gu, out, EPI_SWIGLU, self.ws, self.counters, self.err)
+        out = torch.empty(x.shape[0], w_gu.N // 2, dtype=torch.bfloat16, device=x.device)
+        self.C.linear(x, w_gu.t, w_gu.N, out, EPI_SWIGLU, self.ws, self.counters, self.err)
         self.launches += 1
         return out
 
     def lm_head_argmax(self, x, w, vocab_offset=0):
+        w = self.prepare_weight(w)
         x = x.contiguous()
         T = x.shape[0]
         val = torch.empty(T, dtype=torch.float32, device=x.device)
         idx = torch.empty(T, dtype=torch.int64, device=x.device)
-        self.C.lm_head_argmax(x, w, val, idx, int(vocab_offset), self.amax_val, self.amax_idx, self.ws,
+        self.C.lm_head_argmax(x, w.t, w.N, val, idx, int(vocab_offset), self.amax_val, self.amax_idx, self.ws,
                               self.counters, self.err)
         self.launches += 2
         return val, idx
@@ -116,9 +156,26 @@ class NativeOps(TorchOps):
         return out
 
     def gdn_prefill(self, proj, window, state, conv_w, A_log, dt_bias, norm_w, eps, dims, chunk, out_dtype):
+        """Committed prefill: the chunked tensor-core kernels for head dim 128, the sequential
+        recurrence otherwise (small test shapes)."""
         nk, nv, dk, dv = dims
-        out = torch.empty(proj.shape[0], nv * dv, dtype=torch.bfloat16, device=proj.device)
-        self.C.gdn_recurrent(2, proj, window, state, conv_w, A_log, dt_bias, norm_w, out, proj.shape[0], None,
+        S = proj.shape[0]
+        out = torch.empty(S, nv * dv, dtype=torch.bfloat16, device=proj.device)
+        if dk == 128 and dv == 128 and self.chunked_prefill:
+            need = int(self.C.gdn_chunk_workspace_bytes(S, nv))
+            if self._gdn_work is None or self._gdn_work.numel() < need:
+                self._gdn_work = torch.empty(need, dtype=torch.uint8, device=proj.device)
+            C = conv_w.shape[0]
+            self.C.gdn_chunk_prefill(proj, window, state, conv_w, A_log, dt_bias, norm_w, out, self._gdn_work,
+                                     nk, nv, float(eps))
+            K1 = window.shape[0]
+            if S >= K1:
+                window.copy_(proj[S - K1:, :C])
+            else:
+                window.copy_(torch.cat([window[S:], proj[:, :C]], 0))
+            self.launches += 4
+            return out
+        self.C.gdn_recurrent(2, proj, window, state, conv_w, A_log, dt_bias, norm_w, out, S, None,
                              nk, nv, dk, float(eps))
         self.launches += 2
         return out

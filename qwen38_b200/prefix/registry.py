@@ -122,7 +122,7 @@ class PrefixRegistry:
         self._enforce_budget()
 
     # ---------------------------------------------------------------- capture
-    def capture(self, seq, tokens, drafter=None) -> Checkpoint | None:
+    def capture(self, seq, tokens, drafter=None, dslot: int = 0) -> Checkpoint | None:
         """Checkpoint ``seq`` at its committed length (a boundary multiple)."""
         pos = seq.pos
         if pos <= 0 or pos % self.boundary:
@@ -142,9 +142,9 @@ class PrefixRegistry:
         dsnap = None
         nbytes = snap["nbytes"]
         if drafter is not None:
-            if drafter.position < pos:
+            if drafter.positions[dslot] < pos:
                 raise ValueError("drafter history behind the target at capture")
-            dsnap = {"k": drafter.kctx[:, :pos].clone(), "v": drafter.vctx[:, :pos].clone()}
+            dsnap = {"k": drafter.kctx_all[dslot, :, :pos].clone(), "v": drafter.vctx_all[dslot, :, :pos].clone()}
             nbytes += 2 * dsnap["k"].numel() * dsnap["k"].element_size()
         if nbytes > self.budget:
             self.target.release_prefix(snap)
@@ -159,13 +159,13 @@ class PrefixRegistry:
         self._enforce_budget()
         return ck
 
-    def restore(self, ck: Checkpoint, drafter=None):
+    def restore(self, ck: Checkpoint, drafter=None, dslot: int = 0):
         """New target sequence at ``ck.pos`` (and the drafter history rewound to the same rows)."""
         seq = self.target.sequence_from_prefix(ck.target)
         if drafter is not None and ck.drafter is not None:
-            drafter.kctx[:, :ck.pos].copy_(ck.drafter["k"])
-            drafter.vctx[:, :ck.pos].copy_(ck.drafter["v"])
-            drafter.position = ck.pos
+            drafter.kctx_all[dslot, :, :ck.pos].copy_(ck.drafter["k"])
+            drafter.vctx_all[dslot, :, :ck.pos].copy_(ck.drafter["v"])
+            drafter.positions[dslot] = ck.pos
         return seq
 
     # ---------------------------------------------------------------- eviction

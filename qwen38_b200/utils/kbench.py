@@ -53,7 +53,8 @@ def bench_gemm(a):
     from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU, NativeOps
     ops = NativeOps()
     x = torch.randn(a.T, a.K, device="cuda").to(torch.bfloat16)
-    w = (torch.randn(a.N, a.K, device="cuda") * 0.02).to(torch.bfloat16)
+    w_plain = (torch.randn(a.N, a.K, device="cuda") * 0.02).to(torch.bfloat16)
+    w = ops.prepare_weight(w_plain)              # tile-contiguous storage, done once at load time
     if a.epi == "swiglu":
         fn = lambda: ops.linear_swiglu(x, w, 64)
     elif a.epi == "add":
@@ -76,7 +77,7 @@ def bench_gemm(a):
     out[f"frac_bw_of_{src}"] = round(bytes_ / ms / 1e6 / hbm, 3)
     out[f"frac_tc_of_{src}"] = round(flops / ms / 1e9 / tf, 3)
     if a.compare:
-        ref = lambda: x @ w.t()
+        ref = lambda: x @ w_plain.t()
         out["cublas_ms"] = round(time_kernel(ref, a.iters), 4)
     return out
 

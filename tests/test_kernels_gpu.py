@@ -141,7 +141,9 @@ def test_gdn_prefill_matches_chunked_reference(nops):
     ref = TorchOps().gdn_prefill(proj.float(), ref_win, ref_st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64,
                                  torch.float32)
     st, win = state.clone(), window.clone()
+    nops.chunked_prefill = False            # the sequential prefill kernel
     out = nops.gdn_prefill(proj, win, st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
+    nops.chunked_prefill = True
     assert _rel(out, ref) < 1e-2
     assert _rel(st, ref_st) < 1e-3
     assert torch.equal(win, ref_win.to(torch.bfloat16))
@@ -192,3 +194,24 @@ def test_markov_select(nops):
     out = nops.markov_select(logits, anchor, pred, succ).tolist()
     ref = R.markov_select(logits.cpu(), 17, pred.cpu(), succ.cpu())
     assert out == ref
+
+
+@pytest.mark.parametrize("T", [64, 300, 2048])
+def test_gdn_chunked_prefill_matches_reference(nops, T):
+    proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T, seed=21)
+    ref_st, ref_win = state.clone(), window.float().clone()
+    ref = TorchOps().gdn_prefill(proj.float(), ref_win, ref_st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64,
+                                 torch.float32)
+    st, win = state.clone(), window.clone()
+    nops.chunked_prefill = True
+    out = nops.gdn_prefill(proj, win, st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
+    assert _rel(out, ref) < 3e-2
+    assert _rel(st, ref_st) < 3e-2
+    assert torch.equal(win, ref_win.to(torch.bfloat16))
+    # the sequential kernel agrees too (two independent implementations)
+    st2, win2 = state.clone(), window.clone()
+    nops.chunked_prefill = False
+    out2 = nops.gdn_prefill(proj, win2, st2, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
+    nops.chunked_prefill = True
+    assert _rel(out, out2) < 3e-2
+    nops.check()

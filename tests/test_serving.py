@@ -1,0 +1,92 @@
+"""Serving engine on CPU: continuous batching of several requests through packed verifies matches
+each request's single-stream greedy output; a failing request is quarantined while the others
+finish; prefix reuse inside the engine; scheduler policy (prefill first, no mixed steps)."""
+import torch
+
+from qwen38_b200.config import RuntimeConfig
+from qwen38_b200.models.drafter import BlockDrafter
+from qwen38_b200.models.target import HybridTarget
+from qwen38_b200.prefix.registry import PrefixRegistry
+from qwen38_b200.serving.engine import ServingEngine
+from qwen38_b200.serving.scheduler import ABORTED, FINISHED, DecodeStep, PrefillStep, Request, Scheduler
+from qwen38_b200.spec.engine import PinnedAcceptance, greedy_reference
+
+RT = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
+
+
+def _setup(tiny, slots=3):
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RT, max_slots=slots + 1)
+    dr = BlockDrafter(tiny["dcfg"], tiny["dsrc"], tgt, slots=slots)
+    return tgt, dr
+
+
+def _prompt(seed, n):
+    return torch.randint(0, 4096, (n,), generator=torch.Generator().manual_seed(seed)).tolist()
+
+
+def test_continuous_batching_matches_single_stream(tiny):
+    tgt, dr = _setup(tiny)
+    prompts = [_prompt(1, 100), _prompt(2, 70), _prompt(3, 130)]
+    golds = [greedy_reference(tgt, p, 20) for p in prompts]
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    reqs = [eng.add_request(p, 20, pinned=PinnedAcceptance(g, seed=i, mean_accepted=1))
+            for i, (p, g) in enumerate(zip(prompts, golds))]
+    eng.run()
+    for r, g in zip(reqs, golds):
+        assert r.state == FINISHED, r.error
+        assert r.output == g
+    assert eng.steps["decode"] < sum(len(g) for g in golds)      # blocks were packed
+    assert tgt.allocator.num_free == tgt.allocator.num_blocks
+
+
+def test_quarantine_isolates_a_failing_request(tiny):
+    tgt, dr = _setup(tiny)
+
+    class Boom:
+        def apply(self, *a):
+            raise RuntimeError("injected drafter failure")
+
+    good = _prompt(4, 60)
+    gold = greedy_reference(tgt, good, 12)
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    bad = eng.add_request(_prompt(5, 60), 12, pinned=Boom())
+    ok = eng.add_request(good, 12)
+    eng.run()
+    assert bad.state == ABORTED and "injected" in bad.error
+    assert ok.state == FINISHED and ok.output == gold
+    assert eng.quarantined == 1
+
+
+def test_engine_prefix_reuse(tiny):
+    tgt, dr = _setup(tiny, slots=2)
+    reg = PrefixRegistry(tgt, 1 << 30, boundary=64)
+    shared = _prompt(6, 128)
+    a, b = shared + _prompt(7, 40), shared + _prompt(8, 30)
+    gold_b = greedy_reference(tgt, b, 10)
+    eng = ServingEngine(tgt, dr, verifier_rows=4, prefix=reg)
+    eng.add_request(a, 10)
+    eng.run()
+    rb = eng.add_request(b, 10)
+    eng.run()
+    assert rb.reused_prefix == 128 and rb.output == gold_b
+
+
+def test_scheduler_policy():
+    s = Scheduler(max_running=2, prefill_chunk=64, max_step_rows=32, verifier_rows=16)
+    r1 = Request("a", list(range(100)), 8)
+    r2 = Request("b", list(range(10)), 8)
+    s.add(r1)
+    s.add(r2)
+    st = s.schedule(lambda r: True)
+    assert isinstance(st, PrefillStep) and (st.start, st.end) == (0, 64)
+    r1.prefilled = 64
+    st = s.schedule(lambda r: True)                  # continuation, not a new request
+    assert isinstance(st, PrefillStep) and st.request is r1 and st.end == 100
+    s.prefill_done(r1)
+    st = s.schedule(lambda r: True)                  # prefill first while r2 waits
+    assert isinstance(st, PrefillStep) and st.request is r2
+    s.prefill_done(r2)
+    st = s.schedule(lambda r: True)
+    assert isinstance(st, DecodeStep) and len(st.requests) == 2
+    s.finish(r1)
+    assert s.running == [r2]
