@@ -44,6 +44,8 @@ def parse():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--comm", default="peer", choices=["peer", "nccl"],
+                    help="TP collectives: in-kernel peer memory (default) or NCCL")
     return ap.parse_args()
 
 
@@ -135,7 +137,7 @@ def main():
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    comm = make_comm(world)
+    comm = None
 
     if args.model == "full":
         cfg, dcfg = full_model_config(), full_drafter_config()
@@ -147,6 +149,7 @@ def main():
         cfg = ModelConfig(**{**cfg.__dict__, "num_hidden_layers": args.layers,
                              "layer_types": cfg.layer_types[:args.layers]})
         dcfg.taps = [t for t in dcfg.taps if t < args.layers] or [args.layers - 1]
+    comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm == "peer" and args.ops == "native"))
     rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=2048,
                        use_cuda_graphs=not args.no_graphs)
     if args.ops == "native":
@@ -184,6 +187,8 @@ def main():
         wall = time.perf_counter() - w0
         if hasattr(ops, "check"):
             ops.check()
+        if hasattr(comm, "check"):
+            comm.check()
         if world > 1:
             dist.barrier()
         res["wall_s"] = wall
@@ -224,7 +229,8 @@ def main():
                        "layers": cfg.num_hidden_layers, "global_batch": 1, "seq_len": args.ctx,
                        "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows,
                        "drafter_layers": dcfg.num_hidden_layers, "parallelism": f"tp{world}",
-                       "ops": args.ops, "mean_accepted_target": args.mean_accepted,
+                       "ops": args.ops, "comm": args.comm if world > 1 else None,
+                       "mean_accepted_target": args.mean_accepted,
                        "l2": "inputs larger than L2: every step streams all weights (54 GB at TP1)"},
             "mean_accepted": round(statistics.mean(r["mean_accepted"] for r in results), 3),
             "tokens_per_block": round(statistics.mean(r["tokens_per_block"] for r in results), 3),
@@ -238,6 +244,11 @@ def main():
         if args.layers:
             line["invalid"] = "truncated model (--layers); debug only"
         print(json.dumps(line), flush=True)
+    # graphs may hold NCCL work: release them before the process group goes away
+    sr = None
+    dr.release_graphs()
+    tgt.release_graphs()
+    torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

@@ -30,6 +30,17 @@ void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor
                      torch::Tensor out, c10::optional<torch::Tensor> out_val, torch::Tensor part_val,
                      torch::Tensor part_idx, int64_t vocab_offset, bool write_prev);
 
+torch::Tensor q38_peer_alloc(int64_t bytes, int64_t device);
+torch::Tensor q38_ipc_handle(torch::Tensor buf);
+int64_t q38_ipc_open(torch::Tensor handle, int64_t device);
+void q38_ipc_close(int64_t ptr);
+void q38_allreduce_residual(std::vector<int64_t> data_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                            int64_t slot, int64_t slot_floats, torch::Tensor residual, torch::Tensor epochs,
+                            torch::Tensor err);
+void q38_argmax_allreduce(std::vector<int64_t> data_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                          int64_t slot, int64_t slot_floats, torch::Tensor val, torch::Tensor idx, torch::Tensor out,
+                          torch::Tensor epochs, torch::Tensor err);
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "qwen38_b200 sm_100a kernels";
   m.def("linear", &q38_linear);
@@ -43,4 +54,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm", &q38_rms_norm);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);
+  m.def("peer_alloc", &q38_peer_alloc);
+  m.def("ipc_handle", &q38_ipc_handle);
+  m.def("ipc_open", &q38_ipc_open);
+  m.def("ipc_close", &q38_ipc_close);
+  m.def("allreduce_residual", &q38_allreduce_residual);
+  m.def("argmax_allreduce", &q38_argmax_allreduce);
 }

@@ -132,6 +132,18 @@ class BlockDrafter:
             self.comm.all_reduce_(part)
         return part
 
+    def _row_par_add(self, h, w, x):
+        """x += h @ w^T summed over ranks."""
+        if self.tp == 1:
+            self.ops.linear_residual(h, w, x)
+        elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
+            slot, part = self.comm.slot_out(*x.shape)
+            self.ops.linear(h, w, out=part)
+            self.comm.reduce_slot_add(slot, x)
+        else:
+            x += self._row_par(h, w)
+        return x
+
     def _context_rows(self, feats):
         """fc (row-parallel over tap features) then hidden_norm -> [S, H] in activation dtype."""
         k0, kl = self.fc_k
@@ -177,10 +189,10 @@ class BlockDrafter:
             o = self.ops.draft_block_attention(qkv, L["qn"], L["kn"], self.inv_freq, self.rope_scale, self.heads,
                                                self.eps, positions, self.kctx_all[slot, l],
                                                self.vctx_all[slot, l], self.dtype)
-            h += self._row_par(o, L["w_o"])
+            self._row_par_add(o, L["w_o"], h)
             hn = self.ops.rms_norm(h, L["post_norm"], self.eps, self.dtype)
             gu = self.ops.linear_swiglu(hn, L["w_gu"], GU_BLOCK)
-            h += self._row_par(gu, L["w_down"])
+            self._row_par_add(gu, L["w_down"], h)
         hn = self.ops.rms_norm(h, self.norm, self.eps, self.dtype)
         return self.ops.linear(hn, self.target.lm_head, out_dtype=torch.float32)
 
@@ -215,6 +227,9 @@ class BlockDrafter:
         if hasattr(self.ops, "launches"):
             self.ops.launches += n
         return out
+
+    def release_graphs(self):
+        self._graphs.clear()
 
     def close(self, slot: int = 0):
         self.positions[slot] = 0

@@ -282,8 +282,13 @@ class HybridTarget:
 
     # ------------------------------------------------------------------ blocks
     def _row_parallel(self, h, w, x):
+        """x += h @ w^T summed over ranks (row-parallel out-projection + residual add)."""
         if self.tp == 1:
             self.ops.linear_residual(h, w, x)
+        elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
+            slot, part = self.comm.slot_out(*x.shape)          # GEMM writes into peer memory
+            self.ops.linear(h, w, out=part)
+            self.comm.reduce_slot_add(slot, x)
         else:
             part = self.ops.linear(h, w, out_dtype=torch.float32)
             self.comm.all_reduce_(part)
@@ -389,6 +394,12 @@ class HybridTarget:
         seq.pos, seq.verify_rows = saved
         return dict(graph=graph, tokens=tokens, positions=positions, pos_host=pos_host, pred=pred, feats=feats,
                     launches=launches)
+
+    def release_graphs(self):
+        """Drop captured graphs (they may hold NCCL work: release before destroying the process
+        group, or the exit waits on them)."""
+        self._graphs.clear()
+        self._graph_pool = None
 
     def _pool(self):
         if self._graph_pool is None:

@@ -21,8 +21,11 @@ class TorchOps:
         """Storage layout of a GEMM weight for this op set (identity here)."""
         return w
 
-    def linear(self, x, w, out_dtype=None):
+    def linear(self, x, w, out_dtype=None, out=None):
         y = x @ w.t()
+        if out is not None:
+            out.copy_(y)
+            return out
         return y if out_dtype is None else y.to(out_dtype)
 
     def linear_residual(self, x, w, residual):

@@ -90,12 +90,13 @@ class NativeOps(TorchOps):
     def prepare_weight(self, w):
         return w if isinstance(w, TiledWeight) else tile_weight(w.to(torch.bfloat16).contiguous())
 
-    def linear(self, x, w, out_dtype=None):
+    def linear(self, x, w, out_dtype=None, out=None):
         w = self.prepare_weight(w)
         x = x.contiguous()
         T, N = x.shape[0], w.N
-        if out_dtype == torch.float32:
-            out = torch.empty(T, N, dtype=torch.float32, device=x.device)
+        if out_dtype == torch.float32 or (out is not None and out.dtype == torch.float32):
+            if out is None:
+                out = torch.empty(T, N, dtype=torch.float32, device=x.device)
             self.C.linear(x, w.t, N, out, EPI_F32, self.ws, self.counters, self.err)
         else:
             out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)

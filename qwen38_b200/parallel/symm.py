@@ -1,0 +1,125 @@
+"""Peer-memory tensor-parallel collectives (the in-kernel NVLink path).
+
+``SymmComm`` extends the ``torch.distributed`` communicator: it allocates one peer buffer per
+rank, exchanges CUDA IPC handles over the process group once, and serves the decode / verify
+collectives with the kernels in ``csrc/comm.cu``:
+
+* ``reduce_slot_add(slot, residual)`` - the row-parallel GEMM already wrote this rank's fp32
+  partial into ``slot`` (``slot_out``); one kernel barriers the ranks, sums the partials in rank
+  order and adds into the residual.  No NCCL call, no copy.
+* ``argmax_reduce(val, idx)`` - cross-rank (value, index) argmax for the vocab-parallel LM head
+  and every Markov step.
+
+Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
+
+Slot reuse is safe when two uses of one slot are separated by another collective: a rank writes a
+slot again only after the barrier of a later call, which every peer reaches only after finishing
+its reads of the earlier one.  Graph captures therefore take fresh slots (never shared between
+graphs), and eager calls rotate through a separate range.
+"""
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from ..ops.build import load
+from .comm import TorchComm
+
+MAX_RANKS = 8
+AR_CTAS = 32
+
+
+class SymmComm(TorchComm):
+    def __init__(self, device, hidden: int, group=None, slot_rows: int = 32, graph_slots: int = 768,
+                 eager_slots: int = 64):
+        super().__init__(group)
+        if self.world > MAX_RANKS:
+            raise ValueError("peer-memory collectives serve at most 8 ranks")
+        self.C = load()
+        self.device = torch.device(device)
+        dev = self.device.index if self.device.index is not None else torch.cuda.current_device()
+        self.slot_rows, self.hidden = slot_rows, hidden
+        self.slot_floats = -(-(slot_rows * hidden) // 64) * 64
+        self.n_slots = graph_slots + eager_slots
+        self.graph_slots, self.eager_slots = graph_slots, eager_slots
+        data_bytes = self.n_slots * self.slot_floats * 4
+        flag_bytes = self.n_slots * AR_CTAS * MAX_RANKS * 4
+        self.buf = self.C.peer_alloc(data_bytes + flag_bytes, dev)
+        handle = self.C.ipc_handle(self.buf).to(self.device)
+        handles = [torch.empty_like(handle) for _ in range(self.world)]
+        dist.all_gather(handles, handle, group=self.group)
+        base = self.buf.data_ptr()
+        self._opened = []
+        ptrs = []
+        for p, h in enumerate(handles):
+            if p == self.rank:
+                ptrs.append(base)
+            else:
+                ptr = self.C.ipc_open(h.cpu(), dev)
+                self._opened.append(ptr)
+                ptrs.append(ptr)
+        self.data_ptrs = ptrs
+        self.flag_ptrs = [p + data_bytes for p in ptrs]
+        self.local = self.buf[:data_bytes].view(torch.float32).view(self.n_slots, self.slot_floats)
+        self.epochs = torch.zeros(self.n_slots * AR_CTAS, dtype=torch.int32, device=self.device)
+        self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
+        self._next_graph = 0
+        self._next_eager = 0
+        dist.barrier(group=self.group)
+
+    # ------------------------------------------------------------------ slots
+    def _slot(self) -> int:
+        if torch.cuda.is_current_stream_capturing():
+            if self._next_graph >= self.graph_slots:
+                raise RuntimeError("out of graph collective slots; raise graph_slots")
+            s = self._next_graph
+            self._next_graph += 1
+            return s
+        s = self.graph_slots + self._next_eager
+        self._next_eager = (self._next_eager + 1) % self.eager_slots
+        return s
+
+    def fits(self, rows: int, cols: int) -> bool:
+        return rows * cols <= self.slot_floats and rows <= self.slot_rows
+
+    def slot_out(self, rows: int, cols: int):
+        """A fresh slot and the [rows, cols] fp32 view of this rank's part of it."""
+        s = self._slot()
+        return s, self.local[s, :rows * cols].view(rows, cols)
+
+    # ------------------------------------------------------------------ collectives
+    def reduce_slot_add(self, slot: int, residual: torch.Tensor):
+        self.C.allreduce_residual(self.data_ptrs, self.flag_ptrs, self.rank, slot, self.slot_floats, residual,
+                                  self.epochs, self.err)
+        return residual
+
+    def all_reduce_(self, t):
+        """Sum in place.  Small fp32 tensors go through a slot (copy in, reduce into zeros)."""
+        if t.dtype == torch.float32 and t.is_cuda and t.dim() == 2 and self.fits(*t.shape):
+            s, view = self.slot_out(*t.shape)
+            view.copy_(t)
+            t.zero_()
+            return self.reduce_slot_add(s, t)
+        return super().all_reduce_(t)
+
+    def argmax_reduce(self, val, idx):
+        rows = val.numel()
+        if 2 * rows > self.slot_floats or not val.is_cuda:
+            return super().argmax_reduce(val, idx)
+        out = torch.empty(rows, dtype=torch.int64, device=val.device)
+        s = self._slot()
+        self.C.argmax_allreduce(self.data_ptrs, self.flag_ptrs, self.rank, s, self.slot_floats,
+                                val.float().contiguous(), idx.to(torch.int64).contiguous(), out, self.epochs,
+                                self.err)
+        return out
+
+    def check(self):
+        e = int(self.err.item())
+        if e:
+            self.err.zero_()
+            raise RuntimeError(f"peer collective timed out (device error word {e})")
+
+    def close(self):
+        for p in self._opened:
+            self.C.ipc_close(p)
+        self._opened = []
