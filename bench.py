@@ -233,6 +233,8 @@ def main():
                        "mean_accepted_target": args.mean_accepted,
                        "l2": "inputs larger than L2: every step streams all weights (54 GB at TP1)"},
             "mean_accepted": round(statistics.mean(r["mean_accepted"] for r in results), 3),
+            "block_ms": {k: round(statistics.mean(r[k + "_ms_per_block"] for r in results), 3)
+                         for k in ("draft", "verify", "commit")},
             "tokens_per_block": round(statistics.mean(r["tokens_per_block"] for r in results), 3),
             "clocks": clocks,
             "e2e": {"value": round(e2e_tg, 3), "unit": "tok/s (committed TG, host wall clock via "

@@ -219,6 +219,8 @@ class BlockDrafter:
             torch.cuda.synchronize()
             g = torch.cuda.CUDAGraph()
             l0 = getattr(self.ops, "launches", 0)
+            if hasattr(self.comm, "begin_capture"):
+                self.comm.begin_capture()
             with torch.cuda.graph(g):
                 out = self._propose_eager(ab, pb, slot)
             self._graphs[slot] = (g, out, getattr(self.ops, "launches", 0) - l0)

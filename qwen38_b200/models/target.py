@@ -388,6 +388,8 @@ class HybridTarget:
         torch.cuda.synchronize()
         graph = torch.cuda.CUDAGraph()
         l0 = getattr(self.ops, "launches", 0)
+        if hasattr(self.comm, "begin_capture"):
+            self.comm.begin_capture()
         with torch.cuda.graph(graph):
             pred, feats = self._verify_eager([(seq, tokens)], taps, positions=positions)
         launches = getattr(self.ops, "launches", 0) - l0

@@ -14,8 +14,9 @@ Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
 
 Slot reuse is safe when two uses of one slot are separated by another collective: a rank writes a
 slot again only after the barrier of a later call, which every peer reaches only after finishing
-its reads of the earlier one.  Graph captures therefore take fresh slots (never shared between
-graphs), and eager calls rotate through a separate range.
+its reads of the earlier one.  Each graph capture therefore numbers its collectives from slot 0
+(graphs run one at a time and each holds many collectives, so two uses of a slot always have
+other barriers between them), and eager calls rotate through a separate range.
 """
 from __future__ import annotations
 
@@ -68,6 +69,10 @@ class SymmComm(TorchComm):
         dist.barrier(group=self.group)
 
     # ------------------------------------------------------------------ slots
+    def begin_capture(self):
+        """Called before capturing a graph: its collectives take slots 0, 1, 2, ..."""
+        self._next_graph = 0
+
     def _slot(self) -> int:
         if torch.cuda.is_current_stream_capturing():
             if self._next_graph >= self.graph_slots:

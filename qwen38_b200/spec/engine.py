@@ -130,13 +130,17 @@ class SpecRuntime:
             if tgt.device.type == "cuda":
                 tok_host = tok_host.pin_memory()
             t2 = self._event()
+            marks = []                       # per block: (start, drafted, verified, committed) events
             while not s.finished:
+                e0 = self._event()
                 ticket = s.propose(request_id)
+                e1 = self._event()
                 n = len(ticket.tokens)
                 tok_host[:n] = torch.tensor(ticket.tokens, dtype=torch.long)
                 toks = tok_host[:n].to(tgt.device, non_blocking=True)
                 self.h2d_bytes += 8 * n
                 pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                e2 = self._event()
                 predictions = [int(x) for x in pred.tolist()]
                 self.d2h_bytes += 8 * n
                 pos = seq.pos
@@ -147,18 +151,27 @@ class SpecRuntime:
                         self.drafter.append(vfeats[:rows], pos)
 
                 d = s.commit(request_id, ticket, predictions, publish)
+                marks.append((e0, e1, e2, self._event()))
                 blocks.append((n, d.accepted, len(d.emitted)))
                 if gold_check is not None and s.emitted != gold_check[:len(s.emitted)]:
                     raise AssertionError(f"speculative output diverged from greedy at block {len(blocks)}")
             t3 = self._event()
             tg_ms = self._elapsed_ms(t2, t3)
             committed = s.committed_decode_tokens
+            phase = [0.0, 0.0, 0.0]
+            for a0, a1, a2, a3 in marks:     # draft, verify (+ read-back), select + commit + publish
+                phase[0] += self._elapsed_ms(a0, a1)
+                phase[1] += self._elapsed_ms(a1, a2)
+                phase[2] += self._elapsed_ms(a2, a3)
+            nb = max(1, len(marks))
             return dict(
                 tokens=list(s.emitted), prompt_tokens=int(prompt_host.numel()), pp_ms=pp_ms, tg_ms=tg_ms,
                 pp_tok_s=prompt_host.numel() / (pp_ms / 1e3), committed=committed,
                 tg_tok_s=committed / (tg_ms / 1e3) if tg_ms > 0 else float("nan"), blocks=len(blocks),
                 mean_accepted=sum(b[1] for b in blocks) / max(1, len(blocks)),
-                tokens_per_block=committed / max(1, len(blocks)), reused_prefix=ck.pos if ck else 0)
+                tokens_per_block=committed / max(1, len(blocks)), reused_prefix=ck.pos if ck else 0,
+                draft_ms_per_block=phase[0] / nb, verify_ms_per_block=phase[1] / nb,
+                commit_ms_per_block=phase[2] / nb)
         finally:
             if ck is not None:
                 self.prefix.unpin(ck)
