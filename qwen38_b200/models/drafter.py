@@ -155,7 +155,7 @@ class BlockDrafter:
         self.positions[slot] = 0
 
     @torch.no_grad()
-    def append(self, feats: torch.Tensor, pos: int, slot: int = 0):
+    def append(self, feats: torch.Tensor, pos: int, slot: int = 0, next_tokens=None):
         """Project ``feats`` [n, taps*H] (target rows at positions pos..pos+n-1) into every layer's
         K/V history of ``slot``."""
         if pos != self.positions[slot]:

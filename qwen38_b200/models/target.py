@@ -72,8 +72,8 @@ def pack_gdn(src, i, cfg: ModelConfig, tp, r, device, dtype):
     )
 
 
-def pack_attn(src, i, cfg: ModelConfig, tp, r, device, dtype):
-    p = f"model.layers.{i}.self_attn."
+def pack_attn(src, i, cfg: ModelConfig, tp, r, device, dtype, prefix=None):
+    p = (prefix or f"model.layers.{i}.") + "self_attn."
     H, Hkv, D = cfg.num_attention_heads, cfg.num_key_value_heads, cfg.head_dim
     w = tp_widths(cfg, tp)
     hl = w["n_heads"]
@@ -99,8 +99,8 @@ def pack_attn(src, i, cfg: ModelConfig, tp, r, device, dtype):
     )
 
 
-def pack_mlp(src, i, cfg: ModelConfig, tp, r, device, dtype):
-    p = f"model.layers.{i}.mlp."
+def pack_mlp(src, i, cfg: ModelConfig, tp, r, device, dtype, prefix=None):
+    p = (prefix or f"model.layers.{i}.") + "mlp."
     il = cfg.intermediate_size // tp
     if il % GU_BLOCK:
         raise ValueError(f"per-rank intermediate {il} must be a multiple of {GU_BLOCK}")

@@ -1,0 +1,205 @@
+"""OpenAI-compatible HTTP front end over ``ServingEngine``.
+
+The reference serves through vLLM's OpenAI server with a TT platform plugin
+(``scripts/ci/fixtures/qwen36_vllm.py``, ``fixtures/plugin_scheduler.py``).  Here a single engine
+loop thread owns the GPU and steps the scheduler; HTTP handlers only enqueue requests and wait for
+their completion, so requests arriving concurrently are continuously batched into packed verifies.
+
+Endpoints: ``POST /v1/completions`` (``prompt`` as a list of token ids, or a string encoded with
+the byte-level fallback tokenizer below - checkpoints' own tokenizers need network access to
+fetch), ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).
+
+Run:  python -m qwen38_b200.serving.api --model tiny --port 8000
+"""
+from __future__ import annotations
+
+import argparse
+import queue
+import threading
+import time
+import uuid
+
+from pydantic import BaseModel
+
+from .scheduler import ABORTED, FINISHED
+
+
+class CompletionRequest(BaseModel):
+    model: str | None = None
+    prompt: list[int] | str
+    max_tokens: int = 16
+    stop_token_ids: list[int] | None = None
+
+
+class ByteTokenizer:
+    """Fallback tokenizer: UTF-8 bytes are ids 0..255 (no network access to fetch a real one)."""
+
+    def encode(self, text: str):
+        return list(text.encode("utf-8"))
+
+    def decode(self, ids):
+        return bytes(int(i) for i in ids if 0 <= int(i) < 256).decode("utf-8", errors="replace")
+
+
+class EngineLoop:
+    """Owns the engine: a background thread admits queued requests and steps the scheduler."""
+
+    def __init__(self, engine, idle_sleep: float = 0.001):
+        self.engine = engine
+        self.inbox: "queue.Queue" = queue.Queue()
+        self.waiters: dict = {}
+        self.idle_sleep = idle_sleep
+        self.stop_event = threading.Event()
+        self.completed = self.aborted = self.tokens = 0
+        self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
+        self.thread.start()
+
+    def submit(self, prompt, max_new_tokens, eos_ids=()):
+        done = threading.Event()
+        box = {}
+        self.inbox.put((prompt, max_new_tokens, tuple(eos_ids), done, box))
+        return done, box
+
+    def _run(self):
+        while not self.stop_event.is_set():
+            try:
+                while True:
+                    prompt, n, eos, done, box = self.inbox.get_nowait()
+                    try:
+                        req = self.engine.add_request(prompt, n, eos_ids=eos)
+                        self.waiters[req.request_id] = (done, box, req)
+                    except Exception as e:          # invalid request: answer at once
+                        box["error"] = str(e)
+                        done.set()
+            except queue.Empty:
+                pass
+            if not self.engine.has_work():
+                time.sleep(self.idle_sleep)
+                continue
+            for req in self.engine.step():
+                entry = self.waiters.pop(req.request_id, None)
+                if entry is None:
+                    continue
+                done, box, _ = entry
+                box["request"] = req
+                if req.state == FINISHED:
+                    self.completed += 1
+                    self.tokens += max(0, len(req.output) - 1)
+                elif req.state == ABORTED:
+                    self.aborted += 1
+                done.set()
+
+    def close(self):
+        self.stop_event.set()
+        self.thread.join(timeout=10)
+
+
+def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0):
+    from fastapi import FastAPI, HTTPException
+    from fastapi.responses import PlainTextResponse
+
+    tok = tokenizer or ByteTokenizer()
+    loop = EngineLoop(engine)
+    app = FastAPI(title="qwen38_b200")
+    app.state.loop = loop
+
+    @app.get("/health")
+    def health():
+        return {"status": "ok", "running": len(engine.sched.running), "waiting": len(engine.sched.waiting)}
+
+    @app.get("/v1/models")
+    def models():
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "qwen38_b200"}]}
+
+    @app.post("/v1/completions")
+    def completions(body: CompletionRequest):
+        ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
+        if not ids:
+            raise HTTPException(400, "empty prompt")
+        # the first output token comes from the prefill; max_tokens counts output tokens
+        done, box = loop.submit(ids, body.max_tokens, body.stop_token_ids or ())
+        if not done.wait(timeout_s):
+            raise HTTPException(504, "generation timed out")
+        if "error" in box:
+            raise HTTPException(400, box["error"])
+        req = box["request"]
+        if req.state != FINISHED:
+            raise HTTPException(500, f"request aborted: {req.error}")
+        out = req.output
+        finish = "stop" if out and out[-1] in (body.stop_token_ids or ()) else "length"
+        return {
+            "id": "cmpl-" + uuid.uuid4().hex[:16], "object": "text_completion", "created": int(time.time()),
+            "model": body.model or model_name,
+            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": finish}],
+            "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                      "total_tokens": len(ids) + len(out)},
+        }
+
+    @app.get("/metrics", response_class=PlainTextResponse)
+    def metrics():
+        lines = [
+            "# TYPE q38_requests_completed counter", f"q38_requests_completed {loop.completed}",
+            "# TYPE q38_requests_aborted counter", f"q38_requests_aborted {loop.aborted}",
+            "# TYPE q38_tokens_generated counter", f"q38_tokens_generated {loop.tokens}",
+            "# TYPE q38_steps counter",
+            f"q38_steps{{kind=\"prefill\"}} {engine.steps['prefill']}",
+            f"q38_steps{{kind=\"decode\"}} {engine.steps['decode']}",
+            "# TYPE q38_running gauge", f"q38_running {len(engine.sched.running)}",
+            "# TYPE q38_waiting gauge", f"q38_waiting {len(engine.sched.waiting)}",
+            "# TYPE q38_kv_free_blocks gauge", f"q38_kv_free_blocks {engine.target.allocator.num_free}",
+        ]
+        if engine.prefix is not None:
+            for k, v in engine.prefix.export_stats().items():
+                if isinstance(v, (int, float)):
+                    lines.append(f"q38_prefix_{k} {int(v)}")
+        return "\n".join(lines) + "\n"
+
+    @app.on_event("shutdown")
+    def _shutdown():
+        loop.close()
+
+    return app
+
+
+def main():
+    import torch
+    import uvicorn
+
+    from ..checkpoint import random_drafter_source, random_target_source
+    from ..config import RuntimeConfig, full_drafter_config, full_model_config, tiny_drafter_config, tiny_model_config
+    from ..models.drafter import BlockDrafter
+    from ..models.target import HybridTarget
+    from .engine import ServingEngine
+
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--model", default="tiny", choices=["tiny", "full"])
+    ap.add_argument("--checkpoint", default=None, help="HF-layout checkpoint directory (random init if absent)")
+    ap.add_argument("--slots", type=int, default=4)
+    ap.add_argument("--max-context", type=int, default=8192)
+    ap.add_argument("--host", default="127.0.0.1")
+    ap.add_argument("--port", type=int, default=8000)
+    a = ap.parse_args()
+    cuda = torch.cuda.is_available()
+    cfg, dcfg = (full_model_config(), full_drafter_config()) if a.model == "full" else \
+        (tiny_model_config(), tiny_drafter_config())
+    if a.checkpoint:
+        from ..checkpoint import SafetensorsSource
+        from ..config import ModelConfig
+        cfg = ModelConfig.from_pretrained(a.checkpoint)
+        src = SafetensorsSource(a.checkpoint)
+    else:
+        src = random_target_source(cfg, 0)
+    ops = None
+    if cuda:
+        from ..ops.native import NativeOps
+        ops = NativeOps(max_keys=a.max_context + 64)
+    rt = RuntimeConfig(max_context=a.max_context)
+    tgt = HybridTarget(cfg, src, rt, device="cuda" if cuda else "cpu",
+                       dtype=torch.bfloat16 if cuda else torch.float32, ops=ops, max_slots=a.slots + 1)
+    dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, slots=a.slots)
+    eng = ServingEngine(tgt, dr, verifier_rows=dcfg.block_rows)
+    uvicorn.run(build_app(eng), host=a.host, port=a.port)
+
+
+if __name__ == "__main__":
+    main()

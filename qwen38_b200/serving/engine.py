@@ -134,7 +134,9 @@ class ServingEngine:
             toks = torch.tensor(req.prompt[req.prefilled:end], dtype=torch.long, device=tgt.device)
             nxt, feats = tgt.prefill(req.seq, toks, taps=self.taps)
             if dr is not None:
-                dr.append(feats, req.prefilled, req.dslot)
+                succ = (req.prompt[req.prefilled + 1:end + 1] if end < len(req.prompt)
+                        else req.prompt[req.prefilled + 1:] + [int(nxt.item())])
+                dr.append(feats, req.prefilled, req.dslot, next_tokens=succ)
             req.prefilled = end
             if self.prefix is not None and end % self.prefix.boundary == 0 and end < len(req.prompt):
                 self.prefix.capture(req.seq, req.prompt, dr, req.dslot)
@@ -196,10 +198,11 @@ class ServingEngine:
             rows = feats[o0:o0 + n] if feats is not None else None
             pos = r.seq.pos
 
-            def publish(k, r=r, rows=rows, pos=pos):
+            def publish(k, r=r, rows=rows, pos=pos, pr=preds[o0:o0 + n]):
                 tgt.commit(r.seq, k)
                 if dr is not None:
-                    dr.append(rows[:k], pos, r.dslot)
+                    nxt = list(r.ticket.tokens[1:k]) + [pr[k - 1]]
+                    dr.append(rows[:k], pos, r.dslot, next_tokens=nxt)
 
             try:
                 r.session.commit(r.request_id, r.ticket, preds[o0:o0 + n], publish)

@@ -76,7 +76,7 @@ class SpecRuntime:
         self.taps = tuple(drafter.dcfg.taps) if drafter is not None else ()
         self._anchor_dev = torch.zeros(1, dtype=torch.long, device=target.device)
         self.pinned = None
-        self.session = None
+        self.session = self.last_session = None
         self.h2d_bytes = self.d2h_bytes = 0
 
     # ------------------------------------------------------------------------------ timing
@@ -124,7 +124,7 @@ class SpecRuntime:
             s = GreedySession(request_id, prompt_host.tolist(), seed, vocab_size=tgt.cfg.vocab_size,
                               max_new_tokens=max_new_tokens, eos_ids=eos_ids, drafter=drafter,
                               verifier_rows=self.verifier_rows)
-            self.session = s
+            self.session = self.last_session = s
             blocks = []
             tok_host = torch.zeros(self.verifier_rows, dtype=torch.long)
             if tgt.device.type == "cuda":
@@ -139,16 +139,24 @@ class SpecRuntime:
                 tok_host[:n] = torch.tensor(ticket.tokens, dtype=torch.long)
                 toks = tok_host[:n].to(tgt.device, non_blocking=True)
                 self.h2d_bytes += 8 * n
-                pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                try:
+                    pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                except BaseException:
+                    s.fail_verification(request_id, ticket)     # poison: the block never publishes
+                    tgt.abort(seq)
+                    raise
                 e2 = self._event()
                 predictions = [int(x) for x in pred.tolist()]
                 self.d2h_bytes += 8 * n
                 pos = seq.pos
 
-                def publish(rows, vfeats=vfeats, pos=pos):
+                def publish(rows, vfeats=vfeats, pos=pos, ticket=ticket, predictions=predictions):
                     tgt.commit(seq, rows)
                     if self.drafter is not None:
-                        self.drafter.append(vfeats[:rows], pos)
+                        # successor of committed row i: the ticket's next token, or the target's
+                        # correction after the last accepted row
+                        nxt = list(ticket.tokens[1:rows]) + [predictions[rows - 1]]
+                        self.drafter.append(vfeats[:rows], pos, next_tokens=nxt)
 
                 d = s.commit(request_id, ticket, predictions, publish)
                 marks.append((e0, e1, e2, self._event()))
@@ -204,10 +212,12 @@ class SpecRuntime:
                 b = self.prefix.boundary
                 cuts = [p for p in range((start // b + 1) * b, n, b)] + [n]
             nxt, cur = None, start
+            plist = prompt_host.tolist() if dr is not None else None
             for end in cuts:
                 nxt, feats = tgt.prefill(seq, prompt_dev[cur:end], taps=self.taps)
                 if dr is not None:
-                    dr.append(feats, cur)
+                    succ = plist[cur + 1:end + 1] if end < n else plist[cur + 1:n] + [int(nxt.item())]
+                    dr.append(feats, cur, next_tokens=succ)
                 if self.prefix is not None and end < n:
                     self.prefix.capture(seq, toks, dr)
                 cur = end

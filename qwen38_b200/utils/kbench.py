@@ -8,6 +8,7 @@ bandwidth / throughput against the measured peaks (``MEASURED_PEAKS.json`` at th
     python -m qwen38_b200.utils.kbench gemm --T 16 --N 5120 --K 17408
     python -m qwen38_b200.utils.kbench gemm --T 4096 --N 34816 --K 5120 --epi swiglu
     python -m qwen38_b200.utils.kbench gdn --T 16 --nv 48
+    python -m qwen38_b200.utils.kbench gdnpf --T 2048 --nv 48
     python -m qwen38_b200.utils.kbench attn --T 16 --ctx 4096
 """
 from __future__ import annotations
@@ -106,6 +107,33 @@ def bench_gdn(a):
             f"frac_bw_of_{src}": round(bytes_ / ms / 1e6 / hbm, 3)}
 
 
+def bench_gdn_prefill(a):
+    """Chunked GDN prefill of one layer (prep + scan + gated norm) on T rows."""
+    from ..ops.native import NativeOps
+    ops = NativeOps()
+    nk, nv, D = a.nv // 3, a.nv, 128
+    C = 2 * nk * D + nv * D
+    proj = torch.randn(a.T, C + nv * D + 2 * nv, device="cuda").to(torch.bfloat16)
+    window = torch.randn(3, C, device="cuda").to(torch.bfloat16)
+    state = torch.randn(nv, D, D, device="cuda") * 0.1
+    conv_w = torch.rand(C, 4, device="cuda") - 0.5
+    A_log = torch.rand(nv, device="cuda")
+    dt = torch.ones(nv, device="cuda")
+    nw = torch.ones(D, device="cuda")
+    fn = lambda: ops.gdn_prefill(proj, window, state, conv_w, A_log, dt, nw, 1e-6, (nk, nv, D, D), 64,
+                                 torch.bfloat16)
+    if a.iters == 0:
+        fn()
+        torch.cuda.synchronize()
+        return {}
+    ms = time_kernel(fn, a.iters)
+    nch = -(-a.T // 64)
+    flops = 2.0 * nv * nch * (64 * 64 * D * 2 + 64 * 64 * D * 2 + 64 * D * D * 4 + 64 * 64 * D)
+    hbm, tf, src = peaks()
+    return {"kernel": "gdn_chunk_prefill", "T": a.T, "nv": nv, "ms": round(ms, 4),
+            "tflops": round(flops / ms / 1e9, 1), "us_per_row": round(ms * 1e3 / a.T, 3)}
+
+
 def bench_attn(a):
     from ..ops.native import NativeOps
     ops = NativeOps(max_keys=a.ctx + 64)
@@ -132,7 +160,7 @@ def bench_attn(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "gdn", "attn"])
+    ap.add_argument("kind", choices=["gemm", "gdn", "gdnpf", "attn"])
     ap.add_argument("--T", type=int, default=16)
     ap.add_argument("--N", type=int, default=5120)
     ap.add_argument("--K", type=int, default=17408)
@@ -144,7 +172,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true", help="also time torch/cuBLAS for the same GEMM")
     a = ap.parse_args()
-    out = {"gemm": bench_gemm, "gdn": bench_gdn, "attn": bench_attn}[a.kind](a)
+    out = {"gemm": bench_gemm, "gdn": bench_gdn, "gdnpf": bench_gdn_prefill, "attn": bench_attn}[a.kind](a)
     if out:
         print(json.dumps(out))
 

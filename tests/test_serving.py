@@ -15,7 +15,7 @@ RT = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
 
 
 def _setup(tiny, slots=3):
-    tgt = HybridTarget(tiny["cfg"], tiny["src"], RT, max_slots=slots + 1)
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RT, max_slots=slots + 1, max_verify_rows=4 * slots)
     dr = BlockDrafter(tiny["dcfg"], tiny["dsrc"], tgt, slots=slots)
     return tgt, dr
 
@@ -90,3 +90,41 @@ def test_scheduler_policy():
     assert isinstance(st, DecodeStep) and len(st.requests) == 2
     s.finish(r1)
     assert s.running == [r2]
+
+
+def test_openai_http_front_end(tiny):
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.serving.api import build_app
+    tgt, dr = _setup(tiny, slots=2)
+    p1, p2 = _prompt(11, 50), _prompt(12, 40)
+    g1 = greedy_reference(tgt, p1, 8)
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    app = build_app(eng, model_name="tiny")
+    with TestClient(app) as client:
+        assert client.get("/health").json()["status"] == "ok"
+        assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+        r = client.post("/v1/completions", json={"prompt": p1, "max_tokens": 8})
+        assert r.status_code == 200
+        body = r.json()
+        assert body["choices"][0]["token_ids"] == g1
+        assert body["usage"]["completion_tokens"] == 8
+        r2 = client.post("/v1/completions", json={"prompt": "hello", "max_tokens": 4})
+        assert r2.status_code == 200 and len(r2.json()["choices"][0]["token_ids"]) == 4
+        assert client.post("/v1/completions", json={"prompt": [999999], "max_tokens": 4}).status_code == 400
+        m = client.get("/metrics").text
+        assert "q38_requests_completed 2" in m
+    app.state.loop.close()
+
+
+def test_poisson_loadgen_report(tiny):
+    from qwen38_b200.serving.loadgen import poisson_arrivals, run
+    tgt, dr = _setup(tiny, slots=3)
+    prompts = [_prompt(20 + i, 40 + 10 * i) for i in range(3)]
+    golds = [greedy_reference(tgt, p, 12) for p in prompts]
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    arr = poisson_arrivals(3, 50.0, seed=1)
+    assert arr[0] == 0.0 and arr == sorted(arr)
+    rep = run(eng, prompts, 12, arr, golds=golds, mean_accepted=1)
+    assert rep["finished"] == 3 and rep["exact"]
+    assert rep["committed_tokens"] == 3 * 11 and rep["aggregate_tok_s"] > 0
