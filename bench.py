@@ -44,8 +44,9 @@ def parse():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--comm", default="peer", choices=["peer", "nccl"],
-                    help="TP collectives: in-kernel peer memory (default) or NCCL")
+    ap.add_argument("--comm", default="fused", choices=["fused", "peer", "nccl"],
+                    help="TP collectives: GEMM kernels that carry the all-reduce over peer memory (default), "
+                         "separate peer-memory all-reduce kernels, or NCCL")
     return ap.parse_args()
 
 
@@ -149,7 +150,8 @@ def main():
         cfg = ModelConfig(**{**cfg.__dict__, "num_hidden_layers": args.layers,
                              "layer_types": cfg.layer_types[:args.layers]})
         dcfg.taps = [t for t in dcfg.taps if t < args.layers] or [args.layers - 1]
-    comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm == "peer" and args.ops == "native"))
+    comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm != "nccl" and args.ops == "native"),
+                     fused=(args.comm == "fused"))
     rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=2048,
                        use_cuda_graphs=not args.no_graphs)
     if args.ops == "native":

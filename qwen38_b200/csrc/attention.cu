@@ -161,43 +161,65 @@ attn_decode_kernel(DecodeArgs a) {
   __nv_bfloat16* Vs = Ks + CH * DP;
   __nv_bfloat16* Qs = Vs + CH * DP;          // [MAXW*16][DP]
 
-  // ---- stage the K/V chunk (zeros past the visible keys)
-  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
-    const int j = idx / (D / 8), ch = idx % (D / 8);
-    const int kp = k0 + j;
-    uint4 kv = make_uint4(0, 0, 0, 0), vv = make_uint4(0, 0, 0, 0);
-    if (kp < k1) {
-      size_t base;
-      if (a.block_table) {
-        const int blk = a.block_table[kp / a.block_size];
-        base = ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
-      } else {
-        base = (size_t)kp * a.nkv + g;
-      }
-      kv = reinterpret_cast<const uint4*>(a.kcache + base * D)[ch];
-      vv = reinterpret_cast<const uint4*>(a.vcache + base * D)[ch];
-    }
-    reinterpret_cast<uint4*>(Ks + j * DP)[ch] = kv;
-    reinterpret_cast<uint4*>(Vs + j * DP)[ch] = vv;
-  }
-
+  // ---- stage the chunk with asynchronous copies: group 0 = K (+ the first query group), group 1 =
+  // V, so Q K^T starts while V is still in flight.  Zeros past the visible keys.
   const int nwarps = blockDim.x >> 5;
-  for (int qb = 0; qb < nqv; qb += nwarps * 16) {
-    __syncthreads();
-    // ---- stage this group's query rows (zeros for padding rows)
+  auto kv_base = [&](int kp) -> size_t {
+    if (a.block_table) {
+      const int blk = a.block_table[kp / a.block_size];
+      return ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
+    }
+    return (size_t)kp * a.nkv + g;
+  };
+  auto stage_q = [&](int qb) {
     for (int idx = threadIdx.x; idx < nwarps * 16 * (D / 8); idx += blockDim.x) {
       const int qi = idx / (D / 8), ch = idx % (D / 8);
       const int gq = qb + qi;
-      uint4 v = make_uint4(0, 0, 0, 0);
+      uint4* dst = reinterpret_cast<uint4*>(Qs + qi * DP) + ch;
       if (gq < nqv) {
         const int hq = g * rep + gq / a.T, t = gq % a.T;
-        v = reinterpret_cast<const uint4*>(a.q + ((size_t)t * a.nq + hq) * D)[ch];
+        cp_async16(dst, reinterpret_cast<const uint4*>(a.q + ((size_t)t * a.nq + hq) * D) + ch);
+      } else {
+        *dst = make_uint4(0, 0, 0, 0);
       }
-      reinterpret_cast<uint4*>(Qs + qi * DP)[ch] = v;
+    }
+  };
+  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
+    const int j = idx / (D / 8), ch = idx % (D / 8);
+    const int kp = k0 + j;
+    uint4* dst = reinterpret_cast<uint4*>(Ks + j * DP) + ch;
+    if (kp < k1) cp_async16(dst, reinterpret_cast<const uint4*>(a.kcache + kv_base(kp) * D) + ch);
+    else *dst = make_uint4(0, 0, 0, 0);
+  }
+  stage_q(0);
+  cp_async_commit();
+  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
+    const int j = idx / (D / 8), ch = idx % (D / 8);
+    const int kp = k0 + j;
+    uint4* dst = reinterpret_cast<uint4*>(Vs + j * DP) + ch;
+    if (kp < k1) cp_async16(dst, reinterpret_cast<const uint4*>(a.vcache + kv_base(kp) * D) + ch);
+    else *dst = make_uint4(0, 0, 0, 0);
+  }
+  cp_async_commit();
+
+  for (int qb = 0; qb < nqv; qb += nwarps * 16) {
+    if (qb > 0) {                      // later query groups (more than nwarps*16 rows)
+      __syncthreads();
+      stage_q(qb);
+      cp_async_commit();
+      cp_async_wait<0>();
+    } else {
+      cp_async_wait<1>();              // K and the first query group have landed
     }
     __syncthreads();
     const int row0 = qb + warp * 16;
-    if (row0 >= nqv) continue;
+    if (row0 >= nqv) {                 // idle warp: its V copies still count for the others
+      if (qb == 0) {
+        cp_async_wait<0>();
+        asm volatile("bar.arrive 1, %0;" ::"r"((int)blockDim.x) : "memory");
+      }
+      continue;
+    }
 
     // ---- S = Q K^T  (16 rows x CH keys per warp)
     float S[NT_K][4];
@@ -259,6 +281,10 @@ attn_decode_kernel(DecodeArgs a) {
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
 
     // ---- O = P V  (P re-used from the S accumulators as bf16 A fragments)
+    if (qb == 0) {                     // V has landed (every thread's copies: named barrier 1)
+      cp_async_wait<0>();
+      asm volatile("bar.sync 1, %0;" ::"r"((int)blockDim.x) : "memory");
+    }
     float O[NT_D][4];
 #pragma unroll
     for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;

@@ -31,14 +31,6 @@ struct PeerPtrs {
   int64_t p[MAX_RANKS];
 };
 
-__device__ __forceinline__ void st_release_sys(int* addr, int v) {
-  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(addr), "r"(v) : "memory");
-}
-__device__ __forceinline__ int ld_acquire_sys(const int* addr) {
-  int v;
-  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(addr) : "memory");
-  return v;
-}
 
 // Per-CTA barrier across ranks for (slot, cta).  flag word layout in every rank's buffer:
 // flags[(slot * AR_CTAS + cta) * MAX_RANKS + src].  Returns false on timeout.

@@ -1,6 +1,6 @@
 // Gated DeltaNet recurrence kernels (K-GDN-DECODE / commit / sequential prefill).
 //
-// Per value head h (one CTA) and row t:
+// Per value head h (a cluster of CTAs, one slice of value columns each) and row t:
 //   conv:  u_t = silu(sum_j w[c, j] * x[t - (K-1) + j, c])  over the head's q, k (shared by the
 //          GQA group) and v channels, x = [window (K-1 rows) ; projected rows]
 //   q_t = l2norm(u_q) * Dk^-0.5, k_t = l2norm(u_k), v_t = u_v
@@ -10,15 +10,26 @@
 // (reference: docker/qwen-c2-graft/graft/gdn/tp.py:540-730 prefill, :1176-1408 decode;
 //  scripts/ci/gdn_seq_block_device_test.py:431-456 fp64 recurrence).
 //
-// Layout: 4 threads per value column c; thread (c, p) keeps S[p*D/4 .. p*D/4 + D/4)[c] in
-// registers.  S^T k and S^T q are reduced across the 4 threads with a fixed xor butterfly, so the
-// arithmetic of row t is identical whether it runs inside a verify block, a commit replay or a
-// single-row decode: verify outputs match sequential decode bit for bit and commit publishes
-// exactly the state sequential decode would have produced.
+// Layout: a head's D value columns are split over SPLIT CTAs of one thread-block cluster (D=128:
+// 4 CTAs of 32 columns, so a layer's 48 heads fill 192 SMs' worth of CTAs instead of 48).  The
+// columns of the state evolve independently; only the gated RMSNorm needs whole-row statistics,
+// which the cluster exchanges through distributed shared memory (each CTA stores its partial sum
+// of squares into every peer's buffer, one cluster barrier, then every CTA adds the SPLIT
+// partials in cluster-rank order).  Inside a CTA, 4 threads own a value column c; thread (c, p)
+// keeps S[p*D/4 .. p*D/4 + D/4)[c] in registers.  S^T k and S^T q are reduced with a fixed xor
+// butterfly and a fixed 4-way partial-sum split, so the arithmetic of row t is identical whether
+// it runs inside a verify block, a commit replay or a single-row decode: verify outputs match
+// sequential decode bit for bit and commit publishes exactly the state sequential decode would
+// have produced.
 //
-// Modes: WRITE_OUT (verify, prefill) and WRITE_STATE (commit, prefill).  Rows are processed in
-// sub-blocks of SUB rows staged in shared memory.  The row count may come from device memory
-// (commit: the accepted prefix length, so the launch can live inside a CUDA graph).
+// Each sub-block of SUB rows first stages its raw projected rows (q and k channels of the head's
+// key group, this CTA's v and z columns, for rows r0-(K-1) .. r0+SUB-1) in shared memory with
+// coalesced 4-byte loads, so the conv, the norms and the epilogue read only shared memory.
+//
+// Modes: WRITE_OUT (verify, prefill) and WRITE_STATE (commit, prefill).  The row count may come
+// from device memory (commit: the accepted prefix length, so the launch can live inside a CUDA
+// graph).
+#include <cooperative_groups.h>
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -26,6 +37,8 @@
 #include "common.cuh"
 
 namespace q38 {
+
+namespace cg = cooperative_groups;
 
 struct GdnArgs {
   const __nv_bfloat16* proj;   // [rows, in_width] layer 0; + layer * proj_layer_stride
@@ -47,15 +60,27 @@ struct GdnArgs {
   float eps;
 };
 
-template <int D, int KC, int SUB, bool WRITE_OUT, bool WRITE_STATE>
-__global__ void __launch_bounds__(4 * D)
+template <int D, int SPLIT>
+struct GdnShape {
+  static constexpr int COLS = D / SPLIT;     // value columns per CTA
+  static constexpr int NT = 4 * COLS;        // threads per CTA
+  static constexpr int RPT = D / 4;          // state rows per thread
+  static constexpr int QP = RPT + 4;         // padded quarter of a q/k row (bank spread)
+  static constexpr int RAWW = 2 * D + 2 * COLS;   // staged channels: q | k | v slice | z slice
+};
+
+template <int D, int KC, int SUB, bool WRITE_OUT, bool WRITE_STATE, int SPLIT>
+__global__ void __launch_bounds__(GdnShape<D, SPLIT>::NT)
 gdn_recurrent_kernel(GdnArgs a) {
-  constexpr int NT = 4 * D;
-  constexpr int RPT = D / 4;     // state rows per thread
-  const int h = blockIdx.x;
+  using G = GdnShape<D, SPLIT>;
+  constexpr int COLS = G::COLS, NT = G::NT, RPT = G::RPT, QP = G::QP, RAWW = G::RAWW;
+  static_assert(NT == 128 && SUB * 8 == NT, "128 threads: 16 rows x 8 lanes in the row reductions");
+  constexpr int NPR = 8;                       // threads per row in row reductions
+  const int h = blockIdx.x / SPLIT, sl = blockIdx.x % SPLIT;   // sl == rank in the cluster
   const int layer = blockIdx.y;
   const int tid = threadIdx.x;
   const int col = tid >> 2, part = tid & 3;
+  const int gcol = sl * COLS + col;            // value column inside the head
   const int rep = a.nv / a.nk;
   const int kh = h / rep;
 
@@ -63,74 +88,60 @@ gdn_recurrent_kernel(GdnArgs a) {
   const __nv_bfloat16* __restrict__ window = a.window + layer * a.win_layer_stride;
   float* __restrict__ state = a.state + layer * a.state_layer_stride + (size_t)h * D * D;
   const float* __restrict__ conv_w = a.conv_w + layer * a.convw_layer_stride;
-  __nv_bfloat16* __restrict__ outp = a.out;
   const float A = -__expf(a.A_log[layer * a.nv + h]);
   const float dtb = a.dt_bias[layer * a.nv + h];
   const float* norm_w = a.norm_w + layer * D;
 
-  // channel offsets of this head inside [q | k | v | z | b | a]
-  const int cq = kh * D, ck = a.nk * D + kh * D, cv = 2 * a.nk * D + h * D;
-  const int cz = a.C + h * D, cb = a.C + a.nv * D + h, ca = a.C + a.nv * D + a.nv + h;
+  // channel offsets inside [q | k | v | z | b | a]
+  const int cq = kh * D, ck = a.nk * D + kh * D, cv = 2 * a.nk * D + h * D + sl * COLS;
+  const int cz = a.C + h * D + sl * COLS, cb = a.C + a.nv * D + h, ca = a.C + a.nv * D + a.nv + h;
 
-  // q/k rows are read by the 4 threads of a column at quarter offsets: pad each quarter by 4 floats
-  // so the quarters fall in different banks.
-  constexpr int QP = RPT + 4;
+  __shared__ __align__(16) __nv_bfloat16 raw[SUB + KC - 1][RAWW];
   __shared__ __align__(16) float q_s[SUB][4 * QP], k_s[SUB][4 * QP];
-  __shared__ float v_s[SUB][D];
-  __shared__ float g_s[SUB], b_s[SUB];
-  __shared__ float o_s[SUB][D];
-  __shared__ float red_s[SUB][2][NT / 32];
+  __shared__ float v_s[SUB][COLS];
+  __shared__ float o_s[SUB][COLS];
+  __shared__ float g_s[SUB], b_s[SUB], nq_s[SUB], nk_s[SUB], rs_s[SUB];
+  __shared__ float ss_part[2][SPLIT][SUB];     // DSMEM targets, double-buffered by sub-block parity
 
   // conv taps are static; everything else may come from the previous kernel
-  float wq[KC], wk[KC], wv[KC];
+  constexpr int QK_PER = (2 * D + NT - 1) / NT;   // q/k channels per thread
+  float wqk[QK_PER][KC], wv[KC];
 #pragma unroll
-  for (int j = 0; j < KC; ++j) {
-    wq[j] = conv_w[(size_t)(cq + col) * KC + j];
-    wk[j] = conv_w[(size_t)(ck + col) * KC + j];
-    wv[j] = conv_w[(size_t)(cv + col) * KC + j];
+  for (int u = 0; u < QK_PER; ++u) {
+    const int c = tid + u * NT;
+    const int ch = c < D ? cq + c : ck + (c - D);
+#pragma unroll
+    for (int j = 0; j < KC; ++j) wqk[u][j] = (c < 2 * D) ? conv_w[(size_t)ch * KC + j] : 0.f;
   }
+#pragma unroll
+  for (int j = 0; j < KC; ++j) wv[j] = conv_w[(size_t)(cv + col) * KC + j];
   pdl_wait();
   pdl_trigger();
   const int rows = a.rows_dev ? *a.rows_dev : a.rows;
 
-  // state registers
   float S[RPT];
 #pragma unroll
-  for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + col];
+  for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + gcol];
 
-
-  auto x_at = [&](int r, int ch) -> float {   // r in [-(K-1), rows)
-    if (r < 0) return __bfloat162float(window[(size_t)(r + KC - 1) * a.C + ch]);
-    return __bfloat162float(proj[(size_t)r * a.proj_ld + ch]);
-  };
-
-  const int qidx = (col / RPT) * QP + (col % RPT);   // padded slot of channel `col`
-  for (int r0 = 0; r0 < rows; r0 += SUB) {
+  cg::cluster_group cluster = cg::this_cluster();
+  int parity = 0;
+  for (int r0 = 0; r0 < rows; r0 += SUB, parity ^= 1) {
     const int nsub = min(SUB, rows - r0);
-    // ---- prologue: conv + silu for q/k/v channel `col`, split rows over the 4 parts
-#pragma unroll
-    for (int tt = 0; tt < SUB / 4; ++tt) {
-      const int t = part + 4 * tt;
-      if (t >= nsub) break;
-      const int r = r0 + t;
-      float xq[KC], xk[KC], xv[KC];
-#pragma unroll
-      for (int j = 0; j < KC; ++j) {          // issue all loads before the arithmetic
-        const int rr = r - (KC - 1) + j;
-        xq[j] = x_at(rr, cq + col);
-        xk[j] = x_at(rr, ck + col);
-        xv[j] = x_at(rr, cv + col);
-      }
-      float sq = 0.f, sk = 0.f, sv = 0.f;
-#pragma unroll
-      for (int j = 0; j < KC; ++j) {
-        sq += wq[j] * xq[j];
-        sk += wk[j] * xk[j];
-        sv += wv[j] * xv[j];
-      }
-      q_s[t][qidx] = silu_f(sq);
-      k_s[t][qidx] = silu_f(sk);
-      v_s[t][col] = silu_f(sv);
+    // ---- 1. stage raw rows r0-(K-1) .. r0+nsub-1 (bf16 pairs; z only for rows >= 0)
+    constexpr int PAIRS = RAWW / 2;
+    for (int idx = tid; idx < (nsub + KC - 1) * PAIRS; idx += NT) {
+      const int i = idx / PAIRS, pp = idx % PAIRS;
+      const int c2 = 2 * pp;                       // staged channel
+      const int r = r0 - (KC - 1) + i;
+      int ch;
+      if (c2 < D) ch = cq + c2;
+      else if (c2 < 2 * D) ch = ck + (c2 - D);
+      else if (c2 < 2 * D + COLS) ch = cv + (c2 - 2 * D);
+      else ch = cz + (c2 - 2 * D - COLS);
+      uint32_t v = 0;
+      if (r >= 0) v = *reinterpret_cast<const uint32_t*>(proj + (size_t)r * a.proj_ld + ch);
+      else if (c2 < 2 * D + COLS) v = *reinterpret_cast<const uint32_t*>(window + (size_t)(r + KC - 1) * a.C + ch);
+      *reinterpret_cast<uint32_t*>(&raw[i][c2]) = v;
     }
     if (tid < nsub) {
       const int r = r0 + tid;
@@ -141,56 +152,80 @@ gdn_recurrent_kernel(GdnArgs a) {
       b_s[tid] = 1.f / (1.f + __expf(-bv));
     }
     __syncthreads();
-    // ---- L2 norms of q and k per row (fixed-order block reduction)
-    {
-      const int warp = tid >> 5, lane = tid & 31;
-      for (int t = 0; t < nsub; ++t) {
-        float pq = 0.f, pk = 0.f;
-        for (int c = tid; c < D; c += NT) {
-          const int ci = (c / RPT) * QP + (c % RPT);
-          pq += q_s[t][ci] * q_s[t][ci];
-          pk += k_s[t][ci] * k_s[t][ci];
-        }
-        pq = warp_sum(pq);
-        pk = warp_sum(pk);
-        if (lane == 0) { red_s[t][0][warp] = pq; red_s[t][1][warp] = pk; }
-      }
-      __syncthreads();
-      if (tid < nsub) {
-        float sq = 0.f, sk = 0.f;
-        for (int w = 0; w < NT / 32; ++w) { sq += red_s[tid][0][w]; sk += red_s[tid][1][w]; }
-        red_s[tid][0][0] = rsqrtf(sq + 1e-6f) * rsqrtf((float)D);
-        red_s[tid][1][0] = rsqrtf(sk + 1e-6f);
-      }
-      __syncthreads();
-      for (int t = 0; t < nsub; ++t) {
-        for (int c = tid; c < D; c += NT) {
-          const int ci = (c / RPT) * QP + (c % RPT);
-          q_s[t][ci] *= red_s[t][0][0];
-          k_s[t][ci] *= red_s[t][1][0];
+    // ---- 2. conv + SiLU: q/k channels (one or more per thread, every row), v column per (col, part)
+#pragma unroll
+    for (int u = 0; u < QK_PER; ++u) {
+      const int c = tid + u * NT;
+      if (c < 2 * D) {
+        const int cc = c < D ? c : c - D;
+        const int pi = (cc / RPT) * QP + (cc % RPT);
+        float* dst = c < D ? &q_s[0][pi] : &k_s[0][pi];
+        for (int t = 0; t < nsub; ++t) {
+          float acc = 0.f;
+#pragma unroll
+          for (int j = 0; j < KC; ++j) acc += wqk[u][j] * __bfloat162float(raw[t + j][c]);
+          dst[t * 4 * QP] = silu_f(acc);
         }
       }
-      __syncthreads();
     }
-    // ---- sequential recurrence
+    for (int t = part; t < nsub; t += 4) {
+      float acc = 0.f;
+#pragma unroll
+      for (int j = 0; j < KC; ++j) acc += wv[j] * __bfloat162float(raw[t + j][2 * D + col]);
+      v_s[t][col] = silu_f(acc);
+    }
+    __syncthreads();
+    // ---- 3. L2 norms of q and k per row: 8 threads per row, fixed xor butterfly
+    {
+      const int t = tid / NPR, j = tid % NPR;
+      float pq = 0.f, pk = 0.f;
+#pragma unroll
+      for (int m = 0; m < D / NPR; ++m) {
+        const int c = j * (D / NPR) + m;
+        const int ci = (c / RPT) * QP + (c % RPT);
+        pq += q_s[t][ci] * q_s[t][ci];
+        pk += k_s[t][ci] * k_s[t][ci];
+      }
+#pragma unroll
+      for (int o = 1; o < NPR; o <<= 1) {
+        pq += __shfl_xor_sync(0xffffffffu, pq, o);
+        pk += __shfl_xor_sync(0xffffffffu, pk, o);
+      }
+      if (j == 0) {
+        nq_s[t] = rsqrtf(pq + 1e-6f) * rsqrtf((float)D);
+        nk_s[t] = rsqrtf(pk + 1e-6f);
+      }
+    }
+    __syncthreads();
+    for (int idx = tid; idx < nsub * 4 * QP; idx += NT) {
+      const int t = idx / (4 * QP), ci = idx % (4 * QP);
+      q_s[t][ci] *= nq_s[t];
+      k_s[t][ci] *= nk_s[t];
+    }
+    __syncthreads();
+    // ---- 4. sequential recurrence (fixed 4-way partial sums + xor butterfly over the 4 parts)
     for (int t = 0; t < nsub; ++t) {
       const float decay = __expf(g_s[t]);
-      float kv = 0.f;
+      const float* kr = &k_s[t][part * QP];
+      const float* qr = &q_s[t][part * QP];
+      float kv4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
         S[i] *= decay;
-        kv += S[i] * k_s[t][part * QP + i];
+        kv4[i & 3] += S[i] * kr[i];
       }
+      float kv = (kv4[0] + kv4[1]) + (kv4[2] + kv4[3]);
       kv += __shfl_xor_sync(0xffffffffu, kv, 1);
       kv += __shfl_xor_sync(0xffffffffu, kv, 2);
       const float delta = (v_s[t][col] - kv) * b_s[t];
-      float o = 0.f;
+      float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < RPT; ++i) {
-        S[i] += k_s[t][part * QP + i] * delta;
-        o += S[i] * q_s[t][part * QP + i];
+        S[i] += kr[i] * delta;
+        o4[i & 3] += S[i] * qr[i];
       }
       if constexpr (WRITE_OUT) {
+        float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
         o += __shfl_xor_sync(0xffffffffu, o, 1);
         o += __shfl_xor_sync(0xffffffffu, o, 2);
         if (part == 0) o_s[t][col] = o;
@@ -198,44 +233,46 @@ gdn_recurrent_kernel(GdnArgs a) {
     }
     if constexpr (WRITE_OUT) {
       __syncthreads();
-      // ---- gated RMSNorm epilogue
-      const int warp = tid >> 5, lane = tid & 31;
-      for (int t = 0; t < nsub; ++t) {
+      // ---- 5. gated RMSNorm: partial sums of squares over this CTA's columns, exchanged in the
+      // cluster through DSMEM, summed in cluster-rank order
+      {
+        const int t = tid / NPR, j = tid % NPR;
         float ss = 0.f;
-        for (int c = tid; c < D; c += NT) ss += o_s[t][c] * o_s[t][c];
-        ss = warp_sum(ss);
-        if (lane == 0) red_s[t][0][warp] = ss;
+#pragma unroll
+        for (int m = 0; m < COLS / NPR; ++m) {
+          const float v = o_s[t][j * (COLS / NPR) + m];
+          ss += v * v;
+        }
+#pragma unroll
+        for (int o = 1; o < NPR; o <<= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+        if (j == 0) {
+#pragma unroll
+          for (int p = 0; p < SPLIT; ++p) {
+            float* dst = cluster.map_shared_rank(&ss_part[parity][sl][t], p);
+            *dst = ss;
+          }
+        }
       }
-      __syncthreads();
+      cluster.sync();
       if (tid < nsub) {
         float s = 0.f;
-        for (int w = 0; w < NT / 32; ++w) s += red_s[tid][0][w];
-        red_s[tid][1][0] = rsqrtf(s / D + a.eps);
+#pragma unroll
+        for (int p = 0; p < SPLIT; ++p) s += ss_part[parity][p][tid];
+        rs_s[tid] = rsqrtf(s / D + a.eps);
       }
       __syncthreads();
-      constexpr int PER = (SUB * D + NT - 1) / NT;
-      float zv[PER];
-#pragma unroll
-      for (int u = 0; u < PER; ++u) {            // issue every z load before any store
-        const int idx = tid + u * NT;
-        const int t = idx / D, c = idx % D;
-        zv[u] = (t < nsub) ? __bfloat162float(proj[(size_t)(r0 + t) * a.proj_ld + cz + c]) : 0.f;
-      }
-#pragma unroll
-      for (int u = 0; u < PER; ++u) {
-        const int idx = tid + u * NT;
-        const int t = idx / D, c = idx % D;
-        if (t < nsub) {
-          const float y = o_s[t][c] * red_s[t][1][0] * norm_w[c] * silu_f(zv[u]);
-          outp[(size_t)(r0 + t) * a.out_ld + (size_t)h * D + c] = __float2bfloat16(y);
-        }
+      for (int idx = tid; idx < nsub * COLS; idx += NT) {
+        const int t = idx / COLS, c = idx % COLS;
+        const float z = __bfloat162float(raw[t + KC - 1][2 * D + COLS + c]);
+        const float y = o_s[t][c] * rs_s[t] * norm_w[sl * COLS + c] * silu_f(z);
+        a.out[(size_t)(r0 + t) * a.out_ld + (size_t)h * D + sl * COLS + c] = __float2bfloat16(y);
       }
     }
     __syncthreads();
   }
   if constexpr (WRITE_STATE) {
 #pragma unroll
-    for (int i = 0; i < RPT; ++i) state[(size_t)(part * RPT + i) * D + col] = S[i];
+    for (int i = 0; i < RPT; ++i) state[(size_t)(part * RPT + i) * D + gcol] = S[i];
   }
 }
 
@@ -303,14 +340,37 @@ void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, t
   a.eps = (float)eps;
   TORCH_CHECK(KC == 4, "conv kernel size 4 supported");
   TORCH_CHECK(mode != 0 || out, "verify needs an output");
+  TORCH_CHECK(a.proj_ld % 2 == 0 && C % 2 == 0 && (reinterpret_cast<uintptr_t>(a.proj) & 3) == 0 &&
+                  (reinterpret_cast<uintptr_t>(a.window) & 3) == 0,
+              "GDN rows are staged as bf16 pairs: even row strides and 4-byte aligned bases required");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  dim3 grid((unsigned)nv, (unsigned)layers);
-#define Q38_GDN_LAUNCH(DD)                                                                              \
-  if (mode == 0) q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, true, false>, grid, dim3(4 * DD), 0, st, a); \
-  else if (mode == 1) q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, false, true>, grid, dim3(4 * DD), 0, st, a); \
-  else q38::launch_pdl(q38::gdn_recurrent_kernel<DD, 4, 16, true, true>, grid, dim3(4 * DD), 0, st, a);
-  if (D == 128) { Q38_GDN_LAUNCH(128) }
-  else if (D == 32) { Q38_GDN_LAUNCH(32) }
+  auto launch = [&](auto kern, int split) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3((unsigned)(nv * split), (unsigned)layers);
+    cfg.blockDim = dim3(128);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    int n = 0;
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = split;
+    attr[n].val.clusterDim.y = 1;
+    attr[n].val.clusterDim.z = 1;
+    ++n;
+    if (q38::pdl_enabled()) {
+      attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[n].val.programmaticStreamSerializationAllowed = 1;
+      ++n;
+    }
+    cfg.attrs = attr;
+    cfg.numAttrs = n;
+    TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, a) == cudaSuccess, "GDN recurrence launch failed");
+  };
+#define Q38_GDN_LAUNCH(DD, SP)                                                                   \
+  if (mode == 0) launch(q38::gdn_recurrent_kernel<DD, 4, 16, true, false, SP>, SP);             \
+  else if (mode == 1) launch(q38::gdn_recurrent_kernel<DD, 4, 16, false, true, SP>, SP);        \
+  else launch(q38::gdn_recurrent_kernel<DD, 4, 16, true, true, SP>, SP);
+  if (D == 128) { Q38_GDN_LAUNCH(128, 4) }
+  else if (D == 32) { Q38_GDN_LAUNCH(32, 1) }
   else TORCH_CHECK(false, "GDN head dim 32 or 128 supported");
 #undef Q38_GDN_LAUNCH
   C10_CUDA_KERNEL_LAUNCH_CHECK();

@@ -10,7 +10,17 @@
 // Roles inside a 128-thread CTA: thread 0 issues TMA loads, thread 32 issues tcgen05.mma (one
 // elected thread), all four warps drain TMEM with tcgen05.ld in the epilogue.  Epilogues: bf16
 // store, fp32 store, fp32 accumulate into the residual stream, SwiGLU over [gate 64 | up 64] row
-// blocks, per-tile argmax (LM head).
+// blocks, per-tile argmax (LM head), and (swap mode) the fused tensor-parallel all-reduce:
+//
+// EPI_AR_F32 - GEMM -> all-reduce -> residual add in one kernel (row-parallel out-projections at
+// TP > 1).  As soon as a tile's split-K fix-up is done, the fixing CTA stores its fp32 partial
+// tile into its own block of every rank's receive buffer (plain stores to peer memory over
+// NVLink, so tile t's transfer overlaps the MMA of later tiles), publishes a per-(slot, tile)
+// flag in every rank's flag area with a system-scope release, waits (bounded) for the W flags of
+// that tile in its own flag area, then sums the W partials in rank order 0..W-1 from local memory
+// and adds them into the replicated fp32 residual.  Every rank adds the same bits.  Only the
+// split-K fixing CTA of a tile waits (at most one per tile, far fewer than resident CTA slots),
+// and CTAs that wait on peers never wait on CTAs of their own grid, so the grid always drains.
 #pragma once
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -19,7 +29,20 @@
 
 namespace q38 {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_AR_F32 = 5 };
+
+constexpr int AR_MAX_RANKS = 8;
+
+// Peer buffers of the fused all-reduce epilogue.  Receive area of every rank: blocks
+// [slot][src rank] of `block_floats` floats, each a [tokens, ldo] fp32 partial; flag area:
+// int words [slot][tile < tiles_max][src rank < 8].
+struct ArArgs {
+  long long recv[AR_MAX_RANKS];    // every rank's receive area, mapped into this process
+  long long flags[AR_MAX_RANKS];   // every rank's flag area
+  long long block_floats;
+  int rank, world, slot, tiles_max;
+  int* epochs;                     // this rank's [slots * tiles_max] epoch words
+};
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -35,6 +58,7 @@ struct GemmArgs {
   int* err;
   float* amax_val;            // EPI_ARGMAX partials [m_tiles, N]
   int* amax_idx;
+  ArArgs ar;                  // EPI_AR_F32 only
 };
 
 template <int BN, int STAGES>
@@ -244,6 +268,53 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             g.amax_val[(size_t)m_tile * g.N + n0 + tid] = v;
             g.amax_idx[(size_t)m_tile * g.N + n0 + tid] = idx;
+          }
+        } else if constexpr (EPI == EPI_AR_F32) {
+          const ArArgs& a = g.ar;
+          const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_floats;
+          if (m < g.M) {
+            for (int p = 0; p < a.world; ++p) {        // push: this rank's block in every rank
+              float* dst = reinterpret_cast<float*>(a.recv[p]) + mine;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nvalid) dst[(size_t)(n0 + j) * g.ldo + m] = acc[j];
+            }
+          }
+          __syncthreads();
+          if (tid == 0) {
+            const size_t fw = ((size_t)a.slot * a.tiles_max + m_tile) * AR_MAX_RANKS;
+            int* ep = a.epochs + (size_t)a.slot * a.tiles_max + m_tile;
+            const int e = *ep + 1;
+            __threadfence_system();
+            for (int p = 0; p < a.world; ++p) st_release_sys(reinterpret_cast<int*>(a.flags[p]) + fw + a.rank, e);
+            const int* fl = reinterpret_cast<const int*>(a.flags[a.rank]) + fw;
+            bool arrived = true;
+            const unsigned long long t0 = globaltimer();
+            for (int q = 0; q < a.world && arrived; ++q) {
+              while (ld_acquire_sys(fl + q) < e) {
+                if (globaltimer() - t0 > kWaitLimitNs) {
+                  record_error(g.err, kErrPeer);
+                  arrived = false;
+                  break;
+                }
+              }
+            }
+            if (arrived) *ep = e;
+            *last_flag = arrived;
+          }
+          __syncthreads();
+          if (*last_flag && m < g.M) {
+            const float* rb = reinterpret_cast<const float*>(a.recv[a.rank]) + (size_t)a.slot * a.world * a.block_floats;
+            float* res = reinterpret_cast<float*>(g.out);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < nvalid) {
+                const size_t off = (size_t)(n0 + j) * g.ldo + m;
+                float sum = 0.f;
+                for (int q = 0; q < a.world; ++q) sum += __ldcg(rb + (size_t)q * a.block_floats + off);
+                res[off] += sum;
+              }
+            }
           }
         } else {
           if (m < g.M) {

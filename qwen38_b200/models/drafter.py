@@ -136,6 +136,8 @@ class BlockDrafter:
         """x += h @ w^T summed over ranks."""
         if self.tp == 1:
             self.ops.linear_residual(h, w, x)
+        elif self.target.fused_ar and self.comm.fused_fits(*x.shape):
+            self.ops.linear_allreduce(h, w, x, self.comm)
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
             slot, part = self.comm.slot_out(*x.shape)
             self.ops.linear(h, w, out=part)

@@ -111,12 +111,7 @@ class MTPDrafter:
         return x
 
     def _row_par_add(self, h, w, x):
-        if self.tp == 1:
-            self.ops.linear_residual(h, w, x)
-        else:
-            part = self.ops.linear(h, w, out_dtype=torch.float32)
-            self.comm.all_reduce_(part)
-            x += part
+        self.target._row_parallel(h, w, x)      # same collectives as the target's out-projections
 
     # ------------------------------------------------------------------ driver interface
     # History row p holds (embed(token_{p+1}), h_p) at rotary / cache position p, so every committed

@@ -172,6 +172,7 @@ class HybridTarget:
         self.dtype = dtype
         self.ops = ops or TorchOps()
         self.comm = comm or NullComm()
+        self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_allreduce")
         tp, r = self.comm.world, self.comm.rank
         self.tp, self.rank = tp, r
         self.widths = tp_widths(cfg, tp)
@@ -285,6 +286,8 @@ class HybridTarget:
         """x += h @ w^T summed over ranks (row-parallel out-projection + residual add)."""
         if self.tp == 1:
             self.ops.linear_residual(h, w, x)
+        elif self.fused_ar and self.comm.fused_fits(*x.shape):
+            self.ops.linear_allreduce(h, w, x, self.comm)     # GEMM + all-reduce + residual, one kernel
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
             slot, part = self.comm.slot_out(*x.shape)          # GEMM writes into peer memory
             self.ops.linear(h, w, out=part)

@@ -104,6 +104,18 @@ class NativeOps(TorchOps):
         self.launches += 1
         return out
 
+    def linear_allreduce(self, x, w, residual, comm):
+        """residual += sum over tensor-parallel ranks of x @ w^T in ONE kernel: the GEMM pushes each
+        finished fp32 tile into every rank's receive buffer over NVLink and reduces its own tile
+        (``comm``: a ``SymmComm``; T <= 32 rows)."""
+        w = self.prepare_weight(w)
+        slot = comm.fused_slot()
+        self.C.linear_allreduce(x.contiguous(), w.t, w.N, residual, self.ws, self.counters, self.err,
+                                comm.recv_ptrs, comm.fflag_ptrs, comm.rank, slot, comm.block_floats,
+                                comm.tiles_max, comm.fepochs)
+        self.launches += 1
+        return residual
+
     def linear_residual(self, x, w, residual):
         w = self.prepare_weight(w)
         self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)

@@ -10,6 +10,10 @@ collectives with the kernels in ``csrc/comm.cu``:
 * ``argmax_reduce(val, idx)`` - cross-rank (value, index) argmax for the vocab-parallel LM head
   and every Markov step.
 
+* fused GEMM + all-reduce (``NativeOps.linear_allreduce``): the out-projection kernel itself pushes
+  its fp32 tiles into every rank's receive area and reduces its own tile (the ``fused_*`` areas
+  below: blocks [slot][source rank], flags [slot][tile][source rank]).
+
 Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
 
 Slot reuse is safe when two uses of one slot are separated by another collective: a rank writes a
@@ -32,8 +36,10 @@ AR_CTAS = 32
 
 class SymmComm(TorchComm):
     def __init__(self, device, hidden: int, group=None, slot_rows: int = 32, graph_slots: int = 768,
-                 eager_slots: int = 64):
+                 eager_slots: int = 64, fused_graph_slots: int = 160, fused_eager_slots: int = 32,
+                 tiles_max: int = 64, fused: bool = True):
         super().__init__(group)
+        self.fused = fused          # row-parallel GEMMs use the fused GEMM + all-reduce kernel
         if self.world > MAX_RANKS:
             raise ValueError("peer-memory collectives serve at most 8 ranks")
         self.C = load()
@@ -45,7 +51,14 @@ class SymmComm(TorchComm):
         self.graph_slots, self.eager_slots = graph_slots, eager_slots
         data_bytes = self.n_slots * self.slot_floats * 4
         flag_bytes = self.n_slots * AR_CTAS * MAX_RANKS * 4
-        self.buf = self.C.peer_alloc(data_bytes + flag_bytes, dev)
+        # fused GEMM + all-reduce areas
+        self.block_floats = self.slot_floats
+        self.tiles_max = tiles_max
+        self.fused_graph_slots, self.fused_eager_slots = fused_graph_slots, fused_eager_slots
+        n_fused = fused_graph_slots + fused_eager_slots
+        recv_bytes = n_fused * self.world * self.block_floats * 4
+        fflag_bytes = n_fused * tiles_max * MAX_RANKS * 4
+        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes + fflag_bytes, dev)
         handle = self.C.ipc_handle(self.buf).to(self.device)
         handles = [torch.empty_like(handle) for _ in range(self.world)]
         dist.all_gather(handles, handle, group=self.group)
@@ -61,6 +74,11 @@ class SymmComm(TorchComm):
                 ptrs.append(ptr)
         self.data_ptrs = ptrs
         self.flag_ptrs = [p + data_bytes for p in ptrs]
+        self.recv_ptrs = [p + data_bytes + flag_bytes for p in ptrs]
+        self.fflag_ptrs = [p + data_bytes + flag_bytes + recv_bytes for p in ptrs]
+        self.fepochs = torch.zeros(n_fused * tiles_max, dtype=torch.int32, device=self.device)
+        self._next_fgraph = 0
+        self._next_feager = 0
         self.local = self.buf[:data_bytes].view(torch.float32).view(self.n_slots, self.slot_floats)
         self.epochs = torch.zeros(self.n_slots * AR_CTAS, dtype=torch.int32, device=self.device)
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
@@ -72,6 +90,22 @@ class SymmComm(TorchComm):
     def begin_capture(self):
         """Called before capturing a graph: its collectives take slots 0, 1, 2, ..."""
         self._next_graph = 0
+        self._next_fgraph = 0
+
+    def fused_slot(self) -> int:
+        """Slot of the fused GEMM + all-reduce areas (same reuse rule as ``_slot``)."""
+        if torch.cuda.is_current_stream_capturing():
+            if self._next_fgraph >= self.fused_graph_slots:
+                raise RuntimeError("out of fused collective slots; raise fused_graph_slots")
+            s = self._next_fgraph
+            self._next_fgraph += 1
+            return s
+        s = self.fused_graph_slots + self._next_feager
+        self._next_feager = (self._next_feager + 1) % self.fused_eager_slots
+        return s
+
+    def fused_fits(self, rows: int, cols: int) -> bool:
+        return rows <= min(32, self.slot_rows) and rows * cols <= self.block_floats and -(-cols // 128) <= self.tiles_max
 
     def _slot(self) -> int:
         if torch.cuda.is_current_stream_capturing():

@@ -1,6 +1,8 @@
 """Tensor parallel on GPUs (one process per GPU): at TP2 the native runtime's speculative output
-equals its own greedy decode on full-width layer shapes, with the in-kernel peer-memory
-collectives and with NCCL.  Skipped with fewer than two GPUs."""
+equals its own greedy decode on full-width layer shapes, with the GEMM kernels that carry the
+all-reduce, with the separate peer-memory collectives and with NCCL; the fused GEMM + all-reduce
+kernel adds the same bits on both ranks as GEMM -> peer all-reduce -> add.  Skipped with fewer
+than two GPUs."""
 import os
 import socket
 
@@ -41,7 +43,8 @@ def _worker(rank, world, port, q, mode):
         ops = NativeOps(device=f"cuda:{rank}", max_keys=2048)
         tgt = HybridTarget(cfg, random_target_source(cfg, 0), RuntimeConfig(max_context=1024, prefill_chunk=256),
                            device=f"cuda:{rank}", dtype=torch.bfloat16, ops=ops,
-                           comm=make_comm(2, device=f"cuda:{rank}", hidden=cfg.hidden_size, peer=(mode == "peer")))
+                           comm=make_comm(2, device=f"cuda:{rank}", hidden=cfg.hidden_size, peer=(mode != "nccl"),
+                                          fused=(mode == "fused")))
         dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt)
         prompt = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(2)).tolist()
         gold = greedy_reference(tgt, prompt, 24)
@@ -60,7 +63,7 @@ def _worker(rank, world, port, q, mode):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("mode", ["peer", "nccl"])
+@pytest.mark.parametrize("mode", ["fused", "peer", "nccl"])
 def test_tp2_native_speculative_equals_greedy(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
@@ -80,3 +83,73 @@ def test_tp2_native_speculative_equals_greedy(mode):
         assert err is None, err
         assert spec == gold
     assert out[0][1] == out[1][1]          # both ranks agree on every token
+
+
+def _kernel_worker(rank, world, port, q):
+    import datetime
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    comms = []
+    try:
+        from qwen38_b200.ops.native import NativeOps
+        from qwen38_b200.parallel.symm import SymmComm
+        ops = NativeOps(device=f"cuda:{rank}")
+        H = 5120
+        fused, plain = SymmComm(f"cuda:{rank}", H, fused=True), SymmComm(f"cuda:{rank}", H, fused=False)
+        comms = [fused, plain]
+        res = []
+        for T, K in ((1, 3072), (16, 8704), (32, 3072)):
+            g = torch.Generator(device="cuda").manual_seed(100 * T + rank)      # rank-local operands
+            x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
+            w = ops.prepare_weight((torch.randn(H, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16))
+            g0 = torch.Generator(device="cuda").manual_seed(T)                  # shared residual
+            r0 = torch.randn(T, H, generator=g0, device="cuda")
+            a = r0.clone()
+            for _ in range(3):                                                  # epochs advance
+                a.copy_(r0)
+                ops.linear_allreduce(x, w, a, fused)
+            s, part = plain.slot_out(T, H)
+            ops.linear(x, w, out=part)
+            b = r0.clone()
+            plain.reduce_slot_add(s, b)
+            ref = ops.linear(x, w, out_dtype=torch.float32)
+            dist.all_reduce(ref)
+            torch.cuda.synchronize()
+            res.append((T, bool(torch.equal(a, b)), ((a - (r0 + ref)).abs().max().item()), a.cpu()))
+        ops.check()
+        fused.check()
+        plain.check()
+        q.put((rank, res, None))
+    except BaseException as e:
+        q.put((rank, None, repr(e)))
+    finally:
+        torch.cuda.synchronize()
+        for c in comms:
+            c.close()
+        dist.destroy_process_group()
+
+
+def test_tp2_fused_gemm_allreduce_bits():
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _port()
+    procs = [ctx.Process(target=_kernel_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        out = sorted([q.get(timeout=600) for _ in procs], key=lambda o: o[0])
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    for rank, res, err in out:
+        assert err is None, err
+        for T, same, maxdiff, _ in res:
+            assert same, f"rank {rank} T={T}: fused and separate all-reduce differ"
+            assert maxdiff < 1e-3
+    for (T0, _, _, a0), (T1, _, _, a1) in zip(out[0][1], out[1][1]):
+        assert torch.equal(a0, a1)             # replicated residual: identical bits on both ranks
