@@ -6,6 +6,12 @@ layout the reference loads in ``docker/qwen-c2-graft/graft/model_config.py:366-4
 names follow the DSpark inventory in ``scripts/ci/dspark_intake.py:27-57`` (``fc``,
 ``hidden_norm``, ``layers.N.*``, ``norm``, ``markov_head.markov_w{1,2}``).
 
+Block-FP8 checkpoints (``quantization_config.quant_method == "fp8"``, the format the reference
+dequantises in ``model_config.py:375-377``): a quantised weight is stored as ``float8_e4m3fn``
+with a companion ``<name>_scale_inv`` of one fp32 scale per ``weight_block_size`` block (128 x 128
+by default); ``SafetensorsSource`` dequantises on read (weight = fp8 value x block scale).
+``save_pretrained(..., fp8_block=(128, 128))`` writes that format.
+
 A ``TensorSource`` hands out one tensor at a time so the runtime can pack and shard layer by
 layer without materialising a second full copy of a 27B model; ``RandomSource`` derives every
 tensor from ``(seed, name)`` so all TP ranks see identical full tensors.
@@ -169,6 +175,13 @@ class SafetensorsSource(TensorSource):
     def __init__(self, path: str, prefix: str = ""):
         from safetensors import safe_open
         self.path, self.prefix = path, prefix
+        self.block = (128, 128)
+        cfg_path = os.path.join(path, "config.json")
+        if os.path.exists(cfg_path):
+            with open(cfg_path) as f:
+                qc = json.load(f).get("quantization_config") or {}
+            if qc.get("weight_block_size"):
+                self.block = tuple(int(b) for b in qc["weight_block_size"])
         index = os.path.join(path, "model.safetensors.index.json")
         if os.path.exists(index):
             with open(index) as f:
@@ -186,16 +199,47 @@ class SafetensorsSource(TensorSource):
             self._where.update(wm)
 
     def names(self):
-        return [k[len(self.prefix):] for k in self._where if k.startswith(self.prefix)]
+        return [k[len(self.prefix):] for k in self._where
+                if k.startswith(self.prefix) and not k.endswith("_scale_inv")]
 
     def get(self, name, device=None, dtype=None):
         key = self.prefix + name
         t = self._handles[self._where[key]].get_tensor(key)
+        if t.dtype == torch.float8_e4m3fn and key + "_scale_inv" in self._where:
+            sk = key + "_scale_inv"
+            t = dequant_fp8_block(t, self._handles[self._where[sk]].get_tensor(sk), self.block)
         if device is not None:
             t = t.to(device)
         if dtype is not None and t.is_floating_point() and not name.endswith(("A_log", "dt_bias")):
             t = t.to(dtype)
         return t
+
+
+def quant_fp8_block(w: torch.Tensor, block=(128, 128)):
+    """2-D weight -> (float8_e4m3fn values, fp32 scale_inv [ceil(N/bn), ceil(K/bk)]) with one
+    scale per block chosen so the block's largest magnitude maps to the e4m3 maximum (448)."""
+    bn, bk = block
+    N, K = w.shape
+    nb, kb = -(-N // bn), -(-K // bk)
+    wp = torch.zeros(nb * bn, kb * bk, dtype=torch.float32)
+    wp[:N, :K] = w.float()
+    blocks = wp.view(nb, bn, kb, bk)
+    amax = blocks.abs().amax(dim=(1, 3)).clamp(min=1e-12)
+    scale_inv = amax / 448.0
+    q = (blocks / scale_inv[:, None, :, None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(nb * bn, kb * bk)[:N, :K].contiguous(), scale_inv.contiguous()
+
+
+def dequant_fp8_block(q: torch.Tensor, scale_inv: torch.Tensor, block=(128, 128)) -> torch.Tensor:
+    bn, bk = block
+    N, K = q.shape
+    s = scale_inv.float().repeat_interleave(bn, 0).repeat_interleave(bk, 1)[:N, :K]
+    return q.float() * s
+
+
+def _fp8_quantised(name: str, t: torch.Tensor) -> bool:
+    """Linear-layer weights are quantised; embeddings, LM head, norms and gate parameters stay."""
+    return t.dim() == 2 and name.endswith(("proj.weight", "proj_qkv.weight", "proj_z.weight", "fc.weight"))
 
 
 def random_target_source(cfg: ModelConfig, seed: int = 0) -> RandomSource:
@@ -211,18 +255,33 @@ def materialize(src: TensorSource, device="cpu", dtype=torch.float32) -> dict:
 
 
 def save_pretrained(path: str, cfg: ModelConfig, src: TensorSource, dtype=torch.bfloat16,
-                    shard_bytes: int = 4 << 30, drafter: tuple | None = None):
+                    shard_bytes: int = 4 << 30, drafter: tuple | None = None, fp8_block: tuple | None = None):
     """Write ``config.json`` and (sharded) ``model.safetensors`` in HF layout.  ``drafter`` is an
-    optional ``(DrafterConfig, TensorSource)`` written under ``path/drafter``."""
+    optional ``(DrafterConfig, TensorSource)`` written under ``path/drafter``.  ``fp8_block``
+    (e.g. ``(128, 128)``) stores linear-layer weights as block-scaled FP8."""
     from safetensors.torch import save_file
     os.makedirs(path, exist_ok=True)
+    meta = {"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"],
+            "text_config": cfg.to_hf_text_config(), "tie_word_embeddings": cfg.tie_word_embeddings}
+    if fp8_block:
+        meta["quantization_config"] = {"quant_method": "fp8", "fmt": "e4m3", "activation_scheme": "dynamic",
+                                       "weight_block_size": list(fp8_block)}
     with open(os.path.join(path, "config.json"), "w") as f:
-        json.dump({"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"],
-                   "text_config": cfg.to_hf_text_config(), "tie_word_embeddings": cfg.tie_word_embeddings},
-                  f, indent=1)
+        json.dump(meta, f, indent=1)
     shards, cur, size = [], {}, 0
-    for n in src.names():
-        t = src.get(n, dtype=dtype).contiguous()
+
+    def entries():
+        for n in src.names():
+            if fp8_block:
+                t = src.get(n, dtype=torch.float32)
+                if _fp8_quantised(n, t):
+                    q, si = quant_fp8_block(t, fp8_block)
+                    yield n, q
+                    yield n + "_scale_inv", si
+                    continue
+            yield n, src.get(n, dtype=dtype).contiguous()
+
+    for n, t in entries():
         if size + t.numel() * t.element_size() > shard_bytes and cur:
             shards.append(cur)
             cur, size = {}, 0

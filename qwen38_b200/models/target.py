@@ -431,11 +431,10 @@ class HybridTarget:
         x = self.ops.embedding(tokens, self.embed).float()
         for i, L in enumerate(self.layers):
             h = self.ops.rms_norm(x, L["in_norm"], self.eps, self.dtype)
-            proj = self.ops.linear(h, L["w_in"])
             outs = []
             if L["kind"] == LINEAR:
                 j = self.gdn_index[i]
-                self.gdn_stash[j, :rows].copy_(proj)
+                proj = self.ops.linear(h, L["w_in"], out=self.gdn_stash[j, :rows])   # kept for commit
                 for seq, t in batch:
                     o0, n = seq.verify_rows
                     outs.append(self.ops.gdn_verify(proj[o0:o0 + n], self.conv[seq.slot, j], self.rec[seq.slot, j],
@@ -443,6 +442,7 @@ class HybridTarget:
                                                     L["dims"], self.dtype))
             else:
                 j = self.attn_index[i]
+                proj = self.ops.linear(h, L["w_in"])
                 for seq, t in batch:
                     o0, n = seq.verify_rows
                     pr = positions[o0:o0 + n]

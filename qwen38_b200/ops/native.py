@@ -99,7 +99,8 @@ class NativeOps(TorchOps):
                 out = torch.empty(T, N, dtype=torch.float32, device=x.device)
             self.C.linear(x, w.t, N, out, EPI_F32, self.ws, self.counters, self.err)
         else:
-            out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
+            if out is None:
+                out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
             self.C.linear(x, w.t, N, out, EPI_BF16, self.ws, self.counters, self.err)
         self.launches += 1
         return out

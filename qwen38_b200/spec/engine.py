@@ -20,6 +20,7 @@ from dataclasses import dataclass, field
 
 import torch
 
+from ..utils.trace import nvtx, token_digest
 from .greedy import GreedySession
 from .lookup import HybridDraft, Proposal
 
@@ -112,7 +113,8 @@ class SpecRuntime:
             t0 = self._event()
             prompt_dev = prompt_host.to(tgt.device, non_blocking=True)
             self.h2d_bytes += prompt_host.numel() * 8
-            seq, nxt, ck = self._prefill(prompt_host, prompt_dev)
+            with nvtx("prefill"):
+                seq, nxt, ck = self._prefill(prompt_host, prompt_dev)
             seed = int(nxt.item())
             self.d2h_bytes += 8
             t1 = self._event()
@@ -133,14 +135,16 @@ class SpecRuntime:
             marks = []                       # per block: (start, drafted, verified, committed) events
             while not s.finished:
                 e0 = self._event()
-                ticket = s.propose(request_id)
+                with nvtx("draft"):
+                    ticket = s.propose(request_id)
                 e1 = self._event()
                 n = len(ticket.tokens)
                 tok_host[:n] = torch.tensor(ticket.tokens, dtype=torch.long)
                 toks = tok_host[:n].to(tgt.device, non_blocking=True)
                 self.h2d_bytes += 8 * n
                 try:
-                    pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                    with nvtx("verify"):
+                        pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
                 except BaseException:
                     s.fail_verification(request_id, ticket)     # poison: the block never publishes
                     tgt.abort(seq)
@@ -158,7 +162,8 @@ class SpecRuntime:
                         nxt = list(ticket.tokens[1:rows]) + [predictions[rows - 1]]
                         self.drafter.append(vfeats[:rows], pos, next_tokens=nxt)
 
-                d = s.commit(request_id, ticket, predictions, publish)
+                with nvtx("commit"):
+                    d = s.commit(request_id, ticket, predictions, publish)
                 marks.append((e0, e1, e2, self._event()))
                 blocks.append((n, d.accepted, len(d.emitted)))
                 if gold_check is not None and s.emitted != gold_check[:len(s.emitted)]:
@@ -167,10 +172,15 @@ class SpecRuntime:
             tg_ms = self._elapsed_ms(t2, t3)
             committed = s.committed_decode_tokens
             phase = [0.0, 0.0, 0.0]
-            for a0, a1, a2, a3 in marks:     # draft, verify (+ read-back), select + commit + publish
-                phase[0] += self._elapsed_ms(a0, a1)
-                phase[1] += self._elapsed_ms(a1, a2)
-                phase[2] += self._elapsed_ms(a2, a3)
+            records = []
+            for (a0, a1, a2, a3), (rows, acc, emitted_n) in zip(marks, blocks):
+                # draft, verify (+ read-back), select + commit + publish
+                d_ms, v_ms, c_ms = self._elapsed_ms(a0, a1), self._elapsed_ms(a1, a2), self._elapsed_ms(a2, a3)
+                phase[0] += d_ms
+                phase[1] += v_ms
+                phase[2] += c_ms
+                records.append(dict(rows=rows, accepted=acc, committed=emitted_n, draft_ms=d_ms, verify_ms=v_ms,
+                                    commit_ms=c_ms, cycle_ms=d_ms + v_ms + c_ms))
             nb = max(1, len(marks))
             return dict(
                 tokens=list(s.emitted), prompt_tokens=int(prompt_host.numel()), pp_ms=pp_ms, tg_ms=tg_ms,
@@ -179,7 +189,9 @@ class SpecRuntime:
                 mean_accepted=sum(b[1] for b in blocks) / max(1, len(blocks)),
                 tokens_per_block=committed / max(1, len(blocks)), reused_prefix=ck.pos if ck else 0,
                 draft_ms_per_block=phase[0] / nb, verify_ms_per_block=phase[1] / nb,
-                commit_ms_per_block=phase[2] / nb)
+                commit_ms_per_block=phase[2] / nb,
+                prompt_sha256=token_digest(prompt_host), output_sha256=token_digest(s.emitted),
+                block_records=records)
         finally:
             if ck is not None:
                 self.prefix.unpin(ck)

@@ -1,0 +1,50 @@
+"""Offline lookup-acceptance scoring over a native tape and the block latency budget."""
+import pytest
+
+from qwen38_b200.config import RuntimeConfig
+from qwen38_b200.models.target import HybridTarget
+from qwen38_b200.spec.analysis import latency_budget, score_lookup, sweep_lookup
+from qwen38_b200.spec.engine import SpecRuntime, greedy_reference
+
+
+def test_lookup_scoring_on_a_periodic_tape():
+    prompt = [1, 2, 3, 4, 5, 6, 7, 8] * 4
+    emitted = ([1, 2, 3, 4, 5, 6, 7, 8] * 8)[:40]
+    r = score_lookup(prompt, emitted, vocab_size=16, max_new_tokens=40, max_rows=16)
+    assert r["committed"] == 39                         # every decode token after the prefill seed
+    assert r["mean_committed_per_block"] > 4            # nearest earlier period: 7-token proposals
+    assert [b["accepted"] for b in r["blocks"][:4]] == [7, 7, 7, 7]   # every proposal accepted
+    one = score_lookup(prompt, emitted, vocab_size=16, max_new_tokens=40, max_rows=1)
+    assert one["mean_committed_per_block"] == 1 and len(one["blocks"]) == 39
+    arms = sweep_lookup(prompt, emitted, vocab_size=16, max_new_tokens=40)
+    assert len(arms) == 6 * 4 * 2
+    assert max(a["mean_committed_per_block"] for a in arms) >= r["mean_committed_per_block"]
+
+
+def test_lookup_scoring_rejects_bad_tapes():
+    with pytest.raises(ValueError):
+        score_lookup([1, 2], [3, 4], vocab_size=16, max_new_tokens=4)            # incomplete tape
+    with pytest.raises(ValueError):
+        score_lookup([1, 2], [3, 9, 4], vocab_size=16, max_new_tokens=3, eos_ids=(9,))   # EOS mid-tape
+    with pytest.raises(ValueError):
+        score_lookup([1, 2], [3], vocab_size=16, max_new_tokens=1, max_rows=3)   # not a bucket
+
+
+def test_latency_budget():
+    blocks = [dict(rows=16, committed=8, draft_ms=2.0, verify_ms=12.0, commit_ms=1.0, cycle_ms=15.0)] * 4
+    b = latency_budget(blocks, target_tg=800)
+    assert b["observed_block_tg"] == pytest.approx(1000 * 8 / 15)
+    assert b["required_cycle_ms"] == pytest.approx(10.0)
+    assert b["zero_draft_ceiling_tg"] == pytest.approx(1000 * 8 / 13)
+    with pytest.raises(ValueError):
+        latency_budget(blocks + [dict(blocks[0], rows=8)])
+
+
+def test_generate_block_records_feed_the_budget(tiny):
+    rt = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], rt)
+    gold = greedy_reference(tgt, tiny["prompt"], 12)
+    res = SpecRuntime(tgt, None, verifier_rows=4).generate(tiny["prompt"], 12, gold_check=gold)
+    recs = res["block_records"]
+    assert len(recs) == res["blocks"] and sum(r["committed"] for r in recs) == res["committed"]
+    assert latency_budget(recs)["blocks"] == len(recs)
