@@ -150,6 +150,10 @@ def main():
         cfg = ModelConfig(**{**cfg.__dict__, "num_hidden_layers": args.layers,
                              "layer_types": cfg.layer_types[:args.layers]})
         dcfg.taps = [t for t in dcfg.taps if t < args.layers] or [args.layers - 1]
+    topo = None
+    if world > 1:
+        from qwen38_b200.parallel.topology import check_topology
+        topo = check_topology(world, comm=args.comm if args.ops == "native" else "nccl")
     comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm != "nccl" and args.ops == "native"),
                      fused=(args.comm == "fused"))
     rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=2048,
@@ -232,6 +236,7 @@ def main():
                        "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows,
                        "drafter_layers": dcfg.num_hidden_layers, "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
+                       "nvlinks": (topo or {}).get("nvlink_active_links"),
                        "mean_accepted_target": args.mean_accepted,
                        "l2": "inputs larger than L2: every step streams all weights (54 GB at TP1)"},
             "mean_accepted": round(statistics.mean(r["mean_accepted"] for r in results), 3),

@@ -85,8 +85,10 @@ class MTPDrafter:
         self.max_context = max_context or target.rt.max_context
         cap = self.max_context + 2 * (steps + 2)
         self.slots = slots
-        self.kctx_all = torch.zeros(slots, cap, Hkv, D, device=dev, dtype=dt)
-        self.vctx_all = torch.zeros(slots, cap, Hkv, D, device=dev, dtype=dt)
+        # [slot, layer (one), row, kv head, dim]: the block drafter's layout, so prefix checkpoints
+        # snapshot and restore either drafter the same way
+        self.kctx_all = torch.zeros(slots, 1, cap, Hkv, D, device=dev, dtype=dt)
+        self.vctx_all = torch.zeros(slots, 1, cap, Hkv, D, device=dev, dtype=dt)
         self.positions = [0] * slots         # MTP history rows written so far
         self._last_hidden = [None] * slots   # target hidden of the newest committed row
 
@@ -100,10 +102,10 @@ class MTPDrafter:
         a_in = ops.rms_norm(x, L["in_norm"], self.eps, self.dtype)
         proj = ops.linear(a_in, L["w_in"])
         q, gate = ops.attn_prep(proj, L["qn"], L["kn"], self.target.inv_freq, 1.0, self.cfg.rope_dim, L["dims"],
-                                self.eps, positions, self.kctx_all[slot], self.vctx_all[slot], None, 0)
+                                self.eps, positions, self.kctx_all[slot, 0], self.vctx_all[slot, 0], None, 0)
         if write_only:
             return None
-        o = ops.attn_decode(q, gate, self.kctx_all[slot], self.vctx_all[slot], None, positions, 0, self.dtype)
+        o = ops.attn_decode(q, gate, self.kctx_all[slot, 0], self.vctx_all[slot, 0], None, positions, 0, self.dtype)
         self._row_par_add(o, L["w_out"], x)
         f_in = ops.rms_norm(x, L["post_norm"], self.eps, self.dtype)
         gu = ops.linear_swiglu(f_in, L["w_gu"], GU_BLOCK)
@@ -130,7 +132,7 @@ class MTPDrafter:
             raise ValueError("the MTP drafter needs the committed successor of every published row")
         if pos != self.positions[slot]:
             raise ValueError(f"MTP history at {self.positions[slot]}, publication at {pos}")
-        if pos + n + self.P + 1 > self.kctx_all.shape[1]:
+        if pos + n + self.P + 1 > self.kctx_all.shape[2]:
             raise ValueError("MTP history capacity exceeded")
         hid = feats[:, -self.cfg.hidden_size:].float()
         toks = torch.as_tensor([int(t) for t in next_tokens[:n]], dtype=torch.long, device=self.device)

@@ -9,7 +9,8 @@ Endpoints: ``POST /v1/completions`` (``prompt`` as a list of token ids, or a str
 the byte-level fallback tokenizer below - checkpoints' own tokenizers need network access to
 fetch), ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).
 
-Run:  python -m qwen38_b200.serving.api --model tiny --port 8000
+Run:  python -m qwen38_b200.serving.api --profile single-stream-4k --set serving.port=8000
+      python -m qwen38_b200.serving.api --profile tiny-cpu            (CPU, tiny shape)
 """
 from __future__ import annotations
 
@@ -94,7 +95,8 @@ class EngineLoop:
         self.thread.join(timeout=10)
 
 
-def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0):
+def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0,
+              output_budget_multiple: int = 0):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import PlainTextResponse
 
@@ -116,6 +118,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
         if not ids:
             raise HTTPException(400, "empty prompt")
+        if output_budget_multiple and body.max_tokens % output_budget_multiple:
+            raise HTTPException(400, f"max_tokens must be a multiple of {output_budget_multiple}")
         # the first output token comes from the prefill; max_tokens counts output tokens
         done, box = loop.submit(ids, body.max_tokens, body.stop_token_ids or ())
         if not done.wait(timeout_s):
@@ -162,43 +166,21 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
 
 
 def main():
-    import torch
     import uvicorn
 
-    from ..checkpoint import random_drafter_source, random_target_source
-    from ..config import RuntimeConfig, full_drafter_config, full_model_config, tiny_drafter_config, tiny_model_config
-    from ..models.drafter import BlockDrafter
-    from ..models.target import HybridTarget
-    from .engine import ServingEngine
+    from ..runconfig import load_run_config
+    from .factory import build_engine
 
-    ap = argparse.ArgumentParser()
-    ap.add_argument("--model", default="tiny", choices=["tiny", "full"])
-    ap.add_argument("--checkpoint", default=None, help="HF-layout checkpoint directory (random init if absent)")
-    ap.add_argument("--slots", type=int, default=4)
-    ap.add_argument("--max-context", type=int, default=8192)
-    ap.add_argument("--host", default="127.0.0.1")
-    ap.add_argument("--port", type=int, default=8000)
+    ap = argparse.ArgumentParser(description="OpenAI-compatible completions server")
+    ap.add_argument("--profile", default=None, help="named profile from serving/profiles.yaml")
+    ap.add_argument("--config", default=None, help="YAML run configuration")
+    ap.add_argument("--set", action="append", default=[], metavar="SECTION.FIELD=VALUE")
     a = ap.parse_args()
-    cuda = torch.cuda.is_available()
-    cfg, dcfg = (full_model_config(), full_drafter_config()) if a.model == "full" else \
-        (tiny_model_config(), tiny_drafter_config())
-    if a.checkpoint:
-        from ..checkpoint import SafetensorsSource
-        from ..config import ModelConfig
-        cfg = ModelConfig.from_pretrained(a.checkpoint)
-        src = SafetensorsSource(a.checkpoint)
-    else:
-        src = random_target_source(cfg, 0)
-    ops = None
-    if cuda:
-        from ..ops.native import NativeOps
-        ops = NativeOps(max_keys=a.max_context + 64)
-    rt = RuntimeConfig(max_context=a.max_context)
-    tgt = HybridTarget(cfg, src, rt, device="cuda" if cuda else "cpu",
-                       dtype=torch.bfloat16 if cuda else torch.float32, ops=ops, max_slots=a.slots + 1)
-    dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, slots=a.slots)
-    eng = ServingEngine(tgt, dr, verifier_rows=dcfg.block_rows)
-    uvicorn.run(build_app(eng), host=a.host, port=a.port)
+    rc = load_run_config(a.config, profile=a.profile, overrides=a.set)
+    eng = build_engine(rc)
+    app = build_app(eng, timeout_s=rc.serving.request_timeout_s,
+                    output_budget_multiple=rc.serving.output_budget_multiple)
+    uvicorn.run(app, host=rc.serving.host, port=rc.serving.port)
 
 
 if __name__ == "__main__":

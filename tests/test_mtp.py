@@ -31,7 +31,7 @@ def test_mtp_history_rows_match_recomputation(tiny):
     gold = greedy_reference(tgt, tiny["prompt"], 12)
     SpecRuntime(tgt, mtp, verifier_rows=4).generate(tiny["prompt"], 12, gold_check=gold)
     n = mtp.positions[0]
-    k_inc = mtp.kctx_all[0, :n].clone()
+    k_inc = mtp.kctx_all[0, 0, :n].clone()
     # one-shot: prefill prompt + emitted tokens, publish every row at once
     full = tiny["prompt"] + gold[:-1]
     seq = tgt.new_sequence()
@@ -40,4 +40,4 @@ def test_mtp_history_rows_match_recomputation(tiny):
     mtp2 = MTPDrafter(src, tgt, steps=3)
     mtp2.append(feats, 0, next_tokens=full[1:] + [gold[-1]])
     assert mtp2.positions[0] == n
-    assert torch.allclose(mtp2.kctx_all[0, :n], k_inc, atol=2e-3)
+    assert torch.allclose(mtp2.kctx_all[0, 0, :n], k_inc, atol=2e-3)

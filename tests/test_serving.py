@@ -128,3 +128,34 @@ def test_poisson_loadgen_report(tiny):
     rep = run(eng, prompts, 12, arr, golds=golds, mean_accepted=1)
     assert rep["finished"] == 3 and rep["exact"]
     assert rep["committed_tokens"] == 3 * 11 and rep["aggregate_tok_s"] > 0
+
+
+def test_factory_builds_engines_from_profiles():
+    """``tiny-cpu`` profile -> engine; the MTP drafter serves packed requests token-exact; the
+    output budget multiple is enforced at the HTTP boundary."""
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    rc = load_run_config(profile="tiny-cpu", overrides=["serving.slots=2"])
+    eng = build_engine(rc)
+    assert eng.drafter is not None and eng.verifier_rows == 4
+    p = _prompt(31, 48)
+    gold = greedy_reference(eng.target, p, 8)
+    eng.add_request(p, 8, request_id="a")
+    eng.add_request(_prompt(32, 40), 8, request_id="b")
+    done = eng.run()
+    assert {r.request_id: r.output for r in done}["a"] == gold
+    rc = load_run_config(profile="tiny-cpu", overrides=["spec.drafter=mtp", "spec.block_rows=4", "serving.slots=2"])
+    eng = build_engine(rc)
+    gold = greedy_reference(eng.target, p, 10)
+    eng.add_request(p, 10, request_id="m1")
+    eng.add_request(_prompt(33, 30), 10, request_id="m2")
+    done = {r.request_id: r for r in eng.run()}
+    assert done["m1"].output == gold and done["m2"].state == FINISHED
+    app = build_app(eng, output_budget_multiple=4)
+    with TestClient(app) as client:
+        assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 6}).status_code == 400
+        assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 8}).status_code == 200
+    app.state.loop.close()
