@@ -11,6 +11,11 @@
 //              run in one CTA against one staged K/V tile.  Causal (target) or full (drafter).
 // attn_combine: merges the per-chunk (max, sum, o) partials in chunk order, applies
 //              sigmoid(gate) (graft/attention/tp.py:121-237 gated output), writes bf16.
+// attn_prefill: causal flash attention of a prefill chunk over the paged cache (K-ATTN-PREFILL;
+//              the reference's chunked / paged SDPA, graft/attention/tp.py:476,645).  One CTA per
+//              (16 query positions, KV head): warp w owns q head w of the GQA group, so each
+//              64-key K/V tile is staged once (cp.async, double-buffered) for all its heads;
+//              online softmax in registers, sigmoid(gate) epilogue, bf16 out.
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
@@ -331,17 +336,51 @@ __global__ void attn_combine_kernel(DecodeArgs a, const __nv_bfloat16* gate, lon
   const int qv = (hq % rep) * a.T + t;
   const int n_keys = a.causal ? a.qpos[t] + 1 : a.qpos[a.T - 1] + 1;
   const int ns = (n_keys + CH - 1) / CH;
-  float M = -INFINITY;
-  for (int s = 0; s < ns; ++s) M = fmaxf(M, a.part_ml[(((size_t)g * a.max_splits + s) * nqv + qv) * 2]);
+  // 1. every split's (max, sum) into shared memory in parallel, then the global max and the
+  //    per-split weights exp(m_s - M) once (fixed split order everywhere)
+  extern __shared__ float cm[];                 // [2 * ns]: weight, weighted sum
+  __shared__ float red[32];
+  __shared__ float Ms;
+  float mloc = -INFINITY;
+  for (int s = threadIdx.x; s < ns; s += blockDim.x) {
+    const size_t pidx = ((size_t)g * a.max_splits + s) * nqv + qv;
+    const float ms = a.part_ml[pidx * 2];
+    cm[2 * s] = ms;
+    cm[2 * s + 1] = a.part_ml[pidx * 2 + 1];
+    mloc = fmaxf(mloc, ms);
+  }
+  mloc = warp_max(mloc);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mloc;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    float M = -INFINITY;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) M = fmaxf(M, red[w]);
+    Ms = M;
+  }
+  __syncthreads();
+  const float M = Ms;
+  for (int s = threadIdx.x; s < ns; s += blockDim.x) {
+    const float ms = cm[2 * s];
+    const float wgt = ms == -INFINITY ? 0.f : __expf(ms - M);
+    cm[2 * s] = wgt;
+    cm[2 * s + 1] *= wgt;
+  }
+  __syncthreads();
+  float L = 0.f;
+  for (int s = 0; s < ns; ++s) L += cm[2 * s + 1];
+  // 2. weighted sum of the partial outputs, eight splits' loads in flight at a time
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    float acc = 0.f, L = 0.f;
-    for (int s = 0; s < ns; ++s) {
-      const size_t pidx = ((size_t)g * a.max_splits + s) * nqv + qv;
-      const float ms = a.part_ml[pidx * 2];
-      if (ms == -INFINITY) continue;
-      const float wgt = __expf(ms - M);
-      L += wgt * a.part_ml[pidx * 2 + 1];
-      acc += wgt * a.part_o[pidx * D + c];
+    float acc = 0.f;
+    for (int s0 = 0; s0 < ns; s0 += 8) {
+      float v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const int s = s0 + u;
+        v[u] = s < ns ? __ldg(a.part_o + (((size_t)g * a.max_splits + s) * nqv + qv) * D + c) : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < 8; ++u)
+        if (s0 + u < ns) acc += cm[2 * (s0 + u)] * v[u];
     }
     float y = acc / L;
     if (gate) {
@@ -352,6 +391,204 @@ __global__ void attn_combine_kernel(DecodeArgs a, const __nv_bfloat16* gate, lon
   }
 }
 
+struct PrefillArgs {
+  const __nv_bfloat16* q;      // [T, nq, D]
+  const __nv_bfloat16* kcache;
+  const __nv_bfloat16* vcache;
+  const int* block_table;      // nullptr: contiguous
+  int block_size;
+  const int* qpos;             // [T] absolute positions, increasing
+  int T, nq, nkv;
+  float scale;
+  const __nv_bfloat16* gate;   // [T, gate_ld] (+ head * D), nullptr: no gate
+  long long gate_ld;
+  __nv_bfloat16* out;          // [T, out_ld]
+  long long out_ld;
+};
+
+constexpr int PF_QT = 16;      // query positions per CTA
+constexpr int PF_KT = 64;      // keys per staged tile
+
+template <int D>
+__global__ void __launch_bounds__(256, 1)
+attn_prefill_kernel(PrefillArgs a) {
+  constexpr int DP = D + 8;
+  constexpr int NT_K = PF_KT / 8;
+  constexpr int NT_D = D / 8;
+  pdl_wait();
+  pdl_trigger();
+  const int qt = gridDim.x - 1 - blockIdx.x;     // longest (latest) query tiles first
+  const int g = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rep = a.nq / a.nkv;                  // == warps per CTA
+  const int t0 = qt * PF_QT;
+  const int nt = min(PF_QT, a.T - t0);
+  const int n_keys = a.qpos[t0 + nt - 1] + 1;
+  const int ntiles = (n_keys + PF_KT - 1) / PF_KT;
+
+  extern __shared__ __align__(16) uint8_t smem[];
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);          // [rep*16][DP]
+  __nv_bfloat16* KV = Qs + rep * PF_QT * DP;                            // [2 bufs][K, V][PF_KT][DP]
+  auto Ks = [&](int b) { return KV + (size_t)(2 * b) * PF_KT * DP; };
+  auto Vs = [&](int b) { return KV + (size_t)(2 * b + 1) * PF_KT * DP; };
+
+  auto kv_base = [&](int kp) -> size_t {
+    if (a.block_table) {
+      const int blk = a.block_table[kp / a.block_size];
+      return ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
+    }
+    return (size_t)kp * a.nkv + g;
+  };
+  auto load_tile = [&](int kt, int b) {
+    const int k0 = kt * PF_KT;
+    for (int idx = threadIdx.x; idx < PF_KT * (D / 8); idx += blockDim.x) {
+      const int j = idx / (D / 8), ch = idx % (D / 8);
+      const int kp = k0 + j;
+      uint4* dk = reinterpret_cast<uint4*>(Ks(b) + j * DP) + ch;
+      uint4* dv = reinterpret_cast<uint4*>(Vs(b) + j * DP) + ch;
+      if (kp < n_keys) {
+        const size_t base = kv_base(kp) * D;
+        cp_async16(dk, reinterpret_cast<const uint4*>(a.kcache + base) + ch);
+        cp_async16(dv, reinterpret_cast<const uint4*>(a.vcache + base) + ch);
+      } else {
+        *dk = make_uint4(0, 0, 0, 0);
+        *dv = make_uint4(0, 0, 0, 0);
+      }
+    }
+  };
+  // Q rows: warp w / row i <- q[t0 + i, g*rep + w, :]
+  for (int idx = threadIdx.x; idx < rep * PF_QT * (D / 8); idx += blockDim.x) {
+    const int r = idx / (D / 8), ch = idx % (D / 8);
+    const int w = r / PF_QT, i = r % PF_QT;
+    uint4* dst = reinterpret_cast<uint4*>(Qs + r * DP) + ch;
+    if (i < nt) cp_async16(dst, reinterpret_cast<const uint4*>(a.q + ((size_t)(t0 + i) * a.nq + g * rep + w) * D) + ch);
+    else *dst = make_uint4(0, 0, 0, 0);
+  }
+  load_tile(0, 0);
+  cp_async_commit();
+  if (ntiles > 1) {
+    load_tile(1, 1);
+    cp_async_commit();
+  }
+
+  // rows of this thread inside the warp's 16: lane/4 and lane/4 + 8
+  const int i_lo = lane >> 2, i_hi = i_lo + 8;
+  const int p_lo = i_lo < nt ? a.qpos[t0 + i_lo] : -1;
+  const int p_hi = i_hi < nt ? a.qpos[t0 + i_hi] : -1;
+  float O[NT_D][4];
+#pragma unroll
+  for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  const uint32_t qbase = smem_u32(Qs + (warp * PF_QT) * DP);
+
+  for (int kt = 0; kt < ntiles; ++kt) {
+    const int b = kt & 1;
+    if (kt + 1 < ntiles) cp_async_wait<1>();
+    else cp_async_wait<0>();
+    __syncthreads();
+    const int k0 = kt * PF_KT;
+    {
+      float S[NT_K][4];
+#pragma unroll
+      for (int n = 0; n < NT_K; ++n) S[n][0] = S[n][1] = S[n][2] = S[n][3] = 0.f;
+      const uint32_t kbase = smem_u32(Ks(b));
+#pragma unroll
+      for (int kk = 0; kk < D / 16; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ldsm_x4(qbase + (uint32_t)(((lane & 15) * DP + kk * 16 + (lane >> 4) * 8) * 2), a0, a1, a2, a3);
+#pragma unroll
+        for (int n = 0; n < NT_K; ++n) {
+          uint32_t b0, b1;
+          ldsm_x2(kbase + (uint32_t)(((n * 8 + (lane & 7)) * DP + kk * 16 + ((lane >> 3) & 1) * 8) * 2), b0, b1);
+          mma_bf16_16816(S[n], a0, a1, a2, a3, b0, b1);
+        }
+      }
+      // causal mask + online softmax
+      float tm_lo = -INFINITY, tm_hi = -INFINITY;
+#pragma unroll
+      for (int n = 0; n < NT_K; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int kp = k0 + n * 8 + (lane & 3) * 2 + e;
+          S[n][e] = kp <= p_lo ? S[n][e] * a.scale : -INFINITY;
+          S[n][2 + e] = kp <= p_hi ? S[n][2 + e] * a.scale : -INFINITY;
+          tm_lo = fmaxf(tm_lo, S[n][e]);
+          tm_hi = fmaxf(tm_hi, S[n][2 + e]);
+        }
+      }
+      tm_lo = fmaxf(tm_lo, __shfl_xor_sync(0xffffffffu, tm_lo, 1));
+      tm_lo = fmaxf(tm_lo, __shfl_xor_sync(0xffffffffu, tm_lo, 2));
+      tm_hi = fmaxf(tm_hi, __shfl_xor_sync(0xffffffffu, tm_hi, 1));
+      tm_hi = fmaxf(tm_hi, __shfl_xor_sync(0xffffffffu, tm_hi, 2));
+      const float mn_lo = fmaxf(m_lo, tm_lo), mn_hi = fmaxf(m_hi, tm_hi);
+      const float mz_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
+      const float mz_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+      const float c_lo = __expf(m_lo - mz_lo), c_hi = __expf(m_hi - mz_hi);   // exp(-inf) = 0 on the first tile
+      m_lo = mn_lo;
+      m_hi = mn_hi;
+      l_lo *= c_lo;
+      l_hi *= c_hi;
+#pragma unroll
+      for (int n = 0; n < NT_D; ++n) {
+        O[n][0] *= c_lo; O[n][1] *= c_lo;
+        O[n][2] *= c_hi; O[n][3] *= c_hi;
+      }
+#pragma unroll
+      for (int n = 0; n < NT_K; ++n) {
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          S[n][e] = __expf(S[n][e] - mz_lo);
+          S[n][2 + e] = __expf(S[n][2 + e] - mz_hi);
+          l_lo += S[n][e];
+          l_hi += S[n][2 + e];
+        }
+      }
+      const uint32_t vbase = smem_u32(Vs(b));
+#pragma unroll
+      for (int j = 0; j < PF_KT / 16; ++j) {
+        const uint32_t a0 = pack_bf16(S[2 * j][0], S[2 * j][1]);
+        const uint32_t a1 = pack_bf16(S[2 * j][2], S[2 * j][3]);
+        const uint32_t a2 = pack_bf16(S[2 * j + 1][0], S[2 * j + 1][1]);
+        const uint32_t a3 = pack_bf16(S[2 * j + 1][2], S[2 * j + 1][3]);
+#pragma unroll
+        for (int n = 0; n < NT_D; ++n) {
+          uint32_t b0, b1;
+          ldsm_x2_t(vbase + (uint32_t)(((j * 16 + (lane & 15)) * DP + n * 8) * 2), b0, b1);
+          mma_bf16_16816(O[n], a0, a1, a2, a3, b0, b1);
+        }
+      }
+    }
+    __syncthreads();                       // every warp is done with buffer b
+    if (kt + 2 < ntiles) {
+      load_tile(kt + 2, b);
+      cp_async_commit();
+    }
+  }
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f, inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
+  const int hq = g * rep + warp;
+#pragma unroll
+  for (int n = 0; n < NT_D; ++n) {
+    const int d = n * 8 + (lane & 3) * 2;
+#pragma unroll
+    for (int half = 0; half < 2; ++half) {
+      const int i = half ? i_hi : i_lo;
+      if (i >= nt) continue;
+      const float inv = half ? inv_hi : inv_lo;
+      float y0 = O[n][2 * half] * inv, y1 = O[n][2 * half + 1] * inv;
+      const size_t t = (size_t)(t0 + i);
+      if (a.gate) {
+        const __nv_bfloat162 gv = *reinterpret_cast<const __nv_bfloat162*>(a.gate + t * a.gate_ld + (size_t)hq * D + d);
+        y0 *= 1.f / (1.f + __expf(-__bfloat162float(gv.x)));
+        y1 *= 1.f / (1.f + __expf(-__bfloat162float(gv.y)));
+      }
+      *reinterpret_cast<__nv_bfloat162*>(a.out + t * a.out_ld + (size_t)hq * D + d) = __floats2bfloat162_rn(y0, y1);
+    }
+  }
+}
 }  // namespace q38
 
 // ----------------------------------------------------------------------------- bindings
@@ -428,8 +665,51 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
 #undef Q38_DEC
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   const __nv_bfloat16* gp = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
-  q38::launch_pdl(q38::attn_combine_kernel, dim3(nq, T), dim3(std::min(D, 256)), 0, st, a, gp,
+  q38::launch_pdl(q38::attn_combine_kernel, dim3(nq, T), dim3(std::min(D, 256)),
+                  (size_t)2 * a.max_splits * sizeof(float), st, a, gp,
                   (long long)(gate ? gate->stride(0) : 0), (int)gate_off,
                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
+                      c10::optional<torch::Tensor> gate, torch::Tensor out) {
+  c10::cuda::CUDAGuard guard(q.device());
+  const int T = (int)q.size(0), nq = (int)q.size(1), D = (int)q.size(2);
+  const int nkv = (int)kcache.size(-2);
+  TORCH_CHECK(q.is_contiguous() && q.scalar_type() == at::kBFloat16, "contiguous bf16 q [T, nq, D]");
+  TORCH_CHECK(nq % nkv == 0 && nq / nkv >= 1 && nq / nkv <= 8, "GQA group of 1..8 heads");
+  TORCH_CHECK(qpos.scalar_type() == at::kInt && qpos.numel() == T, "int32 positions [T]");
+  TORCH_CHECK(out.stride(1) == 1 && out.size(0) == T && out.size(1) >= (int64_t)nq * D, "out [T, >= nq*D]");
+  TORCH_CHECK(!gate || (gate->stride(1) == 1 && gate->stride(0) % 2 == 0), "row-contiguous gate");
+  q38::PrefillArgs a{};
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.kcache = reinterpret_cast<const __nv_bfloat16*>(kcache.data_ptr());
+  a.vcache = reinterpret_cast<const __nv_bfloat16*>(vcache.data_ptr());
+  a.block_table = block_table ? block_table->data_ptr<int>() : nullptr;
+  a.block_size = (int)block_size;
+  a.qpos = qpos.data_ptr<int>();
+  a.T = T; a.nq = nq; a.nkv = nkv;
+  a.scale = (float)scale;
+  a.gate = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
+  a.gate_ld = gate ? gate->stride(0) : 0;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.out_ld = out.stride(0);
+  const int rep = nq / nkv;
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  dim3 grid((unsigned)((T + q38::PF_QT - 1) / q38::PF_QT), (unsigned)nkv);
+#define Q38_PF(DD)                                                                                  \
+  {                                                                                                 \
+    const size_t smem = (size_t)(rep * q38::PF_QT + 4 * q38::PF_KT) * (DD + 8) * 2;                 \
+    auto k = q38::attn_prefill_kernel<DD>;                                                          \
+    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                \
+    TORCH_CHECK(q38::launch_pdl(k, grid, dim3(rep * 32), smem, st, a) == cudaSuccess, "prefill attention launch"); \
+  }
+  if (D == 256) Q38_PF(256)
+  else if (D == 128) Q38_PF(128)
+  else if (D == 64) Q38_PF(64)
+  else TORCH_CHECK(false, "head dim 64/128/256 supported");
+#undef Q38_PF
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

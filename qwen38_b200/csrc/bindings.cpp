@@ -24,6 +24,9 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
                      torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
+                      c10::optional<torch::Tensor> gate, torch::Tensor out);
 void q38_gdn_chunk_prefill(torch::Tensor proj, torch::Tensor window, torch::Tensor state, torch::Tensor conv_w,
                            torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor out,
                            torch::Tensor work, int64_t nk, int64_t nv, double eps);
@@ -56,6 +59,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_workspace_bytes", &q38_gdn_chunk_workspace_bytes);
   m.def("attn_prep", &q38_attn_prep);
   m.def("attn_decode", &q38_attn_decode);
+  m.def("attn_prefill", &q38_attn_prefill);
   m.def("rms_norm", &q38_rms_norm);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);

@@ -138,11 +138,12 @@ gdn_recurrent_kernel(GdnArgs a) {
       else if (c2 < 2 * D) ch = ck + (c2 - D);
       else if (c2 < 2 * D + COLS) ch = cv + (c2 - 2 * D);
       else ch = cz + (c2 - 2 * D - COLS);
-      uint32_t v = 0;
-      if (r >= 0) v = *reinterpret_cast<const uint32_t*>(proj + (size_t)r * a.proj_ld + ch);
-      else if (c2 < 2 * D + COLS) v = *reinterpret_cast<const uint32_t*>(window + (size_t)(r + KC - 1) * a.C + ch);
-      *reinterpret_cast<uint32_t*>(&raw[i][c2]) = v;
+      // asynchronous 4-byte copies: every load of the sub-block is in flight at once
+      if (r >= 0) cp_async4(&raw[i][c2], proj + (size_t)r * a.proj_ld + ch);
+      else if (c2 < 2 * D + COLS) cp_async4(&raw[i][c2], window + (size_t)(r + KC - 1) * a.C + ch);
+      else *reinterpret_cast<uint32_t*>(&raw[i][c2]) = 0u;
     }
+    cp_async_commit();
     if (tid < nsub) {
       const int r = r0 + tid;
       const float av = __bfloat162float(proj[(size_t)r * a.proj_ld + ca]);
@@ -151,6 +152,7 @@ gdn_recurrent_kernel(GdnArgs a) {
       g_s[tid] = A * sp;
       b_s[tid] = 1.f / (1.f + __expf(-bv));
     }
+    cp_async_wait<0>();
     __syncthreads();
     // ---- 2. conv + SiLU: q/k channels (one or more per thread, every row), v column per (col, part)
 #pragma unroll

@@ -211,13 +211,28 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         do_epi = *last_flag != 0;
         if (do_epi) {
           __threadfence();
+          // Sum the partials in split order; the loads of two splits are in flight together
+          // (L2 loads: the partials were written by other CTAs of this grid).
           const float* base = g.ws + (size_t)tile * g.splits * (BM * BN);
 #pragma unroll
           for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-          for (int s = 0; s < g.splits; ++s) {
-            const volatile float* p = base + (size_t)s * (BM * BN);
+          int s = 0;
+          for (; s + 1 < g.splits; s += 2) {
+            const float* p0 = base + (size_t)s * (BM * BN);
+            const float* p1 = p0 + BM * BN;
+            float x0[32], x1[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] += p[j * BM + row];
+            for (int j = 0; j < 32; ++j) {
+              x0[j] = __ldcg(p0 + j * BM + row);
+              x1[j] = __ldcg(p1 + j * BM + row);
+            }
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] = (acc[j] + x0[j]) + x1[j];
+          }
+          if (s < g.splits) {
+            const float* p0 = base + (size_t)s * (BM * BN);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) acc[j] += __ldcg(p0 + j * BM + row);
           }
           if (tid == 0) g.counters[tile] = 0;
         }
@@ -304,15 +319,33 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
           __syncthreads();
           if (*last_flag && m < g.M) {
-            const float* rb = reinterpret_cast<const float*>(a.recv[a.rank]) + (size_t)a.slot * a.world * a.block_floats;
-            float* res = reinterpret_cast<float*>(g.out);
+            // Issue every load of a group of 8 token columns (W partials + the residual) before
+            // any arithmetic: one memory round trip per group instead of one per column.
+            const float* __restrict__ rb =
+                reinterpret_cast<const float*>(a.recv[a.rank]) + (size_t)a.slot * a.world * a.block_floats;
+            float* __restrict__ res = reinterpret_cast<float*>(g.out);
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < nvalid) {
-                const size_t off = (size_t)(n0 + j) * g.ldo + m;
-                float sum = 0.f;
-                for (int q = 0; q < a.world; ++q) sum += __ldcg(rb + (size_t)q * a.block_floats + off);
-                res[off] += sum;
+            for (int j0 = 0; j0 < 32; j0 += 8) {
+              float v[8][AR_MAX_RANKS], r[8];
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                const size_t off = (size_t)(n0 + j0 + jj) * g.ldo + m;
+                if (j0 + jj < nvalid) {
+                  r[jj] = res[off];
+#pragma unroll
+                  for (int q = 0; q < AR_MAX_RANKS; ++q)
+                    v[jj][q] = q < a.world ? __ldcg(rb + (size_t)q * a.block_floats + off) : 0.f;
+                }
+              }
+#pragma unroll
+              for (int jj = 0; jj < 8; ++jj) {
+                if (j0 + jj < nvalid) {
+                  float sum = 0.f;
+#pragma unroll
+                  for (int q = 0; q < AR_MAX_RANKS; ++q)
+                    if (q < a.world) sum += v[jj][q];
+                  res[(size_t)(n0 + j0 + jj) * g.ldo + m] = r[jj] + sum;
+                }
               }
             }
           }

@@ -245,24 +245,13 @@ class NativeOps(TorchOps):
         return out
 
     def attn_prefill(self, q, gate, kcache, vcache, block_table, positions, block_size, out_dtype):
-        """Causal prefill attention of a chunk over the paged cache.  Library flash-attention
-        (torch SDPA) on gathered K/V: the baseline path for this op."""
-        import torch.nn.functional as F
-        from torch.nn.attention.bias import causal_lower_right
+        """Causal prefill attention of a chunk over the paged cache (``attn_prefill_kernel``:
+        flash attention on tensor cores, GQA heads of a KV head in one CTA, sigmoid-gate epilogue)."""
         T, H, D = q.shape
-        n = int(positions[-1].item()) + 1
-        K, V = self._gather_kv(kcache, vcache, block_table, block_size, n)
-        qh = q.transpose(0, 1)[None]                     # [1, H, T, D]
-        kh = K.transpose(0, 1)[None]
-        vh = V.transpose(0, 1)[None]
-        rep = H // kh.shape[1]
-        if rep > 1:
-            kh = kh.repeat_interleave(rep, 1)
-            vh = vh.repeat_interleave(rep, 1)
-        o = F.scaled_dot_product_attention(qh, kh, vh, attn_mask=causal_lower_right(T, n))
-        o = o[0].transpose(0, 1).reshape(T, H * D)
-        o = o * torch.sigmoid(gate.float()).to(o.dtype)
-        return o.to(out_dtype)
+        out = torch.empty(T, H * D, dtype=torch.bfloat16, device=q.device)
+        self.C.attn_prefill(q.contiguous(), kcache, vcache, block_table, block_size, positions, D ** -0.5, gate, out)
+        self.launches += 1
+        return out if out_dtype == torch.bfloat16 else out.to(out_dtype)
 
     def kv_append(self, kv, kn_w, inv_freq, rope_scale, rd, nkv, D, eps, positions, kcache, vcache):
         self.C.attn_prep(kv, -1, 0, nkv * D, 0, nkv, D, rd, kn_w, kn_w, inv_freq, float(rope_scale), float(eps),

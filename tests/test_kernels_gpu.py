@@ -184,6 +184,21 @@ def test_attention_prep_and_decode(nops, T, pos0):
     nops.check()
 
 
+@pytest.mark.parametrize("T,pos0,H,Hkv", [(40, 0, 6, 1), (300, 1000, 6, 1), (2048, 2048, 6, 1), (77, 5, 3, 1),
+                                           (64, 64, 4, 2)])
+def test_attention_prefill_kernel(nops, T, pos0, H, Hkv):
+    """Hand-written prefill flash attention (paged, causal, GQA, sigmoid gate) vs the fp32 reference."""
+    proj, qn, kn, inv, rd, dims, pos, kc, vc, bt, bs = _attn_case(T, pos0, H=H, Hkv=Hkv)
+    kc2, vc2 = kc.clone(), vc.clone()
+    tops = TorchOps()
+    q_ref, gate = tops.attn_prep(proj.float(), qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc2, vc2, bt, bs)
+    q, gate_n = nops.attn_prep(proj, qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc, vc, bt, bs)
+    ref = tops.attn_decode(q_ref.float(), gate.float(), kc2.float(), vc2.float(), bt, pos, bs, torch.float32)
+    out = nops.attn_prefill(q, gate_n, kc, vc, bt, pos, bs, torch.bfloat16)
+    assert _rel(out, ref) < 2e-2
+    nops.check()
+
+
 def test_markov_select(nops):
     P, V, Rk = 5, 3000, 64
     g = torch.Generator(device=DEV).manual_seed(15)

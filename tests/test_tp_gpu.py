@@ -4,7 +4,6 @@ all-reduce, with the separate peer-memory collectives and with NCCL; the fused G
 kernel adds the same bits on both ranks as GEMM -> peer all-reduce -> add.  Skipped with fewer
 than two GPUs."""
 import os
-import socket
 
 import pytest
 import torch
@@ -18,18 +17,25 @@ import torch.distributed as dist  # noqa: E402
 import torch.multiprocessing as mp  # noqa: E402
 
 
-def _port():
-    with socket.socket() as s:
-        s.bind(("127.0.0.1", 0))
-        return s.getsockname()[1]
+def _rdv():
+    """File rendezvous (no TCP port to race for between consecutive spawned groups)."""
+    import tempfile
+    fd, path = tempfile.mkstemp(prefix="q38_rdv_")
+    os.close(fd)
+    os.unlink(path)
+    return path
 
 
-def _worker(rank, world, port, q, mode):
+def _init(rank, world, rdv):
     import datetime
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    os.environ.update(NCCL_NVLS_ENABLE="0")
     torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
+    dist.init_process_group("nccl", init_method=f"file://{rdv}", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=120), device_id=torch.device("cuda", rank))
+
+
+def _worker(rank, world, rdv, q, mode):
+    _init(rank, world, rdv)
     try:
         from qwen38_b200.checkpoint import random_drafter_source, random_target_source
         from qwen38_b200.config import FULL, LINEAR, DrafterConfig, ModelConfig, RuntimeConfig
@@ -67,8 +73,8 @@ def _worker(rank, world, port, q, mode):
 def test_tp2_native_speculative_equals_greedy(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    rdv = _rdv()
+    procs = [ctx.Process(target=_worker, args=(r, 2, rdv, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     try:
@@ -85,12 +91,8 @@ def test_tp2_native_speculative_equals_greedy(mode):
     assert out[0][1] == out[1][1]          # both ranks agree on every token
 
 
-def _kernel_worker(rank, world, port, q):
-    import datetime
-    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
-    torch.cuda.set_device(rank)
-    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
-                            device_id=torch.device("cuda", rank))
+def _kernel_worker(rank, world, rdv, q):
+    _init(rank, world, rdv)
     comms = []
     try:
         from qwen38_b200.ops.native import NativeOps
@@ -134,8 +136,8 @@ def _kernel_worker(rank, world, port, q):
 def test_tp2_fused_gemm_allreduce_bits():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
-    port = _port()
-    procs = [ctx.Process(target=_kernel_worker, args=(r, 2, port, q)) for r in range(2)]
+    rdv = _rdv()
+    procs = [ctx.Process(target=_kernel_worker, args=(r, 2, rdv, q)) for r in range(2)]
     for p in procs:
         p.start()
     try:
