@@ -150,6 +150,10 @@ def main():
         cfg = ModelConfig(**{**cfg.__dict__, "num_hidden_layers": args.layers,
                              "layer_types": cfg.layer_types[:args.layers]})
         dcfg.taps = [t for t in dcfg.taps if t < args.layers] or [args.layers - 1]
+    from qwen38_b200.parallel.plan import check_tp_plan
+    bad = check_tp_plan(cfg, dcfg, world)
+    if bad:
+        raise SystemExit(f"TP={world} cannot run this shape: " + "; ".join(bad))
     topo = None
     if world > 1:
         from qwen38_b200.parallel.topology import check_topology

@@ -10,6 +10,8 @@ void q38_linear_allreduce(torch::Tensor x, torch::Tensor w, int64_t N, torch::Te
                           torch::Tensor counters, torch::Tensor err, std::vector<int64_t> recv_ptrs,
                           std::vector<int64_t> flag_ptrs, int64_t rank, int64_t slot, int64_t block_floats,
                           int64_t tiles_max, torch::Tensor epochs);
+int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace);
 void q38_clear_map_cache();
 void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, torch::Tensor state,
                        torch::Tensor conv_w, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
@@ -53,6 +55,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear", &q38_linear);
   m.def("lm_head_argmax", &q38_lm_head_argmax);
   m.def("linear_allreduce", &q38_linear_allreduce);
+  m.def("linear_trace", &q38_linear_trace);
   m.def("clear_map_cache", &q38_clear_map_cache);
   m.def("gdn_recurrent", &q38_gdn_recurrent);
   m.def("gdn_chunk_prefill", &q38_gdn_chunk_prefill);

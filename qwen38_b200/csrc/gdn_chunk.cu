@@ -90,32 +90,35 @@ struct PrepArgs {
   float* dec;                  // [nchunks, nv] exp(G_C)
 };
 
-// shared-memory plan (bytes)
+// shared-memory plan (bytes): two 51 KB regions reused phase by phase, so two CTAs fit per SM
+//   R0: raw rows [C+3][3D] bf16 (conv input)  ->  beta v, beta k exp(G) [C][DPAD] bf16 + A [C][C+4] f32
+//   R1: q, k, v [C][DPAD] bf16                ->  N [C][C+4] f32 + T [C][CPAD] bf16
 constexpr int RAW_B = (C + KC - 1) * 3 * D * 2;                 // 51,456
-constexpr int AM_B = C * (C + 4) * 4;                           // 17,408
-constexpr int TB_B = C * CPAD * 2;                              // 9,216
-constexpr int R1_B = (RAW_B > 2 * AM_B + TB_B) ? RAW_B : 2 * AM_B + TB_B;
-constexpr int Y_B = C * 3 * D * 4;                              // 98,304
 constexpr int QKV_B = 3 * C * DPAD * 2;                         // 52,224
-constexpr int PREP_SMEM = R1_B + Y_B + QKV_B + 4 * C * 4 + 64;
+constexpr int BVK_B = 2 * C * DPAD * 2;                         // 34,816
+constexpr int AM_B = C * (C + 4) * 4;                           // 17,408
+constexpr int R0_B = (RAW_B > BVK_B + AM_B ? RAW_B : BVK_B + AM_B);
+constexpr int R1_B = QKV_B;
+static_assert(R1_B >= AM_B + C * CPAD * 2, "N and T fit in R1");
+constexpr int PREP_SMEM = R0_B + R1_B + 5 * C * 4 + 64;
+constexpr int FB = 16;                                          // forward-substitution block
 
-__global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
-  pdl_wait();
-  pdl_trigger();
+__global__ void __launch_bounds__(256, 2) gdn_chunk_prep_kernel(PrepArgs a) {
   extern __shared__ __align__(16) uint8_t sm[];
-  __nv_bfloat16* raw = reinterpret_cast<__nv_bfloat16*>(sm);                  // [C+3][3D]
-  float* Am = reinterpret_cast<float*>(sm);                                    // [C][C+4] (after conv)
-  float* Nm = Am + C * (C + 4);
-  __nv_bfloat16* Tb = reinterpret_cast<__nv_bfloat16*>(Nm + C * (C + 4));     // [C][CPAD]
-  float* ybuf = reinterpret_cast<float*>(sm + R1_B);                          // [C][3D]
-  __nv_bfloat16* bv = reinterpret_cast<__nv_bfloat16*>(sm + R1_B);            // reuse after l2 norm
+  __nv_bfloat16* raw = reinterpret_cast<__nv_bfloat16*>(sm);                  // R0
+  __nv_bfloat16* bv = reinterpret_cast<__nv_bfloat16*>(sm);                   // R0 after the conv
   __nv_bfloat16* bk = bv + C * DPAD;
-  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(sm + R1_B + Y_B);
+  float* Am = reinterpret_cast<float*>(sm + BVK_B);
+  __nv_bfloat16* qs = reinterpret_cast<__nv_bfloat16*>(sm + R0_B);            // R1
   __nv_bfloat16* ks = qs + C * DPAD;
   __nv_bfloat16* vs = ks + C * DPAD;
-  float* gsh = reinterpret_cast<float*>(sm + R1_B + Y_B + QKV_B);              // g, then cumulative G
+  float* Nm = reinterpret_cast<float*>(sm + R0_B);                            // R1 after Q K^T
+  __nv_bfloat16* Tb = reinterpret_cast<__nv_bfloat16*>(Nm + C * (C + 4));
+  float* gsh = reinterpret_cast<float*>(sm + R0_B + R1_B);                     // g, then cumulative G
   float* bsh = gsh + C;
-  float* nrm = bsh + C;                                                        // [C] q scale, [C] k scale
+  float* nq = bsh + C;
+  float* nkk = nq + C;
+  float* eg = nkk + C;                                                         // exp(G)
 
   const int c = blockIdx.x, h = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -124,20 +127,30 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
   const int rep = a.nv / a.nk, kh = h / rep;
   const int chan[3] = {kh * D, a.nk * D + kh * D, 2 * a.nk * D + h * D};
 
-  // ---- 1. raw projected rows r0-3 .. r0+C-1 for the head's q, k, v channels
+  // conv taps (static weights) before waiting on the previous kernel: thread t owns q/k channel
+  // t (q: t < D, k: t >= D) for every row, and v channel t % D for rows (t / D) * C/2 ..
+  const int qk_part = tid / D, qk_ch = tid % D;
+  float wqk[KC], wv[KC];
+#pragma unroll
+  for (int j = 0; j < KC; ++j) {
+    wqk[j] = a.conv_w[(size_t)(chan[qk_part] + qk_ch) * KC + j];
+    wv[j] = a.conv_w[(size_t)(chan[2] + qk_ch) * KC + j];
+  }
+  pdl_wait();
+  pdl_trigger();
+
+  // ---- 1. raw projected rows r0-3 .. r0+C-1 (q, k, v channels of the head), all copies in flight
   for (int idx = tid; idx < (C + KC - 1) * 3 * (D / 8); idx += blockDim.x) {
     const int i = idx / (3 * (D / 8));
     const int rem = idx % (3 * (D / 8));
     const int part = rem / (D / 8), ch8 = rem % (D / 8);
     const int r = r0 - (KC - 1) + i;
-    uint4 v = make_uint4(0, 0, 0, 0);
-    if (r < 0) {
-      v = *reinterpret_cast<const uint4*>(a.window + (size_t)(r + KC - 1) * a.Cch + chan[part] + ch8 * 8);
-    } else if (r < a.S) {
-      v = *reinterpret_cast<const uint4*>(a.proj + (size_t)r * a.proj_ld + chan[part] + ch8 * 8);
-    }
-    *reinterpret_cast<uint4*>(raw + i * 3 * D + part * D + ch8 * 8) = v;
+    uint4* dst = reinterpret_cast<uint4*>(raw + i * 3 * D + part * D + ch8 * 8);
+    if (r < 0) cp_async16(dst, a.window + (size_t)(r + KC - 1) * a.Cch + chan[part] + ch8 * 8);
+    else if (r < a.S) cp_async16(dst, a.proj + (size_t)r * a.proj_ld + chan[part] + ch8 * 8);
+    else *dst = make_uint4(0, 0, 0, 0);
   }
+  cp_async_commit();
   if (tid < C) {
     const int r = r0 + tid;
     float g = 0.f, be = 0.f;
@@ -153,16 +166,30 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
     gsh[tid] = g;
     bsh[tid] = be;
   }
+  cp_async_wait<0>();
   __syncthreads();
-  // ---- 2. causal conv + SiLU (fp32), cumulative decay
-  for (int idx = tid; idx < C * 3 * D; idx += blockDim.x) {
-    const int i = idx / (3 * D), cc = idx % (3 * D);
-    const int part = cc / D;
-    const int ch = chan[part] + (cc % D);
-    float s = 0.f;
-#pragma unroll
-    for (int j = 0; j < KC; ++j) s += a.conv_w[(size_t)ch * KC + j] * __bfloat162float(raw[(i + j) * 3 * D + cc]);
-    ybuf[i * 3 * D + cc] = (i < nrows) ? silu_f(s) : 0.f;
+  // ---- 2. causal conv + SiLU with a sliding register window; cumulative decay (thread 0)
+  {
+    __nv_bfloat16* dst = qk_part == 0 ? qs : ks;
+    const int col = qk_part * D + qk_ch;
+    float x0 = __bfloat162float(raw[0 * 3 * D + col]), x1 = __bfloat162float(raw[1 * 3 * D + col]);
+    float x2 = __bfloat162float(raw[2 * 3 * D + col]);
+    for (int i = 0; i < C; ++i) {
+      const float x3 = __bfloat162float(raw[(i + 3) * 3 * D + col]);
+      const float y = wqk[0] * x0 + wqk[1] * x1 + wqk[2] * x2 + wqk[3] * x3;
+      dst[i * DPAD + qk_ch] = __float2bfloat16(i < nrows ? silu_f(y) : 0.f);
+      x0 = x1; x1 = x2; x2 = x3;
+    }
+    const int vcol = 2 * D + qk_ch, i0 = qk_part * (C / 2);
+    x0 = __bfloat162float(raw[(i0 + 0) * 3 * D + vcol]);
+    x1 = __bfloat162float(raw[(i0 + 1) * 3 * D + vcol]);
+    x2 = __bfloat162float(raw[(i0 + 2) * 3 * D + vcol]);
+    for (int i = i0; i < i0 + C / 2; ++i) {
+      const float x3 = __bfloat162float(raw[(i + 3) * 3 * D + vcol]);
+      const float y = wv[0] * x0 + wv[1] * x1 + wv[2] * x2 + wv[3] * x3;
+      vs[i * DPAD + qk_ch] = __float2bfloat16(i < nrows ? silu_f(y) : 0.f);
+      x0 = x1; x1 = x2; x2 = x3;
+    }
   }
   if (tid == 0) {
     float acc = 0.f;
@@ -172,43 +199,58 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
     }
   }
   __syncthreads();
-  // ---- 3. L2 norms (warp per row)
+  // ---- 3. L2 norms (warp per row, fixed order), exp(G)
   for (int i = warp; i < C; i += 8) {
     float sq = 0.f, sk = 0.f;
-    for (int d = lane; d < D; d += 32) {
-      const float q = ybuf[i * 3 * D + d], k = ybuf[i * 3 * D + D + d];
+#pragma unroll
+    for (int m = 0; m < D / 32; ++m) {
+      const float q = __bfloat162float(qs[i * DPAD + lane + 32 * m]);
+      const float k = __bfloat162float(ks[i * DPAD + lane + 32 * m]);
       sq += q * q;
       sk += k * k;
     }
     sq = warp_sum(sq);
     sk = warp_sum(sk);
     if (lane == 0) {
-      nrm[i] = rsqrtf(sq + 1e-6f) * rsqrtf((float)D);
-      nrm[C + i] = rsqrtf(sk + 1e-6f);
+      nq[i] = rsqrtf(sq + 1e-6f) * rsqrtf((float)D);
+      nkk[i] = rsqrtf(sk + 1e-6f);
     }
   }
+  if (tid < C) eg[tid] = __expf(gsh[tid]);
   __syncthreads();
   const float GC = gsh[C - 1];
   const size_t ch_base = ((size_t)c * a.nv + h) * C;
-  for (int idx = tid; idx < C * D; idx += blockDim.x) {
-    const int i = idx / D, d = idx % D;
-    const float q = ybuf[i * 3 * D + d] * nrm[i];
-    const float k = ybuf[i * 3 * D + D + d] * nrm[C + i];
-    const float v = ybuf[i * 3 * D + 2 * D + d];
-    qs[i * DPAD + d] = __float2bfloat16(q);
-    ks[i * DPAD + d] = __float2bfloat16(k);
-    vs[i * DPAD + d] = __float2bfloat16(v);
-    a.Qp[(ch_base + i) * D + d] = __float2bfloat16(q * __expf(gsh[i]));
-    a.Kp[(ch_base + i) * D + d] = __float2bfloat16(k * __expf(GC - gsh[i]));
+  // ---- 4. normalise in place, q exp(G) and k exp(G_C - G) to global, beta v and beta k exp(G)
+  for (int idx = tid; idx < C * (D / 8); idx += blockDim.x) {
+    const int i = idx / (D / 8), c8 = (idx % (D / 8)) * 8;
+    const uint4 qu = *reinterpret_cast<const uint4*>(qs + i * DPAD + c8);
+    const uint4 ku = *reinterpret_cast<const uint4*>(ks + i * DPAD + c8);
+    const uint4 vu = *reinterpret_cast<const uint4*>(vs + i * DPAD + c8);
+    const __nv_bfloat16* qv = reinterpret_cast<const __nv_bfloat16*>(&qu);
+    const __nv_bfloat16* kv = reinterpret_cast<const __nv_bfloat16*>(&ku);
+    const __nv_bfloat16* vv = reinterpret_cast<const __nv_bfloat16*>(&vu);
+    const float sq = nq[i], sk = nkk[i], e = eg[i], ekc = __expf(GC - gsh[i]), be = bsh[i];
+    __align__(16) __nv_bfloat16 qn[8], kn[8], qp[8], kp[8], bvo[8], bko[8];
+#pragma unroll
+    for (int u = 0; u < 8; ++u) {
+      const float q = __bfloat162float(qv[u]) * sq;
+      const float k = __bfloat162float(kv[u]) * sk;
+      qn[u] = __float2bfloat16(q);
+      kn[u] = __float2bfloat16(k);
+      qp[u] = __float2bfloat16(q * e);
+      kp[u] = __float2bfloat16(k * ekc);
+      bvo[u] = __float2bfloat16(be * __bfloat162float(vv[u]));
+      bko[u] = __float2bfloat16(be * __bfloat162float(kn[u]) * e);
+    }
+    *reinterpret_cast<uint4*>(qs + i * DPAD + c8) = *reinterpret_cast<const uint4*>(qn);
+    *reinterpret_cast<uint4*>(ks + i * DPAD + c8) = *reinterpret_cast<const uint4*>(kn);
+    *reinterpret_cast<uint4*>(a.Qp + (ch_base + i) * D + c8) = *reinterpret_cast<const uint4*>(qp);
+    *reinterpret_cast<uint4*>(a.Kp + (ch_base + i) * D + c8) = *reinterpret_cast<const uint4*>(kp);
+    *reinterpret_cast<uint4*>(bv + i * DPAD + c8) = *reinterpret_cast<const uint4*>(bvo);
+    *reinterpret_cast<uint4*>(bk + i * DPAD + c8) = *reinterpret_cast<const uint4*>(bko);
   }
   __syncthreads();
-  // ybuf is dead: beta v and beta k exp(G) (bf16) reuse it
-  for (int idx = tid; idx < C * D; idx += blockDim.x) {
-    const int i = idx / D, d = idx % D;
-    bv[i * DPAD + d] = __float2bfloat16(bsh[i] * __bfloat162float(vs[i * DPAD + d]));
-    bk[i * DPAD + d] = __float2bfloat16(bsh[i] * __bfloat162float(ks[i * DPAD + d]) * __expf(gsh[i]));
-  }
-  // ---- 4. K K^T -> A (fp32), Q K^T -> P (bf16 to global).  warp: m-tile warp/2, n-tiles 4*(warp%2)..+3
+  // ---- 5. K K^T -> A (fp32), Q K^T -> P (bf16 to global).  warp: m-tile warp/2, n-tiles 4*(warp%2)..+3
   {
     const int mt = warp >> 1, nt0 = (warp & 1) * 4;
     float kk[4][4], qk[4][4];
@@ -232,25 +274,81 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
 #pragma unroll
     for (int n = 0; n < 4; ++n) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int i = mt * 16 + (lane >> 2) + (e >> 1) * 8;
-        const int j = (nt0 + n) * 8 + (lane & 3) * 2 + (e & 1);
-        const float dec = __expf(gsh[i] - gsh[j]);
-        Am[i * (C + 4) + j] = (j < i) ? -bsh[i] * kk[n][e] * dec : 0.f;
-        a.P[(ch_base + i) * C + j] = __float2bfloat16((j <= i) ? qk[n][e] * dec : 0.f);
+      for (int hh = 0; hh < 2; ++hh) {
+        const int i = mt * 16 + (lane >> 2) + hh * 8;
+        const int j = (nt0 + n) * 8 + (lane & 3) * 2;
+        float pv[2];
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float dec = __expf(gsh[i] - gsh[j + e]);
+          Am[i * (C + 4) + j + e] = (j + e < i) ? -bsh[i] * kk[n][2 * hh + e] * dec : 0.f;
+          pv[e] = (j + e <= i) ? qk[n][2 * hh + e] * dec : 0.f;
+        }
+        *reinterpret_cast<__nv_bfloat162*>(a.P + (ch_base + i) * C + j) = __floats2bfloat162_rn(pv[0], pv[1]);
       }
     }
   }
   __syncthreads();
-  // ---- 5. T = (I - A)^-1 by forward substitution (fp32): N[i][j] = A[i][j] + sum_{j<m<i} A[i][m] N[m][j]
+  // ---- 6. T = (I - A)^-1 (strictly lower part N), blocked over 16-row blocks:
+  //   diagonal blocks by forward substitution (one warp each), then block rows I = 1..3:
+  //   M_IJ = sum_{K=J}^{I-1} A_IK T_KJ,  T_IJ = M_IJ + N_II M_IJ   (T_KK = I + N_KK)
   for (int i = tid; i < C * (C + 4); i += blockDim.x) Nm[i] = 0.f;
   __syncthreads();
-  for (int i = 1; i < C; ++i) {
-    if (tid < i) {
-      const int j = tid;
-      float s = Am[i * (C + 4) + j];
-      for (int m = j + 1; m < i; ++m) s += Am[i * (C + 4) + m] * Nm[m * (C + 4) + j];
-      Nm[i * (C + 4) + j] = s;
+  if (warp < C / FB) {
+    const int b0 = warp * FB;
+    const int j = b0 + (lane & (FB - 1));
+    for (int il = 1; il < FB; ++il) {
+      const int i = b0 + il;
+      if (lane < il) {
+        float s = Am[i * (C + 4) + j];
+        for (int m = j + 1; m < i; ++m) s += Am[i * (C + 4) + m] * Nm[m * (C + 4) + j];
+        Nm[i * (C + 4) + j] = s;
+      }
+      __syncwarp();
+    }
+  }
+  __syncthreads();
+  for (int I = 1; I < C / FB; ++I) {
+    // M for every J < I: entries (J, r, cc) spread over the threads, kept in registers
+    float mval[3];
+    int ment[3];
+    int nm = 0;
+    for (int e = tid; e < I * FB * FB; e += blockDim.x) {
+      const int J = e / (FB * FB), r = (e / FB) % FB, cc = e % FB;
+      const int i = I * FB + r, jcol = J * FB + cc;
+      float s = 0.f;
+      for (int K = J; K < I; ++K) {
+#pragma unroll 4
+        for (int m = 0; m < FB; ++m) {
+          const int km = K * FB + m;
+          const float t = (K == J) ? ((m == cc ? 1.f : 0.f) + Nm[km * (C + 4) + jcol]) : Nm[km * (C + 4) + jcol];
+          s += Am[i * (C + 4) + km] * t;
+        }
+      }
+      mval[nm] = s;
+      ment[nm] = e;
+      ++nm;
+    }
+    __syncthreads();
+    for (int q = 0; q < nm; ++q) {               // stage M in the (still zero) T_IJ blocks
+      const int e = ment[q];
+      const int J = e / (FB * FB), r = (e / FB) % FB, cc = e % FB;
+      Nm[(I * FB + r) * (C + 4) + J * FB + cc] = mval[q];
+    }
+    __syncthreads();
+    for (int q = 0; q < nm; ++q) {               // T_IJ = M + N_II M
+      const int e = ment[q];
+      const int J = e / (FB * FB), r = (e / FB) % FB, cc = e % FB;
+      const int i = I * FB + r, jcol = J * FB + cc;
+      float s = mval[q];
+      for (int m = 0; m < r; ++m) s += Nm[i * (C + 4) + I * FB + m] * Nm[(I * FB + m) * (C + 4) + jcol];
+      mval[q] = s;
+    }
+    __syncthreads();
+    for (int q = 0; q < nm; ++q) {
+      const int e = ment[q];
+      const int J = e / (FB * FB), r = (e / FB) % FB, cc = e % FB;
+      Nm[(I * FB + r) * (C + 4) + J * FB + cc] = mval[q];
     }
     __syncthreads();
   }
@@ -259,7 +357,7 @@ __global__ void __launch_bounds__(256, 1) gdn_chunk_prep_kernel(PrepArgs a) {
     Tb[i * CPAD + j] = __float2bfloat16(i == j ? 1.f : Nm[i * (C + 4) + j]);
   }
   __syncthreads();
-  // ---- 6. U = T (beta v), W = T (beta k exp(G)).  64 x 128 outputs each; warp: m-tile warp/2, 8 n-tiles
+  // ---- 7. U = T (beta v), W = T (beta k exp(G)).  64 x 128 outputs each; warp: m-tile warp/2, 8 n-tiles
   {
     const int mt = warp >> 1, nt0 = (warp & 1) * 8;
     float u[8][4], w[8][4];
@@ -344,22 +442,22 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_scan_kernel(ScanArgs a) {
 
   for (int c = 0; c < a.nchunks; ++c) {
     const size_t base = ((size_t)c * a.nv + h) * C;
-    // ---- stage chunk inputs
+    // ---- stage chunk inputs (asynchronous copies: one memory round trip per chunk)
     for (int idx = tid; idx < C * (D / 8); idx += blockDim.x) {
       const int i = idx / (D / 8), ch = idx % (D / 8);
-      *reinterpret_cast<uint4*>(Ws + i * DPAD + ch * 8) = *reinterpret_cast<const uint4*>(a.W + (base + i) * D + ch * 8);
-      *reinterpret_cast<uint4*>(Qs + i * DPAD + ch * 8) = *reinterpret_cast<const uint4*>(a.Qp + (base + i) * D + ch * 8);
-      *reinterpret_cast<uint4*>(Ks + i * DPAD + ch * 8) = *reinterpret_cast<const uint4*>(a.Kp + (base + i) * D + ch * 8);
+      cp_async16(Ws + i * DPAD + ch * 8, a.W + (base + i) * D + ch * 8);
+      cp_async16(Qs + i * DPAD + ch * 8, a.Qp + (base + i) * D + ch * 8);
+      cp_async16(Ks + i * DPAD + ch * 8, a.Kp + (base + i) * D + ch * 8);
     }
     for (int idx = tid; idx < C * (C / 8); idx += blockDim.x) {
       const int i = idx / (C / 8), ch = idx % (C / 8);
-      *reinterpret_cast<uint4*>(Ps + i * CPAD + ch * 8) = *reinterpret_cast<const uint4*>(a.P + (base + i) * C + ch * 8);
+      cp_async16(Ps + i * CPAD + ch * 8, a.P + (base + i) * C + ch * 8);
     }
     for (int idx = tid; idx < C * (VS / 8); idx += blockDim.x) {
       const int i = idx / (VS / 8), ch = idx % (VS / 8);
-      *reinterpret_cast<uint4*>(Us + i * VSP + ch * 8) =
-          *reinterpret_cast<const uint4*>(a.U + (base + i) * D + col0 + ch * 8);
+      cp_async16(Us + i * VSP + ch * 8, a.U + (base + i) * D + col0 + ch * 8);
     }
+    cp_async_commit();
     // state (bf16) as a B operand [D][VS]
 #pragma unroll
     for (int mt = 0; mt < 2; ++mt)
@@ -372,6 +470,7 @@ __global__ void __launch_bounds__(128, 1) gdn_chunk_scan_kernel(ScanArgs a) {
           *reinterpret_cast<__nv_bfloat162*>(Sb + r * VSP + cc) =
               __floats2bfloat162_rn(Sf[mt][nt][2 * hh], Sf[mt][nt][2 * hh + 1]);
         }
+    cp_async_wait<0>();
     __syncthreads();
     // ---- V' = U - W S   (warp: rows 16*warp.., all VS columns)
     float vp[4][4];

@@ -142,7 +142,7 @@ static int num_sms() {
 // qwen38_b200/ops/native.py) of logical shape [N, K].
 void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
                    const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr,
-                   const ArArgs* ar = nullptr) {
+                   const ArArgs* ar = nullptr, unsigned long long* trace = nullptr) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
@@ -158,6 +158,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
   g.err = sc.err;
   g.ws = sc.ws;
   g.counters = sc.counters;
+  g.trace = trace;
   if (T <= 32) {
     // swap-AB streaming: M = weight rows, N = tokens
     g.M = N;
@@ -246,6 +247,24 @@ void q38_linear_allreduce(torch::Tensor x, torch::Tensor w, int64_t N, torch::Te
   a.epochs = epochs.data_ptr<int>();
   auto sc = q38::scratch_of(ws, counters, err);
   q38::gemm_dispatch(x, w, (int)N, residual, q38::EPI_AR_F32, sc, nullptr, nullptr, nullptr, &a);
+}
+
+// Micro-benchmark entry: q38_linear with per-CTA phase stamps written to `trace` ([grid][8] int64).
+// Returns the grid size.
+int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(trace.scalar_type() == at::kLong && trace.is_contiguous(), "int64 trace buffer");
+  TORCH_CHECK(epi == q38::EPI_BF16 || epi == q38::EPI_F32 || epi == q38::EPI_ADD_F32 || epi == q38::EPI_SWIGLU,
+              "traced epilogues: bf16, f32, add, swiglu");
+  auto sc = q38::scratch_of(ws, counters, err);
+  const int T = (int)x.size(0), K = (int)x.size(1);
+  const int64_t m_tiles = (T <= 32) ? (N + 127) / 128 : ((T + 127) / 128) * ((N + q38::PREFILL_BN - 1) / q38::PREFILL_BN);
+  const int64_t kb = (K + 63) / 64;
+  TORCH_CHECK(trace.numel() >= m_tiles * kb * 8, "trace buffer too small");
+  q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc, nullptr, nullptr, nullptr, nullptr,
+                     reinterpret_cast<unsigned long long*>(trace.data_ptr<int64_t>()));
+  return m_tiles;
 }
 
 void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,

@@ -59,7 +59,17 @@ struct GemmArgs {
   float* amax_val;            // EPI_ARGMAX partials [m_tiles, N]
   int* amax_idx;
   ArArgs ar;                  // EPI_AR_F32 only
+  unsigned long long* trace;  // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
 };
+
+// trace points: 0 entry, 1 setup done, 2 first stage landed, 3 last MMA issued, 4 accumulator
+// ready, 5 split-K partial published, 6 epilogue done, 7 exit
+#define Q38_STAMP(k)                                                                                   \
+  do {                                                                                                 \
+    if (g.trace)                                                                                       \
+      g.trace[((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 8 + (k)] =    \
+          globaltimer();                                                                               \
+  } while (0)
 
 template <int BN, int STAGES>
 struct Smem {
@@ -84,6 +94,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) Q38_STAMP(0);
   const int m_tile = blockIdx.x, n_tile = blockIdx.y, split = blockIdx.z;
   const int m0 = m_tile * BM, n0 = n_tile * BN;
   const int kb0 = split * g.kps;
@@ -110,7 +121,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  if (tid == 0) pdl_trigger();
+  if (tid == 0) {
+    Q38_STAMP(1);
+    pdl_trigger();
+  }
 
   if (tid == 0) {
     // ---------------- TMA producer
@@ -160,6 +174,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     for (int i = 0; i < nk; ++i) {
       const int s = i % STAGES;
       if (!mbar_wait(&full_bar[s], (i / STAGES) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      if (i == 0) Q38_STAMP(2);
       tc_fence_after();
       const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
       const uint32_t sb = sa + S::A_BYTES;
@@ -171,6 +186,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       }
       umma_commit(&empty_bar[s]);
     }
+    Q38_STAMP(3);
     umma_commit(acc_bar);
   }
 
@@ -179,6 +195,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   mbar_wait(acc_bar, 0, g.err, kErrMmaWait, abort_flag);
   tc_fence_after();
   __syncthreads();
+  if (tid == 0) Q38_STAMP(4);
   const bool ok = (*abort_flag == 0);   // CTA-uniform after the barrier
 
   const int row = warp * 32 + lane;   // TMEM lane == tile row m
@@ -206,6 +223,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         if (tid == 0) {
           const int prev = atomicAdd(&g.counters[tile], 1);
           *last_flag = (prev == g.splits - 1);
+          Q38_STAMP(5);
         }
         __syncthreads();
         do_epi = *last_flag != 0;
@@ -437,12 +455,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   }
 
   // ---------------- teardown
+  if (tid == 0) Q38_STAMP(6);
   tc_fence_before();
   __syncthreads();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
   }
+  if (tid == 0) Q38_STAMP(7);
 }
 
 template <int BN, int STAGES, int EPI, bool SWAP>

@@ -23,15 +23,17 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
   const int r = blockIdx.x;
   const TIn* xr = x + (size_t)r * ldx;
   __shared__ float red[32];
-  float v[VPT];
+  float v[VPT], wv[VPT];
   float ss = 0.f;
 #pragma unroll
-  for (int u = 0; u < VPT; ++u) {
+  for (int u = 0; u < VPT; ++u) {             // row and weight loads share one memory round trip
     const int i = threadIdx.x + u * blockDim.x;
     float f = 0.f;
+    wv[u] = 0.f;
     if (i < H) {
       if constexpr (std::is_same<TIn, float>::value) f = xr[i];
       else f = __bfloat162float(xr[i]);
+      wv[u] = w[i];
     }
     v[u] = f;
     ss += f * f;
@@ -51,7 +53,7 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {
     const int i = threadIdx.x + u * blockDim.x;
-    if (i < H) o[i] = __float2bfloat16(v[u] * inv * w[i]);
+    if (i < H) o[i] = __float2bfloat16(v[u] * inv * wv[u]);
   }
 }
 

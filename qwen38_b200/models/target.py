@@ -53,8 +53,11 @@ def pack_gdn(src, i, cfg: ModelConfig, tp, r, device, dtype):
     q_l = _rows(qkv, r * nkl * dk, nkl * dk)
     k_l = _rows(qkv, kd + r * nkl * dk, nkl * dk)
     v_l = _rows(qkv, 2 * kd + r * nvl * dv, nvl * dv)
-    w_in = torch.cat([q_l, k_l, v_l, _rows(z, r * nvl * dv, nvl * dv), _rows(b, r * nvl, nvl),
-                      _rows(a, r * nvl, nvl)], 0).contiguous()
+    parts = [q_l, k_l, v_l, _rows(z, r * nvl * dv, nvl * dv), _rows(b, r * nvl, nvl), _rows(a, r * nvl, nvl)]
+    pad = -sum(t.shape[0] for t in parts) % 8       # projection rows stay 16-byte aligned (e.g. 2060 at TP8)
+    if pad:
+        parts.append(q_l.new_zeros(pad, q_l.shape[1]))
+    w_in = torch.cat(parts, 0).contiguous()
     conv = src.get(p + "conv1d.weight", device=device, dtype=torch.float32)
     conv = conv.reshape(conv.shape[0], -1)
     conv_l = torch.cat([_rows(conv, r * nkl * dk, nkl * dk), _rows(conv, kd + r * nkl * dk, nkl * dk),

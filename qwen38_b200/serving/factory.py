@@ -36,6 +36,10 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
     from .engine import ServingEngine
     rc.validate()
     cfg, dcfg, ckpt = _model(rc)
+    from ..parallel.plan import check_tp_plan
+    bad = check_tp_plan(cfg, dcfg if rc.spec.drafter == "dspark" else None, rc.parallel.tp)
+    if bad:
+        raise ValueError(f"TP={rc.parallel.tp} cannot run this shape: " + "; ".join(bad))
     native = rc.kernels.ops == "native"
     if native and not torch.cuda.is_available():
         raise RuntimeError("kernels.ops=native needs a CUDA device")

@@ -77,10 +77,84 @@ def bench_gemm(a):
            "tflops": round(flops / ms / 1e9, 1), "gbs": round(bytes_ / ms / 1e6, 1)}
     out[f"frac_bw_of_{src}"] = round(bytes_ / ms / 1e6 / hbm, 3)
     out[f"frac_tc_of_{src}"] = round(flops / ms / 1e9 / tf, 3)
+    if a.graph:
+        out.update(gemm_graph(ops, x, w_plain, a))
+    if a.trace:
+        out["trace"] = gemm_trace(ops, x, w, a.epi)
     if a.compare:
         ref = lambda: x @ w_plain.t()
         out["cublas_ms"] = round(time_kernel(ref, a.iters), 4)
     return out
+
+
+def gemm_graph(ops, x, w_plain, a):
+    """Per-GEMM time when ``a.graph`` launches run back to back inside one CUDA graph (the verify
+    setting: no host launch gaps), cycling over enough weight copies that no launch reads a
+    weight another left in L2."""
+    wbytes = w_plain.numel() * 2
+    copies = max(1, -(-3 * 126 * 2 ** 20 // wbytes))
+    ws = [ops.prepare_weight(w_plain.clone()) for _ in range(copies)]
+    if a.epi == "swiglu":
+        calls = [lambda w=w: ops.linear_swiglu(x, w, 64) for w in ws]
+    elif a.epi == "add":
+        res = torch.zeros(a.T, a.N, device="cuda")
+        calls = [lambda w=w: ops.linear_residual(x, w, res) for w in ws]
+    else:
+        out = torch.empty(a.T, a.N, dtype=torch.bfloat16, device="cuda")
+        calls = [lambda w=w: ops.linear(x, w, out=out) for w in ws]
+    for f in calls:
+        f()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(a.graph):
+            calls[i % copies]()
+    g.replay()
+    torch.cuda.synchronize()
+    ms = []
+    for _ in range(5):
+        s0, e0 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s0.record()
+        g.replay()
+        e0.record()
+        torch.cuda.synchronize()
+        ms.append(s0.elapsed_time(e0) / a.graph)
+    ms.sort()
+    hbm, _, src = peaks()
+    per = ms[len(ms) // 2]
+    return {"graph_launches": a.graph, "weight_copies": copies, "graph_ms_per_call": round(per, 4),
+            f"graph_frac_bw_of_{src}": round(wbytes / per / 1e6 / hbm, 3)}
+
+
+def gemm_trace(ops, x, w, epi):
+    """One launch with per-CTA %globaltimer stamps: where a GEMM's time goes (launch skew, setup,
+    first TMA round trip, streaming, epilogue, split-K fix-up) in microseconds."""
+    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU
+    T = x.shape[0]
+    code = {"bf16": EPI_BF16, "add": EPI_ADD_F32, "swiglu": EPI_SWIGLU}[epi]
+    N = w.N
+    if epi == "swiglu":
+        out = torch.empty(T, N // 2, dtype=torch.bfloat16, device="cuda")
+    elif epi == "add":
+        out = torch.zeros(T, N, device="cuda")
+    else:
+        out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
+    kb = -(-x.shape[1] // 64)
+    tiles = -(-N // 128) if T <= 32 else -(-T // 128) * -(-N // 256)
+    tr = torch.zeros(tiles * kb * 8, dtype=torch.int64, device="cuda")
+    torch.empty(64 << 20, dtype=torch.float32, device="cuda").zero_()     # cold L2
+    torch.cuda.synchronize()
+    ops.C.linear_trace(x, w.t, N, out, code, ops.ws, ops.counters, ops.err, tr)
+    torch.cuda.synchronize()
+    t = tr.view(-1, 8).cpu()
+    t = t[t[:, 0] > 0].double()
+    t0 = t[:, 0].min()
+    q = lambda v: [round(float(v.quantile(p)) / 1e3, 2) for p in (0.0, 0.5, 1.0)]
+    return {"ctas": int(t.shape[0]), "span_us": round(float(t[:, 7].max() - t0) / 1e3, 2),
+            "start_skew_us[min,med,max]": q(t[:, 0] - t0), "setup_us": q(t[:, 1] - t[:, 0]),
+            "first_stage_us": q(t[:, 2] - t[:, 1]), "stream_us": q(t[:, 3] - t[:, 2]),
+            "mma_drain_us": q(t[:, 4] - t[:, 3]), "epilogue_us": q(t[:, 6] - t[:, 4]),
+            "teardown_us": q(t[:, 7] - t[:, 6]), "last_stream_end_us": round(float(t[:, 3].max() - t0) / 1e3, 2)}
 
 
 def bench_gdn(a):
@@ -171,6 +245,8 @@ def main():
     ap.add_argument("--kv-heads", type=int, default=4)
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true", help="also time torch/cuBLAS for the same GEMM")
+    ap.add_argument("--trace", action="store_true", help="GEMM: per-CTA phase stamps of one launch")
+    ap.add_argument("--graph", type=int, default=0, help="GEMM: time N back-to-back launches in one CUDA graph")
     a = ap.parse_args()
     out = {"gemm": bench_gemm, "gdn": bench_gdn, "gdnpf": bench_gdn_prefill, "attn": bench_attn}[a.kind](a)
     if out:
