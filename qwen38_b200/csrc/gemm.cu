@@ -11,8 +11,8 @@ namespace q38 {
 bool pdl_enabled() {
   static int on = -1;
   if (on < 0) {
-    const char* e = getenv("Q38_PDL");      // opt-in: measured slower on the verify chain
-    on = (e && e[0] == '1') ? 1 : 0;
+    const char* e = getenv("Q38_PDL");      // on by default; Q38_PDL=0 launches without the attribute
+    on = (e && e[0] == '0') ? 0 : 1;
   }
   return on == 1;
 }

@@ -269,16 +269,21 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           if (row < 64) {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out);
             const int f = m_tile * 64 + row;
-            for (int j = 0; j < nvalid; ++j) {
-              const float u = up_s[j * 64 + row];
-              o[(size_t)(n0 + j) * g.ldo + f] = __float2bfloat16(silu_f(acc[j]) * u);
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              if (j < nvalid) {
+                const float u = up_s[j * 64 + row];
+                o[(size_t)(n0 + j) * g.ldo + f] = __float2bfloat16(silu_f(acc[j]) * u);
+              }
             }
           }
         } else if constexpr (EPI == EPI_ARGMAX) {
           // per token column: max over the 128 rows of this tile, ties -> lowest row
           float* sv = reinterpret_cast<float*>(smem);
           int* si = reinterpret_cast<int*>(smem + 4 * 32 * 4);
-          for (int j = 0; j < nvalid; ++j) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j >= nvalid) break;
             float v = (m < g.M) ? acc[j] : -INFINITY;
             int idx = m;
 #pragma unroll
@@ -368,15 +373,26 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
           }
         } else {
+          // Fully unrolled over the 32 token columns (predicated), so acc[] stays in registers;
+          // the residual accumulate issues every load before any add.
           if (m < g.M) {
-            for (int j = 0; j < nvalid; ++j) {
-              const size_t off = (size_t)(n0 + j) * g.ldo + m;
-              if constexpr (EPI == EPI_BF16) {
-                reinterpret_cast<__nv_bfloat16*>(g.out)[off] = __float2bfloat16(acc[j]);
-              } else if constexpr (EPI == EPI_F32) {
-                reinterpret_cast<float*>(g.out)[off] = acc[j];
-              } else {
-                reinterpret_cast<float*>(g.out)[off] += acc[j];
+            if constexpr (EPI == EPI_ADD_F32) {
+              float* __restrict__ o = reinterpret_cast<float*>(g.out);
+              float r[32];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nvalid) r[j] = o[(size_t)(n0 + j) * g.ldo + m];
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nvalid) o[(size_t)(n0 + j) * g.ldo + m] = r[j] + acc[j];
+            } else {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (j < nvalid) {
+                  const size_t off = (size_t)(n0 + j) * g.ldo + m;
+                  if constexpr (EPI == EPI_BF16) reinterpret_cast<__nv_bfloat16*>(g.out)[off] = __float2bfloat16(acc[j]);
+                  else reinterpret_cast<float*>(g.out)[off] = acc[j];
+                }
               }
             }
           }

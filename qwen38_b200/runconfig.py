@@ -36,7 +36,7 @@ class SpecConfig:
 class KernelConfig:
     ops: str = "native"          # native | torch
     cuda_graphs: bool = True
-    pdl: bool = False
+    pdl: bool = True             # programmatic dependent launch (native kernels)
 
 
 @dataclass
@@ -79,8 +79,6 @@ class RunConfig:
             raise ValueError("spec.drafter=lookup needs spec.lookup=true")
         if v.slots < 1 or v.output_budget_multiple < 0 or v.prefix_budget_gb < 0:
             raise ValueError("serving.slots >= 1, non-negative budgets required")
-        if k.pdl and k.ops != "native":
-            raise ValueError("kernels.pdl applies to the native kernels only")
         return self
 
 
