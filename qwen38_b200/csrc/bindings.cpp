@@ -6,10 +6,12 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
 void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
                         torch::Tensor counters, torch::Tensor err);
-void q38_linear_allreduce(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor ws,
-                          torch::Tensor counters, torch::Tensor err, std::vector<int64_t> recv_ptrs,
-                          std::vector<int64_t> flag_ptrs, int64_t rank, int64_t slot, int64_t block_floats,
-                          int64_t tiles_max, torch::Tensor epochs);
+void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
+                     torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                     int64_t slot, int64_t block_floats, int64_t tiles_max, torch::Tensor epochs);
+void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, c10::optional<torch::Tensor> out,
+                     int64_t recv_local, int64_t flags_local, torch::Tensor epochs, int64_t slot, int64_t world,
+                     int64_t tiles_max, int64_t block_floats, torch::Tensor err);
 int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
                          torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace);
 void q38_clear_map_cache();
@@ -54,7 +56,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "qwen38_b200 sm_100a kernels";
   m.def("linear", &q38_linear);
   m.def("lm_head_argmax", &q38_lm_head_argmax);
-  m.def("linear_allreduce", &q38_linear_allreduce);
+  m.def("linear_push", &q38_linear_push);
+  m.def("rms_norm_ar", &q38_rms_norm_ar);
   m.def("linear_trace", &q38_linear_trace);
   m.def("clear_map_cache", &q38_clear_map_cache);
   m.def("gdn_recurrent", &q38_gdn_recurrent);

@@ -142,7 +142,7 @@ static int num_sms() {
 // qwen38_b200/ops/native.py) of logical shape [N, K].
 void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
                    const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr,
-                   const ArArgs* ar = nullptr, unsigned long long* trace = nullptr) {
+                   const ArArgs* ar = nullptr, unsigned long long* trace = nullptr, int64_t ldo_override = -1) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
@@ -154,7 +154,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
   g.K = K;
   g.kblocks = (K + BK - 1) / BK;
   g.out = out.data_ptr();
-  g.ldo = out.stride(0);
+  g.ldo = ldo_override >= 0 ? ldo_override : out.stride(0);
   g.err = sc.err;
   g.ws = sc.ws;
   g.counters = sc.counters;
@@ -174,8 +174,8 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
       TORCH_CHECK((int64_t)m_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
       TORCH_CHECK(m_tiles <= sc.n_counters, "split-K counter array too small");
     }
-    if (epi == EPI_AR_F32) {
-      TORCH_CHECK(ar != nullptr && m_tiles <= ar->tiles_max, "fused all-reduce: too many output tiles");
+    if (epi == EPI_PUSH_F32) {
+      TORCH_CHECK(ar != nullptr && m_tiles <= ar->tiles_max, "pushed all-reduce: too many output tiles");
       g.ar = *ar;
     }
     if (epi == EPI_ARGMAX) {
@@ -188,7 +188,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     dim3 grid(m_tiles, 1, splits);
     launch_swap(epi, ma, mb, g, grid, st);
   } else {
-    TORCH_CHECK(epi != EPI_ARGMAX && epi != EPI_AR_F32, "argmax / fused all-reduce epilogues serve <= 32 rows");
+    TORCH_CHECK(epi != EPI_ARGMAX && epi != EPI_PUSH_F32, "argmax / pushed all-reduce epilogues serve <= 32 rows");
     g.M = T;
     g.N = N;
     g.splits = 1;
@@ -217,19 +217,16 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
   q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc);
 }
 
-// Row-parallel out-projection fused with the tensor-parallel all-reduce and the residual add:
-// residual[T, N] += sum over ranks of x_r[T, K] @ w_r[N, K]^T, T <= 32 (see EPI_AR_F32).
-// recv_ptrs / flag_ptrs: every rank's receive and flag areas mapped into this process.
-void q38_linear_allreduce(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor ws,
-                          torch::Tensor counters, torch::Tensor err, std::vector<int64_t> recv_ptrs,
-                          std::vector<int64_t> flag_ptrs, int64_t rank, int64_t slot, int64_t block_floats,
-                          int64_t tiles_max, torch::Tensor epochs) {
+// Row-parallel out-projection whose epilogue pushes this rank's fp32 partial [T, N] (T <= 32)
+// into every rank's receive block of `slot` and publishes per-tile flags (EPI_PUSH_F32); the
+// reduction into the residual happens in q38_rms_norm_ar.  recv_ptrs / flag_ptrs: every rank's
+// receive and flag areas mapped into this process.
+void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
+                     torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
+                     int64_t slot, int64_t block_floats, int64_t tiles_max, torch::Tensor epochs) {
   c10::cuda::CUDAGuard guard(x.device());
-  TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous() && residual.dim() == 2,
-              "contiguous fp32 residual [T, N] required");
-  TORCH_CHECK(residual.size(0) == x.size(0) && residual.size(1) == N, "residual shape mismatch");
-  TORCH_CHECK(x.size(0) <= 32, "the fused all-reduce serves <= 32 rows");
-  TORCH_CHECK(residual.numel() <= block_floats, "residual larger than a receive block");
+  TORCH_CHECK(x.size(0) <= 32, "the pushed all-reduce serves <= 32 rows");
+  TORCH_CHECK(x.size(0) * N <= block_floats, "partial larger than a receive block");
   const int world = (int)recv_ptrs.size();
   TORCH_CHECK(world >= 1 && world <= q38::AR_MAX_RANKS && (int)flag_ptrs.size() == world, "1..8 ranks");
   TORCH_CHECK(rank >= 0 && rank < world, "bad rank");
@@ -246,7 +243,9 @@ void q38_linear_allreduce(torch::Tensor x, torch::Tensor w, int64_t N, torch::Te
   a.tiles_max = (int)tiles_max;
   a.epochs = epochs.data_ptr<int>();
   auto sc = q38::scratch_of(ws, counters, err);
-  q38::gemm_dispatch(x, w, (int)N, residual, q38::EPI_AR_F32, sc, nullptr, nullptr, nullptr, &a);
+  // no local output tensor: the epilogue writes the receive blocks, laid out [T, N] (ldo = N)
+  torch::Tensor unused = x;
+  q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_PUSH_F32, sc, nullptr, nullptr, nullptr, &a, nullptr, N);
 }
 
 // Micro-benchmark entry: q38_linear with per-CTA phase stamps written to `trace` ([grid][8] int64).

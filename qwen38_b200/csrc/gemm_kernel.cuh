@@ -12,15 +12,13 @@
 // store, fp32 store, fp32 accumulate into the residual stream, SwiGLU over [gate 64 | up 64] row
 // blocks, per-tile argmax (LM head), and (swap mode) the fused tensor-parallel all-reduce:
 //
-// EPI_AR_F32 - GEMM -> all-reduce -> residual add in one kernel (row-parallel out-projections at
-// TP > 1).  As soon as a tile's split-K fix-up is done, the fixing CTA stores its fp32 partial
-// tile into its own block of every rank's receive buffer (plain stores to peer memory over
-// NVLink, so tile t's transfer overlaps the MMA of later tiles), publishes a per-(slot, tile)
-// flag in every rank's flag area with a system-scope release, waits (bounded) for the W flags of
-// that tile in its own flag area, then sums the W partials in rank order 0..W-1 from local memory
-// and adds them into the replicated fp32 residual.  Every rank adds the same bits.  Only the
-// split-K fixing CTA of a tile waits (at most one per tile, far fewer than resident CTA slots),
-// and CTAs that wait on peers never wait on CTAs of their own grid, so the grid always drains.
+// EPI_PUSH_F32 - the GEMM half of the tensor-parallel all-reduce of a row-parallel out-projection
+// (TP > 1).  As soon as a tile's split-K fix-up is done, the fixing CTA stores its fp32 partial
+// tile into its own block of every rank's receive area (plain stores to peer memory over NVLink,
+// so tile t crosses NVLink while later tiles are still in the MMA), fences them at system scope
+// and publishes a per-(slot, tile) flag in every rank's flag area with a release store.  It never
+// waits: the reduction (wait for the W flags of each tile, rank-ordered sum, residual add) is done
+// by the kernel that consumes the residual next, the RMSNorm (`rms_norm_ar_kernel`, misc.cu).
 #pragma once
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -29,11 +27,11 @@
 
 namespace q38 {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_AR_F32 = 5 };
+enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_PUSH_F32 = 5 };
 
 constexpr int AR_MAX_RANKS = 8;
 
-// Peer buffers of the fused all-reduce epilogue.  Receive area of every rank: blocks
+// Peer buffers of the pushed all-reduce.  Receive area of every rank: blocks
 // [slot][src rank] of `block_floats` floats, each a [tokens, ldo] fp32 partial; flag area:
 // int words [slot][tile < tiles_max][src rank < 8].
 struct ArArgs {
@@ -58,7 +56,7 @@ struct GemmArgs {
   int* err;
   float* amax_val;            // EPI_ARGMAX partials [m_tiles, N]
   int* amax_idx;
-  ArArgs ar;                  // EPI_AR_F32 only
+  ArArgs ar;                  // EPI_PUSH_F32 only
   unsigned long long* trace;  // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
 };
 
@@ -307,7 +305,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             g.amax_val[(size_t)m_tile * g.N + n0 + tid] = v;
             g.amax_idx[(size_t)m_tile * g.N + n0 + tid] = idx;
           }
-        } else if constexpr (EPI == EPI_AR_F32) {
+        } else if constexpr (EPI == EPI_PUSH_F32) {
           const ArArgs& a = g.ar;
           const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_floats;
           if (m < g.M) {
@@ -318,59 +316,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (j < nvalid) dst[(size_t)(n0 + j) * g.ldo + m] = acc[j];
             }
           }
+          __threadfence_system();                      // every thread's pushes, before the flag
           __syncthreads();
           if (tid == 0) {
             const size_t fw = ((size_t)a.slot * a.tiles_max + m_tile) * AR_MAX_RANKS;
             int* ep = a.epochs + (size_t)a.slot * a.tiles_max + m_tile;
             const int e = *ep + 1;
-            __threadfence_system();
+            *ep = e;
             for (int p = 0; p < a.world; ++p) st_release_sys(reinterpret_cast<int*>(a.flags[p]) + fw + a.rank, e);
-            const int* fl = reinterpret_cast<const int*>(a.flags[a.rank]) + fw;
-            bool arrived = true;
-            const unsigned long long t0 = globaltimer();
-            for (int q = 0; q < a.world && arrived; ++q) {
-              while (ld_acquire_sys(fl + q) < e) {
-                if (globaltimer() - t0 > kWaitLimitNs) {
-                  record_error(g.err, kErrPeer);
-                  arrived = false;
-                  break;
-                }
-              }
-            }
-            if (arrived) *ep = e;
-            *last_flag = arrived;
-          }
-          __syncthreads();
-          if (*last_flag && m < g.M) {
-            // Issue every load of a group of 8 token columns (W partials + the residual) before
-            // any arithmetic: one memory round trip per group instead of one per column.
-            const float* __restrict__ rb =
-                reinterpret_cast<const float*>(a.recv[a.rank]) + (size_t)a.slot * a.world * a.block_floats;
-            float* __restrict__ res = reinterpret_cast<float*>(g.out);
-#pragma unroll
-            for (int j0 = 0; j0 < 32; j0 += 8) {
-              float v[8][AR_MAX_RANKS], r[8];
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                const size_t off = (size_t)(n0 + j0 + jj) * g.ldo + m;
-                if (j0 + jj < nvalid) {
-                  r[jj] = res[off];
-#pragma unroll
-                  for (int q = 0; q < AR_MAX_RANKS; ++q)
-                    v[jj][q] = q < a.world ? __ldcg(rb + (size_t)q * a.block_floats + off) : 0.f;
-                }
-              }
-#pragma unroll
-              for (int jj = 0; jj < 8; ++jj) {
-                if (j0 + jj < nvalid) {
-                  float sum = 0.f;
-#pragma unroll
-                  for (int q = 0; q < AR_MAX_RANKS; ++q)
-                    if (q < a.world) sum += v[jj][q];
-                  res[(size_t)(n0 + j0 + jj) * g.ldo + m] = r[jj] + sum;
-                }
-              }
-            }
           }
         } else {
           // Fully unrolled over the 32 token columns (predicated), so acc[] stays in registers;

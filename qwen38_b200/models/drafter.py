@@ -137,7 +137,7 @@ class BlockDrafter:
         if self.tp == 1:
             self.ops.linear_residual(h, w, x)
         elif self.target.fused_ar and self.comm.fused_fits(*x.shape):
-            self.ops.linear_allreduce(h, w, x, self.comm)
+            self.target.push_row_parallel(h, w, x)      # completed by the next norm of x
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
             slot, part = self.comm.slot_out(*x.shape)
             self.ops.linear(h, w, out=part)
@@ -185,17 +185,18 @@ class BlockDrafter:
         h = self.ops.embedding(ids, self.target.embed).float()
         if positions is None:
             positions = torch.arange(pos, pos + P, device=self.device, dtype=torch.int32)
+        norm = self.target.norm
         for l, L in enumerate(self.layers):
-            hn = self.ops.rms_norm(h, L["in_norm"], self.eps, self.dtype)
+            hn = norm(h, L["in_norm"], self.eps)
             qkv = self.ops.linear(hn, L["w_qkv"])
             o = self.ops.draft_block_attention(qkv, L["qn"], L["kn"], self.inv_freq, self.rope_scale, self.heads,
                                                self.eps, positions, self.kctx_all[slot, l],
                                                self.vctx_all[slot, l], self.dtype)
             self._row_par_add(o, L["w_o"], h)
-            hn = self.ops.rms_norm(h, L["post_norm"], self.eps, self.dtype)
+            hn = norm(h, L["post_norm"], self.eps)
             gu = self.ops.linear_swiglu(hn, L["w_gu"], GU_BLOCK)
             self._row_par_add(gu, L["w_down"], h)
-        hn = self.ops.rms_norm(h, self.norm, self.eps, self.dtype)
+        hn = norm(h, self.norm, self.eps)
         return self.ops.linear(hn, self.target.lm_head, out_dtype=torch.float32)
 
     def _propose_eager(self, anchor, positions=None, slot: int = 0):

@@ -107,9 +107,10 @@ class MTPDrafter:
             return None
         o = ops.attn_decode(q, gate, self.kctx_all[slot, 0], self.vctx_all[slot, 0], None, positions, 0, self.dtype)
         self._row_par_add(o, L["w_out"], x)
-        f_in = ops.rms_norm(x, L["post_norm"], self.eps, self.dtype)
+        f_in = self.target.norm(x, L["post_norm"], self.eps)
         gu = ops.linear_swiglu(f_in, L["w_gu"], GU_BLOCK)
         self._row_par_add(gu, L["w_down"], x)
+        self.target.settle(x)             # x is read raw as the next step's hidden input
         return x
 
     def _row_par_add(self, h, w, x):

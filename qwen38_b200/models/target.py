@@ -175,7 +175,10 @@ class HybridTarget:
         self.dtype = dtype
         self.ops = ops or TorchOps()
         self.comm = comm or NullComm()
-        self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_allreduce")
+        # pushed all-reduce: out-projection GEMMs push their partial tiles to every rank; the next
+        # RMSNorm of the residual completes the reduction (``_pending`` = (residual, slot))
+        self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_push")
+        self._pending = None
         tp, r = self.comm.world, self.comm.rank
         self.tp, self.rank = tp, r
         self.widths = tp_widths(cfg, tp)
@@ -290,7 +293,7 @@ class HybridTarget:
         if self.tp == 1:
             self.ops.linear_residual(h, w, x)
         elif self.fused_ar and self.comm.fused_fits(*x.shape):
-            self.ops.linear_allreduce(h, w, x, self.comm)     # GEMM + all-reduce + residual, one kernel
+            self.push_row_parallel(h, w, x)
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
             slot, part = self.comm.slot_out(*x.shape)          # GEMM writes into peer memory
             self.ops.linear(h, w, out=part)
@@ -300,13 +303,36 @@ class HybridTarget:
             self.comm.all_reduce_(part)
             x += part
 
+    def norm(self, x, w, eps=None):
+        """RMSNorm of the residual ``x``; completes a pending pushed all-reduce into ``x`` first
+        (in the same kernel)."""
+        eps = self.eps if eps is None else eps
+        if self._pending is not None and self._pending[0] is x:
+            slot = self._pending[1]
+            self._pending = None
+            return self.ops.rms_norm_ar(x, w, eps, self.dtype, self.comm, slot)
+        return self.ops.rms_norm(x, w, eps, self.dtype)
+
+    def push_row_parallel(self, h, w, x):
+        """Pushed all-reduce of a row-parallel out-projection into the residual ``x`` (any
+        model's residual: the drafters use it too); completed by the next ``norm`` / ``settle``."""
+        self.settle(x)
+        self._pending = (x, self.ops.linear_push(h, w, self.comm))
+
+    def settle(self, x=None):
+        """Complete a pending pushed all-reduce without a norm (before ``x`` is read raw)."""
+        if self._pending is not None and (x is None or self._pending[0] is x):
+            px, slot = self._pending
+            self._pending = None
+            self.ops.rms_norm_ar(px, None, self.eps, self.dtype, self.comm, slot)
+
     def _mlp(self, L, x):
-        h = self.ops.rms_norm(x, L["post_norm"], self.eps, self.dtype)
+        h = self.norm(x, L["post_norm"])
         gu = self.ops.linear_swiglu(h, L["w_gu"], GU_BLOCK)
         self._row_parallel(gu, L["w_down"], x)
 
     def _head(self, x_rows):
-        hn = self.ops.rms_norm(x_rows, self.final_norm, self.eps, self.dtype)
+        hn = self.norm(x_rows, self.final_norm)
         val, idx = self.ops.lm_head_argmax(hn, self.lm_head, self.vocab_offset)
         return self.comm.argmax_reduce(val, idx) if self.tp > 1 else idx
 
@@ -333,7 +359,7 @@ class HybridTarget:
             x = self.ops.embedding(tok, self.embed).float()
             positions = self.positions(pos0, tok.shape[0])
             for i, L in enumerate(self.layers):
-                h = self.ops.rms_norm(x, L["in_norm"], self.eps, self.dtype)
+                h = self.norm(x, L["in_norm"])
                 proj = self.ops.linear(h, L["w_in"])
                 if L["kind"] == LINEAR:
                     j = self.gdn_index[i]
@@ -350,9 +376,11 @@ class HybridTarget:
                 self._row_parallel(o, L["w_out"], x)
                 self._mlp(L, x)
                 if i in tap_pos:
+                    self.settle(x)
                     feats[c0:c1, tap_pos[i]] = x.to(self.dtype)
             seq.pos += tok.shape[0]
             if c1 == S:
+                self.settle(x)
                 nxt = self._head(x[-1:])
         return nxt, (feats.reshape(S, -1) if feats is not None else None)
 
@@ -433,7 +461,7 @@ class HybridTarget:
         tap_pos = {t: j for j, t in enumerate(taps)}
         x = self.ops.embedding(tokens, self.embed).float()
         for i, L in enumerate(self.layers):
-            h = self.ops.rms_norm(x, L["in_norm"], self.eps, self.dtype)
+            h = self.norm(x, L["in_norm"])
             outs = []
             if L["kind"] == LINEAR:
                 j = self.gdn_index[i]
@@ -458,6 +486,7 @@ class HybridTarget:
             self._row_parallel(o, L["w_out"], x)
             self._mlp(L, x)
             if i in tap_pos:
+                self.settle(x)
                 feats[:, tap_pos[i]] = x.to(self.dtype)
         pred = self._head(x)
         return pred, (feats.reshape(rows, -1) if feats is not None else None)

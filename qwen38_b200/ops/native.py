@@ -105,17 +105,25 @@ class NativeOps(TorchOps):
         self.launches += 1
         return out
 
-    def linear_allreduce(self, x, w, residual, comm):
-        """residual += sum over tensor-parallel ranks of x @ w^T in ONE kernel: the GEMM pushes each
-        finished fp32 tile into every rank's receive buffer over NVLink and reduces its own tile
-        (``comm``: a ``SymmComm``; T <= 32 rows)."""
+    def linear_push(self, x, w, comm) -> int:
+        """GEMM half of the tensor-parallel all-reduce: x @ w^T (fp32, T <= 32 rows) goes straight
+        from each finished tile into every rank's receive block of a fresh slot, with per-tile
+        flags; returns the slot for ``rms_norm_ar``."""
         w = self.prepare_weight(w)
         slot = comm.fused_slot()
-        self.C.linear_allreduce(x.contiguous(), w.t, w.N, residual, self.ws, self.counters, self.err,
-                                comm.recv_ptrs, comm.fflag_ptrs, comm.rank, slot, comm.block_floats,
-                                comm.tiles_max, comm.fepochs)
+        self.C.linear_push(x.contiguous(), w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs,
+                           comm.fflag_ptrs, comm.rank, slot, comm.block_floats, comm.tiles_max, comm.fepochs)
         self.launches += 1
-        return residual
+        return slot
+
+    def rms_norm_ar(self, x, w, eps, out_dtype, comm, slot):
+        """Reduction half: waits for every rank's tiles of ``slot``, adds them (rank order) into the
+        fp32 residual ``x`` in place and returns RMSNorm(x) * w in bf16 (``w`` None: reduce only)."""
+        out = None if w is None else torch.empty(x.shape[0], x.shape[1], dtype=torch.bfloat16, device=x.device)
+        self.C.rms_norm_ar(x, w, float(eps), out, comm.recv_ptrs[comm.rank], comm.fflag_ptrs[comm.rank], comm.fepochs,
+                           slot, comm.world, comm.tiles_max, comm.block_floats, self.err)
+        self.launches += 1
+        return out if out is None or out_dtype == torch.bfloat16 else out.to(out_dtype)
 
     def linear_residual(self, x, w, residual):
         w = self.prepare_weight(w)

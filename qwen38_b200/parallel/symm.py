@@ -10,9 +10,10 @@ collectives with the kernels in ``csrc/comm.cu``:
 * ``argmax_reduce(val, idx)`` - cross-rank (value, index) argmax for the vocab-parallel LM head
   and every Markov step.
 
-* fused GEMM + all-reduce (``NativeOps.linear_allreduce``): the out-projection kernel itself pushes
-  its fp32 tiles into every rank's receive area and reduces its own tile (the ``fused_*`` areas
-  below: blocks [slot][source rank], flags [slot][tile][source rank]).
+* pushed all-reduce (``NativeOps.linear_push`` + ``NativeOps.rms_norm_ar``): the out-projection
+  GEMM pushes each finished fp32 tile into every rank's receive area and flags it; the next
+  RMSNorm of the residual waits for the flags, adds the rank-ordered sum and normalises (the
+  ``fused_*`` areas below: blocks [slot][source rank], flags [slot][tile][source rank]).
 
 Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
 
@@ -39,7 +40,7 @@ class SymmComm(TorchComm):
                  eager_slots: int = 64, fused_graph_slots: int = 160, fused_eager_slots: int = 32,
                  tiles_max: int = 64, fused: bool = True):
         super().__init__(group)
-        self.fused = fused          # row-parallel GEMMs use the fused GEMM + all-reduce kernel
+        self.fused = fused          # row-parallel GEMMs push their tiles; the next norm reduces
         if self.world > MAX_RANKS:
             raise ValueError("peer-memory collectives serve at most 8 ranks")
         self.C = load()

@@ -1,7 +1,8 @@
-"""The GEMM kernel that carries the tensor-parallel all-reduce (``linear_allreduce``) on one GPU:
-at one rank it adds exactly what the plain GEMM's residual epilogue adds, and when a peer never
-publishes its tile the bounded flag wait gives up, records the peer-timeout bit in the error word,
-leaves the residual untouched and the context usable.  Two-rank numerics: test_tp_gpu.py."""
+"""The pushed tensor-parallel all-reduce on one GPU: the GEMM that pushes its tiles
+(``linear_push``) plus the reducing RMSNorm (``rms_norm_ar``) add exactly what the plain GEMM's
+residual epilogue adds, and the fused norm equals the plain norm bit for bit; when a peer never
+publishes its tiles the bounded flag wait gives up, records the peer-timeout bit in the error
+word, leaves the residual untouched and the context usable.  Two-rank numerics: test_tp_gpu.py."""
 import time
 
 import pytest
@@ -42,23 +43,29 @@ def ops():
     return NativeOps()
 
 
-@pytest.mark.parametrize("T,N,K", [(1, 5120, 3072), (16, 5120, 8704), (32, 5120, 6144), (7, 1000, 640)])
-def test_one_rank_equals_residual_epilogue(ops, T, N, K):
+@pytest.mark.parametrize("T,N,K", [(1, 5120, 3072), (16, 5120, 8704), (32, 5120, 6144), (7, 1024, 640)])
+def test_one_rank_equals_residual_epilogue_and_plain_norm(ops, T, N, K):
     g = torch.Generator(device="cuda").manual_seed(T * 7 + K)
     x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
     w = ops.prepare_weight((torch.randn(N, K, generator=g, device="cuda") * 0.02).to(torch.bfloat16))
+    nw = 1 + 0.1 * torch.randn(N, generator=g, device="cuda")
     r0 = torch.randn(T, N, generator=g, device="cuda")
     comm = _Areas(1, N)
     a = r0.clone()
-    for _ in range(3):
+    for _ in range(3):                                   # epochs advance call after call
         a.copy_(r0)
-        ops.linear_allreduce(x, w, a, comm)
+        slot = ops.linear_push(x, w, comm)
+        h = ops.rms_norm_ar(a, nw, 1e-6, torch.bfloat16, comm, slot)
     b = r0.clone()
     ops.linear_residual(x, w, b)
+    hb = ops.rms_norm(b, nw, 1e-6, torch.bfloat16)
+    c = r0.clone()
+    ops.rms_norm_ar(c, None, 1e-6, torch.bfloat16, comm, ops.linear_push(x, w, comm))   # reduce only
     ref = r0 + x.float() @ untile_weight(w).float().t()
     torch.cuda.synchronize()
     ops.check()
-    assert torch.equal(a, b)
+    assert torch.equal(a, b) and torch.equal(c, b)
+    assert torch.equal(h, hb)
     assert ((a - ref).norm() / ref.norm()).item() < 1e-3
 
 
@@ -69,7 +76,8 @@ def test_missing_peer_times_out_and_reports(ops):
     comm = _Areas(2, N)          # "rank 1" is this GPU's own area: its flags are never written
     r = torch.full((T, N), 3.0, device="cuda")
     t0 = time.time()
-    ops.linear_allreduce(x, w, r, comm)
+    slot = ops.linear_push(x, w, comm)
+    out = ops.rms_norm_ar(r, torch.ones(N, device="cuda"), 1e-6, torch.bfloat16, comm, slot)
     torch.cuda.synchronize()
     assert time.time() - t0 < 30
     assert int(ops.err.item()) & ERR_PEER
@@ -78,12 +86,12 @@ def test_missing_peer_times_out_and_reports(ops):
     ops.counters.zero_()
     y = torch.randn(64, device="cuda")
     assert torch.allclose((y * 2).sum(), 2 * y.sum(), rtol=1e-4, atol=1e-3)
-    # and the kernel still serves a one-rank call afterwards
-    one = _Areas(1, N)
+    one = _Areas(1, N)                                    # and the kernels still serve a one-rank call
     a = torch.zeros(T, N, device="cuda")
-    ops.linear_allreduce(x, w, a, one)
+    ops.rms_norm_ar(a, None, 1e-6, torch.bfloat16, one, ops.linear_push(x, w, one))
     b = torch.zeros(T, N, device="cuda")
     ops.linear_residual(x, w, b)
     torch.cuda.synchronize()
     ops.check()
     assert torch.equal(a, b)
+    del out

@@ -1,7 +1,8 @@
 """Tensor parallel on GPUs (one process per GPU): at TP2 the native runtime's speculative output
 equals its own greedy decode on full-width layer shapes, with the GEMM kernels that carry the
-all-reduce, with the separate peer-memory collectives and with NCCL; the fused GEMM + all-reduce
-kernel adds the same bits on both ranks as GEMM -> peer all-reduce -> add.  Skipped with fewer
+all-reduce (pushed from the GEMM, reduced in the next norm), with the separate peer-memory
+collectives and with NCCL; the pushed all-reduce adds the same bits on both ranks as GEMM -> peer
+all-reduce -> add.  Skipped with fewer
 than two GPUs."""
 import os
 
@@ -111,7 +112,7 @@ def _kernel_worker(rank, world, rdv, q):
             a = r0.clone()
             for _ in range(3):                                                  # epochs advance
                 a.copy_(r0)
-                ops.linear_allreduce(x, w, a, fused)
+                ops.rms_norm_ar(a, None, 1e-6, torch.bfloat16, fused, ops.linear_push(x, w, fused))
             s, part = plain.slot_out(T, H)
             ops.linear(x, w, out=part)
             b = r0.clone()
