@@ -316,13 +316,15 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
                 if (j < nvalid) dst[(size_t)(n0 + j) * g.ldo + m] = acc[j];
             }
           }
-          __threadfence_system();                      // every thread's pushes, before the flag
+          // The CTA barrier orders every thread's pushes before thread 0's system-scope fence, and
+          // the fence (cumulative) before the release stores of the flags.
           __syncthreads();
           if (tid == 0) {
             const size_t fw = ((size_t)a.slot * a.tiles_max + m_tile) * AR_MAX_RANKS;
             int* ep = a.epochs + (size_t)a.slot * a.tiles_max + m_tile;
             const int e = *ep + 1;
             *ep = e;
+            __threadfence_system();
             for (int p = 0; p < a.world; ++p) st_release_sys(reinterpret_cast<int*>(a.flags[p]) + fw + a.rank, e);
           }
         } else {
