@@ -37,7 +37,6 @@ void q38_gdn_chunk_prefill(torch::Tensor proj, torch::Tensor window, torch::Tens
 size_t q38_gdn_chunk_workspace_bytes(int64_t S, int64_t nv);
 void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
 void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
-void q38_l2_prefetch(torch::Tensor t, int64_t chunk_bytes);
 void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
                      torch::Tensor out, c10::optional<torch::Tensor> out_val, torch::Tensor part_val,
                      torch::Tensor part_idx, int64_t vocab_offset, bool write_prev);
@@ -69,7 +68,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill", &q38_attn_prefill);
   m.def("rms_norm", &q38_rms_norm);
   m.def("embedding", &q38_embedding);
-  m.def("l2_prefetch", &q38_l2_prefetch);
   m.def("markov_step", &q38_markov_step);
   m.def("peer_alloc", &q38_peer_alloc);
   m.def("ipc_handle", &q38_ipc_handle);

@@ -138,20 +138,6 @@ rms_norm_ar_kernel(float* __restrict__ x, int H, const float* __restrict__ w, fl
   }
 }
 
-// Warms L2 with a weight a later kernel of this step streams (the out-projection, while the
-// latency-bound GDN recurrence or attention of the same layer leaves HBM idle).  One thread per
-// CTA issues bulk L2 prefetches of its chunk; nothing is read into registers or written.
-__global__ void l2_prefetch_kernel(const uint8_t* __restrict__ base, long long bytes, long long chunk) {
-  if (threadIdx.x != 0) return;
-  const long long off = (long long)blockIdx.x * chunk;
-  if (off >= bytes) return;
-  const long long n = bytes - off < chunk ? bytes - off : chunk;
-  for (long long o = 0; o < n; o += 65536) {
-    const unsigned sz = (unsigned)(n - o < 65536 ? n - o : 65536);
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(base + off + o), "r"(sz) : "memory");
-  }
-}
-
 __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int H,
                              float* __restrict__ out) {
   pdl_wait();
@@ -344,17 +330,5 @@ void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps
   else if (vpt <= 8) { Q38_NORM_AR(8) }
   else { Q38_NORM_AR(20) }
 #undef Q38_NORM_AR
-  C10_CUDA_KERNEL_LAUNCH_CHECK();
-}
-
-void q38_l2_prefetch(torch::Tensor t, int64_t chunk_bytes) {
-  c10::cuda::CUDAGuard guard(t.device());
-  const long long bytes = (long long)t.numel() * t.element_size();
-  TORCH_CHECK(t.is_contiguous() && bytes % 16 == 0 && (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0,
-              "bulk L2 prefetch needs a contiguous, 16-byte aligned tensor of 16-byte multiple size");
-  TORCH_CHECK(chunk_bytes >= 65536 && chunk_bytes % 16 == 0, "prefetch chunk of at least 64 KB");
-  const unsigned grid = (unsigned)((bytes + chunk_bytes - 1) / chunk_bytes);
-  q38::l2_prefetch_kernel<<<grid, 32, 0, at::cuda::getCurrentCUDAStream()>>>(
-      reinterpret_cast<const uint8_t*>(t.data_ptr()), bytes, (long long)chunk_bytes);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

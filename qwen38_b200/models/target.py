@@ -25,8 +25,6 @@ LM head with a cross-rank (value, index) argmax.  Layout per rank:
 """
 from __future__ import annotations
 
-import os
-
 from dataclasses import dataclass, field
 
 import torch
@@ -181,11 +179,6 @@ class HybridTarget:
         # RMSNorm of the residual completes the reduction (``_pending`` = (residual, slot))
         self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_push")
         self._pending = None
-        # verify: while a layer's latency-bound mixer (GDN recurrence / attention) runs, a side
-        # stream bulk-prefetches the layer's out-projection weight into L2 (Q38_L2PF=0: off)
-        self.l2_prefetch = (hasattr(ops, "l2_prefetch") and self.device.type == "cuda"
-                            and os.environ.get("Q38_L2PF", "1") != "0")
-        self._pf_stream = torch.cuda.Stream(device=self.device) if self.l2_prefetch else None
         tp, r = self.comm.world, self.comm.rank
         self.tp, self.rank = tp, r
         self.widths = tp_widths(cfg, tp)
@@ -319,15 +312,6 @@ class HybridTarget:
             self._pending = None
             return self.ops.rms_norm_ar(x, w, eps, self.dtype, self.comm, slot)
         return self.ops.rms_norm(x, w, eps, self.dtype)
-
-    def _prefetch(self, main, w):
-        """Fork: after everything issued so far on ``main`` (the in-projection GEMM), prefetch
-        ``w`` into L2 on the side stream, concurrently with the mixer kernels that follow."""
-        if main is None:
-            return
-        self._pf_stream.wait_stream(main)
-        with torch.cuda.stream(self._pf_stream):
-            self.ops.l2_prefetch(w)
 
     def push_row_parallel(self, h, w, x):
         """Pushed all-reduce of a row-parallel out-projection into the residual ``x`` (any
@@ -476,14 +460,12 @@ class HybridTarget:
         feats = self._tap_buffer(rows, taps)
         tap_pos = {t: j for j, t in enumerate(taps)}
         x = self.ops.embedding(tokens, self.embed).float()
-        main = torch.cuda.current_stream(self.device) if self.l2_prefetch else None
         for i, L in enumerate(self.layers):
             h = self.norm(x, L["in_norm"])
             outs = []
             if L["kind"] == LINEAR:
                 j = self.gdn_index[i]
                 proj = self.ops.linear(h, L["w_in"], out=self.gdn_stash[j, :rows])   # kept for commit
-                self._prefetch(main, L["w_out"])
                 for seq, t in batch:
                     o0, n = seq.verify_rows
                     outs.append(self.ops.gdn_verify(proj[o0:o0 + n], self.conv[seq.slot, j], self.rec[seq.slot, j],
@@ -492,7 +474,6 @@ class HybridTarget:
             else:
                 j = self.attn_index[i]
                 proj = self.ops.linear(h, L["w_in"])
-                self._prefetch(main, L["w_out"])
                 for seq, t in batch:
                     o0, n = seq.verify_rows
                     pr = positions[o0:o0 + n]
@@ -507,8 +488,6 @@ class HybridTarget:
             if i in tap_pos:
                 self.settle(x)
                 feats[:, tap_pos[i]] = x.to(self.dtype)
-        if main is not None:
-            main.wait_stream(self._pf_stream)          # join the prefetch branch
         pred = self._head(x)
         return pred, (feats.reshape(rows, -1) if feats is not None else None)
 

@@ -125,12 +125,6 @@ class NativeOps(TorchOps):
         self.launches += 1
         return out if out is None or out_dtype == torch.bfloat16 else out.to(out_dtype)
 
-    def l2_prefetch(self, w, chunk_bytes: int = 1 << 20):
-        """Bulk-prefetch a (tile-contiguous) weight into L2 on the current stream."""
-        t = w.t if isinstance(w, TiledWeight) else w
-        self.C.l2_prefetch(t, chunk_bytes)
-        self.launches += 1
-
     def linear_residual(self, x, w, residual):
         w = self.prepare_weight(w)
         self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
