@@ -1,5 +1,7 @@
-"""Tensor parallel on CPU ranks (gloo, world size 2): the TP2 runtime reproduces the TP1
-greedy output and speculative decoding stays token-exact (BASELINE config 1 at TP2)."""
+"""Tensor parallel on CPU ranks (gloo): the TP2 runtime reproduces the TP1 greedy output and
+speculative decoding stays token-exact (BASELINE config 1 at TP2); at TP4 and TP8 (a shape whose
+heads divide by 8, KV heads replicated at TP8, vocab-sharded LM head and Markov selector) every
+rank agrees, speculation stays token-exact and the first tokens match TP1."""
 import os
 import socket
 
@@ -59,3 +61,73 @@ def test_tp2_gloo_matches_tp1(tiny):
         assert spec == gold
         # TP2 sums two partials per element; agreement with TP1 is expected on this seed
         assert gold == gold1
+
+
+def _mini():
+    from qwen38_b200.config import FULL, LINEAR, DrafterConfig, ModelConfig
+    cfg = ModelConfig(vocab_size=4096, hidden_size=256, intermediate_size=512, num_hidden_layers=4,
+                      num_attention_heads=8, num_key_value_heads=4, head_dim=64, rms_norm_eps=1e-6,
+                      rope_theta=1.0e7, partial_rotary_factor=0.5, max_position_embeddings=4096,
+                      linear_num_key_heads=8, linear_num_value_heads=16, linear_key_head_dim=32,
+                      linear_value_head_dim=32, linear_conv_kernel_dim=4,
+                      layer_types=[LINEAR, LINEAR, LINEAR, FULL])
+    dcfg = DrafterConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=1, num_attention_heads=8,
+                         num_key_value_heads=8, head_dim=32, taps=[1, 3], block_rows=4, markov_rank=16,
+                         yarn_original_max_position=512, max_position_embeddings=4096)
+    return cfg, dcfg
+
+
+def _worker_mini(rank, world, port, q):
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from qwen38_b200.checkpoint import random_drafter_source, random_target_source
+        from qwen38_b200.config import RuntimeConfig
+        from qwen38_b200.models.drafter import BlockDrafter
+        from qwen38_b200.models.target import HybridTarget
+        from qwen38_b200.parallel.comm import TorchComm
+        from qwen38_b200.spec.engine import PinnedAcceptance, SpecRuntime, greedy_reference
+        cfg, dcfg = _mini()
+        rt = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
+        prompt = torch.randint(0, cfg.vocab_size, (96,), generator=torch.Generator().manual_seed(5)).tolist()
+        tgt = HybridTarget(cfg, random_target_source(cfg, 3), rt, comm=TorchComm())
+        dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 4), tgt)
+        gold = greedy_reference(tgt, prompt, 16)
+        res = SpecRuntime(tgt, dr, verifier_rows=4).generate(
+            prompt, 16, gold_check=gold, pinned=PinnedAcceptance(gold, seed=1, mean_accepted=2))
+        q.put((rank, gold, res["tokens"]))
+    except BaseException as e:
+        q.put((rank, repr(e), None))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [4, 8])
+def test_tp4_tp8_gloo(world):
+    from qwen38_b200.checkpoint import random_target_source
+    from qwen38_b200.config import RuntimeConfig
+    from qwen38_b200.models.target import HybridTarget
+    cfg, dcfg = _mini()
+    tp1 = HybridTarget(cfg, random_target_source(cfg, 3), RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16))
+    prompt = torch.randint(0, cfg.vocab_size, (96,), generator=torch.Generator().manual_seed(5)).tolist()
+    gold1 = tp1.greedy(torch.tensor(prompt), 16)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker_mini, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    try:
+        out = [q.get(timeout=600) for _ in procs]
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+    golds = []
+    for rank, gold, spec in out:
+        assert spec is not None, gold
+        assert spec == gold
+        golds.append(gold)
+    assert all(g == golds[0] for g in golds)          # every rank emits the same tokens
+    assert golds[0][:4] == gold1[:4]                    # and they start as TP1 does (fp32 CPU sums)
