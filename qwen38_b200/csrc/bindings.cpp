@@ -7,11 +7,11 @@ void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tens
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
                         torch::Tensor counters, torch::Tensor err);
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
-                     torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
-                     int64_t slot, int64_t block_floats, int64_t tiles_max, torch::Tensor epochs);
+                     torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
+                     int64_t block_words, torch::Tensor epochs);
 void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, c10::optional<torch::Tensor> out,
-                     int64_t recv_local, int64_t flags_local, torch::Tensor epochs, int64_t slot, int64_t world,
-                     int64_t tiles_max, int64_t block_floats, torch::Tensor err);
+                     int64_t recv_local, torch::Tensor epochs, int64_t slot, int64_t world, int64_t block_words,
+                     torch::Tensor err);
 int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
                          torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace);
 void q38_clear_map_cache();

@@ -175,7 +175,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
       TORCH_CHECK(m_tiles <= sc.n_counters, "split-K counter array too small");
     }
     if (epi == EPI_PUSH_F32) {
-      TORCH_CHECK(ar != nullptr && m_tiles <= ar->tiles_max, "pushed all-reduce: too many output tiles");
+      TORCH_CHECK(ar != nullptr && (int64_t)T * N <= ar->block_words, "pushed all-reduce: block too small");
       g.ar = *ar;
     }
     if (epi == EPI_ARGMAX) {
@@ -218,29 +218,26 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
 }
 
 // Row-parallel out-projection whose epilogue pushes this rank's fp32 partial [T, N] (T <= 32)
-// into every rank's receive block of `slot` and publishes per-tile flags (EPI_PUSH_F32); the
-// reduction into the residual happens in q38_rms_norm_ar.  recv_ptrs / flag_ptrs: every rank's
-// receive and flag areas mapped into this process.
+// into every rank's receive block of `slot` as {value, epoch} words (EPI_PUSH_F32); the reduction
+// into the residual happens in q38_rms_norm_ar.  recv_ptrs: every rank's receive area mapped into
+// this process; epochs: this rank's [slots][32] per-row epochs.
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
-                     torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> flag_ptrs, int64_t rank,
-                     int64_t slot, int64_t block_floats, int64_t tiles_max, torch::Tensor epochs) {
+                     torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
+                     int64_t block_words, torch::Tensor epochs) {
   c10::cuda::CUDAGuard guard(x.device());
-  TORCH_CHECK(x.size(0) <= 32, "the pushed all-reduce serves <= 32 rows");
-  TORCH_CHECK(x.size(0) * N <= block_floats, "partial larger than a receive block");
+  TORCH_CHECK(x.size(0) <= q38::AR_MAX_ROWS, "the pushed all-reduce serves <= 32 rows");
+  TORCH_CHECK(x.size(0) * N <= block_words, "partial larger than a receive block");
   const int world = (int)recv_ptrs.size();
-  TORCH_CHECK(world >= 1 && world <= q38::AR_MAX_RANKS && (int)flag_ptrs.size() == world, "1..8 ranks");
+  TORCH_CHECK(world >= 1 && world <= q38::AR_MAX_RANKS, "1..8 ranks");
   TORCH_CHECK(rank >= 0 && rank < world, "bad rank");
-  TORCH_CHECK(epochs.numel() >= (slot + 1) * tiles_max, "epoch array too small");
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= (slot + 1) * q38::AR_MAX_ROWS,
+              "epoch array too small");
   q38::ArArgs a{};
-  for (int p = 0; p < world; ++p) {
-    a.recv[p] = recv_ptrs[p];
-    a.flags[p] = flag_ptrs[p];
-  }
-  a.block_floats = block_floats;
+  for (int p = 0; p < world; ++p) a.recv[p] = recv_ptrs[p];
+  a.block_words = block_words;
   a.rank = (int)rank;
   a.world = world;
   a.slot = (int)slot;
-  a.tiles_max = (int)tiles_max;
   a.epochs = epochs.data_ptr<int>();
   auto sc = q38::scratch_of(ws, counters, err);
   // no local output tensor: the epilogue writes the receive blocks, laid out [T, N] (ldo = N)

@@ -14,11 +14,11 @@
 //
 // EPI_PUSH_F32 - the GEMM half of the tensor-parallel all-reduce of a row-parallel out-projection
 // (TP > 1).  As soon as a tile's split-K fix-up is done, the fixing CTA stores its fp32 partial
-// tile into its own block of every rank's receive area (plain stores to peer memory over NVLink,
-// so tile t crosses NVLink while later tiles are still in the MMA), fences them at system scope
-// and publishes a per-(slot, tile) flag in every rank's flag area with a release store.  It never
-// waits: the reduction (wait for the W flags of each tile, rank-ordered sum, residual add) is done
-// by the kernel that consumes the residual next, the RMSNorm (`rms_norm_ar_kernel`, misc.cu).
+// tile into its own block of every rank's receive area over NVLink (tile t crosses NVLink while
+// later tiles are still in the MMA), each value as one 8-byte word {value, epoch}: a single
+// 64-bit store is observed whole, so the reader needs no fence or flag - it spins (bounded) on
+// each word until the epoch of this use of the slot appears.  The GEMM never waits; the kernel
+// that consumes the residual next (`rms_norm_ar_kernel`, misc.cu) completes the reduction.
 #pragma once
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
@@ -31,16 +31,25 @@ enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI
 
 constexpr int AR_MAX_RANKS = 8;
 
-// Peer buffers of the pushed all-reduce.  Receive area of every rank: blocks
-// [slot][src rank] of `block_floats` floats, each a [tokens, ldo] fp32 partial; flag area:
-// int words [slot][tile < tiles_max][src rank < 8].
+// Peer buffers of the pushed all-reduce.  Receive area of every rank: blocks [slot][src rank]
+// of `block_words` 8-byte words {fp32 value, epoch}, each a [tokens, ldo] partial.
+constexpr int AR_MAX_ROWS = 32;
+
 struct ArArgs {
-  long long recv[AR_MAX_RANKS];    // every rank's receive area, mapped into this process
-  long long flags[AR_MAX_RANKS];   // every rank's flag area
-  long long block_floats;
-  int rank, world, slot, tiles_max;
-  int* epochs;                     // this rank's [slots * tiles_max] epoch words
+  long long recv[AR_MAX_RANKS];    // every rank's receive area (8-byte words), mapped into this process
+  long long block_words;           // words per (slot, source rank) block: [AR_MAX_ROWS][ldo]
+  int rank, world, slot;
+  const int* epochs;               // this rank's [slots][AR_MAX_ROWS] epochs (advanced by the reader)
 };
+
+__device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr, unsigned long long v) {
+  asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
+}
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
 
 constexpr int BM = 128;
 constexpr int BK = 64;
@@ -307,25 +316,20 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
         } else if constexpr (EPI == EPI_PUSH_F32) {
           const ArArgs& a = g.ar;
-          const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_floats;
           if (m < g.M) {
+            uint32_t ep[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              ep[j] = j < nvalid ? (uint32_t)a.epochs[(size_t)a.slot * AR_MAX_ROWS + n0 + j] + 1u : 0u;
+            const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_words;
             for (int p = 0; p < a.world; ++p) {        // push: this rank's block in every rank
-              float* dst = reinterpret_cast<float*>(a.recv[p]) + mine;
+              unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.recv[p]) + mine;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
-                if (j < nvalid) dst[(size_t)(n0 + j) * g.ldo + m] = acc[j];
+                if (j < nvalid)
+                  st_relaxed_sys_u64(dst + (size_t)(n0 + j) * g.ldo + m,
+                                     ((unsigned long long)ep[j] << 32) | __float_as_uint(acc[j]));
             }
-          }
-          // The CTA barrier orders every thread's pushes before thread 0's system-scope fence, and
-          // the fence (cumulative) before the release stores of the flags.
-          __syncthreads();
-          if (tid == 0) {
-            const size_t fw = ((size_t)a.slot * a.tiles_max + m_tile) * AR_MAX_RANKS;
-            int* ep = a.epochs + (size_t)a.slot * a.tiles_max + m_tile;
-            const int e = *ep + 1;
-            *ep = e;
-            __threadfence_system();
-            for (int p = 0; p < a.world; ++p) st_release_sys(reinterpret_cast<int*>(a.flags[p]) + fw + a.rank, e);
           }
         } else {
           // Fully unrolled over the 32 token columns (predicated), so acc[] stays in registers;

@@ -58,66 +58,83 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
 }
 
 // The second half of the pushed tensor-parallel all-reduce (the GEMM half is EPI_PUSH_F32): one
-// CTA per token row waits (bounded) until every rank has published every 128-feature tile of the
-// slot, adds the W partials in rank order 0..W-1 to the fp32 residual row (identical bits on every
-// rank), writes the row back, and - when a norm weight is given - emits its RMSNorm in bf16.
-constexpr int AR_TILE = 128;
+// CTA per token row reads every rank's {value, epoch} words of its row, spinning (bounded) on each
+// until this use's epoch appears, adds the W partials in rank order 0..W-1 to the fp32 residual row
+// (identical bits on every rank), writes the row back, advances the row's epoch, and - when a norm
+// weight is given - emits its RMSNorm in bf16.
 constexpr int AR_RANKS = 8;
+constexpr int AR_ROWS = 32;
+
+__device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
+  unsigned long long v;
+  asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
+  return v;
+}
 
 template <int VPT>
 __global__ void __launch_bounds__(256)
 rms_norm_ar_kernel(float* __restrict__ x, int H, const float* __restrict__ w, float eps,
-                   __nv_bfloat16* __restrict__ out, long long ldo, const float* __restrict__ recv,
-                   const int* __restrict__ flags, const int* __restrict__ epochs, int slot, int world,
-                   int tiles_max, long long block_floats, int* err) {
+                   __nv_bfloat16* __restrict__ out, long long ldo, const unsigned long long* __restrict__ recv,
+                   int* __restrict__ epochs, int slot, int world, long long block_words, int* err) {
   pdl_wait();
   pdl_trigger();
   const int r = blockIdx.x;
-  const int tiles = (H + AR_TILE - 1) / AR_TILE;
   __shared__ int ok_s;
   __shared__ float red[32];
   if (threadIdx.x == 0) ok_s = 1;
+  const uint32_t e = (uint32_t)epochs[(size_t)slot * AR_ROWS + r] + 1u;
   __syncthreads();
-  for (int t = threadIdx.x; t < tiles * world; t += blockDim.x) {
-    const int tile = t / world, q = t % world;
-    const size_t fw = ((size_t)slot * tiles_max + tile);
-    const int e = epochs[fw];
-    const int* f = flags + fw * AR_RANKS + q;
-    const unsigned long long t0 = globaltimer();
-    while (ld_acquire_sys(f) < e) {
-      if (globaltimer() - t0 > kWaitLimitNs) {
-        record_error(err, kErrPeer);
-        ok_s = 0;
-        break;
+  const unsigned long long* base = recv + (size_t)slot * world * block_words + (size_t)r * H;
+  float psum[VPT];                         // rank-ordered sums: ((0 + p_0) + p_1) + ...
+  bool ok = true;
+  const unsigned long long t0 = globaltimer();
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) psum[u] = 0.f;
+#pragma unroll
+  for (int q = 0; q < AR_RANKS; ++q) {
+    if (q >= world) break;
+    unsigned long long wv4[VPT];
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {          // issue every load of this source before spinning
+      const int i = threadIdx.x + u * blockDim.x;
+      wv4[u] = i < H ? ld_relaxed_sys_u64(base + (size_t)q * block_words + i) : ((unsigned long long)e << 32);
+    }
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      const int i = threadIdx.x + u * blockDim.x;
+      while (ok && (uint32_t)(wv4[u] >> 32) != e) {
+        if (globaltimer() - t0 > kWaitLimitNs) {
+          ok = false;
+          break;
+        }
+        wv4[u] = ld_relaxed_sys_u64(base + (size_t)q * block_words + i);
       }
+      if (i < H) psum[u] += __uint_as_float((uint32_t)wv4[u]);
     }
   }
+  if (!ok) {
+    record_error(err, kErrPeer);
+    ok_s = 0;
+  }
   __syncthreads();
-  if (!ok_s) return;                       // a peer never published: residual left untouched
+  if (!ok_s) return;                       // a peer never published: residual and epoch untouched
   float* xr = x + (size_t)r * H;
-  const float* base = recv + (size_t)slot * world * block_floats + (size_t)r * H;
   float v[VPT], wv[VPT];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {
     const int i = threadIdx.x + u * blockDim.x;
-    float part[AR_RANKS];
     float xv = 0.f;
     wv[u] = 0.f;
     if (i < H) {
       xv = xr[i];
       if (w) wv[u] = w[i];
-#pragma unroll
-      for (int q = 0; q < AR_RANKS; ++q) part[q] = q < world ? __ldcg(base + (size_t)q * block_floats + i) : 0.f;
     }
-    float sum = 0.f;
-#pragma unroll
-    for (int q = 0; q < AR_RANKS; ++q)
-      if (q < world) sum += part[q];
-    v[u] = xv + sum;
+    v[u] = xv + psum[u];
     if (i < H) xr[i] = v[u];
     ss += v[u] * v[u];
   }
+  if (threadIdx.x == 0) epochs[(size_t)slot * AR_ROWS + r] = (int)e;
   if (!out) return;
   ss = warp_sum(ss);
   const int w_ = threadIdx.x >> 5, l = threadIdx.x & 31;
@@ -304,16 +321,16 @@ void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor
 
 // x [R, H] fp32 residual (updated in place); w / out optional (absent: reduce only).
 void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, c10::optional<torch::Tensor> out,
-                     int64_t recv_local, int64_t flags_local, torch::Tensor epochs, int64_t slot, int64_t world,
-                     int64_t tiles_max, int64_t block_floats, torch::Tensor err) {
+                     int64_t recv_local, torch::Tensor epochs, int64_t slot, int64_t world, int64_t block_words,
+                     torch::Tensor err) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous() && x.dim() == 2, "contiguous fp32 residual");
   TORCH_CHECK((bool)w == (bool)out, "norm weight and output go together");
   if (out) TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->stride(1) == 1, "bf16 row-major output");
   TORCH_CHECK(world >= 1 && world <= q38::AR_RANKS, "1..8 ranks");
   const int R = (int)x.size(0), H = (int)x.size(1);
-  TORCH_CHECK((int64_t)R * H <= block_floats, "residual larger than a receive block");
-  TORCH_CHECK((H + q38::AR_TILE - 1) / q38::AR_TILE <= tiles_max, "too many tiles");
+  TORCH_CHECK(R <= q38::AR_ROWS && (int64_t)R * H <= block_words, "residual larger than a receive block");
+  TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= (slot + 1) * q38::AR_ROWS, "epoch array too small");
   TORCH_CHECK(H <= 256 * 20, "hidden too large");
   if (R == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
@@ -323,9 +340,8 @@ void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps
   const int vpt = (H + 255) / 256;
 #define Q38_NORM_AR(VV)                                                                                          \
   q38::launch_pdl(q38::rms_norm_ar_kernel<VV>, dim3(R), dim3(256), 0, st, x.data_ptr<float>(), H, wp, (float)eps,  \
-                  op, ldo, reinterpret_cast<const float*>(recv_local), reinterpret_cast<const int*>(flags_local),  \
-                  (const int*)epochs.data_ptr<int>(), (int)slot, (int)world, (int)tiles_max, (long long)block_floats, \
-                  err.data_ptr<int>());
+                  op, ldo, reinterpret_cast<const unsigned long long*>(recv_local), epochs.data_ptr<int>(),     \
+                  (int)slot, (int)world, (long long)block_words, err.data_ptr<int>());
   if (vpt <= 4) { Q38_NORM_AR(4) }
   else if (vpt <= 8) { Q38_NORM_AR(8) }
   else { Q38_NORM_AR(20) }

@@ -107,21 +107,21 @@ class NativeOps(TorchOps):
 
     def linear_push(self, x, w, comm) -> int:
         """GEMM half of the tensor-parallel all-reduce: x @ w^T (fp32, T <= 32 rows) goes straight
-        from each finished tile into every rank's receive block of a fresh slot, with per-tile
-        flags; returns the slot for ``rms_norm_ar``."""
+        from each finished tile into every rank's receive block of a fresh slot as {value, epoch}
+        words; returns the slot for ``rms_norm_ar``."""
         w = self.prepare_weight(w)
         slot = comm.fused_slot()
-        self.C.linear_push(x.contiguous(), w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs,
-                           comm.fflag_ptrs, comm.rank, slot, comm.block_floats, comm.tiles_max, comm.fepochs)
+        self.C.linear_push(x.contiguous(), w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs, comm.rank,
+                           slot, comm.block_words, comm.fepochs)
         self.launches += 1
         return slot
 
     def rms_norm_ar(self, x, w, eps, out_dtype, comm, slot):
-        """Reduction half: waits for every rank's tiles of ``slot``, adds them (rank order) into the
+        """Reduction half: waits for every rank's words of ``slot``, adds them (rank order) into the
         fp32 residual ``x`` in place and returns RMSNorm(x) * w in bf16 (``w`` None: reduce only)."""
         out = None if w is None else torch.empty(x.shape[0], x.shape[1], dtype=torch.bfloat16, device=x.device)
-        self.C.rms_norm_ar(x, w, float(eps), out, comm.recv_ptrs[comm.rank], comm.fflag_ptrs[comm.rank], comm.fepochs,
-                           slot, comm.world, comm.tiles_max, comm.block_floats, self.err)
+        self.C.rms_norm_ar(x, w, float(eps), out, comm.recv_ptrs[comm.rank], comm.fepochs, slot, comm.world,
+                           comm.block_words, self.err)
         self.launches += 1
         return out if out is None or out_dtype == torch.bfloat16 else out.to(out_dtype)
 

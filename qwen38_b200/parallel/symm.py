@@ -11,9 +11,9 @@ collectives with the kernels in ``csrc/comm.cu``:
   and every Markov step.
 
 * pushed all-reduce (``NativeOps.linear_push`` + ``NativeOps.rms_norm_ar``): the out-projection
-  GEMM pushes each finished fp32 tile into every rank's receive area and flags it; the next
-  RMSNorm of the residual waits for the flags, adds the rank-ordered sum and normalises (the
-  ``fused_*`` areas below: blocks [slot][source rank], flags [slot][tile][source rank]).
+  GEMM pushes each finished fp32 tile into every rank's receive area as {value, epoch} 8-byte
+  words; the next RMSNorm of the residual spins on the words of its row until this use's epoch
+  appears, adds the rank-ordered sum and normalises (receive blocks [slot][source rank]).
 
 Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
 
@@ -33,12 +33,13 @@ from .comm import TorchComm
 
 MAX_RANKS = 8
 AR_CTAS = 32
+PUSH_ROWS = 32            # rows of a pushed all-reduce (csrc: AR_MAX_ROWS)
 
 
 class SymmComm(TorchComm):
     def __init__(self, device, hidden: int, group=None, slot_rows: int = 32, graph_slots: int = 768,
                  eager_slots: int = 64, fused_graph_slots: int = 160, fused_eager_slots: int = 32,
-                 tiles_max: int = 64, fused: bool = True):
+                 fused: bool = True):
         super().__init__(group)
         self.fused = fused          # row-parallel GEMMs push their tiles; the next norm reduces
         if self.world > MAX_RANKS:
@@ -52,14 +53,13 @@ class SymmComm(TorchComm):
         self.graph_slots, self.eager_slots = graph_slots, eager_slots
         data_bytes = self.n_slots * self.slot_floats * 4
         flag_bytes = self.n_slots * AR_CTAS * MAX_RANKS * 4
-        # fused GEMM + all-reduce areas
-        self.block_floats = self.slot_floats
-        self.tiles_max = tiles_max
+        # pushed all-reduce: receive blocks [slot][source rank][32 rows][hidden] of {value, epoch}
+        # 8-byte words, and this rank's per-(slot, row) epochs
+        self.block_words = PUSH_ROWS * hidden
         self.fused_graph_slots, self.fused_eager_slots = fused_graph_slots, fused_eager_slots
         n_fused = fused_graph_slots + fused_eager_slots
-        recv_bytes = n_fused * self.world * self.block_floats * 4
-        fflag_bytes = n_fused * tiles_max * MAX_RANKS * 4
-        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes + fflag_bytes, dev)
+        recv_bytes = n_fused * self.world * self.block_words * 8
+        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes, dev)
         handle = self.C.ipc_handle(self.buf).to(self.device)
         handles = [torch.empty_like(handle) for _ in range(self.world)]
         dist.all_gather(handles, handle, group=self.group)
@@ -76,8 +76,7 @@ class SymmComm(TorchComm):
         self.data_ptrs = ptrs
         self.flag_ptrs = [p + data_bytes for p in ptrs]
         self.recv_ptrs = [p + data_bytes + flag_bytes for p in ptrs]
-        self.fflag_ptrs = [p + data_bytes + flag_bytes + recv_bytes for p in ptrs]
-        self.fepochs = torch.zeros(n_fused * tiles_max, dtype=torch.int32, device=self.device)
+        self.fepochs = torch.zeros(n_fused * PUSH_ROWS, dtype=torch.int32, device=self.device)
         self._next_fgraph = 0
         self._next_feager = 0
         self.local = self.buf[:data_bytes].view(torch.float32).view(self.n_slots, self.slot_floats)
@@ -106,7 +105,7 @@ class SymmComm(TorchComm):
         return s
 
     def fused_fits(self, rows: int, cols: int) -> bool:
-        return rows <= min(32, self.slot_rows) and rows * cols <= self.block_floats and -(-cols // 128) <= self.tiles_max
+        return rows <= PUSH_ROWS and cols == self.hidden
 
     def _slot(self) -> int:
         if torch.cuda.is_current_stream_capturing():

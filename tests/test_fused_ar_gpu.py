@@ -15,21 +15,18 @@ if not torch.cuda.is_available():
 
 from qwen38_b200.ops.native import NativeOps, untile_weight  # noqa: E402
 
-ERR_PEER, TILES_MAX = 8, 64
+ERR_PEER = 8
 
 
 class _Areas:
-    """Receive / flag areas of a fake communicator; every "rank" maps this GPU's own buffers."""
+    """Receive area of a fake communicator; every "rank" maps this GPU's own buffer."""
 
     def __init__(self, world, hidden, slots=4):
-        self.world, self.rank = world, 0
-        self.block_floats = 32 * hidden
-        self.tiles_max = TILES_MAX
-        self.recv = torch.zeros(slots * world * self.block_floats, device="cuda")
-        self.flags = torch.zeros(slots * TILES_MAX * 8, dtype=torch.int32, device="cuda")
+        self.world, self.rank, self.hidden = world, 0, hidden
+        self.block_words = 32 * hidden
+        self.recv = torch.zeros(slots * world * self.block_words, dtype=torch.int64, device="cuda")
         self.recv_ptrs = [self.recv.data_ptr()] * world
-        self.fflag_ptrs = [self.flags.data_ptr()] * world
-        self.fepochs = torch.zeros(slots * TILES_MAX, dtype=torch.int32, device="cuda")
+        self.fepochs = torch.zeros(slots * 32, dtype=torch.int32, device="cuda")
         self.slots, self._n = slots, 0
 
     def fused_slot(self):
@@ -73,7 +70,7 @@ def test_missing_peer_times_out_and_reports(ops):
     T, N, K = 4, 1024, 512
     x = torch.randn(T, K, device="cuda").to(torch.bfloat16)
     w = ops.prepare_weight((torch.randn(N, K, device="cuda") * 0.02).to(torch.bfloat16))
-    comm = _Areas(2, N)          # "rank 1" is this GPU's own area: its flags are never written
+    comm = _Areas(2, N)          # "rank 1"'s block of this GPU's own area is never written
     r = torch.full((T, N), 3.0, device="cuda")
     t0 = time.time()
     slot = ops.linear_push(x, w, comm)
