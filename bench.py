@@ -44,9 +44,9 @@ def parse():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--comm", default="peer", choices=["fused", "peer", "nccl"],
-                    help="TP collectives: peer-memory all-reduce kernels (default), GEMM kernels that carry "
-                         "the all-reduce themselves, or NCCL")
+    ap.add_argument("--comm", default="fused", choices=["fused", "peer", "nccl"],
+                    help="TP collectives: all-reduce pushed by the out-projection GEMMs and completed by the "
+                         "next RMSNorm (default), separate peer-memory all-reduce kernels, or NCCL")
     return ap.parse_args()
 
 
