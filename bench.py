@@ -55,6 +55,14 @@ REFERENCE_UNAVAILABLE = (
     "package (pip: 'Neither setup.py nor pyproject.toml found') and no CUDA code path; it cannot run on B200")
 
 
+def _provenance():
+    try:
+        from qwen38_b200.utils.provenance import manifest
+        return manifest()
+    except Exception as e:          # provenance never blocks the measurement
+        return {"error": repr(e)}
+
+
 class ClockSampler:
     """Samples nvidia-smi clocks and throttle reasons during the timed region."""
 
@@ -248,6 +256,8 @@ def main():
                          for k in ("draft", "verify", "commit")},
             "tokens_per_block": round(statistics.mean(r["tokens_per_block"] for r in results), 3),
             "clocks": clocks,
+            "provenance": {k: v for k, v in _provenance().items() if k in ("sources_sha256", "extension_sha256",
+                                                                                 "device", "driver", "torch")},
             "e2e": {"value": round(e2e_tg, 3), "unit": "tok/s (committed TG, host wall clock via "
                     "SpecRuntime.generate)", "h2d_bytes_per_step": results[-1]["h2d"],
                     "d2h_bytes_per_step": results[-1]["d2h"]},
