@@ -107,8 +107,6 @@ void clear_map_cache() {
   g_map_cache.clear();
 }
 
-constexpr int kMaxClusterSplits = 8;   // portable cluster size
-
 // Split count for a weight of `m_tiles` row tiles and `kblocks` K blocks: a function of the weight
 // shape only (never of the token count), about two CTAs per SM.
 static int pick_splits(int m_tiles, int kblocks, int sms) {
@@ -168,12 +166,10 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     const int m_tiles = (N + BM - 1) / BM;
     int splits = (epi == EPI_SWIGLU || epi == EPI_ARGMAX) ? std::max(1, std::min(2 * num_sms() / m_tiles, g.kblocks / 4))
                                                          : pick_splits(m_tiles, g.kblocks, num_sms());
-    splits = std::min(splits, kMaxClusterSplits);
     int kps = (g.kblocks + splits - 1) / splits;
     splits = (g.kblocks + kps - 1) / kps;
     g.splits = splits;
     g.kps = kps;
-    g.cluster_red = splits > 1 ? 1 : 0;     // split-K partials reduced through DSMEM in a cluster
     if (splits > 1) {
       TORCH_CHECK((int64_t)m_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
       TORCH_CHECK(m_tiles <= sc.n_counters, "split-K counter array too small");

@@ -23,13 +23,9 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
-#include <cooperative_groups.h>
-
 #include "common.cuh"
 
 namespace q38 {
-
-namespace cg = cooperative_groups;
 
 enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_PUSH_F32 = 5 };
 
@@ -71,7 +67,6 @@ struct GemmArgs {
   int* amax_idx;
   ArArgs ar;                  // EPI_PUSH_F32 only
   unsigned long long* trace;  // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
-  int cluster_red;            // swap mode: the splits of a tile are one cluster, reduced over DSMEM
 };
 
 // trace points: 0 entry, 1 setup done, 2 first stage landed, 3 last MMA issued, 4 accumulator
@@ -213,54 +208,19 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const int row = warp * 32 + lane;   // TMEM lane == tile row m
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 
-  if constexpr (SWAP) {
+  if (ok && nk > 0) {
+    if constexpr (SWAP) {
       // Each thread owns output feature m0+row, tokens n0 .. n0+BN-1 (BN == 32).
       static_assert(BN == 32, "swap mode uses 32 token columns");
-      const bool have = ok && nk > 0;
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(trow, r);
+      tmem_ld_wait();
       float acc[32];
-      if (have) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(trow, r);
-        tmem_ld_wait();
 #pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
-      } else {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-      }
+      for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
 
-      bool do_epi = have;
-      if (g.splits > 1 && g.cluster_red) {
-        // The splits of this tile form one thread-block cluster: every CTA parks its partial in
-        // its own (now idle) ring memory, and split 0 sums the others through distributed shared
-        // memory in split order.  Both cluster barriers are reached by every CTA, whatever
-        // happened before (an aborted CTA reports it through its flag word instead).
-        cg::cluster_group cluster = cg::this_cluster();
-        float* part_s = reinterpret_cast<float*>(smem);          // [32 tokens][128 rows]
-        int* have_s = reinterpret_cast<int*>(smem + BM * BN * 4);
-#pragma unroll
-        for (int j = 0; j < 32; ++j) part_s[j * BM + row] = acc[j];
-        if (tid == 0) *have_s = have ? 1 : 0;
-        cluster.sync();
-        do_epi = false;
-        if (split == 0) {
-          bool all = true;
-          for (int s2 = 0; s2 < g.splits; ++s2) all = all && (*cluster.map_shared_rank(have_s, s2) != 0);
-          if (all) {
-            for (int s2 = 1; s2 < g.splits; ++s2) {
-              const float* rp = cluster.map_shared_rank(part_s, s2);
-              float x[32];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) x[j] = rp[j * BM + row];
-#pragma unroll
-              for (int j = 0; j < 32; ++j) acc[j] += x[j];
-            }
-          }
-          do_epi = all;
-        }
-        if (tid == 0) Q38_STAMP(5);
-        cluster.sync();               // peers' partials stay valid until split 0 has read them
-      } else if (g.splits > 1 && have) {
+      bool do_epi = true;
+      if (g.splits > 1) {
         const int tile = m_tile;  // single n tile in swap mode
         float* part = g.ws + ((size_t)tile * g.splits + split) * (BM * BN);
 #pragma unroll
@@ -397,7 +357,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
         }
       }
-  } else if (ok && nk > 0) {
+    } else {
       // Non-swap: thread owns token row m0+row, features n0 .. n0+BN-1.
       const int m = m0 + row;
       const bool rv = m < g.M;
@@ -466,6 +426,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
         }
       }
+    }
   }
 
   // ---------------- teardown
@@ -489,28 +450,7 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g
                 "cudaFuncSetAttribute failed");
     configured = true;
   }
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = dim3(128);
-  cfg.dynamicSmemBytes = (size_t)smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[2];
-  int n = 0;
-  if (pdl_enabled()) {
-    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[n].val.programmaticStreamSerializationAllowed = 1;
-    ++n;
-  }
-  if (g.cluster_red) {                 // the grid's z extent (the splits of a tile) is one cluster
-    attr[n].id = cudaLaunchAttributeClusterDimension;
-    attr[n].val.clusterDim.x = 1;
-    attr[n].val.clusterDim.y = 1;
-    attr[n].val.clusterDim.z = grid.z;
-    ++n;
-  }
-  cfg.attrs = attr;
-  cfg.numAttrs = n;
-  TORCH_CHECK(cudaLaunchKernelEx(&cfg, kern, ma, mb, g) == cudaSuccess, "GEMM launch failed");
+  TORCH_CHECK(launch_pdl(kern, grid, dim3(128), (size_t)smem, st, ma, mb, g) == cudaSuccess, "GEMM launch failed");
 }
 
 constexpr int SKINNY_STAGES = 5;   // 5 x 20 KB ring: two CTAs per SM
