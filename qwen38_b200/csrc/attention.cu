@@ -189,20 +189,22 @@ attn_decode_kernel(DecodeArgs a) {
       }
     }
   };
+  // cache row offsets of the chunk's keys once (one block-table lookup per key, not per 16 B)
+  __shared__ long long kv_row[CH];
+  for (int j = threadIdx.x; j < CH; j += blockDim.x) kv_row[j] = k0 + j < k1 ? (long long)kv_base(k0 + j) * D : -1;
+  __syncthreads();
   for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
     const int j = idx / (D / 8), ch = idx % (D / 8);
-    const int kp = k0 + j;
     uint4* dst = reinterpret_cast<uint4*>(Ks + j * DP) + ch;
-    if (kp < k1) cp_async16(dst, reinterpret_cast<const uint4*>(a.kcache + kv_base(kp) * D) + ch);
+    if (kv_row[j] >= 0) cp_async16(dst, reinterpret_cast<const uint4*>(a.kcache + kv_row[j]) + ch);
     else *dst = make_uint4(0, 0, 0, 0);
   }
   stage_q(0);
   cp_async_commit();
   for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
     const int j = idx / (D / 8), ch = idx % (D / 8);
-    const int kp = k0 + j;
     uint4* dst = reinterpret_cast<uint4*>(Vs + j * DP) + ch;
-    if (kp < k1) cp_async16(dst, reinterpret_cast<const uint4*>(a.vcache + kv_base(kp) * D) + ch);
+    if (kv_row[j] >= 0) cp_async16(dst, reinterpret_cast<const uint4*>(a.vcache + kv_row[j]) + ch);
     else *dst = make_uint4(0, 0, 0, 0);
   }
   cp_async_commit();

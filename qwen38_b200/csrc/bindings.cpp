@@ -5,7 +5,8 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
                 torch::Tensor counters, torch::Tensor err);
 void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
-                        torch::Tensor counters, torch::Tensor err);
+                        torch::Tensor counters, torch::Tensor err, c10::optional<torch::Tensor> samp_scale,
+                        c10::optional<torch::Tensor> samp_key);
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
                      int64_t block_words, torch::Tensor epochs);

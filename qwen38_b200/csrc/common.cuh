@@ -248,6 +248,23 @@ inline cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cud
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// ------------------------------------------------------------------ sampling noise
+// Counter-based Gumbel noise for sampling by Gumbel-max (argmax of logits / T + G over the
+// vocabulary draws from softmax(logits / T)).  The 64-bit mix is the SplitMix64 finaliser
+// (G. Steele, D. Lea, C. Flood, "Fast splittable pseudorandom number generators", OOPSLA 2014);
+// noise depends only on (row key, global vocabulary index), so a sample does not depend on the
+// batch it runs in or on how the vocabulary is sharded over tensor-parallel ranks.
+__host__ __device__ __forceinline__ unsigned long long mix64(unsigned long long z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ULL;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebULL;
+  return z ^ (z >> 31);
+}
+__device__ __forceinline__ float gumbel_noise(unsigned long long key, unsigned long long index) {
+  const unsigned long long h = mix64(key ^ mix64(index + 0x9e3779b97f4a7c15ULL));
+  const float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);     // (0, 1), 24 bits
+  return -logf(-logf(u));
+}
+
 // ------------------------------------------------------------------ misc math
 __device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
 

@@ -115,13 +115,16 @@ gdn_recurrent_kernel(GdnArgs a) {
   }
 #pragma unroll
   for (int j = 0; j < KC; ++j) wv[j] = conv_w[(size_t)(cv + col) * KC + j];
-  pdl_wait();
-  pdl_trigger();
-  const int rows = a.rows_dev ? *a.rows_dev : a.rows;
-
+  // The recurrent state is written only by commit / prefill launches that completed before the
+  // kernel this one follows began its own wait (every kernel of a step waits on its predecessor
+  // before triggering its successor, except the GEMM, whose predecessor does), so it is read
+  // before griddepcontrol.wait: its DRAM round trip overlaps the previous kernel's tail.
   float S[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + gcol];
+  pdl_wait();
+  pdl_trigger();
+  const int rows = a.rows_dev ? *a.rows_dev : a.rows;
 
   cg::cluster_group cluster = cg::this_cluster();
   int parity = 0;

@@ -115,6 +115,12 @@ static int pick_splits(int m_tiles, int kblocks, int sms) {
   return s;
 }
 
+struct SampleArgs {
+  const float* scale;
+  const unsigned long long* key;
+  long long vocab_off;
+};
+
 struct Scratch {
   float* ws;
   int64_t ws_floats;
@@ -142,7 +148,8 @@ static int num_sms() {
 // qwen38_b200/ops/native.py) of logical shape [N, K].
 void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
                    const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr,
-                   const ArArgs* ar = nullptr, unsigned long long* trace = nullptr, int64_t ldo_override = -1) {
+                   const ArArgs* ar = nullptr, unsigned long long* trace = nullptr, int64_t ldo_override = -1,
+                   const SampleArgs* samp = nullptr) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
@@ -179,6 +186,11 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
       g.ar = *ar;
     }
     if (epi == EPI_ARGMAX) {
+      if (samp) {
+        g.samp_scale = samp->scale;
+        g.samp_key = samp->key;
+        g.vocab_off = samp->vocab_off;
+      }
       g.amax_val = amax_val;
       g.amax_idx = amax_idx;
       *amax_tiles = m_tiles;
@@ -265,7 +277,8 @@ int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Ten
 
 void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out_val, torch::Tensor out_idx,
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
-                        torch::Tensor counters, torch::Tensor err) {
+                        torch::Tensor counters, torch::Tensor err, c10::optional<torch::Tensor> samp_scale,
+                        c10::optional<torch::Tensor> samp_key) {
   c10::cuda::CUDAGuard guard(x.device());
   auto sc = q38::scratch_of(ws, counters, err);
   const int T = (int)x.size(0);
@@ -275,8 +288,16 @@ void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tens
               "argmax partial buffers too small");
   int tiles = 0;
   torch::Tensor dummy = out_val;  // not written by the argmax epilogue
+  q38::SampleArgs sa{};
+  if (samp_scale) {
+    TORCH_CHECK(samp_key && samp_scale->scalar_type() == at::kFloat && samp_key->scalar_type() == at::kLong &&
+                    samp_scale->numel() >= T && samp_key->numel() >= T, "sampling: fp32 scale [T] and int64 key [T]");
+    sa.scale = samp_scale->data_ptr<float>();
+    sa.key = reinterpret_cast<const unsigned long long*>(samp_key->data_ptr<int64_t>());
+  }
+  sa.vocab_off = vocab_offset;
   q38::gemm_dispatch(x, w, (int)N, dummy, q38::EPI_ARGMAX, sc, part_val.data_ptr<float>(), part_idx.data_ptr<int>(),
-                     &tiles);
+                     &tiles, nullptr, nullptr, -1, &sa);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   q38::launch_pdl(q38::argmax_finalize_kernel, dim3(T), dim3(256), 0, st, (const float*)part_val.data_ptr<float>(),
                   (const int*)part_idx.data_ptr<int>(), tiles, T, (long long)vocab_offset, out_val.data_ptr<float>(),

@@ -67,6 +67,9 @@ struct GemmArgs {
   int* amax_idx;
   ArArgs ar;                  // EPI_PUSH_F32 only
   unsigned long long* trace;  // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
+  const float* samp_scale;    // EPI_ARGMAX: per token row 1/temperature (0: greedy), or nullptr
+  const unsigned long long* samp_key;   // per token row noise key
+  long long vocab_off;        // global vocabulary index of weight row 0 (noise index)
 };
 
 // trace points: 0 entry, 1 setup done, 2 first stage landed, 3 last MMA issued, 4 accumulator
@@ -292,6 +295,10 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           for (int j = 0; j < 32; ++j) {
             if (j >= nvalid) break;
             float v = (m < g.M) ? acc[j] : -INFINITY;
+            if (g.samp_scale != nullptr && m < g.M) {      // Gumbel-max sampling rows
+              const float sc = g.samp_scale[n0 + j];
+              if (sc > 0.f) v = acc[j] * sc + gumbel_noise(g.samp_key[n0 + j], (unsigned long long)(g.vocab_off + m));
+            }
             int idx = m;
 #pragma unroll
             for (int o = 16; o > 0; o >>= 1) {

@@ -331,9 +331,10 @@ class HybridTarget:
         gu = self.ops.linear_swiglu(h, L["w_gu"], GU_BLOCK)
         self._row_parallel(gu, L["w_down"], x)
 
-    def _head(self, x_rows):
+    def _head(self, x_rows, sampling=None):
         hn = self.norm(x_rows, self.final_norm)
-        val, idx = self.ops.lm_head_argmax(hn, self.lm_head, self.vocab_offset)
+        val, idx = (self.ops.lm_head_argmax(hn, self.lm_head, self.vocab_offset, sampling) if sampling is not None
+                    else self.ops.lm_head_argmax(hn, self.lm_head, self.vocab_offset))
         return self.comm.argmax_reduce(val, idx) if self.tp > 1 else idx
 
     def _tap_buffer(self, rows, taps):
@@ -343,7 +344,7 @@ class HybridTarget:
 
     # ------------------------------------------------------------------ prefill
     @torch.no_grad()
-    def prefill(self, seq: SeqState, tokens: torch.Tensor, taps=(), return_logits_row=False):
+    def prefill(self, seq: SeqState, tokens: torch.Tensor, taps=(), return_logits_row=False, sampling=None):
         """Committed prefill of ``tokens`` [S] from ``seq.pos``.  Returns (next token [1] int64,
         tap features [S, len(taps)*H] or None)."""
         S = tokens.shape[0]
@@ -381,16 +382,18 @@ class HybridTarget:
             seq.pos += tok.shape[0]
             if c1 == S:
                 self.settle(x)
-                nxt = self._head(x[-1:])
+                nxt = self._head(x[-1:], sampling)
         return nxt, (feats.reshape(S, -1) if feats is not None else None)
 
     # ------------------------------------------------------------------ verify / commit
     @torch.no_grad()
-    def verify(self, batch, taps=()):
-        """Uncommitted forward (CUDA-graph replay for a single sequence when enabled)."""
-        if self.use_graphs and len(batch) == 1:
+    def verify(self, batch, taps=(), sampling=None):
+        """Uncommitted forward (CUDA-graph replay for a single greedy sequence when enabled).
+        ``sampling`` = (scale [rows] fp32, key [rows] int64): rows with scale = 1/temperature > 0
+        return Gumbel-max samples instead of argmax tokens."""
+        if self.use_graphs and len(batch) == 1 and sampling is None:
             return self._verify_graphed(batch[0][0], batch[0][1], tuple(taps))
-        return self._verify_eager(batch, taps)
+        return self._verify_eager(batch, taps, sampling=sampling)
 
     def _verify_graphed(self, seq: SeqState, tokens: torch.Tensor, taps: tuple):
         T = int(tokens.shape[0])
@@ -442,7 +445,7 @@ class HybridTarget:
             self._graph_pool = torch.cuda.graph_pool_handle()
         return self._graph_pool
 
-    def _verify_eager(self, batch, taps=(), positions=None):
+    def _verify_eager(self, batch, taps=(), positions=None, sampling=None):
         """Uncommitted forward.  ``batch``: list of (SeqState, tokens [T_s]) with the tokens at
         positions ``seq.pos ..``.  Returns (argmax [sum T_s] int64, taps [sum T_s, n*H] or None)."""
         rows = sum(int(t.shape[0]) for _, t in batch)
@@ -488,7 +491,7 @@ class HybridTarget:
             if i in tap_pos:
                 self.settle(x)
                 feats[:, tap_pos[i]] = x.to(self.dtype)
-        pred = self._head(x)
+        pred = self._head(x, sampling)
         return pred, (feats.reshape(rows, -1) if feats is not None else None)
 
     @torch.no_grad()
@@ -565,6 +568,36 @@ class HybridTarget:
 
     # ------------------------------------------------------------------ convenience
     @torch.no_grad()
+    def sampling_args(self, temperature: float, seed: int, positions):
+        """(scale, key) device tensors for sampled rows at ``positions`` (temperature > 0)."""
+        from ..ops.torch_ref import sample_key
+        n = len(positions)
+        scale = torch.full((n,), 1.0 / temperature if temperature > 0 else 0.0, dtype=torch.float32)
+        key = torch.tensor([sample_key(seed, int(p)) for p in positions], dtype=torch.int64)
+        return scale.to(self.device, non_blocking=True), key.to(self.device, non_blocking=True)
+
+    @torch.no_grad()
+    def sample(self, tokens: torch.Tensor, max_new_tokens: int, temperature: float, seed: int = 0, eos=None):
+        """Plain (non-speculative) decoding that samples every token from softmax(logits / T) by
+        Gumbel-max inside the LM-head kernel; the token at position p uses the noise key
+        (seed, p), so a sample does not depend on batching or tensor parallelism."""
+        if temperature <= 0:
+            return self.greedy(tokens, max_new_tokens, eos)
+        seq = self.new_sequence()
+        try:
+            n = int(tokens.shape[0])
+            nxt, _ = self.prefill(seq, tokens, sampling=self.sampling_args(temperature, seed, [n]))
+            out = [int(nxt.item())]
+            while len(out) < max_new_tokens and (eos is None or out[-1] != eos):
+                p = seq.pos + 1                     # position of the token this step produces
+                pred, _ = self.verify([(seq, torch.tensor([out[-1]], device=self.device))],
+                                      sampling=self.sampling_args(temperature, seed, [p]))
+                self.commit(seq, 1)
+                out.append(int(pred[0].item()))
+            return out
+        finally:
+            self.release(seq)
+
     def greedy(self, tokens: torch.Tensor, max_new_tokens: int, eos=None):
         seq = self.new_sequence()
         try:

@@ -40,9 +40,19 @@ class TorchOps:
         y = y.view(T, -1, 2, block)
         return R.swiglu(y[:, :, 0], y[:, :, 1]).reshape(T, -1)
 
-    def lm_head_argmax(self, x, w, vocab_offset: int = 0):
-        """Returns (max value fp32 [T], global index int64 [T]); ties take the lowest index."""
+    def lm_head_argmax(self, x, w, vocab_offset: int = 0, sampling=None):
+        """Returns (max value fp32 [T], global index int64 [T]); ties take the lowest index.
+        ``sampling`` = (scale [T], key [T]): rows with scale > 0 take argmax(logits * scale +
+        Gumbel noise(key, global index)), a sample of softmax(logits * scale)."""
         logits = (x @ w.t()).float()
+        if sampling is not None:
+            sc, key = sampling
+            sc = sc.to(logits.device).float()
+            rows = sc > 0
+            if bool(rows.any()):
+                idx = torch.arange(vocab_offset, vocab_offset + logits.shape[1], device=logits.device)
+                g = R.gumbel_noise(key.to(logits.device), idx)
+                logits = torch.where(rows[:, None], logits * sc[:, None] + g, logits)
         v, i = logits.max(-1)
         return v, i + vocab_offset
 

@@ -141,14 +141,17 @@ class NativeOps(TorchOps):
         self.launches += 1
         return out
 
-    def lm_head_argmax(self, x, w, vocab_offset=0):
+    def lm_head_argmax(self, x, w, vocab_offset=0, sampling=None):
+        """Per row (max value, global index) of x @ w^T; rows with a positive scale in ``sampling``
+        = (scale [T] fp32, key [T] int64) take Gumbel-max samples of softmax(logits * scale)."""
         w = self.prepare_weight(w)
         x = x.contiguous()
         T = x.shape[0]
         val = torch.empty(T, dtype=torch.float32, device=x.device)
         idx = torch.empty(T, dtype=torch.int64, device=x.device)
+        sc, key = sampling if sampling is not None else (None, None)
         self.C.lm_head_argmax(x, w.t, w.N, val, idx, int(vocab_offset), self.amax_val, self.amax_idx, self.ws,
-                              self.counters, self.err)
+                              self.counters, self.err, sc, key)
         self.launches += 2
         return val, idx
 

@@ -200,3 +200,38 @@ def yarn_inv_freq(head_dim: int, theta: float, factor: float, beta_fast: float, 
     wl = theta ** (torch.arange(0, head_dim, 2, dtype=torch.float32) / head_dim)
     inv = (1 / (factor * wl)) * (1 - extrap) + (1 / wl) * extrap
     return inv, 1 + 0.1 * math.log(factor)
+
+
+# ---------------------------------------------------------------------------- sampling noise
+_M64 = (1 << 64) - 1
+
+
+def _i64(c: int) -> int:
+    """An unsigned 64-bit constant as the int64 with the same bits."""
+    return c - (1 << 64) if c >= 1 << 63 else c
+
+
+def _shr(z: torch.Tensor, k: int) -> torch.Tensor:
+    """Logical right shift of int64 bit patterns."""
+    return (z >> k) & ((1 << (64 - k)) - 1)
+
+
+def mix64(z: torch.Tensor) -> torch.Tensor:
+    """SplitMix64 finaliser (Steele, Lea, Flood, OOPSLA 2014) on int64 bit patterns (wrapping)."""
+    z = (z ^ _shr(z, 30)) * _i64(0xBF58476D1CE4E5B9)
+    z = (z ^ _shr(z, 27)) * _i64(0x94D049BB133111EB)
+    return z ^ _shr(z, 31)
+
+
+def gumbel_noise(key: torch.Tensor, index: torch.Tensor) -> torch.Tensor:
+    """Gumbel(0, 1) noise [rows, n] from per-row keys [rows] and global indices [n]: the same
+    counter-based construction as the device kernels (24-bit uniforms in (0, 1))."""
+    h = mix64(key.long()[:, None] ^ mix64(index.long()[None, :] + _i64(0x9E3779B97F4A7C15)))
+    u = (_shr(h, 40).double() + 0.5) / 16777216.0
+    return (-torch.log(-torch.log(u))).float()
+
+
+def sample_key(seed: int, position: int) -> int:
+    """Noise key of one sampled token: a mix of the request seed and the token position, as int64."""
+    z = torch.tensor([(seed * 0x9E3779B97F4A7C15 + position) & _M64], dtype=torch.uint64).view(torch.int64)
+    return int(mix64(z)[0])

@@ -30,6 +30,8 @@ class CompletionRequest(BaseModel):
     prompt: list[int] | str
     max_tokens: int = 16
     stop_token_ids: list[int] | None = None
+    temperature: float = 0.0          # 0: greedy with block speculation; > 0: sampled decoding
+    seed: int | None = None
 
 
 class ByteTokenizer:
@@ -55,19 +57,19 @@ class EngineLoop:
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
 
-    def submit(self, prompt, max_new_tokens, eos_ids=()):
+    def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0):
         done = threading.Event()
         box = {}
-        self.inbox.put((prompt, max_new_tokens, tuple(eos_ids), done, box))
+        self.inbox.put((prompt, max_new_tokens, tuple(eos_ids), done, box, float(temperature), int(seed)))
         return done, box
 
     def _run(self):
         while not self.stop_event.is_set():
             try:
                 while True:
-                    prompt, n, eos, done, box = self.inbox.get_nowait()
+                    prompt, n, eos, done, box, temp, seed = self.inbox.get_nowait()
                     try:
-                        req = self.engine.add_request(prompt, n, eos_ids=eos)
+                        req = self.engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed)
                         self.waiters[req.request_id] = (done, box, req)
                     except Exception as e:          # invalid request: answer at once
                         box["error"] = str(e)
@@ -121,7 +123,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         if output_budget_multiple and body.max_tokens % output_budget_multiple:
             raise HTTPException(400, f"max_tokens must be a multiple of {output_budget_multiple}")
         # the first output token comes from the prefill; max_tokens counts output tokens
-        done, box = loop.submit(ids, body.max_tokens, body.stop_token_ids or ())
+        seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
+        done, box = loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed)
         if not done.wait(timeout_s):
             raise HTTPException(504, "generation timed out")
         if "error" in box:

@@ -43,7 +43,8 @@ class ServingEngine:
         self.quarantined = 0
 
     # ------------------------------------------------------------------ API
-    def add_request(self, prompt, max_new_tokens: int, *, eos_ids=(), request_id=None, pinned=None) -> Request:
+    def add_request(self, prompt, max_new_tokens: int, *, eos_ids=(), request_id=None, pinned=None,
+                    temperature: float = 0.0, seed: int = 0) -> Request:
         prompt = [int(t) for t in prompt]
         if not prompt:
             raise ValueError("empty prompt")
@@ -52,7 +53,10 @@ class ServingEngine:
         if len(prompt) + max_new_tokens + self.verifier_rows > self.target.rt.max_context:
             raise ValueError("prompt + budget exceed max_context")
         rid = request_id or f"req-{next(self._ids)}"
-        req = Request(rid, prompt, max_new_tokens, tuple(eos_ids), self.clock(), pinned)
+        if temperature < 0:
+            raise ValueError("temperature must be >= 0")
+        req = Request(rid, prompt, max_new_tokens, tuple(eos_ids), self.clock(), pinned,
+                      temperature=float(temperature), seed=int(seed))
         self.requests[rid] = req
         self.sched.add(req)
         return req
@@ -132,7 +136,9 @@ class ServingEngine:
                 if nb < end:
                     end = nb
             toks = torch.tensor(req.prompt[req.prefilled:end], dtype=torch.long, device=tgt.device)
-            nxt, feats = tgt.prefill(req.seq, toks, taps=self.taps)
+            samp = (tgt.sampling_args(req.temperature, req.seed, [len(req.prompt)])
+                    if req.temperature > 0 and end == len(req.prompt) else None)
+            nxt, feats = tgt.prefill(req.seq, toks, taps=self.taps, sampling=samp)
             if dr is not None:
                 succ = (req.prompt[req.prefilled + 1:end + 1] if end < len(req.prompt)
                         else req.prompt[req.prefilled + 1:] + [int(nxt.item())])
@@ -177,7 +183,9 @@ class ServingEngine:
         live, finished = [], []
         for req in st.requests:
             try:
-                req.ticket = req.session.propose(req.request_id)
+                # sampled requests decode one token per step (speculation is greedy-only)
+                req.ticket = (req.session.propose(req.request_id, max_rows=1) if req.temperature > 0
+                              else req.session.propose(req.request_id))
                 live.append(req)
             except Exception as e:
                 self._quarantine(req, e)
@@ -185,8 +193,17 @@ class ServingEngine:
         if not live:
             return finished
         batch = [(r.seq, torch.tensor(r.ticket.tokens, dtype=torch.long, device=tgt.device)) for r in live]
+        sampling = None
+        if any(r.temperature > 0 for r in live):
+            scales, keys = [], []
+            for r in live:
+                n = len(r.ticket.tokens)
+                sc, ky = tgt.sampling_args(r.temperature, r.seed, range(r.seq.pos + 1, r.seq.pos + 1 + n))
+                scales.append(sc)
+                keys.append(ky)
+            sampling = (torch.cat(scales), torch.cat(keys))
         try:
-            pred, feats = tgt.verify(batch, taps=self.taps)
+            pred, feats = tgt.verify(batch, taps=self.taps, sampling=sampling)
             preds = pred.tolist()
         except Exception as e:          # a failed packed verify poisons every member's block
             for r in live:

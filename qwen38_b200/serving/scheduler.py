@@ -35,6 +35,8 @@ class Request:
     t_done: float | None = None
     decode_time: float = 0.0            # generation-loop time attributed to this request
     reused_prefix: int = 0
+    temperature: float = 0.0            # > 0: sampled, one token per step, no speculation
+    seed: int = 0                       # sampling noise seed
 
     @property
     def output(self):

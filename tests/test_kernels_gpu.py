@@ -199,6 +199,25 @@ def test_attention_prefill_kernel(nops, T, pos0, H, Hkv):
     nops.check()
 
 
+def test_lm_head_gumbel_sampling(nops):
+    """Gumbel-max sampling in the LM-head argmax epilogue: the same samples as the fp32 reference
+    with the same noise (up to bf16 logit rounding), greedy rows unchanged, vocab offsets respected."""
+    from qwen38_b200.ops import torch_ref as R
+    T, V, K = 16, 5000, 512
+    g = torch.Generator(device=DEV).manual_seed(21)
+    x = torch.randn(T, K, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(V, K, generator=g, device=DEV) * 0.1).to(torch.bfloat16)
+    scale = torch.tensor([0.0 if t % 4 == 0 else 1.0 / (0.5 + 0.1 * t) for t in range(T)], device=DEV)
+    key = torch.tensor([R.sample_key(99, 1000 + t) for t in range(T)], device=DEV)
+    _, idx = nops.lm_head_argmax(x, w, 7000, (scale, key))
+    _, ref = TorchOps().lm_head_argmax(x.float(), w.float(), 7000, (scale, key))
+    _, greedy = nops.lm_head_argmax(x, w, 7000)
+    nops.check()
+    assert int((idx == ref).sum()) >= T - 1
+    assert torch.equal(idx[::4], greedy[::4])
+    assert bool((idx >= 7000).all() and (idx < 7000 + V).all())
+
+
 def test_markov_select(nops):
     P, V, Rk = 5, 3000, 64
     g = torch.Generator(device=DEV).manual_seed(15)

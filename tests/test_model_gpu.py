@@ -75,3 +75,13 @@ def test_full_width_slice_runs(nops):
                                                           pinned=PinnedAcceptance(gold, seed=0, mean_accepted=6))
     assert res["tokens"] == gold
     nops.check()
+
+
+def test_native_sampled_decoding_is_reproducible(nops):
+    tgt = _tiny_target(nops)
+    toks = torch.randint(0, tgt.cfg.vocab_size, (64,), generator=torch.Generator().manual_seed(8)).cuda()
+    a = tgt.sample(toks, 10, temperature=0.8, seed=3)
+    b = tgt.sample(toks, 10, temperature=0.8, seed=3)
+    assert a == b and len(set(a)) > 1
+    assert tgt.sample(toks, 6, temperature=0.0) == tgt.greedy(toks, 6)
+    nops.check()

@@ -159,3 +159,19 @@ def test_factory_builds_engines_from_profiles():
         assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 6}).status_code == 400
         assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 8}).status_code == 200
     app.state.loop.close()
+
+
+def test_sampled_requests_next_to_greedy_ones(tiny):
+    """A sampled request (temperature > 0, one token per step) runs packed with greedy speculative
+    ones; its tokens equal the target's own sampled decoding for the same seed, and the greedy
+    request stays token-exact."""
+    tgt, dr = _setup(tiny, slots=2)
+    p1, p2 = _prompt(41, 48), _prompt(42, 40)
+    gold = greedy_reference(tgt, p1, 10)
+    ref = tgt.sample(torch.tensor(p2), 10, temperature=0.9, seed=5)
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    eng.add_request(p1, 10, request_id="g")
+    eng.add_request(p2, 10, request_id="s", temperature=0.9, seed=5)
+    done = {r.request_id: r for r in eng.run()}
+    assert done["g"].output == gold
+    assert done["s"].output == ref
