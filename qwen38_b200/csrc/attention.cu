@@ -5,11 +5,13 @@
 //              buffer, k / v rows written into the KV cache at each row's position (paged through
 //              a block table, or contiguous).  (graft/attention/tp.py:547-641 attn_decode_prep +
 //              paged_update_cache, :779-838 prefill fill.)
-// attn_decode: split-K flash decode for <= 32 query rows (verify / decode / drafter block).  Key
-//              chunks are fixed absolute ranges of CH keys, so a row's result depends only on its
-//              own position, never on how many rows ran with it.  GQA: all q heads of one KV head
-//              run in one CTA against one staged K/V tile.  Causal (target) or full (drafter).
-// attn_combine: merges the per-chunk (max, sum, o) partials in chunk order, applies
+// attn_decode: split-K flash decode for <= 32 query rows (verify / decode / drafter block).  The key
+//              axis is cut into fixed absolute groups of 128-key chunks (1, 4 or 8 chunks per
+//              group, growing with key position), one CTA per (KV head, group) with an online
+//              softmax over its 64-key tiles, so a row's result depends only on its own position,
+//              never on how many rows ran with it.  GQA: all q heads of one KV head run in one CTA
+//              against one staged K/V tile.  Causal (target) or full (drafter).
+// attn_combine: merges the per-group (max, sum, o) partials in group order, applies
 //              sigmoid(gate) (graft/attention/tp.py:121-237 gated output), writes bf16.
 // attn_prefill: causal flash attention of a prefill chunk over the paged cache (K-ATTN-PREFILL;
 //              the reference's chunked / paged SDPA, graft/attention/tp.py:476,645).  One CTA per
@@ -139,44 +141,97 @@ __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// One CTA per (KV head g, 128-key chunk s).  All query vectors of the GQA group (rep heads x T
-// rows) are processed against the chunk staged once in shared memory: warp w owns query rows
-// 16w..16w+15 of the current group of up to 128 rows.  S = Q K^T and O = P V on tensor cores
-// (m16n8k16, fp32 accumulate); the softmax of a row is computed inside the chunk only, and the
-// (max, sum, unnormalised O) partial is merged across chunks in chunk order by the combine kernel.
+// Key groups: the absolute key axis is cut into 128-key chunks and the chunks into groups by a
+// fixed partition - one chunk per group for the first 64 chunks (8,192 keys), four per group up
+// to chunk 512 (65,536 keys), eight beyond - so short contexts keep many CTAs while long ones
+// write few partials.  The partition depends on key positions only, never on how many rows run.
+constexpr int G_T0 = 64, G_T1 = 512;           // tier boundaries in chunks
+__host__ __device__ __forceinline__ int groups_for(int nchunks) {
+  if (nchunks <= G_T0) return nchunks;
+  if (nchunks <= G_T1) return G_T0 + (nchunks - G_T0 + 3) / 4;
+  return G_T0 + (G_T1 - G_T0) / 4 + (nchunks - G_T1 + 7) / 8;
+}
+__host__ __device__ __forceinline__ int group_first_chunk(int grp) {
+  if (grp < G_T0) return grp;
+  if (grp < G_T0 + (G_T1 - G_T0) / 4) return G_T0 + 4 * (grp - G_T0);
+  return G_T1 + 8 * (grp - G_T0 - (G_T1 - G_T0) / 4);
+}
+__host__ __device__ __forceinline__ int group_chunks(int grp) {
+  return grp < G_T0 ? 1 : (grp < G_T0 + (G_T1 - G_T0) / 4 ? 4 : 8);
+}
+
+constexpr int DK_T = 64;       // keys per staged tile inside a group
+
+// One CTA per (KV head g, key group).  All query vectors of the GQA group (rep heads x T rows) run
+// against 64-key K/V tiles staged once in shared memory (cp.async, double-buffered): warp w owns
+// query rows 16w..16w+15 of the current row group of up to 16 x warps rows.  S = Q K^T and O = P V
+// on tensor cores (m16n8k16, fp32 accumulate) with an online softmax over the group's tiles in key
+// order; the (max, sum, unnormalised O) partial of the group is merged across groups in group
+// order by the combine kernel.  A tile beyond a row's own position changes nothing: its
+// probabilities are exact zeros and its rescale factor is exactly 1, so row t gives the same bits
+// in a 16-row verify as in a 1-row decode.
 template <int D>
 __global__ void __launch_bounds__(256, 1)
 attn_decode_kernel(DecodeArgs a) {
   constexpr int DP = D + 8;                 // padded row: conflict-free ldmatrix
-  constexpr int NT_K = CH / 8;              // key n-tiles per chunk
+  constexpr int NT_K = DK_T / 8;            // key n-tiles per tile
   constexpr int NT_D = D / 8;               // output n-tiles
   pdl_wait();
   pdl_trigger();
-  const int g = blockIdx.x, s = blockIdx.y;
+  const int g = blockIdx.x, grp = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int nwarps = blockDim.x >> 5;
   const int rep = a.nq / a.nkv;
   const int nqv = rep * a.T;
   const int n_keys = a.qpos[a.T - 1] + 1;
-  const int k0 = s * CH;
-  if (k0 >= n_keys) return;
-  const int k1 = min(n_keys, k0 + CH);
+  const int c0 = group_first_chunk(grp);
+  const int k_begin = c0 * CH;
+  if (k_begin >= n_keys) return;
+  const int k_end = min(n_keys, (c0 + group_chunks(grp)) * CH);
+  const int ntiles = (k_end - k_begin + DK_T - 1) / DK_T;
 
   extern __shared__ __align__(16) uint8_t smem[];
-  __nv_bfloat16* Ks = reinterpret_cast<__nv_bfloat16*>(smem);
-  __nv_bfloat16* Vs = Ks + CH * DP;
-  __nv_bfloat16* Qs = Vs + CH * DP;          // [MAXW*16][DP]
+  __nv_bfloat16* Qs = reinterpret_cast<__nv_bfloat16*>(smem);                 // [nwarps*16][DP]
+  __nv_bfloat16* KV = Qs + nwarps * 16 * DP;                                  // [2 bufs][K, V][DK_T][DP]
+  auto Ks = [&](int b) { return KV + (size_t)(2 * b) * DK_T * DP; };
+  auto Vs = [&](int b) { return KV + (size_t)(2 * b + 1) * DK_T * DP; };
+  __shared__ long long kv_row[2][DK_T];
 
-  // ---- stage the chunk with asynchronous copies: group 0 = K (+ the first query group), group 1 =
-  // V, so Q K^T starts while V is still in flight.  Zeros past the visible keys.
-  const int nwarps = blockDim.x >> 5;
-  auto kv_base = [&](int kp) -> size_t {
-    if (a.block_table) {
-      const int blk = a.block_table[kp / a.block_size];
-      return ((size_t)blk * a.block_size + (kp % a.block_size)) * a.nkv + g;
+  auto load_tile = [&](int kt, int b) {
+    const int t0 = k_begin + kt * DK_T;
+    // one block-table lookup per key, not per 16-byte copy
+    for (int j = threadIdx.x; j < DK_T; j += blockDim.x) {
+      const int kp = t0 + j;
+      long long base = -1;
+      if (kp < k_end) {
+        if (a.block_table) {
+          const int blk = a.block_table[kp / a.block_size];
+          base = (((long long)blk * a.block_size + (kp % a.block_size)) * a.nkv + g) * D;
+        } else {
+          base = ((long long)kp * a.nkv + g) * D;
+        }
+      }
+      kv_row[b][j] = base;
     }
-    return (size_t)kp * a.nkv + g;
+    __syncthreads();
+    for (int idx = threadIdx.x; idx < DK_T * (D / 8); idx += blockDim.x) {
+      const int j = idx / (D / 8), ch = idx % (D / 8);
+      uint4* dk = reinterpret_cast<uint4*>(Ks(b) + j * DP) + ch;
+      uint4* dv = reinterpret_cast<uint4*>(Vs(b) + j * DP) + ch;
+      const long long base = kv_row[b][j];
+      if (base >= 0) {
+        cp_async16(dk, reinterpret_cast<const uint4*>(a.kcache + base) + ch);
+        cp_async16(dv, reinterpret_cast<const uint4*>(a.vcache + base) + ch);
+      } else {
+        *dk = make_uint4(0, 0, 0, 0);
+        *dv = make_uint4(0, 0, 0, 0);
+      }
+    }
   };
-  auto stage_q = [&](int qb) {
+
+  for (int qb = 0; qb < nqv; qb += nwarps * 16) {
+    __syncthreads();                           // previous row group done with Q and the tiles
+    // ---- this row group's query vectors (zeros for padding rows)
     for (int idx = threadIdx.x; idx < nwarps * 16 * (D / 8); idx += blockDim.x) {
       const int qi = idx / (D / 8), ch = idx % (D / 8);
       const int gq = qb + qi;
@@ -188,131 +243,113 @@ attn_decode_kernel(DecodeArgs a) {
         *dst = make_uint4(0, 0, 0, 0);
       }
     }
-  };
-  // cache row offsets of the chunk's keys once (one block-table lookup per key, not per 16 B)
-  __shared__ long long kv_row[CH];
-  for (int j = threadIdx.x; j < CH; j += blockDim.x) kv_row[j] = k0 + j < k1 ? (long long)kv_base(k0 + j) * D : -1;
-  __syncthreads();
-  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
-    const int j = idx / (D / 8), ch = idx % (D / 8);
-    uint4* dst = reinterpret_cast<uint4*>(Ks + j * DP) + ch;
-    if (kv_row[j] >= 0) cp_async16(dst, reinterpret_cast<const uint4*>(a.kcache + kv_row[j]) + ch);
-    else *dst = make_uint4(0, 0, 0, 0);
-  }
-  stage_q(0);
-  cp_async_commit();
-  for (int idx = threadIdx.x; idx < CH * (D / 8); idx += blockDim.x) {
-    const int j = idx / (D / 8), ch = idx % (D / 8);
-    uint4* dst = reinterpret_cast<uint4*>(Vs + j * DP) + ch;
-    if (kv_row[j] >= 0) cp_async16(dst, reinterpret_cast<const uint4*>(a.vcache + kv_row[j]) + ch);
-    else *dst = make_uint4(0, 0, 0, 0);
-  }
-  cp_async_commit();
-
-  for (int qb = 0; qb < nqv; qb += nwarps * 16) {
-    if (qb > 0) {                      // later query groups (more than nwarps*16 rows)
-      __syncthreads();
-      stage_q(qb);
+    load_tile(0, 0);
+    cp_async_commit();
+    if (ntiles > 1) {
+      load_tile(1, 1);
       cp_async_commit();
-      cp_async_wait<0>();
-    } else {
-      cp_async_wait<1>();              // K and the first query group have landed
     }
-    __syncthreads();
     const int row0 = qb + warp * 16;
-    if (row0 >= nqv) {                 // idle warp: its V copies still count for the others
-      if (qb == 0) {
-        cp_async_wait<0>();
-        asm volatile("bar.arrive 1, %0;" ::"r"((int)blockDim.x) : "memory");
-      }
-      continue;
-    }
-
-    // ---- S = Q K^T  (16 rows x CH keys per warp)
-    float S[NT_K][4];
-#pragma unroll
-    for (int n = 0; n < NT_K; ++n) S[n][0] = S[n][1] = S[n][2] = S[n][3] = 0.f;
-    const uint32_t qbase = smem_u32(Qs + (warp * 16) * DP);
-    const uint32_t kbase = smem_u32(Ks);
-#pragma unroll
-    for (int kk = 0; kk < D / 16; ++kk) {
-      uint32_t a0, a1, a2, a3;
-      // A fragment rows 0-15, cols kk*16 .. +15
-      ldsm_x4(qbase + (uint32_t)(((lane & 15) * DP + kk * 16 + (lane >> 4) * 8) * 2), a0, a1, a2, a3);
-#pragma unroll
-      for (int n = 0; n < NT_K; ++n) {
-        uint32_t b0, b1;
-        // B fragment (col-major 16x8): key rows n*8..n*8+7, d cols kk*16 .. +15
-        ldsm_x2(kbase + (uint32_t)(((n * 8 + (lane & 7)) * DP + kk * 16 + ((lane >> 3) & 1) * 8) * 2), b0, b1);
-        mma_bf16_16816(S[n], a0, a1, a2, a3, b0, b1);
-      }
-    }
-    // ---- mask + row max / sum (rows r_lo = lane/4, r_hi = lane/4 + 8)
+    const bool active = row0 < nqv;
     const int r_lo = row0 + (lane >> 2), r_hi = r_lo + 8;
-    const int p_lo = r_lo < nqv ? a.qpos[r_lo % a.T] : -1;
-    const int p_hi = r_hi < nqv ? a.qpos[r_hi % a.T] : -1;
-    float m_lo = -INFINITY, m_hi = -INFINITY;
+    const int p_lo = (active && r_lo < nqv) ? (a.causal ? a.qpos[r_lo % a.T] : n_keys - 1) : -1;
+    const int p_hi = (active && r_hi < nqv) ? (a.causal ? a.qpos[r_hi % a.T] : n_keys - 1) : -1;
+    float O[NT_D][4];
 #pragma unroll
-    for (int n = 0; n < NT_K; ++n) {
+    for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;
+    float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+    const uint32_t qbase = smem_u32(Qs + (warp * 16) * DP);
+
+    for (int kt = 0; kt < ntiles; ++kt) {
+      const int b = kt & 1;
+      if (kt + 1 < ntiles) cp_async_wait<1>();
+      else cp_async_wait<0>();
+      __syncthreads();
+      if (active) {
+        const int t0 = k_begin + kt * DK_T;
+        float S[NT_K][4];
 #pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        const int kp = k0 + n * 8 + (lane & 3) * 2 + e;
-        const bool ok_lo = kp < k1 && (!a.causal || kp <= p_lo);
-        const bool ok_hi = kp < k1 && (!a.causal || kp <= p_hi);
-        S[n][e] = ok_lo ? S[n][e] * a.scale : -INFINITY;
-        S[n][2 + e] = ok_hi ? S[n][2 + e] * a.scale : -INFINITY;
-        m_lo = fmaxf(m_lo, S[n][e]);
-        m_hi = fmaxf(m_hi, S[n][2 + e]);
+        for (int n = 0; n < NT_K; ++n) S[n][0] = S[n][1] = S[n][2] = S[n][3] = 0.f;
+        const uint32_t kbase = smem_u32(Ks(b));
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          uint32_t a0, a1, a2, a3;
+          ldsm_x4(qbase + (uint32_t)(((lane & 15) * DP + kk * 16 + (lane >> 4) * 8) * 2), a0, a1, a2, a3);
+#pragma unroll
+          for (int n = 0; n < NT_K; ++n) {
+            uint32_t b0, b1;
+            ldsm_x2(kbase + (uint32_t)(((n * 8 + (lane & 7)) * DP + kk * 16 + ((lane >> 3) & 1) * 8) * 2), b0, b1);
+            mma_bf16_16816(S[n], a0, a1, a2, a3, b0, b1);
+          }
+        }
+        float tm_lo = -INFINITY, tm_hi = -INFINITY;
+#pragma unroll
+        for (int n = 0; n < NT_K; ++n) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int kp = t0 + n * 8 + (lane & 3) * 2 + e;
+            S[n][e] = (kp < k_end && kp <= p_lo) ? S[n][e] * a.scale : -INFINITY;
+            S[n][2 + e] = (kp < k_end && kp <= p_hi) ? S[n][2 + e] * a.scale : -INFINITY;
+            tm_lo = fmaxf(tm_lo, S[n][e]);
+            tm_hi = fmaxf(tm_hi, S[n][2 + e]);
+          }
+        }
+        tm_lo = fmaxf(tm_lo, __shfl_xor_sync(0xffffffffu, tm_lo, 1));
+        tm_lo = fmaxf(tm_lo, __shfl_xor_sync(0xffffffffu, tm_lo, 2));
+        tm_hi = fmaxf(tm_hi, __shfl_xor_sync(0xffffffffu, tm_hi, 1));
+        tm_hi = fmaxf(tm_hi, __shfl_xor_sync(0xffffffffu, tm_hi, 2));
+        const float mn_lo = fmaxf(m_lo, tm_lo), mn_hi = fmaxf(m_hi, tm_hi);
+        const float mz_lo = mn_lo == -INFINITY ? 0.f : mn_lo;
+        const float mz_hi = mn_hi == -INFINITY ? 0.f : mn_hi;
+        const float c_lo = __expf(m_lo - mz_lo), c_hi = __expf(m_hi - mz_hi);   // 0 before any key, 1 if unchanged
+        m_lo = mn_lo;
+        m_hi = mn_hi;
+        l_lo *= c_lo;
+        l_hi *= c_hi;
+#pragma unroll
+        for (int n = 0; n < NT_D; ++n) {
+          O[n][0] *= c_lo; O[n][1] *= c_lo;
+          O[n][2] *= c_hi; O[n][3] *= c_hi;
+        }
+#pragma unroll
+        for (int n = 0; n < NT_K; ++n) {
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            S[n][e] = __expf(S[n][e] - mz_lo);
+            S[n][2 + e] = __expf(S[n][2 + e] - mz_hi);
+            l_lo += S[n][e];
+            l_hi += S[n][2 + e];
+          }
+        }
+        const uint32_t vbase = smem_u32(Vs(b));
+#pragma unroll
+        for (int j = 0; j < DK_T / 16; ++j) {
+          const uint32_t a0 = pack_bf16(S[2 * j][0], S[2 * j][1]);
+          const uint32_t a1 = pack_bf16(S[2 * j][2], S[2 * j][3]);
+          const uint32_t a2 = pack_bf16(S[2 * j + 1][0], S[2 * j + 1][1]);
+          const uint32_t a3 = pack_bf16(S[2 * j + 1][2], S[2 * j + 1][3]);
+#pragma unroll
+          for (int n = 0; n < NT_D; ++n) {
+            uint32_t b0, b1;
+            ldsm_x2_t(vbase + (uint32_t)(((j * 16 + (lane & 15)) * DP + n * 8) * 2), b0, b1);
+            mma_bf16_16816(O[n], a0, a1, a2, a3, b0, b1);
+          }
+        }
+      }
+      __syncthreads();                         // every warp is done with buffer b
+      if (kt + 2 < ntiles) {
+        load_tile(kt + 2, b);
+        cp_async_commit();
       }
     }
-    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, 1));
-    m_lo = fmaxf(m_lo, __shfl_xor_sync(0xffffffffu, m_lo, 2));
-    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, 1));
-    m_hi = fmaxf(m_hi, __shfl_xor_sync(0xffffffffu, m_hi, 2));
-    const float mz_lo = m_lo == -INFINITY ? 0.f : m_lo;
-    const float mz_hi = m_hi == -INFINITY ? 0.f : m_hi;
-    float l_lo = 0.f, l_hi = 0.f;
-#pragma unroll
-    for (int n = 0; n < NT_K; ++n) {
-#pragma unroll
-      for (int e = 0; e < 2; ++e) {
-        S[n][e] = __expf(S[n][e] - mz_lo);
-        S[n][2 + e] = __expf(S[n][2 + e] - mz_hi);
-        l_lo += S[n][e];
-        l_hi += S[n][2 + e];
-      }
-    }
+    if (!active) continue;
+    // ---- the group's partial: row sums over the quad, then (m, l) and unnormalised O
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
     l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
     l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-
-    // ---- O = P V  (P re-used from the S accumulators as bf16 A fragments)
-    if (qb == 0) {                     // V has landed (every thread's copies: named barrier 1)
-      cp_async_wait<0>();
-      asm volatile("bar.sync 1, %0;" ::"r"((int)blockDim.x) : "memory");
-    }
-    float O[NT_D][4];
-#pragma unroll
-    for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;
-    const uint32_t vbase = smem_u32(Vs);
-#pragma unroll
-    for (int j = 0; j < CH / 16; ++j) {
-      const uint32_t a0 = pack_bf16(S[2 * j][0], S[2 * j][1]);
-      const uint32_t a1 = pack_bf16(S[2 * j][2], S[2 * j][3]);
-      const uint32_t a2 = pack_bf16(S[2 * j + 1][0], S[2 * j + 1][1]);
-      const uint32_t a3 = pack_bf16(S[2 * j + 1][2], S[2 * j + 1][3]);
-#pragma unroll
-      for (int n = 0; n < NT_D; ++n) {
-        uint32_t b0, b1;
-        // B (16 keys x 8 d) from row-major V via transposed ldmatrix
-        ldsm_x2_t(vbase + (uint32_t)(((j * 16 + (lane & 15)) * DP + n * 8) * 2), b0, b1);
-        mma_bf16_16816(O[n], a0, a1, a2, a3, b0, b1);
-      }
-    }
-    // ---- write partials
-    const size_t plo = ((size_t)g * a.max_splits + s) * nqv + r_lo;
-    const size_t phi = ((size_t)g * a.max_splits + s) * nqv + r_hi;
+    const size_t plo = ((size_t)g * a.max_splits + grp) * nqv + r_lo;
+    const size_t phi = ((size_t)g * a.max_splits + grp) * nqv + r_hi;
 #pragma unroll
     for (int n = 0; n < NT_D; ++n) {
       const int d = n * 8 + (lane & 3) * 2;
@@ -337,7 +374,7 @@ __global__ void attn_combine_kernel(DecodeArgs a, const __nv_bfloat16* gate, lon
   const int nqv = rep * a.T;
   const int qv = (hq % rep) * a.T + t;
   const int n_keys = a.causal ? a.qpos[t] + 1 : a.qpos[a.T - 1] + 1;
-  const int ns = (n_keys + CH - 1) / CH;
+  const int ns = groups_for((n_keys + CH - 1) / CH);        // key groups this row sees
   // 1. every split's (max, sum) into shared memory in parallel, then the global max and the
   //    per-split weights exp(m_s - M) once (fixed split order everywhere)
   extern __shared__ float cm[];                 // [2 * ns]: weight, weighted sum
@@ -652,8 +689,8 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
   a.part_ml = part_ml.data_ptr<float>();
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const int warps = std::max(4, std::min(q38::MAXW, (nqv + 15) / 16));   // >= 4 warps to stage K/V
-  const size_t smem = (size_t)(2 * q38::CH + warps * 16) * (D + 8) * 2;
-  dim3 grid(nkv, a.max_splits);
+  const size_t smem = (size_t)(4 * q38::DK_T + warps * 16) * (D + 8) * 2;
+  dim3 grid(nkv, q38::groups_for(a.max_splits));
 #define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
     auto k = q38::attn_decode_kernel<DD>;                                                                   \

@@ -184,6 +184,24 @@ def test_attention_prep_and_decode(nops, T, pos0):
     nops.check()
 
 
+@pytest.mark.parametrize("T,pos0", [(16, 8180), (16, 9000), (5, 65530), (16, 70000)])
+def test_attention_decode_long_context_groups(nops, T, pos0):
+    """Across the key-group tiers (1, 4 and 8 chunks per CTA): numerics against the fp32 reference
+    and the same bits for a row alone as inside the block."""
+    proj, qn, kn, inv, rd, dims, pos, kc, vc, bt, bs = _attn_case(T, pos0)
+    kc2, vc2 = kc.clone(), vc.clone()
+    tops = TorchOps()
+    q_ref, gate = tops.attn_prep(proj.float(), qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc2, vc2, bt, bs)
+    q, gate_n = nops.attn_prep(proj, qn, kn, inv, 1.0, rd, dims, 1e-6, pos, kc, vc, bt, bs)
+    ref = tops.attn_decode(q_ref.float(), gate.float(), kc2.float(), vc2.float(), bt, pos, bs, torch.float32)
+    out = nops.attn_decode(q, gate_n, kc, vc, bt, pos, bs, torch.bfloat16)
+    assert _rel(out, ref) < 2e-2
+    for t in (0, T - 1):
+        one = nops.attn_decode(q[t:t + 1], gate_n[t:t + 1], kc, vc, bt, pos[t:t + 1], bs, torch.bfloat16)
+        assert torch.equal(one[0], out[t])
+    nops.check()
+
+
 @pytest.mark.parametrize("T,pos0,H,Hkv", [(40, 0, 6, 1), (300, 1000, 6, 1), (2048, 2048, 6, 1), (77, 5, 3, 1),
                                            (64, 64, 4, 2)])
 def test_attention_prefill_kernel(nops, T, pos0, H, Hkv):
