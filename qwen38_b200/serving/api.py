@@ -7,7 +7,10 @@ their completion, so requests arriving concurrently are continuously batched int
 
 Endpoints: ``POST /v1/completions`` (``prompt`` as a list of token ids, or a string encoded with
 the byte-level fallback tokenizer below - checkpoints' own tokenizers need network access to
-fetch), ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).
+fetch), ``POST /v1/chat/completions`` (``messages`` rendered with a plain role template),
+``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  With ``"stream": true``
+both generation endpoints answer with server-sent events, one event per engine step that emitted
+tokens (a speculative block commits several tokens at once), then ``data: [DONE]``.
 
 Run:  python -m qwen38_b200.serving.api --profile single-stream-4k --set serving.port=8000
       python -m qwen38_b200.serving.api --profile tiny-cpu            (CPU, tiny shape)
@@ -32,6 +35,27 @@ class CompletionRequest(BaseModel):
     stop_token_ids: list[int] | None = None
     temperature: float = 0.0          # 0: greedy with block speculation; > 0: sampled decoding
     seed: int | None = None
+    stream: bool = False
+
+
+class ChatMessage(BaseModel):
+    role: str
+    content: str
+
+
+class ChatRequest(BaseModel):
+    model: str | None = None
+    messages: list[ChatMessage]
+    max_tokens: int = 16
+    stop_token_ids: list[int] | None = None
+    temperature: float = 0.0
+    seed: int | None = None
+    stream: bool = False
+
+
+def render_chat(messages) -> str:
+    """Plain role template (the checkpoint's own chat template needs its tokenizer files)."""
+    return "".join(f"<|{m.role}|>\n{m.content}\n" for m in messages) + "<|assistant|>\n"
 
 
 class ByteTokenizer:
@@ -57,9 +81,11 @@ class EngineLoop:
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
 
-    def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0):
+    def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0, stream=False):
+        """Queue a request.  Returns (done event, result box); with ``stream`` the box's "stream"
+        queue receives each step's newly emitted token ids, then None when the request ends."""
         done = threading.Event()
-        box = {}
+        box = {"stream": queue.Queue()} if stream else {}
         self.inbox.put((prompt, max_new_tokens, tuple(eos_ids), done, box, float(temperature), int(seed)))
         return done, box
 
@@ -70,21 +96,33 @@ class EngineLoop:
                     prompt, n, eos, done, box, temp, seed = self.inbox.get_nowait()
                     try:
                         req = self.engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed)
+                        box["sent"] = 0
                         self.waiters[req.request_id] = (done, box, req)
                     except Exception as e:          # invalid request: answer at once
                         box["error"] = str(e)
+                        if "stream" in box:
+                            box["stream"].put(None)
                         done.set()
             except queue.Empty:
                 pass
             if not self.engine.has_work():
                 time.sleep(self.idle_sleep)
                 continue
-            for req in self.engine.step():
+            finished = self.engine.step()
+            for done, box, req in list(self.waiters.values()):     # stream what each step emitted
+                if "stream" in box:
+                    out = req.output
+                    if len(out) > box["sent"]:
+                        box["stream"].put(out[box["sent"]:])
+                        box["sent"] = len(out)
+            for req in finished:
                 entry = self.waiters.pop(req.request_id, None)
                 if entry is None:
                     continue
                 done, box, _ = entry
                 box["request"] = req
+                if "stream" in box:
+                    box["stream"].put(None)
                 if req.state == FINISHED:
                     self.completed += 1
                     self.tokens += max(0, len(req.output) - 1)
@@ -99,8 +137,10 @@ class EngineLoop:
 
 def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0,
               output_budget_multiple: int = 0):
+    import json
+
     from fastapi import FastAPI, HTTPException
-    from fastapi.responses import PlainTextResponse
+    from fastapi.responses import PlainTextResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
     loop = EngineLoop(engine)
@@ -115,16 +155,16 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "qwen38_b200"}]}
 
-    @app.post("/v1/completions")
-    def completions(body: CompletionRequest):
-        ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
+    def _start(ids, body):
         if not ids:
             raise HTTPException(400, "empty prompt")
         if output_budget_multiple and body.max_tokens % output_budget_multiple:
             raise HTTPException(400, f"max_tokens must be a multiple of {output_budget_multiple}")
         # the first output token comes from the prefill; max_tokens counts output tokens
         seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
-        done, box = loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed)
+        return loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed, body.stream)
+
+    def _finished(done, box):
         if not done.wait(timeout_s):
             raise HTTPException(504, "generation timed out")
         if "error" in box:
@@ -132,12 +172,67 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         req = box["request"]
         if req.state != FINISHED:
             raise HTTPException(500, f"request aborted: {req.error}")
-        out = req.output
-        finish = "stop" if out and out[-1] in (body.stop_token_ids or ()) else "length"
+        return req.output
+
+    def _finish_reason(out, body):
+        return "stop" if out and out[-1] in (body.stop_token_ids or ()) else "length"
+
+    def _events(box, body, chunk):
+        """Server-sent events: one per engine step that emitted tokens, then [DONE]."""
+        emitted = []
+        while True:
+            try:
+                new = box["stream"].get(timeout=timeout_s)
+            except queue.Empty:
+                yield "data: " + json.dumps({"error": "generation timed out"}) + "\n\n"
+                break
+            if new is None:
+                if "error" in box or box.get("request") is None or box["request"].state != FINISHED:
+                    reason = box.get("error") or getattr(box.get("request"), "error", "aborted")
+                    yield "data: " + json.dumps({"error": str(reason)}) + "\n\n"
+                else:
+                    yield "data: " + json.dumps(chunk([], _finish_reason(emitted, body))) + "\n\n"
+                break
+            emitted += new
+            yield "data: " + json.dumps(chunk(new, None)) + "\n\n"
+        yield "data: [DONE]\n\n"
+
+    @app.post("/v1/completions")
+    def completions(body: CompletionRequest):
+        ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
+        done, box = _start(ids, body)
+        cid, created, model = "cmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
+        if body.stream:
+            def chunk(new, reason):
+                return {"id": cid, "object": "text_completion", "created": created, "model": model,
+                        "choices": [{"index": 0, "text": tok.decode(new), "token_ids": new, "finish_reason": reason}]}
+            return StreamingResponse(_events(box, body, chunk), media_type="text/event-stream")
+        out = _finished(done, box)
         return {
-            "id": "cmpl-" + uuid.uuid4().hex[:16], "object": "text_completion", "created": int(time.time()),
-            "model": body.model or model_name,
-            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": finish}],
+            "id": cid, "object": "text_completion", "created": created, "model": model,
+            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": _finish_reason(out, body)}],
+            "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                      "total_tokens": len(ids) + len(out)},
+        }
+
+    @app.post("/v1/chat/completions")
+    def chat(body: ChatRequest):
+        if not body.messages:
+            raise HTTPException(400, "no messages")
+        ids = tok.encode(render_chat(body.messages))
+        done, box = _start(ids, body)
+        cid, created, model = "chatcmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
+        if body.stream:
+            def chunk(new, reason):
+                delta = {"role": "assistant", "content": tok.decode(new)} if new else {}
+                return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model,
+                        "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
+            return StreamingResponse(_events(box, body, chunk), media_type="text/event-stream")
+        out = _finished(done, box)
+        return {
+            "id": cid, "object": "chat.completion", "created": created, "model": model,
+            "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
+                         "token_ids": out, "finish_reason": _finish_reason(out, body)}],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                       "total_tokens": len(ids) + len(out)},
         }

@@ -175,3 +175,41 @@ def test_sampled_requests_next_to_greedy_ones(tiny):
     done = {r.request_id: r for r in eng.run()}
     assert done["g"].output == gold
     assert done["s"].output == ref
+
+
+def test_streaming_and_chat_endpoints(tiny):
+    """Server-sent events deliver each step's tokens (their concatenation is the whole greedy
+    output) and end with [DONE]; chat completions render messages and answer in both modes."""
+    import json as _json
+
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.serving.api import ByteTokenizer, build_app, render_chat
+    tgt, dr = _setup(tiny, slots=2)
+    p1 = _prompt(51, 40)
+    gold = greedy_reference(tgt, p1, 12)
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    app = build_app(eng, model_name="tiny")
+    with TestClient(app) as client:
+        r = client.post("/v1/completions", json={"prompt": p1, "max_tokens": 12, "stream": True})
+        assert r.status_code == 200 and r.headers["content-type"].startswith("text/event-stream")
+        events = [ln[len("data: "):] for ln in r.text.splitlines() if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]"
+        chunks = [_json.loads(e) for e in events[:-1]]
+        toks = [t for c in chunks for t in c["choices"][0]["token_ids"]]
+        assert toks == gold
+        assert chunks[-1]["choices"][0]["finish_reason"] == "length"
+        assert len(chunks) > 2                              # several steps, several events
+        msgs = [{"role": "user", "content": "hi"}]
+        r = client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 6})
+        assert r.status_code == 200
+        body = r.json()
+        ids = ByteTokenizer().encode(render_chat([type("M", (), m) for m in msgs]))
+        assert body["choices"][0]["token_ids"] == greedy_reference(tgt, ids, 6)
+        assert body["usage"]["prompt_tokens"] == len(ids)
+        r = client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 6, "stream": True})
+        events = [ln[len("data: "):] for ln in r.text.splitlines() if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]" and _json.loads(events[0])["object"] == "chat.completion.chunk"
+        bad = client.post("/v1/completions", json={"prompt": [999999], "max_tokens": 4, "stream": True})
+        assert "error" in bad.text
+    app.state.loop.close()
