@@ -44,6 +44,7 @@ def parse():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
+    ap.add_argument("--prefill-chunk", type=int, default=2048, help="prefill chunk rows (multiple of 64)")
     ap.add_argument("--comm", default="fused", choices=["fused", "peer", "nccl"],
                     help="TP collectives: all-reduce pushed by the out-projection GEMMs and completed by the "
                          "next RMSNorm (default), separate peer-memory all-reduce kernels, or NCCL")
@@ -168,7 +169,7 @@ def main():
         topo = check_topology(world, comm=args.comm if args.ops == "native" else "nccl")
     comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm != "nccl" and args.ops == "native"),
                      fused=(args.comm == "fused"))
-    rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=2048,
+    rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=args.prefill_chunk,
                        use_cuda_graphs=not args.no_graphs)
     if args.ops == "native":
         from qwen38_b200.ops.native import NativeOps
@@ -245,7 +246,7 @@ def main():
             "pp_tok_s": round(pp, 2), "pp_vs_baseline": round(pp / BASELINE_PP, 3),
             "config": {"model": f"{args.model}-hybrid-27B-class" if args.model == "full" else "tiny",
                        "layers": cfg.num_hidden_layers, "global_batch": 1, "seq_len": args.ctx,
-                       "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows,
+                       "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows, "prefill_chunk": args.prefill_chunk,
                        "drafter_layers": dcfg.num_hidden_layers, "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
