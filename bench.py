@@ -44,7 +44,8 @@ def parse():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
-    ap.add_argument("--prefill-chunk", type=int, default=2048, help="prefill chunk rows (multiple of 64)")
+    ap.add_argument("--prefill-chunk", type=int, default=4096,
+                    help="prefill chunk rows (multiple of 64); 4096 prefills the CTX 4,096 prompt in one chunk")
     ap.add_argument("--comm", default="fused", choices=["fused", "peer", "nccl"],
                     help="TP collectives: all-reduce pushed by the out-projection GEMMs and completed by the "
                          "next RMSNorm (default), separate peer-memory all-reduce kernels, or NCCL")
