@@ -165,14 +165,18 @@ class BlockDrafter:
         n = feats.shape[0]
         if pos + n > self.max_context:
             raise ValueError("drafter history capacity exceeded")
-        ctx = self._context_rows(feats)
         positions = torch.arange(pos, pos + n, device=self.device, dtype=torch.int32)
+        self.append_device(feats, positions, slot)
+        self.positions[slot] = pos + n
+
+    def append_device(self, feats: torch.Tensor, positions: torch.Tensor, slot: int):
+        """The device half of ``append`` (capturable: positions come from a device tensor)."""
+        ctx = self._context_rows(feats)
         hl, kvl, Dh = self.heads
         for l, L in enumerate(self.layers):
             kv = self.ops.linear(ctx, L["w_kv"])
             self.ops.kv_append(kv, L["kn"], self.inv_freq, self.rope_scale, Dh, kvl, Dh, self.eps, positions,
                                self.kctx_all[slot, l], self.vctx_all[slot, l])
-        self.positions[slot] = pos + n
 
     # -------------------------------------------------------------------------------- propose
     @torch.no_grad()

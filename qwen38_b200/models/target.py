@@ -502,12 +502,17 @@ class HybridTarget:
         o0, rows = seq.verify_rows
         if not 0 <= n <= rows:
             raise ValueError(f"commit of {n} rows outside the verified block of {rows}")
-        if self.cfg.linear_layers and n > 0:
-            dims = self.layers[self.cfg.linear_layers[0]]["dims"]
-            self.ops.gdn_commit_layers(self.gdn_stash[:, o0:o0 + rows], n, self.conv[seq.slot], self.rec[seq.slot],
-                                       self.gdn_conv_w, self.gdn_A_log, self.gdn_dt_bias, dims)
+        self.commit_device(seq.slot, o0, rows, n)
         seq.pos += n
         seq.verify_rows = None
+
+    def commit_device(self, slot: int, o0: int, rows: int, n: int):
+        """The device half of ``commit``: replay the first ``n`` kept GDN rows of the verify block
+        at stash rows o0..o0+rows into ``slot``'s state and conv windows (capturable)."""
+        if self.cfg.linear_layers and n > 0:
+            dims = self.layers[self.cfg.linear_layers[0]]["dims"]
+            self.ops.gdn_commit_layers(self.gdn_stash[:, o0:o0 + rows], n, self.conv[slot], self.rec[slot],
+                                       self.gdn_conv_w, self.gdn_A_log, self.gdn_dt_bias, dims)
 
     def abort(self, seq: SeqState):
         """Drop the pending verify: nothing was committed, K/V rows past the frontier are stale."""
