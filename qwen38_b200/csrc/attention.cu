@@ -41,6 +41,9 @@ struct PrepArgs {
   __nv_bfloat16* vcache;
   const int* block_table;      // nullptr: contiguous
   int block_size;
+  long long table_len;         // paged: block-table entries; contiguous: cache rows
+  long long cache_blocks;      // paged: blocks in the cache
+  int* err;                    // bad positions are recorded here and their rows skipped
 };
 
 __global__ void attn_prep_kernel(PrepArgs a) {
@@ -86,11 +89,25 @@ __global__ void attn_prep_kernel(PrepArgs a) {
   if (is_q) {
     a.q_out[((size_t)t * a.nq + head) * D + c] = __float2bfloat16(out);
   } else {
+    // a position outside the cache (a corrupted position or block table) is recorded and its
+    // row skipped instead of written out of bounds
     size_t base;
     if (a.block_table) {
+      if (p < 0 || (long long)(p / a.block_size) >= a.table_len) {
+        if (c == 0) record_error(a.err, kErrShape);
+        return;
+      }
       const int blk = a.block_table[p / a.block_size];
+      if (blk < 0 || blk >= a.cache_blocks) {
+        if (c == 0) record_error(a.err, kErrShape);
+        return;
+      }
       base = ((size_t)blk * a.block_size + (p % a.block_size)) * a.nkv + head;
     } else {
+      if (p < 0 || p >= a.table_len) {
+        if (c == 0) record_error(a.err, kErrShape);
+        return;
+      }
       base = (size_t)p * a.nkv + head;
     }
     a.kcache[base * D + c] = __float2bfloat16(out);
@@ -635,7 +652,7 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
                    int64_t D, int64_t rd, torch::Tensor qn, torch::Tensor kn, torch::Tensor inv_freq,
                    double rope_scale, double eps, torch::Tensor pos, c10::optional<torch::Tensor> q_out,
                    torch::Tensor kcache, torch::Tensor vcache, c10::optional<torch::Tensor> block_table,
-                   int64_t block_size) {
+                   int64_t block_size, torch::Tensor err) {
   c10::cuda::CUDAGuard guard(proj.device());
   TORCH_CHECK(proj.scalar_type() == at::kBFloat16 && kcache.scalar_type() == at::kBFloat16, "bf16 required");
   TORCH_CHECK(pos.scalar_type() == at::kInt, "int32 positions");
@@ -656,6 +673,16 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
   a.vcache = reinterpret_cast<__nv_bfloat16*>(vcache.data_ptr());
   a.block_table = block_table ? block_table->data_ptr<int>() : nullptr;
   a.block_size = (int)block_size;
+  if (block_table) {
+    TORCH_CHECK(kcache.dim() == 4 && block_size == kcache.size(1), "paged cache [blocks, block_size, kv, D]");
+    a.table_len = block_table->numel();
+    a.cache_blocks = kcache.size(0);
+  } else {
+    TORCH_CHECK(kcache.dim() == 3, "contiguous cache [rows, kv, D]");
+    a.table_len = kcache.size(0);
+    a.cache_blocks = 0;
+  }
+  a.err = err.data_ptr<int>();
   const int T = (int)proj.size(0);
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   q38::launch_pdl(q38::attn_prep_kernel, dim3(T, (unsigned)(nq + nkv)), dim3((unsigned)D), D * sizeof(float), st, a);

@@ -24,7 +24,7 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
                    int64_t D, int64_t rd, torch::Tensor qn, torch::Tensor kn, torch::Tensor inv_freq,
                    double rope_scale, double eps, torch::Tensor pos, c10::optional<torch::Tensor> q_out,
                    torch::Tensor kcache, torch::Tensor vcache, c10::optional<torch::Tensor> block_table,
-                   int64_t block_size);
+                   int64_t block_size, torch::Tensor err);
 void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,

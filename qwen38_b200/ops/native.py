@@ -53,7 +53,7 @@ def untile_weight(tw: TiledWeight) -> torch.Tensor:
 
 
 _ERR_NAMES = {1: "TMA/mbarrier wait timeout", 2: "accumulator wait timeout", 4: "split-K fix-up timeout",
-              8: "peer flag timeout", 16: "unsupported shape"}
+              8: "peer flag timeout", 16: "unsupported shape or out-of-range cache position"}
 
 
 class NativeOps(TorchOps):
@@ -238,7 +238,8 @@ class NativeOps(TorchOps):
         T = proj.shape[0]
         q = torch.empty(T, H, D, dtype=torch.bfloat16, device=proj.device)
         self.C.attn_prep(proj, 0, 2 * H * D, 2 * H * D + Hkv * D, H, Hkv, D, rd, qn_w, kn_w, inv_freq,
-                         float(rope_scale), float(eps), positions, q, kcache, vcache, block_table, block_size)
+                         float(rope_scale), float(eps), positions, q, kcache, vcache, block_table, block_size,
+                         self.err)
         self.launches += 1
         return q, proj[:, H * D:2 * H * D]
 
@@ -266,7 +267,7 @@ class NativeOps(TorchOps):
 
     def kv_append(self, kv, kn_w, inv_freq, rope_scale, rd, nkv, D, eps, positions, kcache, vcache):
         self.C.attn_prep(kv, -1, 0, nkv * D, 0, nkv, D, rd, kn_w, kn_w, inv_freq, float(rope_scale), float(eps),
-                         positions, None, kcache, vcache, None, 0)
+                         positions, None, kcache, vcache, None, 0, self.err)
         self.launches += 1
 
     def draft_block_attention(self, qkv, qn_w, kn_w, inv_freq, rope_scale, dims, eps, positions, kcache, vcache,
@@ -275,7 +276,7 @@ class NativeOps(TorchOps):
         T = qkv.shape[0]
         q = torch.empty(T, H, D, dtype=torch.bfloat16, device=qkv.device)
         self.C.attn_prep(qkv, 0, H * D, (H + Hkv) * D, H, Hkv, D, D, qn_w, kn_w, inv_freq, float(rope_scale),
-                         float(eps), positions, q, kcache, vcache, None, 0)
+                         float(eps), positions, q, kcache, vcache, None, 0, self.err)
         po, pml = self._bufs(Hkv, H // Hkv * T, D)
         out = torch.empty(T, H * D, dtype=torch.bfloat16, device=qkv.device)
         self.C.attn_decode(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,

@@ -228,7 +228,9 @@ class SpecRuntime:
             with torch.cuda.graph(graph):
                 tgt.commit_device(seq.slot, o0, T, rows)
                 dr.append_device(vfeats[:rows], pos_dev + ar, 0)
-            g = self._pub_graphs[key] = dict(graph=graph, pos=pos_dev,
+            # every tensor the graph reads stays referenced as long as the graph (a freed input
+            # would be handed to later allocations while replays still read it)
+            g = self._pub_graphs[key] = dict(graph=graph, pos=pos_dev, ar=ar, feats=vfeats,
                                              pos_host=torch.zeros(1, dtype=torch.int32).pin_memory())
         g["pos_host"][0] = pos
         g["pos"].copy_(g["pos_host"], non_blocking=True)
