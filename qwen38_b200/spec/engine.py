@@ -76,7 +76,6 @@ class SpecRuntime:
         self.lookup = lookup
         self.taps = tuple(drafter.dcfg.taps) if drafter is not None else ()
         self._anchor_dev = torch.zeros(1, dtype=torch.long, device=target.device)
-        self._pub_graphs, self._pub_seen = {}, set()
         self.pinned = None
         self.session = self.last_session = None
         self.h2d_bytes = self.d2h_bytes = 0
@@ -199,49 +198,10 @@ class SpecRuntime:
             self.session = None
 
     def _publish(self, seq, rows, vfeats, pos, nxt):
-        """Commit ``rows`` verified rows and append their features to the drafter history.  At TP1
-        with graphs, the device work (GDN commit replay, conv windows, the drafter's fc and K/V
-        projections) runs as one captured graph per (slot, verify block, row count), captured the
-        second time that combination occurs; the host keeps only the bookkeeping."""
-        tgt, dr = self.target, self.drafter
-        graphable = (tgt.use_graphs and tgt.tp == 1 and dr is not None and hasattr(dr, "append_device")
-                     and rows > 0 and seq.verify_rows is not None and vfeats is not None)
-        key = (seq.slot, seq.verify_rows, vfeats.data_ptr() if vfeats is not None else 0, rows)
-        if not graphable or (key not in self._pub_graphs and key not in self._pub_seen):
-            if graphable:
-                self._pub_seen.add(key)
-            tgt.commit(seq, rows)
-            if dr is not None:
-                dr.append(vfeats[:rows], pos, next_tokens=nxt)
-            return
-        o0, T = seq.verify_rows
-        if not 0 < rows <= T:
-            raise ValueError(f"commit of {rows} rows outside the verified block of {T}")
-        if pos != dr.positions[0] or pos + rows > dr.max_context:
-            raise ValueError("drafter history out of step with the target")
-        g = self._pub_graphs.get(key)
-        if g is None:
-            pos_dev = torch.zeros(1, dtype=torch.int32, device=tgt.device)
-            ar = torch.arange(rows, dtype=torch.int32, device=tgt.device)
-            graph = torch.cuda.CUDAGraph()
-            torch.cuda.synchronize()
-            with torch.cuda.graph(graph):
-                tgt.commit_device(seq.slot, o0, T, rows)
-                dr.append_device(vfeats[:rows], pos_dev + ar, 0)
-            # every tensor the graph reads stays referenced as long as the graph (a freed input
-            # would be handed to later allocations while replays still read it)
-            g = self._pub_graphs[key] = dict(graph=graph, pos=pos_dev, ar=ar, feats=vfeats,
-                                             pos_host=torch.zeros(1, dtype=torch.int32).pin_memory())
-        g["pos_host"][0] = pos
-        g["pos"].copy_(g["pos_host"], non_blocking=True)
-        g["graph"].replay()
-        seq.pos += rows
-        seq.verify_rows = None
-        dr.positions[0] = pos + rows
-
-    def release_graphs(self):
-        self._pub_graphs.clear()
-        self._pub_seen.clear()
+        """Commit ``rows`` verified rows and append their features to the drafter history."""
+        self.target.commit(seq, rows)
+        if self.drafter is not None:
+            self.drafter.append(vfeats[:rows], pos, next_tokens=nxt)
 
     def _prefill(self, prompt_host, prompt_dev):
         """Prefill through the prefix registry when attached: restore the longest exact checkpoint,

@@ -86,26 +86,3 @@ def test_native_sampled_decoding_is_reproducible(nops):
     assert tgt.sample(toks, 6, temperature=0.0) == tgt.greedy(toks, 6)
     nops.check()
 
-
-def test_publication_graph_matches_eager(nops):
-    """The captured commit + drafter publication gives the same drafter history and GDN state as
-    the eager path, block after block."""
-    cfg, dcfg = tiny_model_config(), tiny_drafter_config()
-    prompt = torch.randint(0, cfg.vocab_size, (96,), generator=torch.Generator().manual_seed(4)).tolist()
-    runs = []
-    for graphs in (True, False):
-        rt = RuntimeConfig(max_context=1024, prefill_chunk=64, gdn_chunk=16, use_cuda_graphs=graphs)
-        tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, device="cuda", dtype=torch.bfloat16, ops=nops)
-        dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt)
-        gold = greedy_reference(tgt, prompt, 48)
-        sr = SpecRuntime(tgt, dr, verifier_rows=4)
-        res = sr.generate(prompt, 48, gold_check=gold, pinned=PinnedAcceptance(gold, seed=9, mean_accepted=2))
-        assert res["tokens"] == gold
-        n = dr.positions[0]
-        runs.append((n, dr.kctx_all[0, :, :n].clone(), dr.vctx_all[0, :, :n].clone()))
-        if graphs:
-            assert len(sr._pub_graphs) > 0                 # the captured path ran
-        sr.release_graphs()
-    (n0, k0, v0), (n1, k1, v1) = runs
-    assert n0 == n1 and torch.equal(k0, k1) and torch.equal(v0, v1)
-    nops.check()
