@@ -779,3 +779,16 @@ void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcach
 #undef Q38_PF
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
+
+// Host view of the decode attention's key-group partition (for tests and planners): one
+// (first chunk, chunk count) pair per group covering `nchunks` 128-key chunks.
+std::vector<std::pair<int64_t, int64_t>> q38_attn_key_groups(int64_t nchunks) {
+  std::vector<std::pair<int64_t, int64_t>> out;
+  const int n = q38::groups_for((int)nchunks);
+  for (int g = 0; g < n; ++g) {
+    const int c0 = q38::group_first_chunk(g);
+    const int cnt = std::min(q38::group_chunks(g), (int)nchunks - c0);
+    out.emplace_back(c0, cnt);
+  }
+  return out;
+}

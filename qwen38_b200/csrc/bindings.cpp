@@ -29,6 +29,7 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
                      torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+std::vector<std::pair<int64_t, int64_t>> q38_attn_key_groups(int64_t nchunks);
 void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                       c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                       c10::optional<torch::Tensor> gate, torch::Tensor out);
@@ -67,6 +68,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prep", &q38_attn_prep);
   m.def("attn_decode", &q38_attn_decode);
   m.def("attn_prefill", &q38_attn_prefill);
+  m.def("attn_key_groups", &q38_attn_key_groups);
   m.def("rms_norm", &q38_rms_norm);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);
