@@ -90,7 +90,41 @@ def drafter_shapes(d: DrafterConfig, vocab: int) -> dict:
     return out
 
 
+def window_drafter_shapes(d, vocab: int) -> dict:
+    """Tensor names and shapes of the windowed (DFlash2) drafter; per-layer names follow the
+    reference's prepared layer dicts (``scripts/ci/draft_attention_branch.py:55-63``,
+    ``scripts/ci/draft_mlp_branch.py:27-45``, ``scripts/ci/draft_selector_fixture.py:11-13``)."""
+    h, g = d.hidden_size, d.conv_groups
+    out = {
+        "fc.weight": (h, len(d.taps) * h),
+        "hidden_norm.weight": (h,),
+        "norm.weight": (h,),
+        "candidate_selector.hidden_projection.weight": (d.selector_rank, h),
+        "candidate_selector.predecessor_codebook": (vocab, d.selector_rank),
+        "candidate_selector.successor_codebook": (vocab, d.selector_rank),
+    }
+    for l in range(d.num_hidden_layers):
+        p = f"layers.{l}."
+        out[p + "input_layernorm.weight"] = (h,)
+        out[p + "post_attention_layernorm.weight"] = (h,)
+        for branch in ("attention_conv", "mlp_conv"):
+            out[p + branch + ".kernel_projection.weight"] = (4 * g, h)
+            out[p + branch + ".base_kernel"] = (2, 2, h)
+        out[p + "mlp.gate_proj.weight"] = (d.intermediate_size, h)
+        out[p + "mlp.up_proj.weight"] = (d.intermediate_size, h)
+        out[p + "mlp.down_proj.weight"] = (h, d.intermediate_size)
+        out[p + "self_attn.q_proj.weight"] = (d.num_attention_heads * d.head_dim, h)
+        out[p + "self_attn.k_proj.weight"] = (d.num_key_value_heads * d.head_dim, h)
+        out[p + "self_attn.v_proj.weight"] = (d.num_key_value_heads * d.head_dim, h)
+        out[p + "self_attn.o_proj.weight"] = (h, d.num_attention_heads * d.head_dim)
+        out[p + "self_attn.q_norm.weight"] = (d.head_dim,)
+        out[p + "self_attn.k_norm.weight"] = (d.head_dim,)
+    return out
+
+
 def _init_kind(name: str) -> str:
+    if name.endswith("base_kernel"):
+        return "conv_base"
     if name.endswith("A_log"):
         return "alog"
     if name.endswith("dt_bias"):
@@ -142,13 +176,17 @@ class RandomSource(TensorSource):
         elif kind == "conv":
             k = shape[-1]
             t = (torch.rand(shape, generator=gen, **f32) * 2 - 1) / math.sqrt(k)
+        elif kind == "conv_base":
+            # [phase, tap, channel]: tap 0 near identity, tap 1 (the previous row) small
+            t = torch.randn(shape, generator=gen, **f32) * self.std
+            t[:, 0] += 1.0
         elif kind == "alog":
             t = torch.log(1 + 15 * torch.rand(shape, generator=gen, **f32))
         elif kind == "dt":
             t = 1.0 + 0.1 * torch.randn(shape, generator=gen, **f32)
         else:
             raise AssertionError(kind)
-        if dtype is not None and kind in ("normal", "zc", "one", "conv"):
+        if dtype is not None and kind in ("normal", "zc", "one", "conv", "conv_base"):
             t = t.to(dtype)
         return t
 
@@ -250,6 +288,10 @@ def random_drafter_source(d: DrafterConfig, vocab: int, seed: int = 1) -> Random
     return RandomSource(drafter_shapes(d, vocab), seed=seed, direct_norms=True)
 
 
+def random_window_drafter_source(d, vocab: int, seed: int = 3) -> RandomSource:
+    return RandomSource(window_drafter_shapes(d, vocab), seed=seed, direct_norms=True)
+
+
 def materialize(src: TensorSource, device="cpu", dtype=torch.float32) -> dict:
     return {n: src.get(n, device=device, dtype=dtype) for n in src.names()}
 
@@ -305,6 +347,27 @@ def save_pretrained(path: str, cfg: ModelConfig, src: TensorSource, dtype=torch.
             json.dump(dict(dataclasses.asdict(dcfg), architectures=["DSparkDraftModel"]), f, indent=1)
         save_file({n: dsrc.get(n, dtype=dtype).contiguous() for n in dsrc.names()},
                   os.path.join(dpath, "model.safetensors"), metadata={"format": "pt"})
+
+
+def load_window_drafter_config(path: str):
+    """``WindowDrafterConfig`` from a ``window_drafter/config.json``."""
+    import dataclasses
+    from .config import WindowDrafterConfig
+    with open(os.path.join(path, "config.json")) as f:
+        raw = json.load(f)
+    names = {f.name for f in dataclasses.fields(WindowDrafterConfig)}
+    return WindowDrafterConfig(**{k: v for k, v in raw.items() if k in names})
+
+
+def save_window_drafter(path: str, dcfg, src: TensorSource, dtype=torch.bfloat16):
+    """Write a windowed drafter as ``path/config.json`` + ``path/model.safetensors``."""
+    import dataclasses
+    from safetensors.torch import save_file
+    os.makedirs(path, exist_ok=True)
+    with open(os.path.join(path, "config.json"), "w") as f:
+        json.dump(dict(dataclasses.asdict(dcfg), architectures=["DFlash2DraftModel"]), f, indent=1)
+    save_file({n: src.get(n, dtype=dtype).contiguous() for n in src.names()},
+              os.path.join(path, "model.safetensors"), metadata={"format": "pt"})
 
 
 def load_drafter_config(path: str) -> DrafterConfig:

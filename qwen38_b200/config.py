@@ -202,6 +202,42 @@ class DrafterConfig:
 
 
 @dataclass
+class WindowDrafterConfig(DrafterConfig):
+    """Windowed block drafter (DFlash2 family), the DSpark drafter's predecessor in the reference.
+
+    Shape and geometry pinned by ``scripts/ci/dflash_device.py:515-560`` (five layers, 8/16/32-row
+    blocks, a 2,048-row sliding history window), ``scripts/ci/draft_attention.py:4-18`` (the window
+    mask), ``scripts/ci/draft_convolution.py:6-37`` (group-16 dynamic causal convolutions, two
+    taps), ``scripts/ci/draft_shared_head.py`` (top-16 candidates per row) and
+    ``scripts/ci/draft_selector.py`` (rank-256 predecessor / successor codebooks).  RoPE is the plain
+    rotary table over the whole head (``scripts/ci/draft_head_preparation.py:4-12``, theta 1e7).
+    """
+    block_rows: int = 8
+    window: int = 2048            # block row at position p sees history keys k with p - k < window
+    conv_group: int = 16          # channels sharing one dynamic convolution weight
+    selector_rank: int = 256
+    candidates: int = 16          # top candidates per row handed to the selector
+    rope_type: str = "default"
+
+    def __post_init__(self):
+        super().__post_init__()
+        if self.hidden_size % self.conv_group:
+            raise ValueError("hidden size must be a multiple of the convolution group")
+        if self.window < self.block_rows:
+            raise ValueError("the history window must cover a whole block")
+        if not 1 <= self.candidates <= 32:
+            raise ValueError("1..32 selector candidates per row")
+
+    @property
+    def proposals(self) -> int:
+        return self.block_rows - 1
+
+    @property
+    def conv_groups(self) -> int:
+        return self.hidden_size // self.conv_group
+
+
+@dataclass
 class RuntimeConfig:
     """Serving/runtime knobs (paged KV, prefill chunking, verifier buckets, graphs)."""
     max_context: int = 8192
@@ -240,6 +276,15 @@ def tiny_drafter_config() -> DrafterConfig:
                          num_attention_heads=4, num_key_value_heads=2, head_dim=64, taps=[3],
                          block_rows=4, markov_rank=16, yarn_original_max_position=512,
                          max_position_embeddings=4096)
+
+
+def tiny_window_drafter_config() -> WindowDrafterConfig:
+    """Windowed drafter of the tiny target's width: one layer, 4-row blocks, a 24-row window (so
+    CPU tests reach the sliding part), 8 candidates."""
+    return WindowDrafterConfig(hidden_size=256, intermediate_size=768, num_hidden_layers=1,
+                               num_attention_heads=4, num_key_value_heads=2, head_dim=64, taps=[3],
+                               block_rows=4, window=24, selector_rank=16, candidates=8,
+                               max_position_embeddings=4096)
 
 
 def full_model_config() -> ModelConfig:

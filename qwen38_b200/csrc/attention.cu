@@ -133,6 +133,7 @@ struct DecodeArgs {
   float* part_o;               // [nkv, splits, nqv, D]
   float* part_ml;              // [nkv, splits, nqv, 2]
   int max_splits;
+  int window;                  // > 0: row at position p sees keys k with p - k < window
 };
 
 __device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
@@ -186,8 +187,9 @@ constexpr int DK_T = 64;       // keys per staged tile inside a group
 // order; the (max, sum, unnormalised O) partial of the group is merged across groups in group
 // order by the combine kernel.  A tile beyond a row's own position changes nothing: its
 // probabilities are exact zeros and its rescale factor is exactly 1, so row t gives the same bits
-// in a 16-row verify as in a 1-row decode.
-template <int D>
+// in a 16-row verify as in a 1-row decode.  WIN adds a sliding-window lower bound per row (the
+// windowed block drafter): keys below it are masked the same exact-zero way.
+template <int D, bool WIN>
 __global__ void __launch_bounds__(256, 1)
 attn_decode_kernel(DecodeArgs a) {
   constexpr int DP = D + 8;                 // padded row: conflict-free ldmatrix
@@ -271,6 +273,11 @@ attn_decode_kernel(DecodeArgs a) {
     const int r_lo = row0 + (lane >> 2), r_hi = r_lo + 8;
     const int p_lo = (active && r_lo < nqv) ? (a.causal ? a.qpos[r_lo % a.T] : n_keys - 1) : -1;
     const int p_hi = (active && r_hi < nqv) ? (a.causal ? a.qpos[r_hi % a.T] : n_keys - 1) : -1;
+    int w_lo = 0, w_hi = 0;                    // lowest visible key of each row (WIN only)
+    if constexpr (WIN) {
+      w_lo = (active && r_lo < nqv) ? a.qpos[r_lo % a.T] - a.window + 1 : 0;
+      w_hi = (active && r_hi < nqv) ? a.qpos[r_hi % a.T] - a.window + 1 : 0;
+    }
     float O[NT_D][4];
 #pragma unroll
     for (int n = 0; n < NT_D; ++n) O[n][0] = O[n][1] = O[n][2] = O[n][3] = 0.f;
@@ -305,8 +312,13 @@ attn_decode_kernel(DecodeArgs a) {
 #pragma unroll
           for (int e = 0; e < 2; ++e) {
             const int kp = t0 + n * 8 + (lane & 3) * 2 + e;
-            S[n][e] = (kp < k_end && kp <= p_lo) ? S[n][e] * a.scale : -INFINITY;
-            S[n][2 + e] = (kp < k_end && kp <= p_hi) ? S[n][2 + e] * a.scale : -INFINITY;
+            bool ok_lo = kp < k_end && kp <= p_lo, ok_hi = kp < k_end && kp <= p_hi;
+            if constexpr (WIN) {
+              ok_lo = ok_lo && kp >= w_lo;
+              ok_hi = ok_hi && kp >= w_hi;
+            }
+            S[n][e] = ok_lo ? S[n][e] * a.scale : -INFINITY;
+            S[n][2 + e] = ok_hi ? S[n][2 + e] * a.scale : -INFINITY;
             tm_lo = fmaxf(tm_lo, S[n][e]);
             tm_hi = fmaxf(tm_hi, S[n][2 + e]);
           }
@@ -689,10 +701,11 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
-void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
-                     c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
-                     int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
-                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys) {
+void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                            c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos,
+                            double scale, int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off,
+                            torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys,
+                            int64_t window) {
   c10::cuda::CUDAGuard guard(q.device());
   const int T = (int)q.size(0), nq = (int)q.size(1), D = (int)q.size(2);
   const int nkv = (int)kcache.size(-2);
@@ -709,6 +722,8 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
   a.scale = (float)scale;
   a.causal = (int)causal;
   a.max_splits = (int)((max_keys + q38::CH - 1) / q38::CH);
+  TORCH_CHECK(window >= 0 && window <= (int64_t)1 << 30, "window out of range");
+  a.window = (int)window;
   const int nqv = nq / nkv * T;
   TORCH_CHECK(part_o.numel() >= (int64_t)nkv * a.max_splits * nqv * D, "attention partial buffer too small");
   TORCH_CHECK(part_ml.numel() >= (int64_t)nkv * a.max_splits * nqv * 2, "attention partial buffer too small");
@@ -720,7 +735,7 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
   dim3 grid(nkv, q38::groups_for(a.max_splits));
 #define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
-    auto k = q38::attn_decode_kernel<DD>;                                                                   \
+    auto k = a.window > 0 ? q38::attn_decode_kernel<DD, true> : q38::attn_decode_kernel<DD, false>;         \
     cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                        \
     q38::launch_pdl(k, grid, dim3(warps * 32), smem, st, a);                                               \
   }
@@ -736,6 +751,14 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
                   (long long)(gate ? gate->stride(0) : 0), (int)gate_off,
                   reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));
   C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                     c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
+                     int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
+                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys) {
+  q38_attn_decode_window(q, kcache, vcache, block_table, block_size, qpos, scale, causal, gate, gate_off, out, part_o,
+                         part_ml, max_keys, 0);
 }
 
 void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,

@@ -29,7 +29,16 @@ void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
                      torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
+                            c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos,
+                            double scale, int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off,
+                            torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys,
+                            int64_t window);
 std::vector<std::pair<int64_t, int64_t>> q38_attn_key_groups(int64_t nchunks);
+void q38_draft_conv(torch::Tensor x, torch::Tensor dyn, int64_t tap0, torch::Tensor base, int64_t group,
+                    c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> resid);
+void q38_draft_select(torch::Tensor feats, torch::Tensor cand, torch::Tensor unary, torch::Tensor anchor,
+                      torch::Tensor pred, torch::Tensor succ, torch::Tensor out, torch::Tensor err);
 void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                       c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                       c10::optional<torch::Tensor> gate, torch::Tensor out);
@@ -67,6 +76,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn_chunk_workspace_bytes", &q38_gdn_chunk_workspace_bytes);
   m.def("attn_prep", &q38_attn_prep);
   m.def("attn_decode", &q38_attn_decode);
+  m.def("attn_decode_window", &q38_attn_decode_window);
+  m.def("draft_conv", &q38_draft_conv);
+  m.def("draft_select", &q38_draft_select);
   m.def("attn_prefill", &q38_attn_prefill);
   m.def("attn_key_groups", &q38_attn_key_groups);
   m.def("rms_norm", &q38_rms_norm);

@@ -104,9 +104,15 @@ class BlockDrafter:
         self.positions = [0] * slots
         self.use_graphs = target.use_graphs
         self._graphs = {}
+        self._init_propose_buffers(self.P)
+
+    def _init_propose_buffers(self, rows: int):
+        """Static anchor / position buffers of the captured propose step (``rows`` block rows)."""
+        dev, slots = self.device, self.slots
+        self.rows = rows
         self._anchor_buf = torch.zeros(slots, 1, dtype=torch.long, device=dev)
-        self._pos_buf = torch.zeros(slots, self.P, dtype=torch.int32, device=dev)
-        self._pos_host = torch.zeros(self.P, dtype=torch.int32).pin_memory() if dev.type == "cuda" else None
+        self._pos_buf = torch.zeros(slots, rows, dtype=torch.int32, device=dev)
+        self._pos_host = torch.zeros(rows, dtype=torch.int32).pin_memory() if dev.type == "cuda" else None
 
     # slot-0 views (single-stream API)
     @property
@@ -215,11 +221,11 @@ class BlockDrafter:
         if not self.use_graphs:
             return self._propose_eager(anchor, None, slot)
         pos = self.positions[slot]
-        if pos + self.P > self.kctx_all.shape[2]:
+        if pos + self.rows > self.kctx_all.shape[2]:
             raise ValueError("drafter history capacity exceeded")
         ab, pb = self._anchor_buf[slot], self._pos_buf[slot]
         ab.copy_(anchor.reshape(1))
-        self._pos_host.copy_(torch.arange(pos, pos + self.P, dtype=torch.int32))
+        self._pos_host.copy_(torch.arange(pos, pos + self.rows, dtype=torch.int32))
         pb.copy_(self._pos_host, non_blocking=True)
         if slot not in self._graphs:
             self._propose_eager(ab, pb, slot)          # warm-up

@@ -173,9 +173,10 @@ class TorchOps:
         self._write_kv(k, v, positions, kcache, vcache, None, 0)
 
     def draft_block_attention(self, qkv, qn_w, kn_w, inv_freq, rope_scale, dims, eps, positions, kcache, vcache,
-                              out_dtype):
+                              out_dtype, window: int = 0):
         """Drafter block rows [q | k | v]: norm + RoPE, block K/V written after the history at
-        ``positions``, then every block row attends the whole history and every block row."""
+        ``positions``, then every block row attends the whole history and every block row (with
+        ``window`` > 0: only keys k with position - k < window)."""
         H, Hkv, D = dims
         T = qkv.shape[0]
         q = qkv[:, :H * D].reshape(T, H, D)
@@ -185,7 +186,36 @@ class TorchOps:
         q = R.apply_rope(self.rms_norm(q, qn_w, eps, torch.float32), cos, sin).to(qkv.dtype)
         k = R.apply_rope(self.rms_norm(k, kn_w, eps, torch.float32), cos, sin)
         self._write_kv(k, v, positions, kcache, vcache, None, 0)
-        return self.attn_decode(q, None, kcache, vcache, None, positions, 0, out_dtype, causal=False)
+        if window <= 0:
+            return self.attn_decode(q, None, kcache, vcache, None, positions, 0, out_dtype, causal=False)
+        n = int(positions[-1]) + 1
+        kpos = torch.arange(n, device=q.device)
+        o = R.attention(q, kcache[:n], vcache[:n], positions.long(), kpos, D ** -0.5, causal=False, window=window)
+        return o.reshape(T, H * D).to(out_dtype)
+
+    def draft_conv(self, x, dyn, tap0: int, base, group: int, residual=None, out_dtype=torch.bfloat16):
+        """Windowed drafter's dynamic grouped causal convolution (``torch_ref.draft_conv``) of
+        x [R, H] with dynamic kernels dyn [R, >= (tap0 + 2) * H / group] and base [2, H] (fp32):
+        an ``out_dtype`` result, or added into the fp32 ``residual``."""
+        y = R.draft_conv(x, dyn, tap0, base, group)
+        if residual is None:
+            return y.to(out_dtype)
+        residual += y
+        return residual
+
+    def draft_select(self, feats, cand, unary, anchor, pred, succ):
+        """Greedy selector over block rows 1..R-1 (fp64, device tensors only, no host sync):
+        candidates cand [R, C] (global ids) with logits unary [R, C], selector features feats [R, rank],
+        codebooks pred / succ [V, rank]; returns proposal ids [R-1] (int64)."""
+        prev = anchor.reshape(1).long()
+        out = []
+        for i in range(1, cand.shape[0]):
+            pv = pred.index_select(0, prev)[0].double() * feats[i].double()
+            sv = succ.index_select(0, cand[i]).double()
+            sc = unary[i].double() + sv @ pv
+            prev = cand[i].index_select(0, torch.argmax(sc).reshape(1))
+            out.append(prev)
+        return torch.cat(out)
 
     def gdn_commit_layers(self, stash, n, conv, rec, conv_w, A_log, dt_bias, dims):
         """Commit the first ``n`` rows of every layer's kept projection rows (stacked [L, ...])."""

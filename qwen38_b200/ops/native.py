@@ -271,7 +271,7 @@ class NativeOps(TorchOps):
         self.launches += 1
 
     def draft_block_attention(self, qkv, qn_w, kn_w, inv_freq, rope_scale, dims, eps, positions, kcache, vcache,
-                              out_dtype):
+                              out_dtype, window: int = 0):
         H, Hkv, D = dims
         T = qkv.shape[0]
         q = torch.empty(T, H, D, dtype=torch.bfloat16, device=qkv.device)
@@ -279,9 +279,32 @@ class NativeOps(TorchOps):
                          float(eps), positions, q, kcache, vcache, None, 0, self.err)
         po, pml = self._bufs(Hkv, H // Hkv * T, D)
         out = torch.empty(T, H * D, dtype=torch.bfloat16, device=qkv.device)
-        self.C.attn_decode(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
-                           self.max_keys)
+        if window > 0:
+            self.C.attn_decode_window(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
+                                      self.max_keys, int(window))
+        else:
+            self.C.attn_decode(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
+                               self.max_keys)
         self.launches += 3
+        return out
+
+    def draft_conv(self, x, dyn, tap0: int, base, group: int, residual=None, out_dtype=torch.bfloat16):
+        if residual is None:
+            if out_dtype != torch.bfloat16:
+                raise ValueError("the native convolution writes bf16 rows")
+            out = torch.empty(x.shape, dtype=torch.bfloat16, device=x.device)
+            self.C.draft_conv(x.contiguous(), dyn, int(tap0), base, int(group), out, None)
+        else:
+            out = residual
+            self.C.draft_conv(x.contiguous(), dyn, int(tap0), base, int(group), None, residual)
+        self.launches += 1
+        return out
+
+    def draft_select(self, feats, cand, unary, anchor, pred, succ):
+        out = torch.empty(cand.shape[0] - 1, dtype=torch.int64, device=cand.device)
+        self.C.draft_select(feats, cand.contiguous(), unary.contiguous(), anchor.reshape(-1), pred, succ, out,
+                            self.err)
+        self.launches += 1
         return out
 
     # ------------------------------------------------------------------ sampling

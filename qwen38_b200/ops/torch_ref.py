@@ -151,9 +151,10 @@ def apply_rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.T
     return torch.cat([y.to(x.dtype), xp], -1)
 
 
-def attention(q, k, v, q_pos, k_pos, scale: float, causal: bool = True):
+def attention(q, k, v, q_pos, k_pos, scale: float, causal: bool = True, window: int = 0):
     """GQA attention. q: [T, Hq, D], k/v: [S, Hkv, D]; q_pos [T], k_pos [S].
-    A query at position p sees keys at positions <= p (causal) or all keys."""
+    A query at position p sees keys at positions <= p (causal) or all keys; with ``window`` > 0
+    only keys k with p - k < window (the windowed drafter's mask, ``scripts/ci/draft_attention.py:14``)."""
     Hq, Hkv = q.shape[1], k.shape[1]
     rep = Hq // Hkv
     kf = k.float().repeat_interleave(rep, 1)
@@ -161,6 +162,9 @@ def attention(q, k, v, q_pos, k_pos, scale: float, causal: bool = True):
     s = torch.einsum("thd,shd->hts", q.float(), kf) * scale
     if causal:
         mask = k_pos[None, :] > q_pos[:, None]
+        s = s.masked_fill(mask[None], float("-inf"))
+    if window > 0:
+        mask = (q_pos[:, None] - k_pos[None, :]) >= window
         s = s.masked_fill(mask[None], float("-inf"))
     p = torch.softmax(s, -1)
     return torch.einsum("hts,shd->thd", p, vf)
@@ -235,3 +239,36 @@ def sample_key(seed: int, position: int) -> int:
     """Noise key of one sampled token: a mix of the request seed and the token position, as int64."""
     z = torch.tensor([(seed * 0x9E3779B97F4A7C15 + position) & _M64], dtype=torch.uint64).view(torch.int64)
     return int(mix64(z)[0])
+
+
+def draft_conv(x, dyn, tap0: int, base, group: int):
+    """Dynamic grouped causal convolution of the windowed drafter (``scripts/ci/draft_convolution.py:17-37``):
+    y[r, c] = (base[0, c] + dyn[r, tap0, c // group]) x[r, c] + (base[1, c] + dyn[r, tap0 + 1, c // group]) x[r - 1, c],
+    x[-1] = 0, fp32 inputs rounded to bf16 first, the four products summed in that order in fp32."""
+    R, H = x.shape
+    G = H // group
+    x0 = x.to(torch.bfloat16).float()
+    x1 = torch.cat([torch.zeros_like(x0[:1]), x0[:-1]])
+    d0 = dyn[:, tap0 * G:(tap0 + 1) * G].float().repeat_interleave(group, -1)
+    d1 = dyn[:, (tap0 + 1) * G:(tap0 + 2) * G].float().repeat_interleave(group, -1)
+    b = base.float().reshape(2, H)
+    y = b[0] * x0
+    y = y + d0 * x0
+    y = y + b[1] * x1
+    return y + d1 * x1
+
+
+def greedy_select(feats, cand, unary, anchor: int, pred, succ):
+    """fp64 greedy path through the candidates of rows 1..R-1 (``scripts/ci/draft_selector.py:37-56``):
+    score(c) = unary[i, c] + sum_k pred[prev, k] f[i, k] succ[c, k], first maximum wins, prev starts at
+    the anchor.  Returns (ids [R-1], per-row score vectors [R-1, C])."""
+    prev = int(anchor)
+    ids, rows = [], []
+    for i in range(1, cand.shape[0]):
+        c = cand[i].long().cpu()
+        e = (pred[prev].double().cpu()[None, :] * feats[i].double().cpu()[None, :] * succ[c].double().cpu()).sum(-1)
+        sc = unary[i].double().cpu() + e
+        prev = int(c[int(torch.argmax(sc))])
+        ids.append(prev)
+        rows.append(sc)
+    return torch.tensor(ids, dtype=torch.int64), torch.stack(rows)

@@ -26,7 +26,7 @@ class ParallelConfig:
 
 @dataclass
 class SpecConfig:
-    drafter: str = "dspark"      # dspark | mtp | lookup | none
+    drafter: str = "dspark"      # dspark | dflash2 | mtp | lookup | none
     block_rows: int = 16
     lookup: bool = False         # lookup drafter first, neural drafter second
     mtp_steps: int = 3
@@ -69,8 +69,8 @@ class RunConfig:
         if p.tp > 1 and k.ops == "torch" and p.comm != "nccl":
             raise ValueError("peer-memory collectives run inside the native kernels: use parallel.comm=nccl "
                              "with kernels.ops=torch")
-        if s.drafter not in ("dspark", "mtp", "lookup", "none"):
-            raise ValueError("spec.drafter must be dspark, mtp, lookup or none")
+        if s.drafter not in ("dspark", "dflash2", "mtp", "lookup", "none"):
+            raise ValueError("spec.drafter must be dspark, dflash2, mtp, lookup or none")
         if s.block_rows not in (2, 4, 8, 16, 32):
             raise ValueError("spec.block_rows must be a verifier bucket of at least 2")
         if s.drafter == "mtp" and s.block_rows != s.mtp_steps + 1:

@@ -70,6 +70,19 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
         dsrc = SafetensorsSource(os.path.join(ckpt, "drafter")) if ckpt else \
             random_drafter_source(dcfg, cfg.vocab_size, seed + 1)
         drafter = BlockDrafter(dcfg, dsrc, tgt, slots=slots)
+    elif rc.spec.drafter == "dflash2":
+        import dataclasses
+        from ..checkpoint import load_window_drafter_config, random_window_drafter_source
+        from ..config import tiny_window_drafter_config, WindowDrafterConfig
+        from ..models.window_drafter import WindowDrafter
+        wpath = os.path.join(ckpt, "window_drafter") if ckpt else None
+        if wpath is not None and not os.path.isdir(wpath):
+            raise ValueError("the checkpoint has no window_drafter/ directory for spec.drafter=dflash2")
+        wcfg = load_window_drafter_config(wpath) if wpath else \
+            (tiny_window_drafter_config() if rc.model == "tiny" else WindowDrafterConfig())
+        wcfg = dataclasses.replace(wcfg, block_rows=rc.spec.block_rows)
+        wsrc = SafetensorsSource(wpath) if wpath else random_window_drafter_source(wcfg, cfg.vocab_size, seed + 3)
+        drafter = WindowDrafter(wcfg, wsrc, tgt, slots=slots)
     elif rc.spec.drafter == "mtp":
         from ..models.mtp import MTPDrafter, random_mtp_source
         msrc = SafetensorsSource(ckpt) if ckpt else random_mtp_source(cfg, seed + 2)
