@@ -206,6 +206,64 @@ def test_serving_engine_with_window_drafter():
         assert o == greedy_reference(eng.target, p, len(o))
 
 
+def _tp_worker(rank, world, port, q):
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from qwen38_b200.checkpoint import random_target_source
+        from qwen38_b200.config import tiny_model_config
+        from qwen38_b200.parallel.comm import TorchComm
+        cfg, wcfg = tiny_model_config(), tiny_window_drafter_config()
+        rt = RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16)
+        prompt = torch.randint(0, cfg.vocab_size, (128,), generator=torch.Generator().manual_seed(0)).tolist()
+        tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, comm=TorchComm())
+        dr = WindowDrafter(wcfg, random_window_drafter_source(wcfg, cfg.vocab_size), tgt)
+        seq = tgt.new_sequence()
+        _, feats = tgt.prefill(seq, torch.tensor(prompt), taps=wcfg.taps)
+        tgt.release(seq)
+        dr.append(feats, 0)
+        props = dr.propose(torch.tensor([prompt[-1]])).tolist()
+        dr.reset()
+        gold = greedy_reference(tgt, prompt, 20)
+        res = SpecRuntime(tgt, dr, verifier_rows=wcfg.block_rows).generate(prompt, 20, gold_check=gold)
+        q.put((rank, props, gold, res["tokens"]))
+    except BaseException as e:   # report instead of hanging the parent
+        q.put((rank, repr(e), None, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_window_drafter_tp2_gloo(tiny):
+    """Two gloo ranks: identical proposals on both ranks (candidates gathered over the vocabulary
+    shards), equal to the single-rank drafter's on this seed, and token-exact speculation."""
+    import socket
+    import torch.multiprocessing as mp
+    tgt = _target(tiny)
+    wcfg = tiny_window_drafter_config()
+    dr = WindowDrafter(wcfg, random_window_drafter_source(wcfg, tiny["cfg"].vocab_size), tgt)
+    seq = tgt.new_sequence()
+    _, feats = tgt.prefill(seq, torch.tensor(tiny["prompt"]), taps=wcfg.taps)
+    tgt.release(seq)
+    dr.append(feats, 0)
+    props1 = dr.propose(torch.tensor([tiny["prompt"][-1]])).tolist()
+    with socket.socket() as sk:
+        sk.bind(("127.0.0.1", 0))
+        port = sk.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, props, gold, spec in out:
+        assert spec is not None, props
+        assert spec == gold
+    assert out[0][1] == out[1][1] == props1
+
+
 # ------------------------------------------------------------------------------------------ GPU
 @pytest.fixture(scope="module")
 def nops():
