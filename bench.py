@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--model", default="full", choices=["full", "tiny"])
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the target (invalid as a bench)")
     ap.add_argument("--mean-accepted", type=int, default=6)
+    ap.add_argument("--drafter", default="dspark", choices=["dspark", "dflash2"],
+                    help="dspark: the headline drafter; dflash2: the windowed drafter (same block rows)")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--no-graphs", action="store_true")
     ap.add_argument("--prefill-chunk", type=int, default=4096,
@@ -180,7 +182,16 @@ def main():
     t_load = time.time()
     tgt = HybridTarget(cfg, random_target_source(cfg, args.seed), rt, device=device, dtype=torch.bfloat16,
                        ops=ops, comm=comm)
-    dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, args.seed + 1), tgt)
+    if args.drafter == "dflash2":
+        import dataclasses
+        from qwen38_b200.checkpoint import random_window_drafter_source
+        from qwen38_b200.config import WindowDrafterConfig, tiny_window_drafter_config
+        from qwen38_b200.models.window_drafter import WindowDrafter
+        wcfg = WindowDrafterConfig() if args.model == "full" else tiny_window_drafter_config()
+        dcfg = dataclasses.replace(wcfg, block_rows=dcfg.block_rows, taps=dcfg.taps)
+        dr = WindowDrafter(dcfg, random_window_drafter_source(dcfg, cfg.vocab_size, args.seed + 3), tgt)
+    else:
+        dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, args.seed + 1), tgt)
     torch.cuda.synchronize()
     t_load = time.time() - t_load
 
@@ -248,7 +259,8 @@ def main():
             "config": {"model": f"{args.model}-hybrid-27B-class" if args.model == "full" else "tiny",
                        "layers": cfg.num_hidden_layers, "global_batch": 1, "seq_len": args.ctx,
                        "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows, "prefill_chunk": args.prefill_chunk,
-                       "drafter_layers": dcfg.num_hidden_layers, "parallelism": f"tp{world}",
+                       "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers,
+                       "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
                        "mean_accepted_target": args.mean_accepted,
