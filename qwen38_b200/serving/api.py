@@ -28,6 +28,10 @@ from pydantic import BaseModel
 from .scheduler import ABORTED, FINISHED
 
 
+class StreamOptions(BaseModel):
+    include_usage: bool = False       # a last event carrying the token accounting
+
+
 class CompletionRequest(BaseModel):
     model: str | None = None
     prompt: list[int] | str
@@ -36,6 +40,7 @@ class CompletionRequest(BaseModel):
     temperature: float = 0.0          # 0: greedy with block speculation; > 0: sampled decoding
     seed: int | None = None
     stream: bool = False
+    stream_options: StreamOptions | None = None
 
 
 class ChatMessage(BaseModel):
@@ -51,6 +56,7 @@ class ChatRequest(BaseModel):
     temperature: float = 0.0
     seed: int | None = None
     stream: bool = False
+    stream_options: StreamOptions | None = None
 
 
 def render_chat(messages) -> str:
@@ -177,8 +183,9 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def _finish_reason(out, body):
         return "stop" if out and out[-1] in (body.stop_token_ids or ()) else "length"
 
-    def _events(box, body, chunk):
-        """Server-sent events: one per engine step that emitted tokens, then [DONE]."""
+    def _events(box, body, chunk, n_prompt):
+        """Server-sent events: one per engine step that emitted tokens, the finish event (with the
+        token accounting when ``stream_options.include_usage``), then [DONE]."""
         emitted = []
         while True:
             try:
@@ -191,7 +198,11 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                     reason = box.get("error") or getattr(box.get("request"), "error", "aborted")
                     yield "data: " + json.dumps({"error": str(reason)}) + "\n\n"
                 else:
-                    yield "data: " + json.dumps(chunk([], _finish_reason(emitted, body))) + "\n\n"
+                    last = chunk([], _finish_reason(emitted, body))
+                    if body.stream_options is not None and body.stream_options.include_usage:
+                        last["usage"] = {"prompt_tokens": n_prompt, "completion_tokens": len(emitted),
+                                         "total_tokens": n_prompt + len(emitted)}
+                    yield "data: " + json.dumps(last) + "\n\n"
                 break
             emitted += new
             yield "data: " + json.dumps(chunk(new, None)) + "\n\n"
@@ -206,7 +217,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             def chunk(new, reason):
                 return {"id": cid, "object": "text_completion", "created": created, "model": model,
                         "choices": [{"index": 0, "text": tok.decode(new), "token_ids": new, "finish_reason": reason}]}
-            return StreamingResponse(_events(box, body, chunk), media_type="text/event-stream")
+            return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
         return {
             "id": cid, "object": "text_completion", "created": created, "model": model,
@@ -227,7 +238,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 delta = {"role": "assistant", "content": tok.decode(new)} if new else {}
                 return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model,
                         "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
-            return StreamingResponse(_events(box, body, chunk), media_type="text/event-stream")
+            return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
         return {
             "id": cid, "object": "chat.completion", "created": created, "model": model,

@@ -213,3 +213,41 @@ def test_streaming_and_chat_endpoints(tiny):
         bad = client.post("/v1/completions", json={"prompt": [999999], "max_tokens": 4, "stream": True})
         assert "error" in bad.text
     app.state.loop.close()
+
+
+def test_endpoint_isolation_gate():
+    """The isolation gate against a live server (uvicorn on 127.0.0.1): streamed greedy outputs are
+    the same alone and concurrent, the decoders keep streaming through a long prefill, and the
+    token accounting of every stream adds up."""
+    import socket
+    import threading
+    import time
+
+    import uvicorn
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.serving.isolation import measure
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=4"]))
+    app = build_app(eng)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    try:
+        for _ in range(500):
+            if server.started:
+                break
+            time.sleep(0.01)
+        rep = measure(f"http://127.0.0.1:{port}", prompt_length=600, decoders=2, decode_tokens=40,
+                      short_delay=0.0, ready_timeout=120.0, short_tokens=8)
+        assert rep["passed"], rep["checks"]
+        assert set(rep["concurrent"]) == {"A", "B0", "B1", "C"}
+        assert all(r["tokens"] == rep["baseline"][n]["tokens"] for n, r in rep["concurrent"].items())
+    finally:
+        server.should_exit = True
+        th.join(timeout=30)
+        app.state.loop.close()
