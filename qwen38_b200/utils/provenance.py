@@ -34,6 +34,7 @@ def manifest(full: bool = False) -> dict:
     out = {
         "sources_sha256": combined,
         "extension_sha256": _sha(so) if so else None,
+        "extension_matches_sources": None if build.stale() is None else not build.stale(),
         "nvcc_flags": " ".join(build.CUDA_FLAGS),
         "torch": torch.__version__,
         "cuda_runtime": torch.version.cuda,
