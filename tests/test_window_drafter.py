@@ -206,6 +206,41 @@ def test_serving_engine_with_window_drafter():
         assert o == greedy_reference(eng.target, p, len(o))
 
 
+def test_window_drafter_prefix_reuse(tiny):
+    """A prefix checkpoint carries the windowed drafter's history: the second request restores it,
+    prefills only the suffix and proposes exactly what a cold run proposes."""
+    from qwen38_b200.prefix.registry import PrefixRegistry
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16),
+                       max_slots=2)
+    wcfg = tiny_window_drafter_config()
+    src = random_window_drafter_source(wcfg, tiny["cfg"].vocab_size)
+    dr = WindowDrafter(wcfg, src, tgt)
+    g = torch.Generator().manual_seed(7)
+    prefix = torch.randint(0, 4096, (128,), generator=g).tolist()
+    a = prefix + torch.randint(0, 4096, (100,), generator=g).tolist()
+    b = prefix + torch.randint(0, 4096, (90,), generator=g).tolist()
+    gold_b = greedy_reference(tgt, b, 20)
+    reg = PrefixRegistry(tgt, budget_bytes=1 << 30, boundary=64)
+    sr = SpecRuntime(tgt, dr, verifier_rows=wcfg.block_rows, prefix=reg)
+    sr.generate(a, 20)
+    rb = sr.generate(b, 20, gold_check=gold_b)
+    assert rb["reused_prefix"] == 128 and rb["tokens"] == gold_b
+    # warm (restored + suffix) drafter history proposes what a cold full publication proposes
+    cold = WindowDrafter(wcfg, src, tgt)
+    seq = tgt.new_sequence()
+    _, feats = tgt.prefill(seq, torch.tensor(b), taps=wcfg.taps)
+    tgt.release(seq)
+    cold.append(feats, 0)
+    ck = reg.lookup(b)                # b's own deepest boundary by now
+    assert ck is not None and 128 <= ck.pos < len(b)
+    seq = reg.restore(ck, dr)
+    _, feats = tgt.prefill(seq, torch.tensor(b[ck.pos:]), taps=wcfg.taps)
+    tgt.release(seq)
+    dr.append(feats, ck.pos)
+    anchor = torch.tensor([b[-1]])
+    assert torch.equal(dr.propose(anchor), cold.propose(anchor))
+
+
 def _tp_worker(rank, world, port, q):
     import torch.distributed as dist
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
