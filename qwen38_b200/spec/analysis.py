@@ -8,7 +8,8 @@ mismatching proposal (what the selection rule consumes).  ``sweep_lookup`` runs 
 scorer does (``speculative-decoding/harness/lookup_acceptance.py:17-100``).  Nothing here runs a
 device or measures time.
 
-``latency_budget`` turns measured per-block phase times (``SpecRuntime.generate`` returns them in
+``acceptance_report`` summarises one request's blocks (full-draft mean acceptance, per-position
+acceptance rates, histogram).  ``latency_budget`` turns measured per-block phase times (``SpecRuntime.generate`` returns them in
 ``block_records``) into the cycle time a target TG needs at the observed acceptance, and the
 TG ceiling if drafting were free (``speculative-decoding/harness/speculative_latency_budget.py``).
 """
@@ -102,3 +103,38 @@ def latency_budget(blocks, target_tg: float = 200.0) -> dict:
                 required_committed_at_current_latency=target_tg * mean["cycle_ms"] / 1000.0,
                 zero_draft_ceiling_tg=(1000.0 * per_block / (mean["cycle_ms"] - mean["draft_ms"])
                                        if mean["cycle_ms"] > mean["draft_ms"] else None))
+
+
+def acceptance_report(blocks) -> dict:
+    """Acceptance statistics of one request's blocks (``SpecRuntime.generate``'s ``block_records``:
+    rows, accepted, committed per block), as the reference's acceptance report computes them
+    (``scripts/ci/acceptance_report.py``, ``block_stats`` / ``per_position``):
+
+    * ``full_draft``: blocks that verified the widest row count seen, excluding the request's last
+      block (cut by EOS or the budget, not by a rejection); their mean accepted drafts is the
+      acceptance measurement;
+    * per draft position i = 1..rows-1 over the full-draft blocks: ``unconditional`` = share of
+      blocks accepting at least i drafts, ``conditional`` = share accepting i among those that
+      accepted i - 1 (None once no block got that far);
+    * histogram of accepted drafts and the mean committed tokens per block over all blocks."""
+    if not blocks:
+        raise ValueError("no blocks")
+    for b in blocks:
+        if not (isinstance(b.get("rows"), int) and b["rows"] >= 1 and 0 <= b.get("accepted", -1) < b["rows"]
+                and 1 <= b.get("committed", 0) <= b["rows"]):
+            raise ValueError("blocks with rows, accepted < rows and committed in 1..rows required")
+    width = max(b["rows"] for b in blocks)
+    full = [b for b in blocks[:-1] if b["rows"] == width]
+    hist = [0] * width
+    for b in full:
+        hist[b["accepted"]] += 1
+    uncond, cond = [], []
+    for i in range(1, width):
+        at_least = sum(1 for b in full if b["accepted"] >= i)
+        prev = sum(1 for b in full if b["accepted"] >= i - 1)
+        uncond.append(at_least / len(full) if full else None)
+        cond.append(at_least / prev if prev else None)
+    return dict(rows=width, blocks=len(blocks), full_draft_blocks=len(full),
+                mean_accepted=(sum(b["accepted"] for b in full) / len(full)) if full else None,
+                mean_committed_per_block=sum(b["committed"] for b in blocks) / len(blocks),
+                histogram=hist, unconditional=uncond, conditional=cond)

@@ -23,6 +23,7 @@ def main():
     from ..config import RuntimeConfig, full_drafter_config, full_model_config, tiny_drafter_config, tiny_model_config
     from ..models.drafter import BlockDrafter
     from ..models.target import HybridTarget
+    from ..spec.analysis import acceptance_report
     from ..spec.engine import PinnedAcceptance, SpecRuntime, greedy_reference
 
     ap = argparse.ArgumentParser()
@@ -61,6 +62,7 @@ def main():
                "pp_tok_s": round(sum(x["pp_tok_s"] for x in rows) / len(rows), 1),
                "verify_ms_per_block": round(sum(x["verify_ms_per_block"] for x in rows) / len(rows), 3),
                "draft_ms_per_block": round(sum(x["draft_ms_per_block"] for x in rows) / len(rows), 3),
+               "acceptance": acceptance_report(rows[-1]["block_records"]),
                "model": a.model, "device": dev}
         print(json.dumps(out), flush=True)
 

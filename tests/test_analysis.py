@@ -4,7 +4,7 @@ import pytest
 from qwen38_b200.config import RuntimeConfig
 from qwen38_b200.models.target import HybridTarget
 from qwen38_b200.spec.analysis import latency_budget, score_lookup, sweep_lookup
-from qwen38_b200.spec.engine import SpecRuntime, greedy_reference
+from qwen38_b200.spec.engine import PinnedAcceptance, SpecRuntime, greedy_reference
 
 
 def test_lookup_scoring_on_a_periodic_tape():
@@ -48,3 +48,36 @@ def test_generate_block_records_feed_the_budget(tiny):
     recs = res["block_records"]
     assert len(recs) == res["blocks"] and sum(r["committed"] for r in recs) == res["committed"]
     assert latency_budget(recs)["blocks"] == len(recs)
+
+
+def test_acceptance_report_statistics():
+    from qwen38_b200.spec.analysis import acceptance_report
+    blocks = [dict(rows=4, accepted=a, committed=a + 1) for a in (3, 1, 0, 2, 3)] + [dict(rows=4, accepted=1,
+                                                                                            committed=1)]
+    r = acceptance_report(blocks)
+    assert r["full_draft_blocks"] == 5 and r["histogram"] == [1, 1, 1, 2]
+    assert r["mean_accepted"] == 9 / 5
+    assert r["unconditional"] == [4 / 5, 3 / 5, 2 / 5]
+    assert r["conditional"] == [4 / 5, 3 / 4, 2 / 3]
+    assert abs(r["mean_committed_per_block"] - 15 / 6) < 1e-12
+    with pytest.raises(ValueError):
+        acceptance_report([dict(rows=4, accepted=4, committed=4)])
+    with pytest.raises(ValueError):
+        acceptance_report([])
+
+
+def test_acceptance_report_of_a_pinned_run(tiny):
+    """Pinned acceptance with mean m cuts each block at a uniform position in [0, 2m]: the report
+    of a real run sees a mean accepted near m and a decreasing unconditional curve."""
+    from qwen38_b200.spec.analysis import acceptance_report
+    from qwen38_b200.models.drafter import BlockDrafter
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16))
+    dr = BlockDrafter(tiny["dcfg"], tiny["dsrc"], tgt)
+    gold = greedy_reference(tgt, tiny["prompt"], 120)
+    res = SpecRuntime(tgt, dr, verifier_rows=4).generate(
+        tiny["prompt"], 120, pinned=PinnedAcceptance(gold, seed=1, mean_accepted=1), gold_check=gold)
+    r = acceptance_report(res["block_records"])
+    assert r["rows"] == 4 and r["full_draft_blocks"] >= 10
+    assert 0.5 <= r["mean_accepted"] <= 1.6
+    u = [x for x in r["unconditional"] if x is not None]
+    assert all(a >= b for a, b in zip(u, u[1:]))
