@@ -195,15 +195,12 @@ def test_serving_engine_with_window_drafter():
     rc = load_run_config(None, profile="tiny-cpu", overrides=["spec.drafter=dflash2"])
     eng = build_engine(rc)
     assert isinstance(eng.drafter, WindowDrafter)
-    prompts = [list(range(3, 40)), list(range(100, 160))]
-    outs = eng.generate_all(prompts, max_new_tokens=12) if hasattr(eng, "generate_all") else None
-    if outs is None:
-        reqs = [eng.add_request(p, 12) for p in prompts]
-        while eng.has_work():
-            eng.step()
-        outs = [r.output for r in reqs]
-    for p, o in zip(prompts, outs):
-        assert o == greedy_reference(eng.target, p, len(o))
+    prompts = {"a": list(range(3, 40)), "b": list(range(100, 160))}
+    for rid, p in prompts.items():
+        eng.add_request(p, 12, request_id=rid)
+    done = {r.request_id: r.output for r in eng.run()}
+    for rid, p in prompts.items():
+        assert done[rid] == greedy_reference(eng.target, p, len(done[rid]))
 
 
 def test_window_drafter_prefix_reuse(tiny):
