@@ -253,6 +253,50 @@ class SafetensorsSource(TensorSource):
         return t
 
 
+class CachedSource(TensorSource):
+    """A converted-tensor cache in front of another source (the reference keeps per-mesh converted
+    tensor caches, ``graft/model_config.py:347-364``).  The first ``get`` of a (name, dtype) pair
+    reads the base source (dequantising block-FP8 weights, converting dtype) and writes the result
+    to ``cache_dir`` as one safetensors file; later loads, in this process or the next, map that
+    file instead.  A ``manifest.json`` pins the base source's description so a cache made from other
+    weights is never used."""
+
+    def __init__(self, base: TensorSource, cache_dir: str, base_id: str):
+        self.base, self.dir, self.base_id = base, cache_dir, base_id
+        os.makedirs(cache_dir, exist_ok=True)
+        man = os.path.join(cache_dir, "manifest.json")
+        if os.path.exists(man):
+            with open(man) as f:
+                if json.load(f).get("base") != base_id:
+                    raise ValueError(f"{cache_dir} caches another checkpoint; use a fresh directory")
+        else:
+            with open(man, "w") as f:
+                json.dump({"base": base_id}, f)
+        self.hits = self.misses = 0
+
+    def names(self):
+        return self.base.names()
+
+    def _file(self, name, dtype):
+        tag = str(dtype).replace("torch.", "") if dtype is not None else "native"
+        safe = name.replace("/", "_")
+        return os.path.join(self.dir, f"{safe}.{tag}.safetensors")
+
+    def get(self, name, device=None, dtype=None):
+        from safetensors.torch import load_file, save_file
+        path = self._file(name, dtype)
+        if os.path.exists(path):
+            self.hits += 1
+            t = load_file(path)["t"]
+        else:
+            self.misses += 1
+            t = self.base.get(name, dtype=dtype).contiguous()
+            tmp = path + ".tmp"
+            save_file({"t": t}, tmp)
+            os.replace(tmp, path)               # readers never see a partial file
+        return t.to(device) if device is not None else t
+
+
 def quant_fp8_block(w: torch.Tensor, block=(128, 128)):
     """2-D weight -> (float8_e4m3fn values, fp32 scale_inv [ceil(N/bn), ceil(K/bk)]) with one
     scale per block chosen so the block's largest magnitude maps to the e4m3 maximum (448)."""

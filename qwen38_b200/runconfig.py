@@ -52,6 +52,7 @@ class ServingConfig:
 @dataclass
 class RunConfig:
     model: str = "full"                  # "full", "tiny" or an HF checkpoint directory
+    weight_cache: str = ""               # directory of converted target weights ("" : off)
     runtime: RuntimeConfig = field(default_factory=RuntimeConfig)
     parallel: ParallelConfig = field(default_factory=ParallelConfig)
     spec: SpecConfig = field(default_factory=SpecConfig)

@@ -29,6 +29,17 @@ def _model(rc: RunConfig):
     return cfg, dcfg, rc.model
 
 
+def _checkpoint_id(path: str) -> str:
+    """Identity of a checkpoint directory for the weight cache: its path, and the names, sizes and
+    modification times of its files."""
+    import hashlib
+    h = hashlib.sha256(os.path.abspath(path).encode())
+    for f in sorted(os.listdir(path)):
+        st = os.stat(os.path.join(path, f))
+        h.update(f"{f}:{st.st_size}:{int(st.st_mtime)}".encode())
+    return h.hexdigest()
+
+
 def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
     """Returns ``ServingEngine``.  ``comm``: an existing communicator (TP > 1), else one is made."""
     from ..models.drafter import BlockDrafter
@@ -58,6 +69,9 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
                          peer=native and rc.parallel.comm != "nccl", fused=rc.parallel.comm == "fused")
     slots = rc.serving.slots
     src = SafetensorsSource(ckpt) if ckpt else random_target_source(cfg, seed)
+    if ckpt and rc.weight_cache:
+        from ..checkpoint import CachedSource
+        src = CachedSource(src, rc.weight_cache, base_id=_checkpoint_id(ckpt))
     rt = rc.runtime
     tgt = HybridTarget(cfg, src, rt, device=device, dtype=dtype, ops=ops, comm=comm, max_slots=slots + 1,
                        max_verify_rows=slots * rc.spec.block_rows)

@@ -54,3 +54,47 @@ def test_fp8_checkpoint_loads_and_runs(tiny, tmp_path):
     toks = torch.tensor(tiny["prompt"][:64])
     tgt = HybridTarget(tiny["cfg"], src, RT)
     assert tgt.greedy(toks, 16) == ref.greedy(toks, 16)
+
+
+def test_cached_source_roundtrip_and_pinning(tmp_path):
+    """The converted-tensor cache returns the base source's tensors (an fp8-block checkpoint is
+    dequantised once), serves later loads without the base, and refuses another checkpoint's cache."""
+    import pytest
+    from qwen38_b200.checkpoint import CachedSource, DictSource, quant_fp8_block, dequant_fp8_block
+    g = torch.Generator().manual_seed(0)
+    w = torch.randn(256, 384, generator=g)
+    q, si = quant_fp8_block(w)
+    base = DictSource({"a.weight": dequant_fp8_block(q, si), "b.norm.weight": torch.randn(384, generator=g)})
+    calls = []
+    real_get = base.get
+    base.get = lambda n, device=None, dtype=None: calls.append(n) or real_get(n, device=device, dtype=dtype)
+    c = CachedSource(base, str(tmp_path / "cache"), base_id="ckpt-1")
+    a = c.get("a.weight", dtype=torch.bfloat16)
+    assert torch.equal(a, base.sd["a.weight"].bfloat16()) and c.misses == 1
+    c2 = CachedSource(base, str(tmp_path / "cache"), base_id="ckpt-1")
+    assert torch.equal(c2.get("a.weight", dtype=torch.bfloat16), a) and c2.hits == 1
+    assert calls == ["a.weight"]                      # the second load never read the base
+    assert torch.equal(c2.get("b.norm.weight"), base.sd["b.norm.weight"])
+    with pytest.raises(ValueError):
+        CachedSource(base, str(tmp_path / "cache"), base_id="ckpt-2")
+
+
+def test_factory_weight_cache(tmp_path):
+    """An engine built through the weight cache equals one built from the checkpoint directly; the
+    second build reads the cache only."""
+    from qwen38_b200.checkpoint import random_target_source, save_pretrained
+    from qwen38_b200.config import tiny_model_config
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.spec.engine import greedy_reference
+    cfg = tiny_model_config()
+    ck = str(tmp_path / "ckpt")
+    save_pretrained(ck, cfg, random_target_source(cfg, 0), dtype=torch.float32)
+    base = ["spec.drafter=none", f"model={ck}"]
+    plain = build_engine(load_run_config(None, profile="tiny-cpu", overrides=base))
+    cache = str(tmp_path / "cache")
+    for _ in range(2):
+        eng = build_engine(load_run_config(None, profile="tiny-cpu", overrides=base + [f"weight_cache={cache}"]))
+    assert len([f for f in os.listdir(cache) if f.endswith(".safetensors")]) > 10
+    p = list(range(5, 40))
+    assert greedy_reference(eng.target, p, 8) == greedy_reference(plain.target, p, 8)
