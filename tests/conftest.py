@@ -1,6 +1,10 @@
 import os
 import sys
 
+# Multi-process tests spawn up to 8 CPU ranks; with every process using all cores' OpenMP threads
+# the machine is oversubscribed many times over and spin-waiting threads stall the whole suite.
+os.environ.setdefault("OMP_NUM_THREADS", "4")
+
 import pytest
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))

@@ -148,6 +148,28 @@ def test_window_drafter_speculative_equals_greedy(tiny):
     assert res["tokens"] == gold
 
 
+@pytest.mark.parametrize("rows,window,cand", [(2, 2, 1), (8, 8, 4), (16, 40, 16)])
+def test_window_drafter_geometries(tiny, rows, window, cand):
+    """Block widths 2..16, a window as small as the block, one candidate: still token-exact."""
+    import dataclasses
+    tgt = _target(tiny)
+    wcfg = dataclasses.replace(tiny_window_drafter_config(), block_rows=rows, window=window, candidates=cand)
+    dr = WindowDrafter(wcfg, random_window_drafter_source(wcfg, tiny["cfg"].vocab_size), tgt)
+    gold = greedy_reference(tgt, tiny["prompt"], 20)
+    res = SpecRuntime(tgt, dr, verifier_rows=rows).generate(tiny["prompt"], 20, gold_check=gold)
+    assert res["tokens"] == gold
+
+
+def test_window_drafter_config_checks():
+    import dataclasses
+    with pytest.raises(ValueError):
+        dataclasses.replace(tiny_window_drafter_config(), window=2)          # smaller than a block
+    with pytest.raises(ValueError):
+        dataclasses.replace(tiny_window_drafter_config(), conv_group=48)     # 256 % 48 != 0
+    with pytest.raises(ValueError):
+        dataclasses.replace(tiny_window_drafter_config(), candidates=0)
+
+
 def test_window_limits_what_the_block_sees(tiny):
     """With a history longer than the window, keys older than the window change nothing; a wider
     window sees them."""
