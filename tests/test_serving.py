@@ -251,3 +251,16 @@ def test_endpoint_isolation_gate():
         server.should_exit = True
         th.join(timeout=30)
         app.state.loop.close()
+
+
+def test_real_text_concurrent_equals_sequential():
+    """Repository text as prompts: every answer is byte-identical alone and packed with the others."""
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.serving.realtext import compare, text_prompts
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=4"]))
+    prompts = text_prompts(chars=300)
+    assert len(prompts) == 4
+    rep = compare(eng, prompts, max_tokens=16)
+    assert rep["passed"], rep
+    assert all(r["tokens"] == 16 for r in rep["prompts"])
