@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--model", default="full", choices=["full", "tiny"])
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the target (invalid as a bench)")
     ap.add_argument("--mean-accepted", type=int, default=6)
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "mxfp8"],
+                    help="mxfp8: target linear weights are their MXFP8 round trip (computed in bf16)")
     ap.add_argument("--drafter", default="dspark", choices=["dspark", "dflash2"],
                     help="dspark: the headline drafter; dflash2: the windowed drafter (same block rows)")
     ap.add_argument("--seed", type=int, default=0)
@@ -180,8 +182,11 @@ def main():
     else:
         ops = TorchOps()
     t_load = time.time()
-    tgt = HybridTarget(cfg, random_target_source(cfg, args.seed), rt, device=device, dtype=torch.bfloat16,
-                       ops=ops, comm=comm)
+    tsrc = random_target_source(cfg, args.seed)
+    if args.weights == "mxfp8":
+        from qwen38_b200.checkpoint import MXFP8Source
+        tsrc = MXFP8Source(tsrc)
+    tgt = HybridTarget(cfg, tsrc, rt, device=device, dtype=torch.bfloat16, ops=ops, comm=comm)
     if args.drafter == "dflash2":
         import dataclasses
         from qwen38_b200.checkpoint import random_window_drafter_source
@@ -259,7 +264,7 @@ def main():
             "config": {"model": f"{args.model}-hybrid-27B-class" if args.model == "full" else "tiny",
                        "layers": cfg.num_hidden_layers, "global_batch": 1, "seq_len": args.ctx,
                        "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows, "prefill_chunk": args.prefill_chunk,
-                       "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers,
+                       "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers, "weights": args.weights,
                        "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),

@@ -214,12 +214,14 @@ class SafetensorsSource(TensorSource):
         from safetensors import safe_open
         self.path, self.prefix = path, prefix
         self.block = (128, 128)
+        self.mx_block = MX_BLOCK
         cfg_path = os.path.join(path, "config.json")
         if os.path.exists(cfg_path):
             with open(cfg_path) as f:
                 qc = json.load(f).get("quantization_config") or {}
             if qc.get("weight_block_size"):
                 self.block = tuple(int(b) for b in qc["weight_block_size"])
+            self.mx_block = int(qc.get("mx_block_size", MX_BLOCK))
         index = os.path.join(path, "model.safetensors.index.json")
         if os.path.exists(index):
             with open(index) as f:
@@ -238,7 +240,7 @@ class SafetensorsSource(TensorSource):
 
     def names(self):
         return [k[len(self.prefix):] for k in self._where
-                if k.startswith(self.prefix) and not k.endswith("_scale_inv")]
+                if k.startswith(self.prefix) and not k.endswith(("_scale_inv", "_scale_e8m0"))]
 
     def get(self, name, device=None, dtype=None):
         key = self.prefix + name
@@ -246,6 +248,9 @@ class SafetensorsSource(TensorSource):
         if t.dtype == torch.float8_e4m3fn and key + "_scale_inv" in self._where:
             sk = key + "_scale_inv"
             t = dequant_fp8_block(t, self._handles[self._where[sk]].get_tensor(sk), self.block)
+        elif t.dtype == torch.float8_e4m3fn and key + "_scale_e8m0" in self._where:
+            sk = key + "_scale_e8m0"
+            t = dequant_mxfp8(t, self._handles[self._where[sk]].get_tensor(sk), self.mx_block)
         if device is not None:
             t = t.to(device)
         if dtype is not None and t.is_floating_point() and not name.endswith(("A_log", "dt_bias")):
@@ -319,6 +324,57 @@ def dequant_fp8_block(q: torch.Tensor, scale_inv: torch.Tensor, block=(128, 128)
     return q.float() * s
 
 
+MX_BLOCK = 32
+E4M3_EMAX = 8          # largest normal e4m3 value is 1.75 * 2^8 = 448
+
+
+def quant_mxfp8(w: torch.Tensor, block: int = MX_BLOCK):
+    """2-D weight -> (float8_e4m3fn values [N, K], E8M0 scales uint8 [N, ceil(K / block)]).
+
+    OCP Microscaling (MX) v1.0 format: every ``block`` consecutive elements of a row share one
+    power-of-two scale X = 2^(floor(log2(amax)) - emax(e4m3)); elements are stored as e4m3 of
+    w / X (saturated to +-448) and the scale as its biased exponent (bias 127)."""
+    N, K = w.shape
+    kb = -(-K // block)
+    wp = torch.zeros(N, kb * block, dtype=torch.float32, device=w.device)
+    wp[:, :K] = w.float()
+    blocks = wp.view(N, kb, block)
+    amax = blocks.abs().amax(-1)
+    exp = torch.where(amax > 0, torch.floor(torch.log2(amax.clamp(min=torch.finfo(torch.float32).tiny))),
+                      torch.full_like(amax, -127.0)) - E4M3_EMAX
+    exp = exp.clamp(-127, 127)
+    scale = torch.exp2(exp)
+    q = (blocks / scale[..., None]).clamp(-448.0, 448.0).to(torch.float8_e4m3fn)
+    return q.view(N, kb * block)[:, :K].contiguous(), (exp + 127).to(torch.uint8).contiguous()
+
+
+def dequant_mxfp8(q: torch.Tensor, scale_e8m0: torch.Tensor, block: int = MX_BLOCK) -> torch.Tensor:
+    """fp32 weight from MXFP8 storage (exact: an e4m3 value times a power of two)."""
+    N, K = q.shape
+    s = torch.exp2(scale_e8m0.float() - 127.0).repeat_interleave(block, 1)[:, :K]
+    return q.float() * s
+
+
+class MXFP8Source(TensorSource):
+    """Serves the base source's linear-layer weights as their MXFP8 round trip (e4m3 values with
+    32-element power-of-two scales, dequantised exactly), everything else unchanged: a model built
+    from it computes with exactly the weights an MXFP8 checkpoint holds."""
+
+    def __init__(self, base: TensorSource, block: int = MX_BLOCK):
+        self.base, self.block = base, block
+
+    def names(self):
+        return self.base.names()
+
+    def get(self, name, device=None, dtype=None):
+        t = self.base.get(name, device=device, dtype=torch.float32).float()     # quantised where it lives
+        if _fp8_quantised(name, t):
+            t = dequant_mxfp8(*quant_mxfp8(t, self.block), self.block)
+        if dtype is not None and t.is_floating_point() and not name.endswith(("A_log", "dt_bias")):
+            t = t.to(dtype)
+        return t
+
+
 def _fp8_quantised(name: str, t: torch.Tensor) -> bool:
     """Linear-layer weights are quantised; embeddings, LM head, norms and gate parameters stay."""
     return t.dim() == 2 and name.endswith(("proj.weight", "proj_qkv.weight", "proj_z.weight", "fc.weight"))
@@ -341,17 +397,24 @@ def materialize(src: TensorSource, device="cpu", dtype=torch.float32) -> dict:
 
 
 def save_pretrained(path: str, cfg: ModelConfig, src: TensorSource, dtype=torch.bfloat16,
-                    shard_bytes: int = 4 << 30, drafter: tuple | None = None, fp8_block: tuple | None = None):
+                    shard_bytes: int = 4 << 30, drafter: tuple | None = None, fp8_block: tuple | None = None,
+                    mxfp8: bool = False):
     """Write ``config.json`` and (sharded) ``model.safetensors`` in HF layout.  ``drafter`` is an
     optional ``(DrafterConfig, TensorSource)`` written under ``path/drafter``.  ``fp8_block``
-    (e.g. ``(128, 128)``) stores linear-layer weights as block-scaled FP8."""
+    (e.g. ``(128, 128)``) stores linear-layer weights as block-scaled FP8; ``mxfp8`` stores them as
+    MXFP8 (e4m3 values, one E8M0 scale per 32 elements of a row in ``<name>_scale_e8m0``)."""
     from safetensors.torch import save_file
+    if fp8_block and mxfp8:
+        raise ValueError("choose one weight quantisation")
     os.makedirs(path, exist_ok=True)
     meta = {"model_type": "qwen3_5", "architectures": ["Qwen3_5ForConditionalGeneration"],
             "text_config": cfg.to_hf_text_config(), "tie_word_embeddings": cfg.tie_word_embeddings}
     if fp8_block:
         meta["quantization_config"] = {"quant_method": "fp8", "fmt": "e4m3", "activation_scheme": "dynamic",
                                        "weight_block_size": list(fp8_block)}
+    if mxfp8:
+        meta["quantization_config"] = {"quant_method": "mxfp8", "fmt": "e4m3", "scale_fmt": "e8m0",
+                                       "activation_scheme": "none", "mx_block_size": MX_BLOCK}
     with open(os.path.join(path, "config.json"), "w") as f:
         json.dump(meta, f, indent=1)
     shards, cur, size = [], {}, 0
@@ -364,6 +427,13 @@ def save_pretrained(path: str, cfg: ModelConfig, src: TensorSource, dtype=torch.
                     q, si = quant_fp8_block(t, fp8_block)
                     yield n, q
                     yield n + "_scale_inv", si
+                    continue
+            if mxfp8:
+                t = src.get(n, dtype=torch.float32)
+                if _fp8_quantised(n, t):
+                    q, se = quant_mxfp8(t)
+                    yield n, q
+                    yield n + "_scale_e8m0", se
                     continue
             yield n, src.get(n, dtype=dtype).contiguous()
 

@@ -29,6 +29,17 @@ def _model(rc: RunConfig):
     return cfg, dcfg, rc.model
 
 
+def _is_mxfp8_checkpoint(path) -> bool:
+    if not path:
+        return False
+    import json
+    cfg = os.path.join(path, "config.json")
+    if not os.path.exists(cfg):
+        return False
+    with open(cfg) as f:
+        return (json.load(f).get("quantization_config") or {}).get("quant_method") == "mxfp8"
+
+
 def _checkpoint_id(path: str) -> str:
     """Identity of a checkpoint directory for the weight cache: its path, and the names, sizes and
     modification times of its files."""
@@ -69,9 +80,12 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
                          peer=native and rc.parallel.comm != "nccl", fused=rc.parallel.comm == "fused")
     slots = rc.serving.slots
     src = SafetensorsSource(ckpt) if ckpt else random_target_source(cfg, seed)
+    if rc.runtime.weight_format == "mxfp8" and not _is_mxfp8_checkpoint(ckpt):
+        from ..checkpoint import MXFP8Source
+        src = MXFP8Source(src)              # compute with the MXFP8 round trip of the weights
     if ckpt and rc.weight_cache:
         from ..checkpoint import CachedSource
-        src = CachedSource(src, rc.weight_cache, base_id=_checkpoint_id(ckpt))
+        src = CachedSource(src, rc.weight_cache, base_id=_checkpoint_id(ckpt) + ":" + rc.runtime.weight_format)
     rt = rc.runtime
     tgt = HybridTarget(cfg, src, rt, device=device, dtype=dtype, ops=ops, comm=comm, max_slots=slots + 1,
                        max_verify_rows=slots * rc.spec.block_rows)

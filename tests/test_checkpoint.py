@@ -98,3 +98,52 @@ def test_factory_weight_cache(tmp_path):
     assert len([f for f in os.listdir(cache) if f.endswith(".safetensors")]) > 10
     p = list(range(5, 40))
     assert greedy_reference(eng.target, p, 8) == greedy_reference(plain.target, p, 8)
+
+
+def test_mxfp8_quantisation():
+    """OCP MX e4m3 with 32-element power-of-two scales: scale exponent floor(log2 amax) - 8, values
+    within e4m3 precision, dequantised weights exact in bf16."""
+    from qwen38_b200.checkpoint import dequant_mxfp8, quant_mxfp8
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(64, 100, generator=g) * torch.logspace(-3, 2, 100)[None, :]
+    q, se = quant_mxfp8(w)
+    assert q.dtype == torch.float8_e4m3fn and q.shape == w.shape and se.shape == (64, 4) and se.dtype == torch.uint8
+    d = dequant_mxfp8(q, se)
+    assert torch.equal(d.bfloat16().float(), d)                          # exact in bf16
+    blocks = torch.nn.functional.pad(w, (0, 28)).view(64, 4, 32)
+    amax = blocks.abs().amax(-1)
+    assert torch.equal(se.long(), (torch.floor(torch.log2(amax)) - 8 + 127).long())
+    scale = torch.exp2(se.float() - 127).repeat_interleave(32, 1)[:, :100]
+    err = (d - w).abs()
+    sat = w.abs() > 448 * scale                                           # saturated by the MX rule
+    assert bool((err[~sat] <= torch.maximum(w.abs()[~sat] * 2.0 ** -4, scale[~sat] * 2.0 ** -9)).all())
+    z, sz = quant_mxfp8(torch.zeros(2, 32))
+    assert torch.equal(dequant_mxfp8(z, sz), torch.zeros(2, 32))
+
+
+def test_mxfp8_checkpoint_and_weight_format(tmp_path):
+    """An MXFP8 checkpoint reads back the MXFP8 round trip of its weights; runtime.weight_format=mxfp8
+    builds the same model from bf16 weights; norms and embeddings stay unquantised."""
+    from qwen38_b200.checkpoint import MXFP8Source, random_target_source, save_pretrained
+    from qwen38_b200.config import tiny_model_config
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.spec.engine import greedy_reference
+    cfg = tiny_model_config()
+    src = random_target_source(cfg, 0)
+    ck = str(tmp_path / "mx")
+    save_pretrained(ck, cfg, src, dtype=torch.float32, mxfp8=True)
+    st = SafetensorsSource(ck)
+    mx = MXFP8Source(src)
+    for n in st.names():
+        assert torch.equal(st.get(n, dtype=torch.float32), mx.get(n, dtype=torch.float32)), n
+    name = next(n for n in st.names() if n.endswith("mlp.down_proj.weight"))
+    assert not torch.equal(mx.get(name, dtype=torch.float32), src.get(name, dtype=torch.float32))
+    assert torch.equal(mx.get("model.norm.weight"), src.get("model.norm.weight"))
+    p = list(range(7, 50))
+    a = build_engine(load_run_config(None, profile="tiny-cpu", overrides=["spec.drafter=none", f"model={ck}"]))
+    ck2 = str(tmp_path / "bf")
+    save_pretrained(ck2, cfg, src, dtype=torch.float32)
+    b = build_engine(load_run_config(None, profile="tiny-cpu", overrides=[
+        "spec.drafter=none", f"model={ck2}", "runtime.weight_format=mxfp8"]))
+    assert greedy_reference(a.target, p, 10) == greedy_reference(b.target, p, 10)
