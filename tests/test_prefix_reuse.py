@@ -74,3 +74,58 @@ def test_registry_budget_pins_and_kill_switch(tiny, tmp_path):
     assert reg.lookup(b) is None and reg.export_stats()["disabled"]
     reg.clear()
     assert tgt.allocator.num_free == tgt.allocator.num_blocks
+
+
+def _tp_rank(rank, port, q):
+    import os
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        from qwen38_b200.checkpoint import random_drafter_source, random_target_source
+        from qwen38_b200.config import tiny_drafter_config, tiny_model_config
+        from qwen38_b200.parallel.comm import TorchComm
+        cfg, dcfg = tiny_model_config(), tiny_drafter_config()
+        tgt = HybridTarget(cfg, random_target_source(cfg, 0), RT, comm=TorchComm(), max_slots=2)
+        dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt)
+        a, b = _prompts(None)
+        gold_b = greedy_reference(tgt, b, 24)
+        seq = tgt.new_sequence()
+        tgt.prefill(seq, torch.tensor(b))
+        cold = tgt.rec[seq.slot].clone()
+        tgt.release(seq)
+        reg = PrefixRegistry(tgt, budget_bytes=1 << 30, boundary=64)
+        sr = SpecRuntime(tgt, dr, verifier_rows=4, prefix=reg)
+        sr.generate(a, 24)
+        rb = sr.generate(b, 24, gold_check=gold_b)
+        ck = reg.lookup(b)
+        seq = reg.restore(ck, dr)
+        tgt.prefill(seq, torch.tensor(b[ck.pos:]))
+        exact = torch.equal(tgt.rec[seq.slot], cold)
+        tgt.release(seq)
+        q.put((rank, rb["reused_prefix"], rb["tokens"] == gold_b, exact))
+    except BaseException as e:
+        q.put((rank, repr(e), False, False))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_prefix_reuse_tp2_gloo():
+    """BASELINE config 4 at TP2 (gloo ranks): the second request reuses the 128-token prefix on both
+    ranks, stays token-exact, and each rank's restored + suffix GDN state equals its cold prefill."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_tp_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    for rank, reused, exact_tokens, exact_state in out:
+        assert reused == 128, reused
+        assert exact_tokens and exact_state
