@@ -8,6 +8,11 @@ is stepped in real time; reported: aggregate committed tok/s over the run and pe
 bench reports them (``scripts/ci/longctx_cycle_bench.py``, ``docs/baseline-2026-09-05.md``).
 
     python -m qwen38_b200.serving.loadgen --model full --streams 8 --rate 2 --prompt-len 4096 --new-tokens 256
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 -m qwen38_b200.serving.loadgen --model full \
+        --streams 32 --rate 2 --prompt-len 32768 --new-tokens 512 --weights mxfp8
+
+Under torchrun every rank runs the engine tensor-parallel; rank 0's clock decides which arrivals are
+due before each step and the others follow it, so every rank admits the same requests in lockstep.
 """
 from __future__ import annotations
 
@@ -32,15 +37,24 @@ def poisson_arrivals(n: int, rate: float, seed: int):
 
 
 def run(engine, prompts, new_tokens: int, arrivals, *, golds=None, mean_accepted: int = 6, seed: int = 0,
-        clock=time.perf_counter, sync=None):
-    """Feeds requests at their arrival times and steps until all finish; returns the report."""
+        clock=time.perf_counter, sync=None, agree=None):
+    """Feeds requests at their arrival times and steps until all finish; returns the report.
+
+    ``agree(n)``: under tensor parallelism every rank must admit the same requests before the same
+    step, so the number of arrivals due is decided by one rank's clock and shared (rank 0's value,
+    one small broadcast per step); None on one rank."""
     order = sorted(range(len(prompts)), key=lambda i: arrivals[i])
     t0 = clock()
     nxt = 0
     reqs = [None] * len(prompts)
     while nxt < len(order) or engine.has_work():
         now = clock() - t0
-        while nxt < len(order) and arrivals[order[nxt]] <= now:
+        due = nxt
+        while due < len(order) and arrivals[order[due]] <= now:
+            due += 1
+        if agree is not None:
+            due = agree(due)
+        while nxt < due:
             i = order[nxt]
             pinned = PinnedAcceptance(golds[i], seed=seed + i, mean_accepted=mean_accepted) if golds else None
             reqs[i] = engine.add_request(prompts[i], new_tokens, pinned=pinned, request_id=f"s{i}")
@@ -85,29 +99,51 @@ def main():
     ap.add_argument("--mean-accepted", type=int, default=6)
     ap.add_argument("--no-pinned", action="store_true")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--weights", default="bf16", choices=["bf16", "mxfp8"])
+    ap.add_argument("--comm", default="fused", choices=["fused", "peer", "nccl"])
     a = ap.parse_args()
+    from ..parallel.comm import init_distributed, make_comm
+    rank, world, local = init_distributed()
     cuda = torch.cuda.is_available()
+    if cuda:
+        torch.cuda.set_device(local)
+    dev = torch.device("cuda", local) if cuda else torch.device("cpu")
     cfg, dcfg = (full_model_config(), full_drafter_config()) if a.model == "full" else \
         (tiny_model_config(), tiny_drafter_config())
     ops = None
     max_ctx = a.prompt_len + a.new_tokens + 64
     if cuda:
         from ..ops.native import NativeOps
-        ops = NativeOps(max_keys=max_ctx + 64)
-    rt = RuntimeConfig(max_context=max_ctx)
-    tgt = HybridTarget(cfg, random_target_source(cfg, a.seed), rt, device="cuda" if cuda else "cpu",
-                       dtype=torch.bfloat16 if cuda else torch.float32, ops=ops, max_slots=a.streams + 1,
-                       max_verify_rows=a.streams * dcfg.block_rows)
+        ops = NativeOps(device=dev, max_keys=max_ctx + 64)
+    rt = RuntimeConfig(max_context=max_ctx, weight_format=a.weights)
+    comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=cuda and a.comm != "nccl",
+                     fused=a.comm == "fused")
+    tsrc = random_target_source(cfg, a.seed)
+    if a.weights == "mxfp8":
+        from ..checkpoint import MXFP8Source
+        tsrc = MXFP8Source(tsrc)
+    tgt = HybridTarget(cfg, tsrc, rt, device=dev, dtype=torch.bfloat16 if cuda else torch.float32, ops=ops,
+                       comm=comm, max_slots=a.streams + 1, max_verify_rows=a.streams * dcfg.block_rows)
     dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, a.seed + 1), tgt, slots=a.streams)
     g = torch.Generator().manual_seed(a.seed)
     prompts = [torch.randint(0, cfg.vocab_size, (a.prompt_len,), generator=g).tolist() for _ in range(a.streams)]
     golds = None if a.no_pinned else [greedy_reference(tgt, p, a.new_tokens) for p in prompts]
     eng = ServingEngine(tgt, dr, verifier_rows=dcfg.block_rows)
+    agree = None
+    if world > 1:
+        import torch.distributed as dist
+
+        def agree(n):
+            t = torch.tensor([n], dtype=torch.int64, device=dev if dist.get_backend() == "nccl" else "cpu")
+            dist.broadcast(t, 0)
+            return int(t.item())
     rep = run(eng, prompts, a.new_tokens, poisson_arrivals(a.streams, a.rate, a.seed), golds=golds,
-              mean_accepted=a.mean_accepted, seed=a.seed, sync=torch.cuda.synchronize if cuda else None)
+              mean_accepted=a.mean_accepted, seed=a.seed, sync=torch.cuda.synchronize if cuda else None,
+              agree=agree)
     rep.update(model=a.model, prompt_len=a.prompt_len, new_tokens=a.new_tokens, rate=a.rate,
-               weights="bf16", device="cuda" if cuda else "cpu")
-    print(json.dumps(rep))
+               weights=a.weights, tp=world, device=dev.type)
+    if rank == 0:
+        print(json.dumps(rep))
 
 
 if __name__ == "__main__":

@@ -264,3 +264,55 @@ def test_real_text_concurrent_equals_sequential():
     rep = compare(eng, prompts, max_tokens=16)
     assert rep["passed"], rep
     assert all(r["tokens"] == 16 for r in rep["prompts"])
+
+
+def _loadgen_rank(rank, port, q):
+    import os
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        from qwen38_b200.checkpoint import MXFP8Source, random_drafter_source, random_target_source
+        from qwen38_b200.config import tiny_drafter_config, tiny_model_config
+        from qwen38_b200.parallel.comm import TorchComm
+        from qwen38_b200.serving.loadgen import poisson_arrivals, run
+        cfg, dcfg = tiny_model_config(), tiny_drafter_config()
+        tgt = HybridTarget(cfg, MXFP8Source(random_target_source(cfg, 0)), RuntimeConfig(max_context=512),
+                           comm=TorchComm(), max_slots=4, max_verify_rows=3 * dcfg.block_rows)
+        dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, slots=3)
+        g = torch.Generator().manual_seed(0)
+        prompts = [torch.randint(0, cfg.vocab_size, (80,), generator=g).tolist() for _ in range(3)]
+        golds = [greedy_reference(tgt, p, 12) for p in prompts]
+
+        def agree(n):
+            t = torch.tensor([n])
+            dist.broadcast(t, 0)
+            return int(t.item())
+        rep = run(ServingEngine(tgt, dr, verifier_rows=dcfg.block_rows), prompts, 12,
+                  poisson_arrivals(3, 50.0, 0), golds=golds, mean_accepted=1, agree=agree)
+        q.put((rank, rep["finished"], rep["exact"], rep["decode_steps"]))
+    except BaseException as e:
+        q.put((rank, repr(e), False, -1))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_loadgen_tp2_ranks_admit_in_lockstep():
+    """Two gloo ranks with MXFP8 weights: rank 0's clock decides the arrivals, both ranks run the
+    same steps, every stream finishes token-exact."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_loadgen_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = sorted(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert out[0][1:] == out[1][1:], out
+    assert out[0][1] == 3 and out[0][2] is True
