@@ -8,7 +8,9 @@ their completion, so requests arriving concurrently are continuously batched int
 Endpoints: ``POST /v1/completions`` (``prompt`` as a list of token ids, or a string encoded with
 the byte-level fallback tokenizer below - checkpoints' own tokenizers need network access to
 fetch), ``POST /v1/chat/completions`` (``messages`` rendered with a plain role template),
-``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  With ``"stream": true``
+``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  ``"logprobs": k`` on a
+non-streaming completion returns each output token's log-probability and the top k, scored on the
+engine thread by the model's own final norm and LM head (TP=1).  With ``"stream": true``
 both generation endpoints answer with server-sent events, one event per engine step that emitted
 tokens (a speculative block commits several tokens at once), then ``data: [DONE]``.
 
@@ -41,6 +43,7 @@ class CompletionRequest(BaseModel):
     seed: int | None = None
     stream: bool = False
     stream_options: StreamOptions | None = None
+    logprobs: int | None = None       # > 0: log-probability of each output token and the top-k
 
 
 class ChatMessage(BaseModel):
@@ -84,8 +87,19 @@ class EngineLoop:
         self.idle_sleep = idle_sleep
         self.stop_event = threading.Event()
         self.completed = self.aborted = self.tokens = 0
+        self.calls: "queue.Queue" = queue.Queue()
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
+
+    def call(self, fn, timeout: float = 600.0):
+        """Run ``fn()`` on the engine thread between two steps (the model is not thread-safe)."""
+        done, box = threading.Event(), {}
+        self.calls.put((fn, done, box))
+        if not done.wait(timeout):
+            raise TimeoutError("engine call timed out")
+        if "error" in box:
+            raise box["error"]
+        return box["value"]
 
     def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0, stream=False):
         """Queue a request.  Returns (done event, result box); with ``stream`` the box's "stream"
@@ -97,6 +111,13 @@ class EngineLoop:
 
     def _run(self):
         while not self.stop_event.is_set():
+            while not self.calls.empty():
+                fn, done, box = self.calls.get_nowait()
+                try:
+                    box["value"] = fn()
+                except Exception as e:          # handed back to the caller's thread
+                    box["error"] = e
+                done.set()
             try:
                 while True:
                     prompt, n, eos, done, box, temp, seed = self.inbox.get_nowait()
@@ -208,9 +229,27 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             yield "data: " + json.dumps(chunk(new, None)) + "\n\n"
         yield "data: [DONE]\n\n"
 
+    def _logprobs(ids, out, k):
+        """OpenAI completions ``logprobs`` object: each output token's log-probability and the top
+        k, scored by the engine's own final norm and LM head on the engine thread."""
+        from ..utils.tp_agreement import score
+        if engine.target.tp > 1:
+            raise HTTPException(400, "logprobs are served at TP=1")
+        try:
+            chosen, ti, tv = loop.call(lambda: score(engine.target, ids, out, top_k=k))
+        except MemoryError:
+            raise HTTPException(503, "no free sequence slot to score the output")
+        return {"tokens": [tok.decode([t]) for t in out], "token_ids": out,
+                "token_logprobs": [float(v) for v in chosen],
+                "top_logprobs": [{tok.decode([int(i)]): float(v) for i, v in zip(ir, vr)}
+                                 for ir, vr in zip(ti.tolist(), tv.tolist())],
+                "top_token_ids": ti.tolist()}
+
     @app.post("/v1/completions")
     def completions(body: CompletionRequest):
         ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
+        if body.logprobs is not None and (body.logprobs < 0 or body.logprobs > 20 or body.stream):
+            raise HTTPException(400, "logprobs: 0..20, non-streaming requests")
         done, box = _start(ids, body)
         cid, created, model = "cmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
         if body.stream:
@@ -219,9 +258,11 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                         "choices": [{"index": 0, "text": tok.decode(new), "token_ids": new, "finish_reason": reason}]}
             return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
+        lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
         return {
             "id": cid, "object": "text_completion", "created": created, "model": model,
-            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "finish_reason": _finish_reason(out, body)}],
+            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "logprobs": lp,
+                         "finish_reason": _finish_reason(out, body)}],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                       "total_tokens": len(ids) + len(out)},
         }

@@ -316,3 +316,29 @@ def test_loadgen_tp2_ranks_admit_in_lockstep():
         p.join(timeout=60)
     assert out[0][1:] == out[1][1:], out
     assert out[0][1] == 3 and out[0][2] is True
+
+
+def test_completion_logprobs():
+    """``logprobs`` on a greedy completion: every output token is its own row's top-1, with a
+    non-positive log-probability; streaming requests refuse the option."""
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=2"]))
+    app = build_app(eng)
+    with TestClient(app) as client:
+        r = client.post("/v1/completions", json={"prompt": list(range(20, 60)), "max_tokens": 10, "logprobs": 3})
+        assert r.status_code == 200, r.text
+        ch = r.json()["choices"][0]
+        lp = ch["logprobs"]
+        assert lp["token_ids"] == ch["token_ids"] and len(lp["token_logprobs"]) == 10
+        assert all(v <= 0 for v in lp["token_logprobs"])
+        assert all(top[0] == t for top, t in zip(lp["top_token_ids"], ch["token_ids"]))
+        assert all(len(d) <= 3 for d in lp["top_logprobs"])
+        assert client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 2}).json()["choices"][0][
+            "logprobs"] is None
+        bad = client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 2, "logprobs": 2, "stream": True})
+        assert bad.status_code == 400
+    app.state.loop.close()
