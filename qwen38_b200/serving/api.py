@@ -243,7 +243,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 "token_logprobs": [float(v) for v in chosen],
                 "top_logprobs": [{tok.decode([int(i)]): float(v) for i, v in zip(ir, vr)}
                                  for ir, vr in zip(ti.tolist(), tv.tolist())],
-                "top_token_ids": ti.tolist()}
+                "top_token_ids": ti.tolist(), "top_token_logprobs": tv.tolist()}
 
     @app.post("/v1/completions")
     def completions(body: CompletionRequest):

@@ -17,6 +17,7 @@ ids, so a run needs no corpus and no tokenizer download.
     torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m qwen38_b200.utils.tp_agreement collect \\
         --profile single-stream-4k --set parallel.tp=2 --out tp2.json
     python -m qwen38_b200.utils.tp_agreement compare tp1.json tp2.json --report agreement.json
+    python -m qwen38_b200.utils.tp_agreement collect --url http://127.0.0.1:8000 --tp 2 --out srv.json
 """
 from __future__ import annotations
 
@@ -95,6 +96,27 @@ def collect(target, prompts, max_tokens: int = 64, top_k: int = TOP_K, runtime=N
     return dict(schema=1, tp=int(getattr(target, "tp", 1)), top_k=top_k, prompts=recs)
 
 
+def collect_http(base_url: str, prompts, max_tokens: int = 64, top_k: int = TOP_K, model: str | None = None,
+                 tp: int | None = None, timeout: float = 1800.0):
+    """``collect`` through a running server's ``/v1/completions`` (greedy, ``logprobs=top_k``), as
+    the reference collects over the OpenAI API."""
+    import urllib.request
+    recs = []
+    for name, ids in prompts:
+        payload = dict(prompt=list(ids), max_tokens=max_tokens, temperature=0.0, logprobs=top_k)
+        if model:
+            payload["model"] = model
+        req = urllib.request.Request(base_url.rstrip("/") + "/v1/completions", json.dumps(payload).encode(),
+                                     {"Content-Type": "application/json"})
+        with urllib.request.urlopen(req, timeout=timeout) as resp:
+            ch = json.loads(resp.read())["choices"][0]
+        lp = ch["logprobs"]
+        recs.append(dict(name=name, prompt_sha256=hashlib.sha256(bytes(str(list(ids)), "utf-8")).hexdigest(),
+                         tokens=list(ch["token_ids"]), logprobs=list(lp["token_logprobs"]),
+                         top_ids=lp["top_token_ids"], top_logprobs=lp["top_token_logprobs"]))
+    return dict(schema=1, tp=tp, top_k=top_k, prompts=recs)
+
+
 def _coherent(tokens):
     return len(tokens) >= 2 and len(set(tokens)) / len(tokens) >= MIN_UNIQUE_RATIO
 
@@ -146,6 +168,8 @@ def main(argv=None):
     c.add_argument("--config", default=None)
     c.add_argument("--set", action="append", default=[])
     c.add_argument("--max-tokens", type=int, default=64)
+    c.add_argument("--url", default=None, help="collect through a running server's /v1/completions instead")
+    c.add_argument("--tp", type=int, default=None, help="TP degree of that server (recorded only)")
     c.add_argument("--out", required=True)
     m = sub.add_parser("compare")
     m.add_argument("ref")
@@ -163,6 +187,11 @@ def main(argv=None):
                 json.dump(rep, f, indent=1)
         print(json.dumps({k: v for k, v in rep.items() if k != "prompts"}))
         return 0 if rep["ok"] else 1
+    if a.url:
+        rec = collect_http(a.url, repo_prompts(), a.max_tokens, tp=a.tp)
+        with open(a.out, "w") as f:
+            json.dump(rec, f)
+        return 0
     from ..parallel.comm import init_distributed
     from ..runconfig import load_run_config
     from ..serving.factory import build_engine

@@ -99,3 +99,40 @@ def test_tp2_gloo_agrees_with_tp1(tiny):
         rep = compare(ref, rec)
         assert rep["ok"], rep
     assert out[0][1]["prompts"] == out[1][1]["prompts"]
+
+
+def test_http_collection_equals_in_process(tiny):
+    """Collecting through the server's logprobs gives the in-process record of the same engine."""
+    import threading
+    import time
+
+    import uvicorn
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.utils.tp_agreement import collect_http
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["spec.drafter=none", "serving.slots=1"]))
+    prompts = [(n, ids[:120]) for n, ids in _prompts()]
+    local = collect(eng.target, prompts, max_tokens=12, top_k=3)
+    app = build_app(eng)
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    server = uvicorn.Server(uvicorn.Config(app, host="127.0.0.1", port=port, log_level="warning"))
+    th = threading.Thread(target=server.run, daemon=True)
+    th.start()
+    try:
+        for _ in range(500):
+            if server.started:
+                break
+            time.sleep(0.01)
+        remote = collect_http(f"http://127.0.0.1:{port}", prompts, max_tokens=12, top_k=3, tp=1)
+    finally:
+        server.should_exit = True
+        th.join(timeout=30)
+        app.state.loop.close()
+    assert compare(local, remote)["ok"]
+    for a, b in zip(local["prompts"], remote["prompts"]):
+        assert a["tokens"] == b["tokens"] and a["top_ids"] == b["top_ids"]
+        assert max(abs(x - y) for x, y in zip(a["logprobs"], b["logprobs"])) < 1e-9
