@@ -117,6 +117,12 @@ class WindowDrafter(BlockDrafter):
         self._graphs = {}
         self._init_propose_buffers(dcfg.block_rows)
 
+    def history_floor(self, pos: int) -> int:
+        """Lowest history row a block at ``pos`` or later can still see: older rows are masked for
+        good, so a prefix checkpoint need not keep them (rows below it only have to stay finite,
+        which every row ever written or zero-initialised is)."""
+        return max(0, pos - self.window)
+
     # -------------------------------------------------------------------------------- propose
     def _branch_open(self, h, norm_w, w_kernel, base):
         """RMSNorm, the branch's dynamic kernels and its opening convolution -> (bf16 rows, kernels)."""

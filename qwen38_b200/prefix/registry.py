@@ -38,7 +38,7 @@ class Checkpoint:
     pos: int
     token_ids: array
     target: dict                   # HybridTarget.prefix_snapshot
-    drafter: dict | None           # {"k": [L, pos, kv, D], "v": ...}
+    drafter: dict | None           # {"lo": first row, "k": [L, pos - lo, kv, D], "v": ...}
     nbytes: int
     pins: int = 0
     serial: int = 0
@@ -144,7 +144,10 @@ class PrefixRegistry:
         if drafter is not None:
             if drafter.positions[dslot] < pos:
                 raise ValueError("drafter history behind the target at capture")
-            dsnap = {"k": drafter.kctx_all[dslot, :, :pos].clone(), "v": drafter.vctx_all[dslot, :, :pos].clone()}
+            # rows below the drafter's floor are never read again (a windowed drafter's older rows)
+            lo = drafter.history_floor(pos) if hasattr(drafter, "history_floor") else 0
+            dsnap = {"lo": lo, "k": drafter.kctx_all[dslot, :, lo:pos].clone(),
+                     "v": drafter.vctx_all[dslot, :, lo:pos].clone()}
             nbytes += 2 * dsnap["k"].numel() * dsnap["k"].element_size()
         if nbytes > self.budget:
             self.target.release_prefix(snap)
@@ -163,8 +166,9 @@ class PrefixRegistry:
         """New target sequence at ``ck.pos`` (and the drafter history rewound to the same rows)."""
         seq = self.target.sequence_from_prefix(ck.target)
         if drafter is not None and ck.drafter is not None:
-            drafter.kctx_all[dslot, :, :ck.pos].copy_(ck.drafter["k"])
-            drafter.vctx_all[dslot, :, :ck.pos].copy_(ck.drafter["v"])
+            lo = ck.drafter.get("lo", 0)
+            drafter.kctx_all[dslot, :, lo:ck.pos].copy_(ck.drafter["k"])
+            drafter.vctx_all[dslot, :, lo:ck.pos].copy_(ck.drafter["v"])
             drafter.positions[dslot] = ck.pos
         return seq
 

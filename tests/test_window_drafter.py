@@ -252,6 +252,8 @@ def test_window_drafter_prefix_reuse(tiny):
     cold.append(feats, 0)
     ck = reg.lookup(b)                # b's own deepest boundary by now
     assert ck is not None and 128 <= ck.pos < len(b)
+    # only the rows the window can still reach are kept
+    assert ck.drafter["lo"] == ck.pos - wcfg.window and ck.drafter["k"].shape[1] == wcfg.window
     seq = reg.restore(ck, dr)
     _, feats = tgt.prefill(seq, torch.tensor(b[ck.pos:]), taps=wcfg.taps)
     tgt.release(seq)
