@@ -50,9 +50,13 @@ class ServingEngine:
             raise ValueError("empty prompt")
         if any(not 0 <= t < self.target.cfg.vocab_size for t in prompt):
             raise ValueError("token outside the vocabulary")
+        if int(max_new_tokens) < 1:
+            raise ValueError("max_new_tokens must be >= 1")
         if len(prompt) + max_new_tokens + self.verifier_rows > self.target.rt.max_context:
             raise ValueError("prompt + budget exceed max_context")
         rid = request_id or f"req-{next(self._ids)}"
+        if rid in self.requests and self.requests[rid].state not in (FINISHED, ABORTED):
+            raise ValueError(f"request id {rid!r} is already in flight")
         if temperature < 0:
             raise ValueError("temperature must be >= 0")
         req = Request(rid, prompt, max_new_tokens, tuple(eos_ids), self.clock(), pinned,

@@ -342,3 +342,22 @@ def test_completion_logprobs():
         bad = client.post("/v1/completions", json={"prompt": [5, 6], "max_tokens": 2, "logprobs": 2, "stream": True})
         assert bad.status_code == 400
     app.state.loop.close()
+
+
+def test_request_validation(tiny):
+    """Bad budgets and a request id already in flight are refused at admission."""
+    import pytest
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16),
+                       max_slots=3)
+    eng = ServingEngine(tgt, None, verifier_rows=4)
+    with pytest.raises(ValueError):
+        eng.add_request([1, 2, 3], 0)
+    with pytest.raises(ValueError):
+        eng.add_request([1, 2, 3], 600)
+    eng.add_request([1, 2, 3], 4, request_id="x")
+    with pytest.raises(ValueError):
+        eng.add_request([4, 5], 4, request_id="x")
+    done = {r.request_id for r in eng.run()}
+    assert "x" in done
+    eng.add_request([4, 5], 4, request_id="x")          # finished ids may be reused
+    assert {r.request_id for r in eng.run()} == {"x"}
