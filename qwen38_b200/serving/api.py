@@ -16,6 +16,8 @@ tokens (a speculative block commits several tokens at once), then ``data: [DONE]
 
 Run:  python -m qwen38_b200.serving.api --profile single-stream-4k --set serving.port=8000
       python -m qwen38_b200.serving.api --profile tiny-cpu            (CPU, tiny shape)
+      torchrun --nproc-per-node 2 --master-addr 127.0.0.1 -m qwen38_b200.serving.api \
+          --profile single-stream-4k --set parallel.tp=2              (TP2: rank 0 serves HTTP)
 """
 from __future__ import annotations
 
@@ -25,6 +27,7 @@ import threading
 import time
 import uuid
 
+import torch
 from pydantic import BaseModel
 
 from .scheduler import ABORTED, FINISHED
@@ -78,10 +81,17 @@ class ByteTokenizer:
 
 
 class EngineLoop:
-    """Owns the engine: a background thread admits queued requests and steps the scheduler."""
+    """Owns the engine: a background thread admits queued requests and steps the scheduler.
 
-    def __init__(self, engine, idle_sleep: float = 0.001):
+    Tensor parallel (one process per GPU): rank 0 runs this loop and the HTTP server; before each
+    iteration it hands ``sync`` the requests it admitted and whether it steps, and the other ranks,
+    running ``follow``, admit the same requests under the same ids and take the same step, so every
+    rank's engine runs in lockstep.  While idle, rank 0 still syncs every ``heartbeat_s`` so the
+    followers' waiting collective never runs into the process-group timeout."""
+
+    def __init__(self, engine, idle_sleep: float = 0.001, sync=None, heartbeat_s: float = 1.0):
         self.engine = engine
+        self.sync, self.heartbeat_s = sync, heartbeat_s
         self.inbox: "queue.Queue" = queue.Queue()
         self.waiters: dict = {}
         self.idle_sleep = idle_sleep
@@ -110,7 +120,9 @@ class EngineLoop:
         return done, box
 
     def _run(self):
-        while not self.stop_event.is_set():
+        last_sync = time.monotonic()
+        while True:
+            stop = self.stop_event.is_set()
             while not self.calls.empty():
                 fn, done, box = self.calls.get_nowait()
                 try:
@@ -118,13 +130,15 @@ class EngineLoop:
                 except Exception as e:          # handed back to the caller's thread
                     box["error"] = e
                 done.set()
+            adds = []
             try:
-                while True:
+                while not stop:
                     prompt, n, eos, done, box, temp, seed = self.inbox.get_nowait()
                     try:
                         req = self.engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed)
                         box["sent"] = 0
                         self.waiters[req.request_id] = (done, box, req)
+                        adds.append((req.request_id, list(req.prompt), n, eos, temp, seed))
                     except Exception as e:          # invalid request: answer at once
                         box["error"] = str(e)
                         if "stream" in box:
@@ -132,7 +146,13 @@ class EngineLoop:
                         done.set()
             except queue.Empty:
                 pass
-            if not self.engine.has_work():
+            step = not stop and self.engine.has_work()
+            if self.sync is not None and (adds or step or stop or time.monotonic() - last_sync >= self.heartbeat_s):
+                self.sync({"add": adds, "step": step, "stop": stop})
+                last_sync = time.monotonic()
+            if stop:
+                break
+            if not step:
                 time.sleep(self.idle_sleep)
                 continue
             finished = self.engine.step()
@@ -162,15 +182,39 @@ class EngineLoop:
         self.thread.join(timeout=10)
 
 
+def broadcast_sync(group=None):
+    """``sync`` for ``EngineLoop`` / ``follow``: rank 0's command object, broadcast to every rank."""
+    import torch.distributed as dist
+
+    def sync(cmd):
+        box = [cmd]
+        dist.broadcast_object_list(box, src=0, group=group)
+        return box[0]
+    return sync
+
+
+def follow(engine, sync):
+    """Rank > 0 of a tensor-parallel server: admit what rank 0 admitted, step when it steps, return
+    when it stops."""
+    while True:
+        cmd = sync(None)
+        for rid, prompt, n, eos, temp, seed in cmd["add"]:
+            engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed, request_id=rid)
+        if cmd["stop"]:
+            return
+        if cmd["step"]:
+            engine.step()
+
+
 def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0,
-              output_budget_multiple: int = 0):
+              output_budget_multiple: int = 0, sync=None):
     import json
 
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import PlainTextResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
-    loop = EngineLoop(engine)
+    loop = EngineLoop(engine, sync=sync)
     app = FastAPI(title="qwen38_b200")
     app.state.loop = loop
 
@@ -327,9 +371,21 @@ def main():
     ap.add_argument("--set", action="append", default=[], metavar="SECTION.FIELD=VALUE")
     a = ap.parse_args()
     rc = load_run_config(a.config, profile=a.profile, overrides=a.set)
-    eng = build_engine(rc)
+    from ..parallel.comm import init_distributed
+    rank, world, local = init_distributed()
+    if world != rc.parallel.tp:
+        raise SystemExit(f"parallel.tp={rc.parallel.tp} but {world} processes: launch one per GPU with torchrun")
+    device = None
+    if torch.cuda.is_available() and rc.kernels.ops == "native":
+        torch.cuda.set_device(local)
+        device = torch.device("cuda", local)
+    eng = build_engine(rc, device=device)
+    sync = broadcast_sync() if world > 1 else None
+    if rank > 0:
+        follow(eng, sync)                       # rank 0 serves HTTP; the others follow its steps
+        return
     app = build_app(eng, timeout_s=rc.serving.request_timeout_s,
-                    output_budget_multiple=rc.serving.output_budget_multiple)
+                    output_budget_multiple=rc.serving.output_budget_multiple, sync=sync)
     uvicorn.run(app, host=rc.serving.host, port=rc.serving.port)
 
 

@@ -361,3 +361,65 @@ def test_request_validation(tiny):
     assert "x" in done
     eng.add_request([4, 5], 4, request_id="x")          # finished ids may be reused
     assert {r.request_id for r in eng.run()} == {"x"}
+
+
+def _serve_rank(rank, port, q):
+    import os
+    import time
+
+    import torch.distributed as dist
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=2)
+    try:
+        from qwen38_b200.parallel.comm import TorchComm
+        from qwen38_b200.runconfig import load_run_config
+        from qwen38_b200.serving.api import EngineLoop, broadcast_sync, follow
+        from qwen38_b200.serving.factory import build_engine
+        rc = load_run_config(profile="tiny-cpu", overrides=["parallel.tp=2", "serving.slots=3"])
+        eng = build_engine(rc, comm=TorchComm())
+        sync = broadcast_sync()
+        if rank > 0:
+            follow(eng, sync)
+            q.put((rank, "followed"))
+            return
+        loop = EngineLoop(eng, sync=sync, heartbeat_s=0.05)
+        prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)]
+        boxes = [loop.submit(p, 8) for p in prompts]
+        bad = loop.submit([10 ** 6], 4)                  # refused on rank 0, never sent to the others
+        time.sleep(0.3)                                  # idle heartbeats in between
+        late = loop.submit(list(range(7, 30)), 8)
+        outs = []
+        for done, box in boxes + [late]:
+            assert done.wait(300)
+            outs.append(box["request"].output)
+        assert bad[0].wait(10) and "error" in bad[1]
+        loop.close()
+        q.put((rank, outs))
+    except BaseException as e:
+        q.put((rank, repr(e)))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_tensor_parallel_server_ranks_follow_rank0(tiny):
+    """A TP2 server on gloo ranks: rank 0 admits and steps, rank 1 follows its commands; outputs
+    equal single-rank greedy decode, idle heartbeats and a refused request keep the ranks in step."""
+    import socket
+    import torch.multiprocessing as mp
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=_serve_rank, args=(r, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    out = dict(q.get(timeout=300) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert out[1] == "followed", out
+    assert isinstance(out[0], list), out[0]
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=2048, prefill_chunk=256, gdn_chunk=16))
+    prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)] + [list(range(7, 30))]
+    for p, o in zip(prompts, out[0]):
+        assert o == greedy_reference(tgt, p, len(o))
