@@ -75,7 +75,8 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
     if comm is None and rc.parallel.tp > 1:
         from ..parallel.comm import make_comm
         from ..parallel.topology import check_topology
-        check_topology(rc.parallel.tp, comm=rc.parallel.comm if native else "nccl")
+        if torch.cuda.is_available():          # GPU ranks: peer access / NVLink preflight
+            check_topology(rc.parallel.tp, comm=rc.parallel.comm if native else "nccl")
         comm = make_comm(rc.parallel.tp, device=device, hidden=cfg.hidden_size,
                          peer=native and rc.parallel.comm != "nccl", fused=rc.parallel.comm == "fused")
     slots = rc.serving.slots
