@@ -47,6 +47,7 @@ class CompletionRequest(BaseModel):
     stream: bool = False
     stream_options: StreamOptions | None = None
     logprobs: int | None = None       # > 0: log-probability of each output token and the top-k
+    stop: str | list[str] | None = None   # text ends before the first stop string (non-streaming)
 
 
 class ChatMessage(BaseModel):
@@ -63,6 +64,7 @@ class ChatRequest(BaseModel):
     seed: int | None = None
     stream: bool = False
     stream_options: StreamOptions | None = None
+    stop: str | list[str] | None = None
 
 
 def render_chat(messages) -> str:
@@ -89,9 +91,11 @@ class EngineLoop:
     rank's engine runs in lockstep.  While idle, rank 0 still syncs every ``heartbeat_s`` so the
     followers' waiting collective never runs into the process-group timeout."""
 
-    def __init__(self, engine, idle_sleep: float = 0.001, sync=None, heartbeat_s: float = 1.0):
+    def __init__(self, engine, idle_sleep: float = 0.001, sync=None, heartbeat_s: float = 1.0, decode=None):
         self.engine = engine
         self.sync, self.heartbeat_s = sync, heartbeat_s
+        self.decode = decode or ByteTokenizer().decode
+        self._completes = []                # stop-string completions the followers still have to apply
         self.inbox: "queue.Queue" = queue.Queue()
         self.waiters: dict = {}
         self.idle_sleep = idle_sleep
@@ -111,11 +115,14 @@ class EngineLoop:
             raise box["error"]
         return box["value"]
 
-    def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0, stream=False):
+    def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0, stream=False, stop=()):
         """Queue a request.  Returns (done event, result box); with ``stream`` the box's "stream"
-        queue receives each step's newly emitted token ids, then None when the request ends."""
+        queue receives each step's newly emitted token ids, then None when the request ends.  With
+        ``stop`` strings the request ends early once one appears in its decoded output."""
         done = threading.Event()
         box = {"stream": queue.Queue()} if stream else {}
+        if stop:
+            box["stop"] = list(stop)
         self.inbox.put((prompt, max_new_tokens, tuple(eos_ids), done, box, float(temperature), int(seed)))
         return done, box
 
@@ -147,8 +154,10 @@ class EngineLoop:
             except queue.Empty:
                 pass
             step = not stop and self.engine.has_work()
-            if self.sync is not None and (adds or step or stop or time.monotonic() - last_sync >= self.heartbeat_s):
-                self.sync({"add": adds, "step": step, "stop": stop})
+            if self.sync is not None and (adds or step or stop or self._completes
+                                          or time.monotonic() - last_sync >= self.heartbeat_s):
+                self.sync({"add": adds, "complete": self._completes, "step": step, "stop": stop})
+                self._completes = []
                 last_sync = time.monotonic()
             if stop:
                 break
@@ -156,6 +165,13 @@ class EngineLoop:
                 time.sleep(self.idle_sleep)
                 continue
             finished = self.engine.step()
+            for rid, (done, box, req) in list(self.waiters.items()):    # stop strings end a request early
+                if "stop" in box and req.state not in (FINISHED, ABORTED) and req not in finished:
+                    text = self.decode(req.output)
+                    if any(st in text for st in box["stop"]):
+                        self.engine.complete(rid)
+                        self._completes.append(rid)
+                        finished.append(req)
             for done, box, req in list(self.waiters.values()):     # stream what each step emitted
                 if "stream" in box:
                     out = req.output
@@ -198,6 +214,8 @@ def follow(engine, sync):
     when it stops."""
     while True:
         cmd = sync(None)
+        for rid in cmd.get("complete", ()):
+            engine.complete(rid)
         for rid, prompt, n, eos, temp, seed in cmd["add"]:
             engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed, request_id=rid)
         if cmd["stop"]:
@@ -214,7 +232,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     from fastapi.responses import PlainTextResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
-    loop = EngineLoop(engine, sync=sync)
+    loop = EngineLoop(engine, sync=sync, decode=tok.decode)
     app = FastAPI(title="qwen38_b200")
     app.state.loop = loop
 
@@ -233,7 +251,26 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             raise HTTPException(400, f"max_tokens must be a multiple of {output_budget_multiple}")
         # the first output token comes from the prefill; max_tokens counts output tokens
         seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
-        return loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed, body.stream)
+        stops = _stops(body)
+        if stops and body.stream:
+            raise HTTPException(400, "stop strings are served on non-streaming requests")
+        return loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed, body.stream,
+                           stop=stops)
+
+    def _stops(body):
+        st = body.stop
+        stops = [st] if isinstance(st, str) else list(st or [])
+        if any(not x for x in stops) or len(stops) > 4:
+            raise HTTPException(400, "stop: up to 4 non-empty strings")
+        return stops
+
+    def _text(out, body):
+        """(text, finish reason): the text ends before the first stop string, if one appears."""
+        text = tok.decode(out)
+        cuts = [text.find(x) for x in _stops(body) if x in text]
+        if cuts:
+            return text[:min(cuts)], "stop"
+        return text, _finish_reason(out, body)
 
     def _finished(done, box):
         if not done.wait(timeout_s):
@@ -303,10 +340,10 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
         lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
+        text, reason = _text(out, body)
         return {
             "id": cid, "object": "text_completion", "created": created, "model": model,
-            "choices": [{"index": 0, "text": tok.decode(out), "token_ids": out, "logprobs": lp,
-                         "finish_reason": _finish_reason(out, body)}],
+            "choices": [{"index": 0, "text": text, "token_ids": out, "logprobs": lp, "finish_reason": reason}],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                       "total_tokens": len(ids) + len(out)},
         }
@@ -325,10 +362,11 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                         "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
             return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
+        text, reason = _text(out, body)
         return {
             "id": cid, "object": "chat.completion", "created": created, "model": model,
-            "choices": [{"index": 0, "message": {"role": "assistant", "content": tok.decode(out)},
-                         "token_ids": out, "finish_reason": _finish_reason(out, body)}],
+            "choices": [{"index": 0, "message": {"role": "assistant", "content": text},
+                         "token_ids": out, "finish_reason": reason}],
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                       "total_tokens": len(ids) + len(out)},
         }

@@ -65,6 +65,16 @@ class ServingEngine:
         self.sched.add(req)
         return req
 
+    def complete(self, request_id: str):
+        """End a request now as finished (a stop string appeared in its output): its sequence and
+        drafter slot are released, its output is kept."""
+        req = self.requests[request_id]
+        if req.state in (FINISHED, ABORTED):
+            return
+        req.t_done = self.clock()
+        self._release(req)
+        self.sched.finish(req, FINISHED)
+
     def abort(self, request_id: str, reason: str = "aborted by caller"):
         req = self.requests[request_id]
         self._quarantine(req, reason)

@@ -382,9 +382,11 @@ def _serve_rank(rank, port, q):
             follow(eng, sync)
             q.put((rank, "followed"))
             return
-        loop = EngineLoop(eng, sync=sync, heartbeat_s=0.05)
+        # decode stand-in: a request's text contains "STOP" once it has 5 tokens
+        loop = EngineLoop(eng, sync=sync, heartbeat_s=0.05, decode=lambda ids: "STOP" if len(ids) >= 5 else "")
         prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)]
         boxes = [loop.submit(p, 8) for p in prompts]
+        stopped = loop.submit(list(range(60, 100)), 30, stop=["STOP"])     # ends early on every rank
         bad = loop.submit([10 ** 6], 4)                  # refused on rank 0, never sent to the others
         time.sleep(0.3)                                  # idle heartbeats in between
         late = loop.submit(list(range(7, 30)), 8)
@@ -393,6 +395,7 @@ def _serve_rank(rank, port, q):
             assert done.wait(300)
             outs.append(box["request"].output)
         assert bad[0].wait(10) and "error" in bad[1]
+        assert stopped[0].wait(300) and 5 <= len(stopped[1]["request"].output) < 30
         loop.close()
         q.put((rank, outs))
     except BaseException as e:
@@ -423,3 +426,31 @@ def test_tensor_parallel_server_ranks_follow_rank0(tiny):
     prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)] + [list(range(7, 30))]
     for p, o in zip(prompts, out[0]):
         assert o == greedy_reference(tgt, p, len(o))
+
+
+def test_stop_strings_end_requests_early():
+    """A stop string cuts the text before it, reports finish_reason "stop" and ends generation at
+    the step it appears in (fewer tokens than the budget); streaming refuses the option."""
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import ByteTokenizer, build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=2"]))
+    tok = ByteTokenizer()
+    app = build_app(eng)
+    with TestClient(app) as client:
+        prompt = list(range(40, 90))
+        full = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 80}).json()["choices"][0]
+        ids = full["token_ids"]
+        text = tok.decode(ids)
+        # a printable character the greedy output emits early on serves as the stop string
+        k = next(i for i in range(3, 70) if 32 <= ids[i] < 127)
+        stop = chr(ids[k])
+        r = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 80, "stop": [stop]}).json()
+        ch = r["choices"][0]
+        assert ch["finish_reason"] == "stop" and ch["text"] == text[:text.find(stop)]
+        assert len(ch["token_ids"]) < 80 and ch["token_ids"] == ids[:len(ch["token_ids"])]
+        bad = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 4, "stop": "x", "stream": True})
+        assert bad.status_code == 400
+    app.state.loop.close()
