@@ -10,7 +10,8 @@ the byte-level fallback tokenizer below - checkpoints' own tokenizers need netwo
 fetch), ``POST /v1/chat/completions`` (``messages`` rendered with a plain role template),
 ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  ``"logprobs": k`` on a
 non-streaming completion returns each output token's log-probability and the top k, scored on the
-engine thread by the model's own final norm and LM head (TP=1).  With ``"stream": true``
+engine thread by the model's own final norm and LM head (TP=1); ``"stop"`` strings end a
+non-streaming request at the step they appear in and cut the text before them.  With ``"stream": true``
 both generation endpoints answer with server-sent events, one event per engine step that emitted
 tokens (a speculative block commits several tokens at once), then ``data: [DONE]``.
 
