@@ -40,7 +40,8 @@ class StreamOptions(BaseModel):
 
 class CompletionRequest(BaseModel):
     model: str | None = None
-    prompt: list[int] | str
+    prompt: list[int] | str | list[str] | list[list[int]]     # one prompt, or a batch of them
+    n: int = 1                        # completions per prompt (seeds seed, seed+1, ... when sampled)
     max_tokens: int = 16
     stop_token_ids: list[int] | None = None
     temperature: float = 0.0          # 0: greedy with block speculation; > 0: sampled decoding
@@ -245,13 +246,14 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def models():
         return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "qwen38_b200"}]}
 
-    def _start(ids, body):
+    def _start(ids, body, seed=None):
         if not ids:
             raise HTTPException(400, "empty prompt")
         if output_budget_multiple and body.max_tokens % output_budget_multiple:
             raise HTTPException(400, f"max_tokens must be a multiple of {output_budget_multiple}")
         # the first output token comes from the prefill; max_tokens counts output tokens
-        seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
+        if seed is None:
+            seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
         stops = _stops(body)
         if stops and body.stream:
             raise HTTPException(400, "stop strings are served on non-streaming requests")
@@ -327,11 +329,27 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                                  for ir, vr in zip(ti.tolist(), tv.tolist())],
                 "top_token_ids": ti.tolist(), "top_token_logprobs": tv.tolist()}
 
+    def _prompt_list(p):
+        if isinstance(p, str):
+            return [tok.encode(p)]
+        if p and all(isinstance(x, str) for x in p):
+            return [tok.encode(x) for x in p]
+        if p and all(isinstance(x, list) for x in p):
+            return [list(x) for x in p]
+        return [list(p)]
+
     @app.post("/v1/completions")
     def completions(body: CompletionRequest):
-        ids = tok.encode(body.prompt) if isinstance(body.prompt, str) else list(body.prompt)
+        prompts = _prompt_list(body.prompt)
         if body.logprobs is not None and (body.logprobs < 0 or body.logprobs > 20 or body.stream):
             raise HTTPException(400, "logprobs: 0..20, non-streaming requests")
+        if not 1 <= body.n <= 16 or len(prompts) > 64:
+            raise HTTPException(400, "n: 1..16 completions per prompt, up to 64 prompts")
+        if len(prompts) * body.n > 1:
+            if body.stream:
+                raise HTTPException(400, "streaming serves one completion per request")
+            return _batch(prompts, body)
+        ids = prompts[0]
         done, box = _start(ids, body)
         cid, created, model = "cmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
         if body.stream:
@@ -348,6 +366,23 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
                       "total_tokens": len(ids) + len(out)},
         }
+
+    def _batch(prompts, body):
+        """Several prompts and / or ``n`` completions each: all are queued at once (continuous
+        batching packs them), choice ``i * n + j`` is completion j of prompt i."""
+        base = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
+        jobs = [(ids, _start(ids, body, seed=base + j)) for ids in prompts for j in range(body.n)]
+        choices, n_out = [], 0
+        for i, (ids, (done, box)) in enumerate(jobs):
+            out = _finished(done, box)
+            lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
+            text, reason = _text(out, body)
+            choices.append({"index": i, "text": text, "token_ids": out, "logprobs": lp, "finish_reason": reason})
+            n_out += len(out)
+        n_in = sum(len(p) for p in prompts)
+        return {"id": "cmpl-" + uuid.uuid4().hex[:16], "object": "text_completion", "created": int(time.time()),
+                "model": body.model or model_name, "choices": choices,
+                "usage": {"prompt_tokens": n_in, "completion_tokens": n_out, "total_tokens": n_in + n_out}}
 
     @app.post("/v1/chat/completions")
     def chat(body: ChatRequest):

@@ -454,3 +454,33 @@ def test_stop_strings_end_requests_early():
         bad = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 4, "stop": "x", "stream": True})
         assert bad.status_code == 400
     app.state.loop.close()
+
+
+def test_batched_prompts_and_n_choices():
+    """A batch of prompts with n completions each: greedy choices of one prompt are identical and
+    equal single-request greedy decode; sampled choices use seeds seed, seed+1, ..."""
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=4"]))
+    app = build_app(eng)
+    pa, pb = list(range(30, 70)), list(range(100, 130))
+    with TestClient(app) as client:
+        r = client.post("/v1/completions", json={"prompt": [pa, pb], "max_tokens": 6, "n": 2}).json()
+        ch = r["choices"]
+        assert [c["index"] for c in ch] == [0, 1, 2, 3]
+        assert ch[0]["token_ids"] == ch[1]["token_ids"] == greedy_reference(eng.target, pa, 6)
+        assert ch[2]["token_ids"] == ch[3]["token_ids"] == greedy_reference(eng.target, pb, 6)
+        assert r["usage"]["prompt_tokens"] == len(pa) + len(pb) and r["usage"]["completion_tokens"] == 24
+        s = client.post("/v1/completions", json={"prompt": pa, "max_tokens": 6, "n": 2, "temperature": 1.0,
+                                                  "seed": 11}).json()["choices"]
+        one = [client.post("/v1/completions", json={"prompt": pa, "max_tokens": 6, "temperature": 1.0,
+                                                     "seed": 11 + j}).json()["choices"][0]["token_ids"]
+               for j in range(2)]
+        assert [c["token_ids"] for c in s] == one
+        assert client.post("/v1/completions", json={"prompt": [pa, pb], "max_tokens": 2,
+                                                    "stream": True}).status_code == 400
+        assert client.post("/v1/completions", json={"prompt": pa, "max_tokens": 2, "n": 0}).status_code == 400
+    app.state.loop.close()
