@@ -84,6 +84,29 @@ class ByteTokenizer:
         return bytes(int(i) for i in ids if 0 <= int(i) < 256).decode("utf-8", errors="replace")
 
 
+class Histogram:
+    """Prometheus-style cumulative histogram (seconds)."""
+
+    BUCKETS = (0.005, 0.01, 0.025, 0.05, 0.1, 0.25, 0.5, 1.0, 2.5, 5.0, 10.0, 30.0, 60.0)
+
+    def __init__(self):
+        self.counts = [0] * len(self.BUCKETS)
+        self.n, self.total = 0, 0.0
+
+    def observe(self, v: float):
+        self.n += 1
+        self.total += v
+        for i, b in enumerate(self.BUCKETS):
+            if v <= b:
+                self.counts[i] += 1
+
+    def lines(self, name: str):
+        out = [f"# TYPE {name} histogram"]
+        out += [f'{name}_bucket{{le="{b}"}} {c}' for b, c in zip(self.BUCKETS, self.counts)]
+        out += [f'{name}_bucket{{le="+Inf"}} {self.n}', f"{name}_sum {self.total}", f"{name}_count {self.n}"]
+        return out
+
+
 class EngineLoop:
     """Owns the engine: a background thread admits queued requests and steps the scheduler.
 
@@ -103,6 +126,7 @@ class EngineLoop:
         self.idle_sleep = idle_sleep
         self.stop_event = threading.Event()
         self.completed = self.aborted = self.tokens = 0
+        self.ttft, self.tpot = Histogram(), Histogram()      # time to first token, time per output token
         self.calls: "queue.Queue" = queue.Queue()
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
@@ -191,6 +215,10 @@ class EngineLoop:
                 if req.state == FINISHED:
                     self.completed += 1
                     self.tokens += max(0, len(req.output) - 1)
+                    if req.t_first is not None:
+                        self.ttft.observe(max(0.0, req.t_first - req.arrival))
+                        if req.t_done is not None and len(req.output) > 1:
+                            self.tpot.observe(max(0.0, req.t_done - req.t_first) / (len(req.output) - 1))
                 elif req.state == ABORTED:
                     self.aborted += 1
                 done.set()
@@ -419,6 +447,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             "# TYPE q38_running gauge", f"q38_running {len(engine.sched.running)}",
             "# TYPE q38_waiting gauge", f"q38_waiting {len(engine.sched.waiting)}",
             "# TYPE q38_kv_free_blocks gauge", f"q38_kv_free_blocks {engine.target.allocator.num_free}",
+            *loop.ttft.lines("q38_time_to_first_token_seconds"),
+            *loop.tpot.lines("q38_time_per_output_token_seconds"),
         ]
         if engine.prefix is not None:
             for k, v in engine.prefix.export_stats().items():

@@ -114,6 +114,8 @@ def test_openai_http_front_end(tiny):
         assert client.post("/v1/completions", json={"prompt": [999999], "max_tokens": 4}).status_code == 400
         m = client.get("/metrics").text
         assert "q38_requests_completed 2" in m
+        assert "q38_time_to_first_token_seconds_count 2" in m
+        assert 'q38_time_per_output_token_seconds_bucket{le="+Inf"} 2' in m
     app.state.loop.close()
 
 
