@@ -22,11 +22,11 @@ import json
 import math
 import os
 import zlib
-from typing import Callable, Iterable
+from typing import Iterable
 
 import torch
 
-from .config import FULL, LINEAR, DrafterConfig, ModelConfig
+from .config import LINEAR, DrafterConfig, ModelConfig
 
 
 def target_shapes(cfg: ModelConfig) -> dict:

@@ -17,7 +17,7 @@ from dataclasses import dataclass, field
 import torch
 import torch.nn.functional as F
 
-from ..config import FULL, LINEAR, ModelConfig
+from ..config import LINEAR, ModelConfig
 from ..ops import torch_ref as R
 
 

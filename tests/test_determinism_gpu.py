@@ -9,7 +9,7 @@ pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():
     pytest.skip("needs a CUDA device", allow_module_level=True)
 
-from qwen38_b200.checkpoint import random_drafter_source, random_target_source  # noqa: E402
+from qwen38_b200.checkpoint import random_target_source  # noqa: E402
 from qwen38_b200.config import RuntimeConfig, tiny_drafter_config, tiny_model_config  # noqa: E402
 from qwen38_b200.models.target import HybridTarget  # noqa: E402
 from qwen38_b200.ops.native import NativeOps  # noqa: E402

@@ -1,7 +1,6 @@
 """Prefix reuse (BASELINE config 4 on the tiny shape): a request whose prefix matches an earlier
 one restores KV blocks + GDN state + drafter history at the boundary and prefills only the
 suffix; output, GDN state and logits equal a cold full prefill exactly."""
-import pytest
 import torch
 
 from qwen38_b200.config import RuntimeConfig

@@ -2,7 +2,7 @@
 (behaviours of speculative-decoding/harness/test_greedy_*.py and test_lookup_draft.py)."""
 import pytest
 
-from qwen38_b200.spec.greedy import BlockTicket, GreedySession, select_prefix
+from qwen38_b200.spec.greedy import GreedySession, select_prefix
 from qwen38_b200.spec.lookup import HybridDraft, LookupDraft
 
 V = 100

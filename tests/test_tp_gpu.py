@@ -43,7 +43,7 @@ def _worker(rank, world, rdv, q, mode):
         from qwen38_b200.models.drafter import BlockDrafter
         from qwen38_b200.models.target import HybridTarget
         from qwen38_b200.ops.native import NativeOps
-        from qwen38_b200.parallel.comm import TorchComm, make_comm
+        from qwen38_b200.parallel.comm import make_comm
         from qwen38_b200.spec.engine import PinnedAcceptance, SpecRuntime, greedy_reference
         cfg = ModelConfig(num_hidden_layers=4, layer_types=[LINEAR, LINEAR, LINEAR, FULL])
         dcfg = DrafterConfig(num_hidden_layers=1, taps=[1, 3])
