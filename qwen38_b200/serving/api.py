@@ -67,6 +67,9 @@ class ChatRequest(BaseModel):
     stream: bool = False
     stream_options: StreamOptions | None = None
     stop: str | list[str] | None = None
+    n: int = 1
+    logprobs: bool = False            # per-token log-probabilities of the answer ...
+    top_logprobs: int = 0             # ... with this many alternatives each (0..20)
 
 
 def render_chat(messages) -> str:
@@ -417,8 +420,34 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         if not body.messages:
             raise HTTPException(400, "no messages")
         ids = tok.encode(render_chat(body.messages))
-        done, box = _start(ids, body)
+        if not 1 <= body.n <= 16 or not 0 <= body.top_logprobs <= 20:
+            raise HTTPException(400, "n: 1..16, top_logprobs: 0..20")
+        if body.stream and (body.n > 1 or body.logprobs):
+            raise HTTPException(400, "streaming serves one completion without logprobs")
         cid, created, model = "chatcmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
+        if body.n > 1 or body.logprobs:
+            base = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
+            jobs = [_start(ids, body, seed=base + j) for j in range(body.n)]
+            choices, n_out = [], 0
+            for j, (done, box) in enumerate(jobs):
+                out = _finished(done, box)
+                text, reason = _text(out, body)
+                c = {"index": j, "message": {"role": "assistant", "content": text}, "token_ids": out,
+                     "finish_reason": reason, "logprobs": None}
+                if body.logprobs:
+                    lp = _logprobs(ids, out, max(1, body.top_logprobs))
+                    c["logprobs"] = {"content": [
+                        {"token": t, "token_id": i, "logprob": v,
+                         "top_logprobs": [{"token": tok.decode([a]), "token_id": a, "logprob": b}
+                                          for a, b in zip(ti, tv)][:body.top_logprobs]}
+                        for t, i, v, ti, tv in zip(lp["tokens"], lp["token_ids"], lp["token_logprobs"],
+                                                   lp["top_token_ids"], lp["top_token_logprobs"])]}
+                choices.append(c)
+                n_out += len(out)
+            return {"id": cid, "object": "chat.completion", "created": created, "model": model, "choices": choices,
+                    "usage": {"prompt_tokens": len(ids), "completion_tokens": n_out,
+                              "total_tokens": len(ids) + n_out}}
+        done, box = _start(ids, body)
         if body.stream:
             def chunk(new, reason):
                 delta = {"role": "assistant", "content": tok.decode(new)} if new else {}

@@ -486,3 +486,28 @@ def test_batched_prompts_and_n_choices():
                                                     "stream": True}).status_code == 400
         assert client.post("/v1/completions", json={"prompt": pa, "max_tokens": 2, "n": 0}).status_code == 400
     app.state.loop.close()
+
+
+def test_chat_n_and_logprobs():
+    """Chat with n answers and per-token log-probabilities (OpenAI chat layout)."""
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=3"]))
+    app = build_app(eng)
+    msgs = [{"role": "user", "content": "hello there"}]
+    with TestClient(app) as client:
+        r = client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 5, "n": 2, "logprobs": True,
+                                                       "top_logprobs": 2})
+        assert r.status_code == 200, r.text
+        ch = r.json()["choices"]
+        assert len(ch) == 2 and ch[0]["token_ids"] == ch[1]["token_ids"]        # greedy: the same answer
+        content = ch[0]["logprobs"]["content"]
+        assert [c["token_id"] for c in content] == ch[0]["token_ids"]
+        assert all(c["logprob"] <= 0 and len(c["top_logprobs"]) == 2 for c in content)
+        assert all(c["top_logprobs"][0]["token_id"] == c["token_id"] for c in content)
+        assert client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "n": 2,
+                                                         "stream": True}).status_code == 400
+    app.state.loop.close()
