@@ -131,6 +131,7 @@ class EngineLoop:
         self.completed = self.aborted = self.tokens = 0
         self.ttft, self.tpot = Histogram(), Histogram()      # time to first token, time per output token
         self.calls: "queue.Queue" = queue.Queue()
+        self.cancels: "queue.Queue" = queue.Queue()
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
 
@@ -143,6 +144,11 @@ class EngineLoop:
         if "error" in box:
             raise box["error"]
         return box["value"]
+
+    def cancel(self, request_id: str):
+        """Abort a request (its client went away); applied on the engine thread before the next step,
+        on every tensor-parallel rank."""
+        self.cancels.put(request_id)
 
     def submit(self, prompt, max_new_tokens, eos_ids=(), temperature=0.0, seed=0, stream=False, stop=()):
         """Queue a request.  Returns (done event, result box); with ``stream`` the box's "stream"
@@ -173,6 +179,7 @@ class EngineLoop:
                     try:
                         req = self.engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed)
                         box["sent"] = 0
+                        box["rid"] = req.request_id
                         self.waiters[req.request_id] = (done, box, req)
                         adds.append((req.request_id, list(req.prompt), n, eos, temp, seed))
                     except Exception as e:          # invalid request: answer at once
@@ -182,10 +189,18 @@ class EngineLoop:
                         done.set()
             except queue.Empty:
                 pass
+            aborted = []
+            while not self.cancels.empty():
+                rid = self.cancels.get_nowait()
+                req = self.engine.requests.get(rid)
+                if req is not None and req.state not in (FINISHED, ABORTED):
+                    self.engine.abort(rid, "cancelled by the client")
+                    aborted.append(rid)
+                    self._settle(req)
             step = not stop and self.engine.has_work()
-            if self.sync is not None and (adds or step or stop or self._completes
+            if self.sync is not None and (adds or step or stop or self._completes or aborted
                                           or time.monotonic() - last_sync >= self.heartbeat_s):
-                self.sync({"add": adds, "complete": self._completes, "step": step, "stop": stop})
+                self.sync({"add": adds, "complete": self._completes, "abort": aborted, "step": step, "stop": stop})
                 self._completes = []
                 last_sync = time.monotonic()
             if stop:
@@ -208,23 +223,27 @@ class EngineLoop:
                         box["stream"].put(out[box["sent"]:])
                         box["sent"] = len(out)
             for req in finished:
-                entry = self.waiters.pop(req.request_id, None)
-                if entry is None:
-                    continue
-                done, box, _ = entry
-                box["request"] = req
-                if "stream" in box:
-                    box["stream"].put(None)
-                if req.state == FINISHED:
-                    self.completed += 1
-                    self.tokens += max(0, len(req.output) - 1)
-                    if req.t_first is not None:
-                        self.ttft.observe(max(0.0, req.t_first - req.arrival))
-                        if req.t_done is not None and len(req.output) > 1:
-                            self.tpot.observe(max(0.0, req.t_done - req.t_first) / (len(req.output) - 1))
-                elif req.state == ABORTED:
-                    self.aborted += 1
-                done.set()
+                self._settle(req)
+
+    def _settle(self, req):
+        """Hand a finished or aborted request to its waiter."""
+        entry = self.waiters.pop(req.request_id, None)
+        if entry is None:
+            return
+        done, box, _ = entry
+        box["request"] = req
+        if "stream" in box:
+            box["stream"].put(None)
+        if req.state == FINISHED:
+            self.completed += 1
+            self.tokens += max(0, len(req.output) - 1)
+            if req.t_first is not None:
+                self.ttft.observe(max(0.0, req.t_first - req.arrival))
+                if req.t_done is not None and len(req.output) > 1:
+                    self.tpot.observe(max(0.0, req.t_done - req.t_first) / (len(req.output) - 1))
+        elif req.state == ABORTED:
+            self.aborted += 1
+        done.set()
 
     def close(self):
         self.stop_event.set()
@@ -249,6 +268,8 @@ def follow(engine, sync):
         cmd = sync(None)
         for rid in cmd.get("complete", ()):
             engine.complete(rid)
+        for rid in cmd.get("abort", ()):
+            engine.abort(rid, "cancelled by the client")
         for rid, prompt, n, eos, temp, seed in cmd["add"]:
             engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed, request_id=rid)
         if cmd["stop"]:
@@ -322,7 +343,15 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def _events(box, body, chunk, n_prompt):
         """Server-sent events: one per engine step that emitted tokens, the finish event (with the
         token accounting when ``stream_options.include_usage``), then [DONE]."""
-        emitted = []
+        emitted, ended = [], False
+        try:
+            yield from _event_lines(box, body, chunk, n_prompt, emitted)
+            ended = True
+        finally:
+            if not ended and "rid" in box:          # the client went away mid-stream
+                loop.cancel(box["rid"])
+
+    def _event_lines(box, body, chunk, n_prompt, emitted):
         while True:
             try:
                 new = box["stream"].get(timeout=timeout_s)

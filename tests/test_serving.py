@@ -389,6 +389,12 @@ def _serve_rank(rank, port, q):
         prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)]
         boxes = [loop.submit(p, 8) for p in prompts]
         stopped = loop.submit(list(range(60, 100)), 30, stop=["STOP"])     # ends early on every rank
+        gone = loop.submit(list(range(61, 90)), 200)                        # cancelled once admitted
+        for _ in range(3000):
+            if "rid" in gone[1]:
+                break
+            time.sleep(0.01)
+        loop.cancel(gone[1]["rid"])
         bad = loop.submit([10 ** 6], 4)                  # refused on rank 0, never sent to the others
         time.sleep(0.3)                                  # idle heartbeats in between
         late = loop.submit(list(range(7, 30)), 8)
@@ -398,6 +404,7 @@ def _serve_rank(rank, port, q):
             outs.append(box["request"].output)
         assert bad[0].wait(10) and "error" in bad[1]
         assert stopped[0].wait(300) and 5 <= len(stopped[1]["request"].output) < 30
+        assert gone[0].wait(300) and gone[1]["request"].state == "aborted"
         loop.close()
         q.put((rank, outs))
     except BaseException as e:
@@ -511,3 +518,26 @@ def test_chat_n_and_logprobs():
         assert client.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 2, "n": 2,
                                                          "stream": True}).status_code == 400
     app.state.loop.close()
+
+
+def test_cancel_aborts_a_running_request(tiny):
+    """A cancelled request (its client went away) is aborted before its budget and frees its slot."""
+    import time as _t
+
+    from qwen38_b200.serving.api import EngineLoop
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=1024, prefill_chunk=64, gdn_chunk=16),
+                       max_slots=2)
+    eng = ServingEngine(tgt, None, verifier_rows=4)
+    free0 = tgt.allocator.num_free
+    loop = EngineLoop(eng)
+    done, box = loop.submit(list(range(10, 40)), 500)
+    for _ in range(3000):
+        if box.get("rid") and len(eng.requests[box["rid"]].output) > 2:
+            break
+        _t.sleep(0.01)
+    loop.cancel(box["rid"])
+    assert done.wait(60)
+    req = box["request"]
+    assert req.state == ABORTED and len(req.output) < 500 and "cancelled" in req.error
+    assert tgt.allocator.num_free == free0 and loop.aborted == 1
+    loop.close()
