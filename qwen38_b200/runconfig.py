@@ -47,6 +47,7 @@ class ServingConfig:
     output_budget_multiple: int = 0      # > 0: max_tokens must be a multiple of it
     prefix_budget_gb: float = 0.0        # 0: prefix reuse off
     request_timeout_s: float = 600.0
+    phase_log: str = ""                  # file for one JSON line per finished request ("": off)
 
 
 @dataclass

@@ -23,6 +23,8 @@ Run:  python -m qwen38_b200.serving.api --profile single-stream-4k --set serving
 from __future__ import annotations
 
 import argparse
+import collections
+import json
 import queue
 import threading
 import time
@@ -119,8 +121,11 @@ class EngineLoop:
     rank's engine runs in lockstep.  While idle, rank 0 still syncs every ``heartbeat_s`` so the
     followers' waiting collective never runs into the process-group timeout."""
 
-    def __init__(self, engine, idle_sleep: float = 0.001, sync=None, heartbeat_s: float = 1.0, decode=None):
+    def __init__(self, engine, idle_sleep: float = 0.001, sync=None, heartbeat_s: float = 1.0, decode=None,
+                 phase_log: str | None = None):
         self.engine = engine
+        self.phase_log = phase_log          # one JSON line per finished request (blocks, timings)
+        self.recent_blocks = collections.deque(maxlen=256)     # block records of the last requests
         self.sync, self.heartbeat_s = sync, heartbeat_s
         self.decode = decode or ByteTokenizer().decode
         self._completes = []                # stop-string completions the followers still have to apply
@@ -237,6 +242,15 @@ class EngineLoop:
         if req.state == FINISHED:
             self.completed += 1
             self.tokens += max(0, len(req.output) - 1)
+            if req.blocks:
+                self.recent_blocks.append(list(req.blocks))
+            if self.phase_log:
+                rec = {"stage": "request_phases", "request_id": req.request_id, "prompt_tokens": len(req.prompt),
+                       "output_tokens": len(req.output), "blocks": req.blocks,
+                       "ttft_s": None if req.t_first is None else req.t_first - req.arrival,
+                       "decode_s": None if req.t_first is None or req.t_done is None else req.t_done - req.t_first}
+                with open(self.phase_log, "a") as f:
+                    f.write(json.dumps(rec) + "\n")
             if req.t_first is not None:
                 self.ttft.observe(max(0.0, req.t_first - req.arrival))
                 if req.t_done is not None and len(req.output) > 1:
@@ -279,14 +293,12 @@ def follow(engine, sync):
 
 
 def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0,
-              output_budget_multiple: int = 0, sync=None):
-    import json
-
+              output_budget_multiple: int = 0, sync=None, phase_log: str | None = None):
     from fastapi import FastAPI, HTTPException
     from fastapi.responses import PlainTextResponse, StreamingResponse
 
     tok = tokenizer or ByteTokenizer()
-    loop = EngineLoop(engine, sync=sync, decode=tok.decode)
+    loop = EngineLoop(engine, sync=sync, decode=tok.decode, phase_log=phase_log)
     app = FastAPI(title="qwen38_b200")
     app.state.loop = loop
 
@@ -508,6 +520,13 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             *loop.ttft.lines("q38_time_to_first_token_seconds"),
             *loop.tpot.lines("q38_time_per_output_token_seconds"),
         ]
+        if loop.recent_blocks:
+            from ..spec.analysis import acceptance_report_requests
+            rep = acceptance_report_requests(list(loop.recent_blocks))
+            lines += ["# TYPE q38_committed_tokens_per_block gauge",
+                      f"q38_committed_tokens_per_block {rep['mean_committed_per_block']}"]
+            if rep["mean_accepted"] is not None:
+                lines += ["# TYPE q38_mean_accepted_drafts gauge", f"q38_mean_accepted_drafts {rep['mean_accepted']}"]
         if engine.prefix is not None:
             for k, v in engine.prefix.export_stats().items():
                 if isinstance(v, (int, float)):
@@ -547,7 +566,8 @@ def main():
         follow(eng, sync)                       # rank 0 serves HTTP; the others follow its steps
         return
     app = build_app(eng, timeout_s=rc.serving.request_timeout_s,
-                    output_budget_multiple=rc.serving.output_budget_multiple, sync=sync)
+                    output_budget_multiple=rc.serving.output_budget_multiple, sync=sync,
+                    phase_log=rc.serving.phase_log or None)
     uvicorn.run(app, host=rc.serving.host, port=rc.serving.port)
 
 

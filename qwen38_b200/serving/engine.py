@@ -236,11 +236,12 @@ class ServingEngine:
                     dr.append(rows[:k], pos, r.dslot, next_tokens=nxt)
 
             try:
-                r.session.commit(r.request_id, r.ticket, preds[o0:o0 + n], publish)
+                d = r.session.commit(r.request_id, r.ticket, preds[o0:o0 + n], publish)
             except Exception as e:
                 self._quarantine(r, e)
                 finished.append(r)
                 continue
+            r.blocks.append({"rows": n, "accepted": int(d.accepted), "committed": len(d.emitted)})
             if r.session.finished:
                 r.t_done = self.clock()
                 self._release(r)

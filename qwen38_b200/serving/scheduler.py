@@ -37,6 +37,7 @@ class Request:
     reused_prefix: int = 0
     temperature: float = 0.0            # > 0: sampled, one token per step, no speculation
     seed: int = 0                       # sampling noise seed
+    blocks: list = field(default_factory=list)   # per verified block: {rows, accepted, committed}
 
     @property
     def output(self):

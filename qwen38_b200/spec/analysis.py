@@ -117,6 +117,13 @@ def acceptance_report(blocks) -> dict:
       blocks accepting at least i drafts, ``conditional`` = share accepting i among those that
       accepted i - 1 (None once no block got that far);
     * histogram of accepted drafts and the mean committed tokens per block over all blocks."""
+    return acceptance_report_requests([blocks])
+
+
+def acceptance_report_requests(requests) -> dict:
+    """``acceptance_report`` over several requests' block lists (each request's last block is left
+    out of the full-draft set; every block counts toward the committed mean)."""
+    blocks = [b for r in requests for b in r]
     if not blocks:
         raise ValueError("no blocks")
     for b in blocks:
@@ -124,7 +131,7 @@ def acceptance_report(blocks) -> dict:
                 and 1 <= b.get("committed", 0) <= b["rows"]):
             raise ValueError("blocks with rows, accepted < rows and committed in 1..rows required")
     width = max(b["rows"] for b in blocks)
-    full = [b for b in blocks[:-1] if b["rows"] == width]
+    full = [b for r in requests for b in r[:-1] if b["rows"] == width]
     hist = [0] * width
     for b in full:
         hist[b["accepted"]] += 1
@@ -138,3 +145,27 @@ def acceptance_report(blocks) -> dict:
                 mean_accepted=(sum(b["accepted"] for b in full) / len(full)) if full else None,
                 mean_committed_per_block=sum(b["committed"] for b in blocks) / len(blocks),
                 histogram=hist, unconditional=uncond, conditional=cond)
+
+
+def main(argv=None):
+    """Acceptance report of a server's phase log (``serving.phase_log``: one JSON line per finished
+    request with its block records)."""
+    import argparse
+    import json
+    ap = argparse.ArgumentParser(description="acceptance report from a serving phase log")
+    ap.add_argument("log")
+    a = ap.parse_args(argv)
+    reqs = []
+    with open(a.log) as f:
+        for line in f:
+            line = line.strip()
+            if line.startswith("{"):
+                rec = json.loads(line)
+                if rec.get("stage") == "request_phases" and rec.get("blocks"):
+                    reqs.append(rec["blocks"])
+    print(json.dumps(dict(requests=len(reqs), **acceptance_report_requests(reqs))))
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

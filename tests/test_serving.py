@@ -541,3 +541,34 @@ def test_cancel_aborts_a_running_request(tiny):
     assert req.state == ABORTED and len(req.output) < 500 and "cancelled" in req.error
     assert tgt.allocator.num_free == free0 and loop.aborted == 1
     loop.close()
+
+
+def test_phase_log_and_acceptance_metrics(tmp_path):
+    """Finished requests land in the phase log with their block records; the acceptance report of
+    the log and the /metrics gauges agree with the engine's blocks."""
+    import json
+    import subprocess
+    import sys
+
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    from qwen38_b200.spec.analysis import acceptance_report_requests
+    log = str(tmp_path / "phases.jsonl")
+    eng = build_engine(load_run_config(profile="tiny-cpu", overrides=["serving.slots=2"]))
+    app = build_app(eng, phase_log=log)
+    with TestClient(app) as client:
+        for p in (list(range(20, 60)), list(range(70, 99))):
+            assert client.post("/v1/completions", json={"prompt": p, "max_tokens": 12}).status_code == 200
+        m = client.get("/metrics").text
+    app.state.loop.close()
+    recs = [json.loads(l) for l in open(log)]
+    assert len(recs) == 2 and all(r["output_tokens"] == 12 for r in recs)
+    assert all(sum(b["committed"] for b in r["blocks"]) == 11 for r in recs)   # the first token is the prefill's
+    rep = acceptance_report_requests([r["blocks"] for r in recs])
+    assert f"q38_committed_tokens_per_block {rep['mean_committed_per_block']}" in m
+    out = subprocess.run([sys.executable, "-m", "qwen38_b200.spec.analysis", log], capture_output=True, text=True,
+                         timeout=120)
+    assert out.returncode == 0 and json.loads(out.stdout)["requests"] == 2
