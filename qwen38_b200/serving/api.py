@@ -10,7 +10,7 @@ the byte-level fallback tokenizer below - checkpoints' own tokenizers need netwo
 fetch), ``POST /v1/chat/completions`` (``messages`` rendered with a plain role template),
 ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  ``"logprobs": k`` on a
 non-streaming completion returns each output token's log-probability and the top k, scored on the
-engine thread by the model's own final norm and LM head (TP=1); ``"stop"`` strings end a
+engine thread(s) by the model's own final norm and LM head; ``"stop"`` strings end a
 non-streaming request at the step they appear in and cut the text before them.  With ``"stream": true``
 both generation endpoints answer with server-sent events, one event per engine step that emitted
 tokens (a speculative block commits several tokens at once), then ``data: [DONE]``.
@@ -89,6 +89,14 @@ class ByteTokenizer:
         return bytes(int(i) for i in ids if 0 <= int(i) < 256).decode("utf-8", errors="replace")
 
 
+def _score_op(engine, ids, out, k):
+    from ..utils.tp_agreement import score
+    return score(engine.target, ids, out, top_k=k)
+
+
+SHARED_OPS = {"score": _score_op}        # engine operations every tensor-parallel rank runs together
+
+
 class Histogram:
     """Prometheus-style cumulative histogram (seconds)."""
 
@@ -137,6 +145,7 @@ class EngineLoop:
         self.ttft, self.tpot = Histogram(), Histogram()      # time to first token, time per output token
         self.calls: "queue.Queue" = queue.Queue()
         self.cancels: "queue.Queue" = queue.Queue()
+        self.shared: "queue.Queue" = queue.Queue()
         self.thread = threading.Thread(target=self._run, name="q38-engine", daemon=True)
         self.thread.start()
 
@@ -144,6 +153,17 @@ class EngineLoop:
         """Run ``fn()`` on the engine thread between two steps (the model is not thread-safe)."""
         done, box = threading.Event(), {}
         self.calls.put((fn, done, box))
+        if not done.wait(timeout):
+            raise TimeoutError("engine call timed out")
+        if "error" in box:
+            raise box["error"]
+        return box["value"]
+
+    def call_shared(self, name: str, *args, timeout: float = 600.0):
+        """Run ``SHARED_OPS[name](engine, *args)`` on the engine thread of every tensor-parallel rank
+        (an operation with collectives inside, such as scoring with the vocabulary-sharded head)."""
+        done, box = threading.Event(), {}
+        self.shared.put((name, args, done, box))
         if not done.wait(timeout):
             raise TimeoutError("engine call timed out")
         if "error" in box:
@@ -202,12 +222,22 @@ class EngineLoop:
                     self.engine.abort(rid, "cancelled by the client")
                     aborted.append(rid)
                     self._settle(req)
+            shared = []
+            while not stop and not self.shared.empty():
+                shared.append(self.shared.get_nowait())
             step = not stop and self.engine.has_work()
-            if self.sync is not None and (adds or step or stop or self._completes or aborted
+            if self.sync is not None and (adds or step or stop or self._completes or aborted or shared
                                           or time.monotonic() - last_sync >= self.heartbeat_s):
-                self.sync({"add": adds, "complete": self._completes, "abort": aborted, "step": step, "stop": stop})
+                self.sync({"add": adds, "complete": self._completes, "abort": aborted,
+                           "shared": [(name, args) for name, args, _, _ in shared], "step": step, "stop": stop})
                 self._completes = []
                 last_sync = time.monotonic()
+            for name, args, done, box in shared:        # every rank runs these at this point
+                try:
+                    box["value"] = SHARED_OPS[name](self.engine, *args)
+                except Exception as e:
+                    box["error"] = e
+                done.set()
             if stop:
                 break
             if not step:
@@ -286,6 +316,11 @@ def follow(engine, sync):
             engine.abort(rid, "cancelled by the client")
         for rid, prompt, n, eos, temp, seed in cmd["add"]:
             engine.add_request(prompt, n, eos_ids=eos, temperature=temp, seed=seed, request_id=rid)
+        for name, args in cmd.get("shared", ()):
+            try:
+                SHARED_OPS[name](engine, *args)
+            except Exception:                   # rank 0 reports the error; stay in step
+                pass
         if cmd["stop"]:
             return
         if cmd["step"]:
@@ -388,11 +423,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def _logprobs(ids, out, k):
         """OpenAI completions ``logprobs`` object: each output token's log-probability and the top
         k, scored by the engine's own final norm and LM head on the engine thread."""
-        from ..utils.tp_agreement import score
-        if engine.target.tp > 1:
-            raise HTTPException(400, "logprobs are served at TP=1")
         try:
-            chosen, ti, tv = loop.call(lambda: score(engine.target, ids, out, top_k=k))
+            chosen, ti, tv = loop.call_shared("score", list(ids), list(out), int(k))
         except MemoryError:
             raise HTTPException(503, "no free sequence slot to score the output")
         return {"tokens": [tok.decode([t]) for t in out], "token_ids": out,

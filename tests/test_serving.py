@@ -405,8 +405,9 @@ def _serve_rank(rank, port, q):
         assert bad[0].wait(10) and "error" in bad[1]
         assert stopped[0].wait(300) and 5 <= len(stopped[1]["request"].output) < 30
         assert gone[0].wait(300) and gone[1]["request"].state == "aborted"
+        chosen, top_ids, _ = loop.call_shared("score", prompts[0], outs[0], 3)    # collectives on both ranks
         loop.close()
-        q.put((rank, outs))
+        q.put((rank, (outs, chosen.tolist(), top_ids.tolist())))
     except BaseException as e:
         q.put((rank, repr(e)))
     finally:
@@ -430,11 +431,15 @@ def test_tensor_parallel_server_ranks_follow_rank0(tiny):
     for p in procs:
         p.join(timeout=60)
     assert out[1] == "followed", out
-    assert isinstance(out[0], list), out[0]
+    assert isinstance(out[0], tuple), out[0]
+    outs, chosen, top_ids = out[0]
     tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=2048, prefill_chunk=256, gdn_chunk=16))
     prompts = [list(range(10 + i, 50 + 3 * i)) for i in range(3)] + [list(range(7, 30))]
-    for p, o in zip(prompts, out[0]):
+    for p, o in zip(prompts, outs):
         assert o == greedy_reference(tgt, p, len(o))
+    from qwen38_b200.utils.tp_agreement import score
+    c1, t1, _ = score(tgt, prompts[0], outs[0], 3)
+    assert t1.tolist() == top_ids and max(abs(a - b) for a, b in zip(c1.tolist(), chosen)) < 1e-4
 
 
 def test_stop_strings_end_requests_early():
