@@ -137,6 +137,8 @@ class EngineLoop:
         self.sync, self.heartbeat_s = sync, heartbeat_s
         self.decode = decode or ByteTokenizer().decode
         self._completes = []                # stop-string completions the followers still have to apply
+        self._aborts_pending = []           # fault aborts the followers still have to apply
+        self.faults = 0
         self.inbox: "queue.Queue" = queue.Queue()
         self.waiters: dict = {}
         self.idle_sleep = idle_sleep
@@ -222,6 +224,8 @@ class EngineLoop:
                     self.engine.abort(rid, "cancelled by the client")
                     aborted.append(rid)
                     self._settle(req)
+            aborted += self._aborts_pending
+            self._aborts_pending = []
             shared = []
             while not stop and not self.shared.empty():
                 shared.append(self.shared.get_nowait())
@@ -243,7 +247,16 @@ class EngineLoop:
             if not step:
                 time.sleep(self.idle_sleep)
                 continue
-            finished = self.engine.step()
+            try:
+                finished = self.engine.step()
+            except Exception as e:              # an engine fault: fail the requests, keep serving
+                self.faults += 1
+                finished = []
+                for rid, req in list(self.engine.requests.items()):
+                    if req.state not in (FINISHED, ABORTED):
+                        self.engine.abort(rid, f"engine fault: {e}")
+                        self._aborts_pending.append(rid)
+                        finished.append(req)
             for rid, (done, box, req) in list(self.waiters.items()):    # stop strings end a request early
                 if "stop" in box and req.state not in (FINISHED, ABORTED) and req not in finished:
                     text = self.decode(req.output)
@@ -542,6 +555,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         lines = [
             "# TYPE q38_requests_completed counter", f"q38_requests_completed {loop.completed}",
             "# TYPE q38_requests_aborted counter", f"q38_requests_aborted {loop.aborted}",
+            "# TYPE q38_engine_faults counter", f"q38_engine_faults {loop.faults}",
             "# TYPE q38_tokens_generated counter", f"q38_tokens_generated {loop.tokens}",
             "# TYPE q38_steps counter",
             f"q38_steps{{kind=\"prefill\"}} {engine.steps['prefill']}",

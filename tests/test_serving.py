@@ -577,3 +577,29 @@ def test_phase_log_and_acceptance_metrics(tmp_path):
     out = subprocess.run([sys.executable, "-m", "qwen38_b200.spec.analysis", log], capture_output=True, text=True,
                          timeout=120)
     assert out.returncode == 0 and json.loads(out.stdout)["requests"] == 2
+
+
+def test_engine_fault_fails_requests_and_serving_continues(tiny):
+    """An exception escaping an engine step fails the requests in flight (their waiters get the
+    error) and releases them; the loop keeps serving the next request."""
+    from qwen38_b200.serving.api import EngineLoop
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16),
+                       max_slots=3)
+    eng = ServingEngine(tgt, None, verifier_rows=4)
+    free0 = tgt.allocator.num_free
+    real = eng.step
+    state = {"n": 0}
+
+    def flaky():
+        state["n"] += 1
+        if state["n"] == 3:
+            raise RuntimeError("injected engine fault")
+        return real()
+    eng.step = flaky
+    loop = EngineLoop(eng)
+    d1, b1 = loop.submit(list(range(10, 40)), 30)
+    assert d1.wait(60) and b1["request"].state == ABORTED and "injected" in b1["request"].error
+    d2, b2 = loop.submit(list(range(50, 70)), 6)
+    assert d2.wait(60) and b2["request"].output == greedy_reference(tgt, list(range(50, 70)), 6)
+    assert loop.faults == 1 and tgt.allocator.num_free == free0
+    loop.close()
