@@ -352,7 +352,9 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
 
     @app.get("/health")
     def health():
-        return {"status": "ok", "running": len(engine.sched.running), "waiting": len(engine.sched.waiting)}
+        return {"status": "ok" if loop.thread.is_alive() else "engine loop stopped",
+                "running": len(engine.sched.running), "waiting": len(engine.sched.waiting),
+                "tp": engine.target.tp, "engine_faults": loop.faults}
 
     @app.get("/v1/models")
     def models():
