@@ -77,6 +77,9 @@ def run(engine, prompts, new_tokens: int, arrivals, *, golds=None, mean_accepted
                p50_stream_tg=statistics.median(per_stream) if per_stream else 0.0,
                p90_stream_tg=sorted(per_stream)[int(0.9 * (len(per_stream) - 1))] if per_stream else 0.0,
                prefill_steps=engine.steps["prefill"], decode_steps=engine.steps["decode"])
+    ttft = sorted(r.t_first - r.arrival for r in done if r.t_first is not None)
+    if ttft:
+        out.update(p50_ttft_s=statistics.median(ttft), p90_ttft_s=ttft[int(0.9 * (len(ttft) - 1))])
     if golds:
         out["exact"] = all(r.output == golds[i][:len(r.output)] for i, r in enumerate(reqs) if r is not None)
     return out

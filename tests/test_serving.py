@@ -130,6 +130,7 @@ def test_poisson_loadgen_report(tiny):
     rep = run(eng, prompts, 12, arr, golds=golds, mean_accepted=1)
     assert rep["finished"] == 3 and rep["exact"]
     assert rep["committed_tokens"] == 3 * 11 and rep["aggregate_tok_s"] > 0
+    assert 0 <= rep["p50_ttft_s"] <= rep["p90_ttft_s"]
 
 
 def test_factory_builds_engines_from_profiles():
