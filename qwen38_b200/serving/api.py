@@ -189,6 +189,9 @@ class EngineLoop:
         return done, box
 
     def _run(self):
+        dev = getattr(self.engine.target, "device", None)
+        if dev is not None and torch.device(dev).type == "cuda" and torch.device(dev).index is not None:
+            torch.cuda.set_device(torch.device(dev))     # the current device is per thread
         last_sync = time.monotonic()
         while True:
             stop = self.stop_event.is_set()
