@@ -46,7 +46,7 @@ class CompletionRequest(BaseModel):
     n: int = 1                        # completions per prompt (seeds seed, seed+1, ... when sampled)
     max_tokens: int = 16
     stop_token_ids: list[int] | None = None
-    temperature: float = 0.0          # 0: greedy with block speculation; > 0: sampled decoding
+    temperature: float = 0.0          # 0: greedy; > 0: sampled (both run block speculation)
     seed: int | None = None
     stream: bool = False
     stream_options: StreamOptions | None = None

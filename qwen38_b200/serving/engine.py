@@ -25,8 +25,13 @@ from .scheduler import ABORTED, FINISHED, DecodeStep, PrefillStep, Request, Sche
 class ServingEngine:
     def __init__(self, target, drafter=None, *, verifier_rows: int = 16, max_running: int | None = None,
                  prefill_chunk: int | None = None, max_step_rows: int | None = None, prefix=None,
-                 lookup: bool = False, clock=time.perf_counter):
+                 lookup: bool = False, clock=time.perf_counter, speculate_sampled: bool = True):
         self.target, self.drafter, self.prefix = target, drafter, prefix
+        # Sampled requests speculate too: the Gumbel noise of a position depends only on (seed,
+        # position), so the sampled token of every verified row is a fixed function of its prefix and
+        # the greedy acceptance rule applied to sampled tokens reproduces one-token-per-step sampling
+        # exactly.  False: sampled requests decode one token per step.
+        self.speculate_sampled = speculate_sampled
         self.verifier_rows, self.lookup, self.clock = verifier_rows, lookup, clock
         slots = target.max_slots if drafter is None else min(target.max_slots, drafter.slots)
         self.max_running = max_running or slots
@@ -197,8 +202,8 @@ class ServingEngine:
         live, finished = [], []
         for req in st.requests:
             try:
-                # sampled requests decode one token per step (speculation is greedy-only)
-                req.ticket = (req.session.propose(req.request_id, max_rows=1) if req.temperature > 0
+                one = req.temperature > 0 and not self.speculate_sampled
+                req.ticket = (req.session.propose(req.request_id, max_rows=1) if one
                               else req.session.propose(req.request_id))
                 live.append(req)
             except Exception as e:

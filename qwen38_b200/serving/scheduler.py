@@ -35,7 +35,7 @@ class Request:
     t_done: float | None = None
     decode_time: float = 0.0            # generation-loop time attributed to this request
     reused_prefix: int = 0
-    temperature: float = 0.0            # > 0: sampled, one token per step, no speculation
+    temperature: float = 0.0            # > 0: sampled (Gumbel-max keyed by seed and position)
     seed: int = 0                       # sampling noise seed
     blocks: list = field(default_factory=list)   # per verified block: {rows, accepted, committed}
 

@@ -604,3 +604,21 @@ def test_engine_fault_fails_requests_and_serving_continues(tiny):
     assert d2.wait(60) and b2["request"].output == greedy_reference(tgt, list(range(50, 70)), 6)
     assert loop.faults == 1 and tgt.allocator.num_free == free0
     loop.close()
+
+
+def test_sampled_requests_speculate_exactly(tiny):
+    """With counter-based Gumbel noise a sampled token depends only on its prefix, seed and position,
+    so block speculation on a sampled request commits several tokens per block and still yields
+    exactly the one-token-per-step sample."""
+    tgt, dr = _setup(tiny, slots=2)
+    p = _prompt(43, 44)
+    ref = tgt.sample(torch.tensor(p), 24, temperature=0.8, seed=9)
+    for speculate, pinned in ((True, PinnedAcceptance(ref, seed=4, mean_accepted=2)), (True, None), (False, None)):
+        eng = ServingEngine(tgt, dr, verifier_rows=4, speculate_sampled=speculate)
+        eng.add_request(p, 24, request_id="s", temperature=0.8, seed=9, pinned=pinned)
+        req = {r.request_id: r for r in eng.run()}["s"]
+        assert req.output == ref
+        if pinned is not None:
+            assert max(b["committed"] for b in req.blocks) > 1 and len(req.blocks) < 23
+        if not speculate:
+            assert all(b["rows"] == 1 for b in req.blocks)
