@@ -77,6 +77,7 @@ class SpecRuntime:
         self.taps = tuple(drafter.dcfg.taps) if drafter is not None else ()
         self._anchor_dev = torch.zeros(1, dtype=torch.long, device=target.device)
         self.pinned = None
+        self._sampling = None
         self.session = self.last_session = None
         self.h2d_bytes = self.d2h_bytes = 0
 
@@ -97,10 +98,12 @@ class SpecRuntime:
     # ------------------------------------------------------------------------------ request
     @torch.no_grad()
     def generate(self, prompt, max_new_tokens: int, *, request_id="req", eos_ids=(), pinned=None,
-                 gold_check=None, prompt_host=None):
+                 gold_check=None, prompt_host=None, temperature: float = 0.0, seed: int = 0):
         """Runs one request.  ``prompt``: list/1-D tensor of ids.  Returns a result dict with the
-        emitted tokens and PP/TG figures."""
+        emitted tokens and PP/TG figures.  ``temperature`` > 0 samples (Gumbel-max keyed by seed
+        and position, so block speculation reproduces ``HybridTarget.sample`` exactly)."""
         tgt = self.target
+        self._sampling = (float(temperature), int(seed)) if temperature > 0 else None
         self.pinned = pinned
         if prompt_host is None:
             prompt_host = torch.as_tensor(list(prompt) if not torch.is_tensor(prompt) else prompt.cpu(),
@@ -144,7 +147,11 @@ class SpecRuntime:
                 self.h2d_bytes += 8 * n
                 try:
                     with nvtx("verify"):
-                        pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                        if self._sampling is None:
+                            pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps)
+                        else:
+                            samp = tgt.sampling_args(*self._sampling, range(seq.pos + 1, seq.pos + 1 + n))
+                            pred, vfeats = tgt.verify([(seq, toks)], taps=self.taps, sampling=samp)
                 except BaseException:
                     s.fail_verification(request_id, ticket)     # poison: the block never publishes
                     tgt.abort(seq)
@@ -230,7 +237,10 @@ class SpecRuntime:
             nxt, cur = None, start
             plist = prompt_host.tolist() if dr is not None else None
             for end in cuts:
-                nxt, feats = tgt.prefill(seq, prompt_dev[cur:end], taps=self.taps)
+                samp = None
+                if getattr(self, "_sampling", None) is not None and end == n:
+                    samp = tgt.sampling_args(*self._sampling, [n])
+                nxt, feats = tgt.prefill(seq, prompt_dev[cur:end], taps=self.taps, sampling=samp)
                 if dr is not None:
                     succ = plist[cur + 1:end + 1] if end < n else plist[cur + 1:n] + [int(nxt.item())]
                     dr.append(feats, cur, next_tokens=succ)

@@ -61,3 +61,18 @@ def test_pinned_acceptance_mean():
         gold = list(range(10, 25))
         cuts.append(next((i for i, (a, b) in enumerate(zip(props, gold)) if a != b), 15))
     assert abs(sum(cuts) / len(cuts) - 6) < 0.7
+
+
+def test_sampled_generate_speculates_exactly(tiny):
+    """``SpecRuntime.generate`` with a temperature reproduces the target's own one-token-per-step
+    sample while committing several tokens per block."""
+    from qwen38_b200.models.drafter import BlockDrafter
+    from qwen38_b200.spec.engine import PinnedAcceptance, SpecRuntime
+    tgt = HybridTarget(tiny["cfg"], tiny["src"], RuntimeConfig(max_context=512, prefill_chunk=64, gdn_chunk=16))
+    dr = BlockDrafter(tiny["dcfg"], tiny["dsrc"], tgt)
+    ref = tgt.sample(torch.tensor(tiny["prompt"]), 24, temperature=0.7, seed=3)
+    res = SpecRuntime(tgt, dr, verifier_rows=4).generate(
+        tiny["prompt"], 24, temperature=0.7, seed=3, pinned=PinnedAcceptance(ref, seed=1, mean_accepted=2))
+    assert res["tokens"] == ref and res["tokens_per_block"] > 1
+    greedy = SpecRuntime(tgt, dr, verifier_rows=4).generate(tiny["prompt"], 24)["tokens"]
+    assert greedy == tgt.greedy(torch.tensor(tiny["prompt"]), 24)
