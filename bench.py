@@ -42,6 +42,8 @@ def parse():
     ap.add_argument("--model", default="full", choices=["full", "tiny"])
     ap.add_argument("--layers", type=int, default=0, help="debug only: truncate the target (invalid as a bench)")
     ap.add_argument("--mean-accepted", type=int, default=6)
+    ap.add_argument("--temperature", type=float, default=0.0,
+                    help="> 0: sampled decoding (speculative, exact against the target's own sampler)")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "mxfp8"],
                     help="mxfp8: target linear weights are their MXFP8 round trip (computed in bf16)")
     ap.add_argument("--drafter", default="dspark", choices=["dspark", "dflash2"],
@@ -205,7 +207,10 @@ def main():
     prompt_host = prompt.pin_memory()
     n_out = args.new_tokens + 1                      # the prefill seed + committed decode tokens
     t_gold = time.time()
-    gold = greedy_reference(tgt, prompt.tolist(), n_out)
+    if args.temperature > 0:
+        gold = tgt.sample(prompt.to(device), n_out, temperature=args.temperature, seed=args.seed)
+    else:
+        gold = greedy_reference(tgt, prompt.tolist(), n_out)
     torch.cuda.synchronize()
     t_gold = time.time() - t_gold
     sr = SpecRuntime(tgt, dr, verifier_rows=dcfg.block_rows)
@@ -218,7 +223,8 @@ def main():
         w0 = time.perf_counter()
         res = sr.generate(prompt_host, n_out, pinned=PinnedAcceptance(gold, seed=1000 + step,
                                                                      mean_accepted=args.mean_accepted),
-                          gold_check=gold, prompt_host=prompt_host)
+                          gold_check=gold, prompt_host=prompt_host,
+                          **({"temperature": args.temperature, "seed": args.seed} if args.temperature > 0 else {}))
         torch.cuda.synchronize()
         wall = time.perf_counter() - w0
         if hasattr(ops, "check"):
@@ -264,7 +270,7 @@ def main():
             "config": {"model": f"{args.model}-hybrid-27B-class" if args.model == "full" else "tiny",
                        "layers": cfg.num_hidden_layers, "global_batch": 1, "seq_len": args.ctx,
                        "new_tokens": args.new_tokens, "block_rows": dcfg.block_rows, "prefill_chunk": args.prefill_chunk,
-                       "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers, "weights": args.weights,
+                       "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers, "weights": args.weights, "temperature": args.temperature,
                        "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
