@@ -10,8 +10,8 @@ the byte-level fallback tokenizer below - checkpoints' own tokenizers need netwo
 fetch), ``POST /v1/chat/completions`` (``messages`` rendered with a plain role template),
 ``GET /v1/models``, ``GET /health``, ``GET /metrics`` (Prometheus text).  ``"logprobs": k`` on a
 non-streaming completion returns each output token's log-probability and the top k, scored on the
-engine thread(s) by the model's own final norm and LM head; ``"stop"`` strings end a
-non-streaming request at the step they appear in and cut the text before them.  With ``"stream": true``
+engine thread(s) by the model's own final norm and LM head; ``"stop"`` strings end a request at
+the step they appear in and cut the text before them (streams hold back a possible partial match).  With ``"stream": true``
 both generation endpoints answer with server-sent events, one event per engine step that emitted
 tokens (a speculative block commits several tokens at once), then ``data: [DONE]``.
 
@@ -51,7 +51,7 @@ class CompletionRequest(BaseModel):
     stream: bool = False
     stream_options: StreamOptions | None = None
     logprobs: int | None = None       # > 0: log-probability of each output token and the top-k
-    stop: str | list[str] | None = None   # text ends before the first stop string (non-streaming)
+    stop: str | list[str] | None = None   # text ends before the first stop string
 
 
 class ChatMessage(BaseModel):
@@ -372,8 +372,6 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         if seed is None:
             seed = body.seed if body.seed is not None else uuid.uuid4().int & 0x7FFFFFFF
         stops = _stops(body)
-        if stops and body.stream:
-            raise HTTPException(400, "stop strings are served on non-streaming requests")
         return loop.submit(ids, body.max_tokens, body.stop_token_ids or (), body.temperature, seed, body.stream,
                            stop=stops)
 
@@ -417,6 +415,10 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 loop.cancel(box["rid"])
 
     def _event_lines(box, body, chunk, n_prompt, emitted):
+        stops = _stops(body)
+        if stops:
+            yield from _event_lines_stop(box, body, chunk, n_prompt, emitted, stops)
+            return
         while True:
             try:
                 new = box["stream"].get(timeout=timeout_s)
@@ -436,6 +438,46 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 break
             emitted += new
             yield "data: " + json.dumps(chunk(new, None)) + "\n\n"
+        yield "data: [DONE]\n\n"
+
+    def _event_lines_stop(box, body, chunk, n_prompt, emitted, stops):
+        """Streaming with stop strings: text that could still be the start of a stop string is held
+        back until the next tokens settle it; at a stop string the text before it goes out and the
+        stream ends with finish_reason "stop" (the engine ends the request at the same step)."""
+        hold, sent = max(len(x) for x in stops) - 1, 0
+
+        def usage(last):
+            if body.stream_options is not None and body.stream_options.include_usage:
+                last["usage"] = {"prompt_tokens": n_prompt, "completion_tokens": len(emitted),
+                                 "total_tokens": n_prompt + len(emitted)}
+            return last
+        while True:
+            try:
+                new = box["stream"].get(timeout=timeout_s)
+            except queue.Empty:
+                yield "data: " + json.dumps({"error": "generation timed out"}) + "\n\n"
+                break
+            if new is None:
+                req = box.get("request")
+                if "error" in box or req is None or req.state != FINISHED:
+                    reason = box.get("error") or getattr(req, "error", "aborted")
+                    yield "data: " + json.dumps({"error": str(reason)}) + "\n\n"
+                else:
+                    text = tok.decode(emitted)
+                    cuts = [text.find(x) for x in stops if x in text]
+                    end = min(cuts) if cuts else len(text)
+                    yield "data: " + json.dumps(usage(chunk([], "stop" if cuts else _finish_reason(emitted, body),
+                                                             text=text[sent:end]))) + "\n\n"
+                break
+            emitted += new
+            text = tok.decode(emitted)
+            cuts = [text.find(x) for x in stops if x in text]
+            if cuts:
+                yield "data: " + json.dumps(usage(chunk(new, "stop", text=text[sent:min(cuts)]))) + "\n\n"
+                break
+            safe = max(sent, len(text) - hold)
+            yield "data: " + json.dumps(chunk(new, None, text=text[sent:safe])) + "\n\n"
+            sent = safe
         yield "data: [DONE]\n\n"
 
     def _logprobs(ids, out, k):
@@ -475,9 +517,10 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         done, box = _start(ids, body)
         cid, created, model = "cmpl-" + uuid.uuid4().hex[:16], int(time.time()), body.model or model_name
         if body.stream:
-            def chunk(new, reason):
+            def chunk(new, reason, text=None):
                 return {"id": cid, "object": "text_completion", "created": created, "model": model,
-                        "choices": [{"index": 0, "text": tok.decode(new), "token_ids": new, "finish_reason": reason}]}
+                        "choices": [{"index": 0, "text": tok.decode(new) if text is None else text,
+                                     "token_ids": new, "finish_reason": reason}]}
             return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
         out = _finished(done, box)
         lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
@@ -540,8 +583,9 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                               "total_tokens": len(ids) + n_out}}
         done, box = _start(ids, body)
         if body.stream:
-            def chunk(new, reason):
-                delta = {"role": "assistant", "content": tok.decode(new)} if new else {}
+            def chunk(new, reason, text=None):
+                content = tok.decode(new) if text is None else text
+                delta = {"role": "assistant", "content": content} if (new or content) else {}
                 return {"id": cid, "object": "chat.completion.chunk", "created": created, "model": model,
                         "choices": [{"index": 0, "delta": delta, "finish_reason": reason}]}
             return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")

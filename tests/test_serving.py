@@ -445,7 +445,7 @@ def test_tensor_parallel_server_ranks_follow_rank0(tiny):
 
 def test_stop_strings_end_requests_early():
     """A stop string cuts the text before it, reports finish_reason "stop" and ends generation at
-    the step it appears in (fewer tokens than the budget); streaming refuses the option."""
+    the step it appears in (fewer tokens than the budget), streamed or not."""
     from fastapi.testclient import TestClient
 
     from qwen38_b200.runconfig import load_run_config
@@ -466,8 +466,13 @@ def test_stop_strings_end_requests_early():
         ch = r["choices"][0]
         assert ch["finish_reason"] == "stop" and ch["text"] == text[:text.find(stop)]
         assert len(ch["token_ids"]) < 80 and ch["token_ids"] == ids[:len(ch["token_ids"])]
-        bad = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 4, "stop": "x", "stream": True})
-        assert bad.status_code == 400
+        # streamed: the text before the stop string arrives in pieces, then finish_reason "stop"
+        import json as _json
+        sr = client.post("/v1/completions", json={"prompt": prompt, "max_tokens": 80, "stop": [stop, "zzz"],
+                                                  "stream": True})
+        events = [_json.loads(l[6:]) for l in sr.text.splitlines() if l.startswith("data: {")]
+        assert "".join(e["choices"][0]["text"] for e in events) == text[:text.find(stop)]
+        assert events[-1]["choices"][0]["finish_reason"] == "stop"
     app.state.loop.close()
 
 
