@@ -52,6 +52,7 @@ class CompletionRequest(BaseModel):
     stream_options: StreamOptions | None = None
     logprobs: int | None = None       # > 0: log-probability of each output token and the top-k
     stop: str | list[str] | None = None   # text ends before the first stop string
+    echo: bool = False                # the prompt's text is prepended to the completion's text
 
 
 class ChatMessage(BaseModel):
@@ -525,6 +526,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         out = _finished(done, box)
         lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
         text, reason = _text(out, body)
+        if body.echo:
+            text = tok.decode(ids) + text
         return {
             "id": cid, "object": "text_completion", "created": created, "model": model,
             "choices": [{"index": 0, "text": text, "token_ids": out, "logprobs": lp, "finish_reason": reason}],
@@ -542,6 +545,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
             out = _finished(done, box)
             lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
             text, reason = _text(out, body)
+            if body.echo:
+                text = tok.decode(ids) + text
             choices.append({"index": i, "text": text, "token_ids": out, "logprobs": lp, "finish_reason": reason})
             n_out += len(out)
         n_in = sum(len(p) for p in prompts)

@@ -627,3 +627,18 @@ def test_sampled_requests_speculate_exactly(tiny):
             assert max(b["committed"] for b in req.blocks) > 1 and len(req.blocks) < 23
         if not speculate:
             assert all(b["rows"] == 1 for b in req.blocks)
+
+
+def test_completion_echo():
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu"))
+    app = build_app(eng)
+    with TestClient(app) as client:
+        a = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4}).json()["choices"][0]
+        b = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4, "echo": True}).json()["choices"][0]
+        assert b["text"] == "abc" + a["text"] and b["token_ids"] == a["token_ids"]
+    app.state.loop.close()
