@@ -362,7 +362,8 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
 
     @app.get("/v1/models")
     def models():
-        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "qwen38_b200"}]}
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "qwen38_b200",
+                                            "max_model_len": engine.target.rt.max_context}]}
 
     def _start(ids, body, seed=None):
         if not ids:

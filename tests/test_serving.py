@@ -104,6 +104,7 @@ def test_openai_http_front_end(tiny):
     with TestClient(app) as client:
         assert client.get("/health").json()["status"] == "ok"
         assert client.get("/v1/models").json()["data"][0]["id"] == "tiny"
+        assert client.get("/v1/models").json()["data"][0]["max_model_len"] == eng.target.rt.max_context
         r = client.post("/v1/completions", json={"prompt": p1, "max_tokens": 8})
         assert r.status_code == 200
         body = r.json()
