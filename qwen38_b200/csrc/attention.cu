@@ -736,7 +736,9 @@ void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor
 #define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
     auto k = a.window > 0 ? q38::attn_decode_kernel<DD, true> : q38::attn_decode_kernel<DD, false>;         \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                        \
+    TORCH_CHECK((a.window > 0 ? q38::set_smem_once<q38::attn_decode_kernel<DD, true>>((int)smem)             \
+                              : q38::set_smem_once<q38::attn_decode_kernel<DD, false>>((int)smem)) == cudaSuccess, \
+                "cudaFuncSetAttribute failed");                                                             \
     q38::launch_pdl(k, grid, dim3(warps * 32), smem, st, a);                                               \
   }
   if (D == 256) Q38_DEC(256)
@@ -792,7 +794,8 @@ void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcach
   {                                                                                                 \
     const size_t smem = (size_t)(rep * q38::PF_QT + 4 * q38::PF_KT) * (DD + 8) * 2;                 \
     auto k = q38::attn_prefill_kernel<DD>;                                                          \
-    cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);                \
+    TORCH_CHECK(q38::set_smem_once<q38::attn_prefill_kernel<DD>>((int)smem) == cudaSuccess,          \
+                "cudaFuncSetAttribute failed");                                                     \
     TORCH_CHECK(q38::launch_pdl(k, grid, dim3(rep * 32), smem, st, a) == cudaSuccess, "prefill attention launch"); \
   }
   if (D == 256) Q38_PF(256)

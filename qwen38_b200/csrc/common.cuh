@@ -11,6 +11,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <atomic>
+
 namespace q38 {
 
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;  // 2 s
@@ -232,6 +234,40 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 bool pdl_enabled();   // host: on by default, Q38_PDL=0 disables the launch attribute
+
+// Host: makes sure kernel K may use `bytes` of dynamic shared memory on the current device (the
+// attribute belongs to the device's context, so a process driving several GPUs sets it on each);
+// the attribute call is made only when a device first needs a larger limit.
+template <auto K>
+inline cudaError_t set_smem_once(int bytes) {
+  static std::atomic<int> done[64];          // largest limit set so far, per device ordinal < 64
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 64 && done[dev].load(std::memory_order_acquire) >= bytes) return cudaSuccess;
+  e = cudaFuncSetAttribute(K, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e == cudaSuccess && dev < 64) {
+    int cur = done[dev].load(std::memory_order_relaxed);
+    while (cur < bytes && !done[dev].compare_exchange_weak(cur, bytes, std::memory_order_acq_rel)) {
+    }
+  }
+  return e;
+}
+
+// Host: number of SMs of the current device (cached per device ordinal).
+inline int device_sms() {
+  static std::atomic<int> cache[64];
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 148;
+  if (dev < 64) {
+    const int c = cache[dev].load(std::memory_order_relaxed);
+    if (c > 0) return c;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess || n <= 0) n = 148;
+  if (dev < 64) cache[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
 
 template <typename Kern, typename... Args>
 inline cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {

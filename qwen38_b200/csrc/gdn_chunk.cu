@@ -644,12 +644,8 @@ void q38_gdn_chunk_prefill(torch::Tensor proj, torch::Tensor window, torch::Tens
   TORCH_CHECK((size_t)(wp - reinterpret_cast<uint8_t*>(work.data_ptr())) <=
                   (size_t)work.numel() * work.element_size(), "GDN chunk workspace too small");
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  static bool cfg = false;
-  if (!cfg) {
-    cudaFuncSetAttribute(gdn_chunk_prep_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, PREP_SMEM);
-    cudaFuncSetAttribute(gdn_chunk_scan_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SCAN_SMEM);
-    cfg = true;
-  }
+  TORCH_CHECK(q38::set_smem_once<gdn_chunk_prep_kernel>(PREP_SMEM) == cudaSuccess &&
+                  q38::set_smem_once<gdn_chunk_scan_kernel>(SCAN_SMEM) == cudaSuccess, "cudaFuncSetAttribute failed");
   gdn_chunk_prep_kernel<<<dim3(nch, (unsigned)nv), 256, PREP_SMEM, st>>>(pa);
   C10_CUDA_KERNEL_LAUNCH_CHECK();
   ScanArgs sa{};

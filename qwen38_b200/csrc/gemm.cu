@@ -133,15 +133,7 @@ static Scratch scratch_of(torch::Tensor ws, torch::Tensor counters, torch::Tenso
   return Scratch{ws.data_ptr<float>(), ws.numel(), counters.data_ptr<int>(), counters.numel(), err.data_ptr<int>()};
 }
 
-static int num_sms() {
-  static int n = 0;
-  if (!n) {
-    int dev;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-  }
-  return n;
-}
+static int num_sms() { return device_sms(); }
 
 // out (m, n) layout: swap -> out[n * ldo + m]; prefill -> out[m * ldo + n]
 // `w` is a tile-contiguous weight ([ceil(N/128) * ceil(K/64) * 128, 64], see tile_weight in

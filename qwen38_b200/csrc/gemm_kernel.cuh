@@ -451,12 +451,8 @@ template <int BN, int STAGES, int EPI, bool SWAP>
 void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st) {
   auto kern = gemm_tn_kernel<BN, STAGES, EPI, SWAP>;
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
-  static bool configured = false;
-  if (!configured) {
-    TORCH_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) == cudaSuccess,
-                "cudaFuncSetAttribute failed");
-    configured = true;
-  }
+  const cudaError_t attr = set_smem_once<gemm_tn_kernel<BN, STAGES, EPI, SWAP>>(smem);
+  TORCH_CHECK(attr == cudaSuccess, "cudaFuncSetAttribute failed");
   TORCH_CHECK(launch_pdl(kern, grid, dim3(128), (size_t)smem, st, ma, mb, g) == cudaSuccess, "GEMM launch failed");
 }
 

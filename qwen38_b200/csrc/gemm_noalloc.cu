@@ -11,6 +11,8 @@
 // `g_scratch` below, a fixed 8 MiB + 16 KiB that every GPU loading this library holds until the
 // process exits.
 //
+// C interface (prototypes, return codes, limits): q38_noalloc.h.
+//
 //   int q38_linear_noalloc(x, T, K, w_tiled, N, out, ldo, epi, stream)
 //     x        bf16 [T, K] row-major, T <= 32, K % 8 == 0, 16-byte aligned
 //     w_tiled  bf16 weight of logical shape [N, K] in the tile-contiguous layout of
@@ -27,6 +29,7 @@
 // its stream) before launching.  Calls that overlap on the GPU (different streams, or a second
 // host thread) race on the scratch: serialise them.
 #include "gemm_kernel.cuh"
+#include "q38_noalloc.h"
 
 #include <mutex>
 
@@ -86,13 +89,12 @@ static cudaError_t launch(const CUtensorMap& ma, const CUtensorMap& mb, const Ge
 }  // namespace noalloc
 }  // namespace q38
 
-enum {
-  Q38_NOALLOC_OK = 0,
-  Q38_NOALLOC_EARG = 1,      // shape / alignment / epilogue not served
-  Q38_NOALLOC_ESIZE = 2,     // the call needs more scratch than g_scratch holds
-  Q38_NOALLOC_ECUDA = 3,     // set-up, map encoding or launch failed
-};
+static_assert(q38::noalloc::kCounters == Q38_NOALLOC_MAX_TILES, "header limit out of date");
+static_assert(q38::noalloc::kPartialFloats == Q38_NOALLOC_MAX_PARTIAL_FLOATS, "header limit out of date");
+static_assert(Q38_NOALLOC_EPI_BF16 == q38::EPI_BF16 && Q38_NOALLOC_EPI_F32 == q38::EPI_F32 &&
+                  Q38_NOALLOC_EPI_ADD_F32 == q38::EPI_ADD_F32, "header epilogue codes out of date");
 
+// Declared in q38_noalloc.h (the C interface); the definitions below must match it.
 extern "C" __attribute__((visibility("default"))) int q38_linear_noalloc(const void* x, int T, int K,
                                                                           const void* w_tiled, int N, void* out,
                                                                           int ldo, int epi, cudaStream_t stream) {
@@ -156,7 +158,7 @@ extern "C" __attribute__((visibility("default"))) int q38_linear_noalloc(const v
 
 // Error word of the last call on the current device (wait timeouts, see csrc/common.cuh); copies one
 // int to the host after synchronising the device.  Returns -1 if the scratch is not set up.
-extern "C" __attribute__((visibility("default"))) int q38_linear_noalloc_status() {
+extern "C" __attribute__((visibility("default"))) int q38_linear_noalloc_status(void) {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= q38::noalloc::kMaxDevices) return -1;
   if (q38::noalloc::g_scratch_dev[dev] == nullptr) return -1;

@@ -18,6 +18,7 @@ if not torch.cuda.is_available():
 
 from qwen38_b200.ops.build import so_path  # noqa: E402
 from qwen38_b200.ops.native import NativeOps  # noqa: E402
+from qwen38_b200.ops.noalloc import bind  # noqa: E402
 
 EPI_BF16, EPI_F32, EPI_ADD_F32 = 0, 1, 2
 
@@ -25,15 +26,7 @@ EPI_BF16, EPI_F32, EPI_ADD_F32 = 0, 1, 2
 @pytest.fixture(scope="module")
 def lib():
     NativeOps()                       # loads the extension (and libtorch) into this process
-    so = ctypes.CDLL(so_path())
-    fn = so.q38_linear_noalloc
-    fn.restype = ctypes.c_int
-    fn.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p,
-                   ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
-    st = so.q38_linear_noalloc_status
-    st.restype = ctypes.c_int
-    st.argtypes = []
-    return fn, st
+    return bind(so_path())            # argument types from csrc/q38_noalloc.h's prototypes
 
 
 def _call(fn, x, tw, out, epi):
