@@ -344,6 +344,55 @@ def follow(engine, sync):
             engine.step()
 
 
+class TextStream:
+    """Incremental text of a streamed completion.  Every step decodes the whole output so far and
+    returns only the part no later token can change:
+
+    * a multi-byte character whose bytes arrive over several steps decodes as trailing replacement
+      characters until its last byte lands, so up to three trailing U+FFFD are held back (the
+      character then goes out once, whole);
+    * with stop strings, text that could still be the start of one is held back; when a stop
+      string appears, the text before it is returned with ``stopped`` set.
+
+    ``finish()`` returns whatever is still held when generation ends."""
+
+    def __init__(self, tok, stops=()):
+        self.tok, self.stops = tok, list(stops)
+        self.hold = max((len(x) for x in self.stops), default=1) - 1
+        self.ids, self.sent = [], 0
+
+    @staticmethod
+    def settled(text: str) -> int:
+        n, k = len(text), 0
+        while k < 3 and n - k > 0 and text[n - k - 1] == "\ufffd":
+            k += 1
+        return n - k
+
+    def _stop_at(self, text):
+        cuts = [text.find(x) for x in self.stops if x in text]
+        return min(cuts) if cuts else None
+
+    def push(self, new):
+        """(new text, stopped) after the step's tokens ``new``."""
+        self.ids += list(new)
+        text = self.tok.decode(self.ids)
+        cut = self._stop_at(text)
+        if cut is not None:
+            out, self.sent = text[self.sent:cut], cut
+            return out, True
+        safe = max(self.sent, self.settled(text) - self.hold)
+        out, self.sent = text[self.sent:safe], safe
+        return out, False
+
+    def finish(self):
+        """(remaining text, stopped) at the end of generation."""
+        text = self.tok.decode(self.ids)
+        cut = self._stop_at(text)
+        end = len(text) if cut is None else cut
+        out, self.sent = text[self.sent:end], max(self.sent, end)
+        return out, cut is not None
+
+
 def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout_s: float = 600.0,
               output_budget_multiple: int = 0, sync=None, phase_log: str | None = None):
     from fastapi import FastAPI, HTTPException
@@ -405,81 +454,56 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
     def _finish_reason(out, body):
         return "stop" if out and out[-1] in (body.stop_token_ids or ()) else "length"
 
-    def _events(box, body, chunk, n_prompt):
-        """Server-sent events: one per engine step that emitted tokens, the finish event (with the
-        token accounting when ``stream_options.include_usage``), then [DONE]."""
+    def _events(box, body, chunk, n_prompt, echo_text=""):
+        """Server-sent events: the echoed prompt (completions with ``echo``), one event per engine
+        step that emitted tokens, the finish event (with the token accounting when
+        ``stream_options.include_usage``), then [DONE]."""
         emitted, ended = [], False
         try:
-            yield from _event_lines(box, body, chunk, n_prompt, emitted)
+            yield from _event_lines(box, body, chunk, n_prompt, emitted, echo_text)
             ended = True
         finally:
             if not ended and "rid" in box:          # the client went away mid-stream
                 loop.cancel(box["rid"])
 
-    def _event_lines(box, body, chunk, n_prompt, emitted):
-        stops = _stops(body)
-        if stops:
-            yield from _event_lines_stop(box, body, chunk, n_prompt, emitted, stops)
-            return
-        while True:
-            try:
-                new = box["stream"].get(timeout=timeout_s)
-            except queue.Empty:
-                yield "data: " + json.dumps({"error": "generation timed out"}) + "\n\n"
-                break
-            if new is None:
-                if "error" in box or box.get("request") is None or box["request"].state != FINISHED:
-                    reason = box.get("error") or getattr(box.get("request"), "error", "aborted")
-                    yield "data: " + json.dumps({"error": str(reason)}) + "\n\n"
-                else:
-                    last = chunk([], _finish_reason(emitted, body))
-                    if body.stream_options is not None and body.stream_options.include_usage:
-                        last["usage"] = {"prompt_tokens": n_prompt, "completion_tokens": len(emitted),
-                                         "total_tokens": n_prompt + len(emitted)}
-                    yield "data: " + json.dumps(last) + "\n\n"
-                break
-            emitted += new
-            yield "data: " + json.dumps(chunk(new, None)) + "\n\n"
-        yield "data: [DONE]\n\n"
+    def _event_lines(box, body, chunk, n_prompt, emitted, echo_text=""):
+        """Each event carries the new part of the decoded output text (``TextStream``); at a stop
+        string the stream ends with finish_reason "stop" (the engine ends the request at the same
+        step)."""
+        ts = TextStream(tok, _stops(body))
 
-    def _event_lines_stop(box, body, chunk, n_prompt, emitted, stops):
-        """Streaming with stop strings: text that could still be the start of a stop string is held
-        back until the next tokens settle it; at a stop string the text before it goes out and the
-        stream ends with finish_reason "stop" (the engine ends the request at the same step)."""
-        hold, sent = max(len(x) for x in stops) - 1, 0
+        def event(obj):
+            return "data: " + json.dumps(obj) + "\n\n"
 
         def usage(last):
             if body.stream_options is not None and body.stream_options.include_usage:
                 last["usage"] = {"prompt_tokens": n_prompt, "completion_tokens": len(emitted),
                                  "total_tokens": n_prompt + len(emitted)}
             return last
+
+        if echo_text:
+            yield event(chunk([], None, text=echo_text))
         while True:
             try:
                 new = box["stream"].get(timeout=timeout_s)
             except queue.Empty:
-                yield "data: " + json.dumps({"error": "generation timed out"}) + "\n\n"
+                yield event({"error": "generation timed out"})
                 break
             if new is None:
                 req = box.get("request")
                 if "error" in box or req is None or req.state != FINISHED:
                     reason = box.get("error") or getattr(req, "error", "aborted")
-                    yield "data: " + json.dumps({"error": str(reason)}) + "\n\n"
+                    yield event({"error": str(reason)})
                 else:
-                    text = tok.decode(emitted)
-                    cuts = [text.find(x) for x in stops if x in text]
-                    end = min(cuts) if cuts else len(text)
-                    yield "data: " + json.dumps(usage(chunk([], "stop" if cuts else _finish_reason(emitted, body),
-                                                             text=text[sent:end]))) + "\n\n"
+                    text, stopped = ts.finish()
+                    yield event(usage(chunk([], "stop" if stopped else _finish_reason(emitted, body), text=text)))
                 break
             emitted += new
-            text = tok.decode(emitted)
-            cuts = [text.find(x) for x in stops if x in text]
-            if cuts:
-                yield "data: " + json.dumps(usage(chunk(new, "stop", text=text[sent:min(cuts)]))) + "\n\n"
+            text, stopped = ts.push(new)
+            if stopped:
+                yield event(usage(chunk(new, "stop", text=text)))
                 break
-            safe = max(sent, len(text) - hold)
-            yield "data: " + json.dumps(chunk(new, None, text=text[sent:safe])) + "\n\n"
-            sent = safe
+            yield event(chunk(new, None, text=text))
         yield "data: [DONE]\n\n"
 
     def _logprobs(ids, out, k):
@@ -494,6 +518,20 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 "top_logprobs": [{tok.decode([int(i)]): float(v) for i, v in zip(ir, vr)}
                                  for ir, vr in zip(ti.tolist(), tv.tolist())],
                 "top_token_ids": ti.tolist(), "top_token_logprobs": tv.tolist()}
+
+    def _completion_logprobs(ids, out, body):
+        """``logprobs`` of a completion; with ``echo`` they cover the prompt tokens too (the first
+        prompt token has no context, so its entries are null, as in the OpenAI API)."""
+        if body.logprobs is None:
+            return None
+        k = max(1, body.logprobs)
+        if not body.echo or len(ids) < 1:
+            return _logprobs(ids, out, k)
+        lp = _logprobs(ids[:1], list(ids[1:]) + list(out), k)
+        return {"tokens": [tok.decode([ids[0]])] + lp["tokens"], "token_ids": [ids[0]] + lp["token_ids"],
+                "token_logprobs": [None] + lp["token_logprobs"], "top_logprobs": [None] + lp["top_logprobs"],
+                "top_token_ids": [None] + lp["top_token_ids"],
+                "top_token_logprobs": [None] + lp["top_token_logprobs"]}
 
     def _prompt_list(p):
         if isinstance(p, str):
@@ -523,9 +561,10 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
                 return {"id": cid, "object": "text_completion", "created": created, "model": model,
                         "choices": [{"index": 0, "text": tok.decode(new) if text is None else text,
                                      "token_ids": new, "finish_reason": reason}]}
-            return StreamingResponse(_events(box, body, chunk, len(ids)), media_type="text/event-stream")
+            return StreamingResponse(_events(box, body, chunk, len(ids), tok.decode(ids) if body.echo else ""),
+                                     media_type="text/event-stream")
         out = _finished(done, box)
-        lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
+        lp = _completion_logprobs(ids, out, body)
         text, reason = _text(out, body)
         if body.echo:
             text = tok.decode(ids) + text
@@ -544,7 +583,7 @@ def build_app(engine, model_name: str = "qwen38-hybrid", tokenizer=None, timeout
         choices, n_out = [], 0
         for i, (ids, (done, box)) in enumerate(jobs):
             out = _finished(done, box)
-            lp = _logprobs(ids, out, max(1, body.logprobs)) if body.logprobs is not None else None
+            lp = _completion_logprobs(ids, out, body)
             text, reason = _text(out, body)
             if body.echo:
                 text = tok.decode(ids) + text

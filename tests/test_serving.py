@@ -643,3 +643,48 @@ def test_completion_echo():
         b = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4, "echo": True}).json()["choices"][0]
         assert b["text"] == "abc" + a["text"] and b["token_ids"] == a["token_ids"]
     app.state.loop.close()
+
+
+def test_text_stream_keeps_split_characters_whole():
+    """A multi-byte UTF-8 character whose bytes arrive in two engine steps goes out once, whole,
+    with and without stop strings (the streamed text equals the non-streamed text)."""
+    from qwen38_b200.serving.api import ByteTokenizer, TextStream
+    tok = ByteTokenizer()
+    text = "a€b→c"
+    ids = tok.encode(text)
+    steps = [ids[:2], ids[2:3], ids[3:6], ids[6:8], ids[8:]]       # '€' and '→' split over steps
+    for stops in ([], ["x"], ["zz"]):
+        ts = TextStream(tok, stops)
+        parts = [ts.push(s) for s in steps]
+        assert not any(stopped for _, stopped in parts)
+        streamed = "".join(p for p, _ in parts) + ts.finish()[0]
+        assert streamed == text and "�" not in streamed
+    ts = TextStream(tok, ["→"])
+    parts = [ts.push(s) for s in steps]
+    stopped_at = [i for i, (_, st) in enumerate(parts) if st]
+    assert stopped_at and "".join(p for p, _ in parts[:stopped_at[0] + 1]) == "a€b"
+
+
+def test_streaming_completion_echo():
+    """``echo`` on a streamed completion: the prompt text is the first event, then the completion
+    text, which together equal the non-streamed echoed text."""
+    import json
+
+    from fastapi.testclient import TestClient
+
+    from qwen38_b200.runconfig import load_run_config
+    from qwen38_b200.serving.api import build_app
+    from qwen38_b200.serving.factory import build_engine
+    eng = build_engine(load_run_config(profile="tiny-cpu"))
+    app = build_app(eng)
+    with TestClient(app) as client:
+        ref = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4, "echo": True}).json()
+        r = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 4, "echo": True, "stream": True})
+        events = [json.loads(l[6:]) for l in r.text.split("\n") if l.startswith("data: {")]
+        assert events[0]["choices"][0]["text"] == "abc"
+        assert "".join(e["choices"][0]["text"] for e in events) == ref["choices"][0]["text"]
+        lp = client.post("/v1/completions", json={"prompt": "abc", "max_tokens": 3, "echo": True,
+                                                  "logprobs": 2}).json()["choices"][0]["logprobs"]
+        assert lp["token_ids"][:3] == [97, 98, 99] and lp["token_logprobs"][0] is None
+        assert len(lp["token_logprobs"]) == 3 + 3 and all(v is not None for v in lp["token_logprobs"][1:])
+    app.state.loop.close()
