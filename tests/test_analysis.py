@@ -33,11 +33,16 @@ def test_lookup_scoring_rejects_bad_tapes():
 def test_latency_budget():
     blocks = [dict(rows=16, committed=8, draft_ms=2.0, verify_ms=12.0, commit_ms=1.0, cycle_ms=15.0)] * 4
     b = latency_budget(blocks, target_tg=800)
-    assert b["observed_block_tg"] == pytest.approx(1000 * 8 / 15)
-    assert b["required_cycle_ms"] == pytest.approx(10.0)
-    assert b["zero_draft_ceiling_tg"] == pytest.approx(1000 * 8 / 13)
+    assert b["observed_tg"] == pytest.approx(1000 * 8 / 15)
+    assert b["cycle_needed_ms"] == pytest.approx(10.0)
+    assert b["cycle_cut_needed_pct"] == pytest.approx(100 * (1 - 10 / 15))
+    assert b["tokens_per_block_needed"] == pytest.approx(800 * 15 / 1000)
+    assert b["tg_if_free"]["draft"] == pytest.approx(1000 * 8 / 13)
+    assert b["tg_if_free"]["verify"] == pytest.approx(1000 * 8 / 3)
     with pytest.raises(ValueError):
         latency_budget(blocks + [dict(blocks[0], rows=8)])
+    with pytest.raises(ValueError):
+        latency_budget([dict(blocks[0], verify_ms=16.0)])          # a phase longer than the cycle
 
 
 def test_generate_block_records_feed_the_budget(tiny):
@@ -47,7 +52,7 @@ def test_generate_block_records_feed_the_budget(tiny):
     res = SpecRuntime(tgt, None, verifier_rows=4).generate(tiny["prompt"], 12, gold_check=gold)
     recs = res["block_records"]
     assert len(recs) == res["blocks"] and sum(r["committed"] for r in recs) == res["committed"]
-    assert latency_budget(recs)["blocks"] == len(recs)
+    assert latency_budget(recs)["profile"]["blocks"] == len(recs)
 
 
 def test_acceptance_report_statistics():

@@ -144,3 +144,69 @@ def test_hybrid_routing():
     with pytest.raises(ValueError):
         h3.propose("r", 1, selected="n")
     assert h2.propose("r", 1, selected="missing").source == "target"
+
+
+def test_bucket_widths():
+    from qwen38_b200.spec.greedy import bucket_at_most
+    assert [bucket_at_most(n) for n in (1, 2, 3, 5, 8, 15, 16, 31, 40)] == [1, 2, 2, 4, 8, 8, 16, 16, 32]
+
+
+def test_device_selection_matches_host_rule():
+    """``device_accept`` (tensor ops, no read-back) publishes the rows and next seed that the host
+    rule ``select_prefix`` gives, for every cut of a 16-row block."""
+    import random
+
+    import torch
+
+    from qwen38_b200.spec.greedy import accepted_length, device_accept
+    rng = random.Random(3)
+    for cut in range(17):
+        drafts = [rng.randrange(V) for _ in range(15)]
+        preds = list(drafts) + [rng.randrange(V)]
+        if cut < 15:
+            preds[cut] = (drafts[cut] + 1) % V
+        d = select_prefix(drafts, preds, vocab_size=V)
+        block = torch.tensor([7] + drafts)
+        rows, nxt = device_accept(block, torch.tensor(preds))
+        assert int(rows) == d.state_rows and int(nxt) == d.next_input
+        assert int(accepted_length(block[1:], torch.tensor(preds))) == accepted_length(drafts, preds) == d.accepted
+
+
+def _lookup_spec(hist, count, match_limit, prefer_full):
+    """Specification of the lookup policy: among earlier occurrences of the last token, the one
+    with the longest backwards match (capped), then (optionally) the most continuation tokens,
+    then the most recent."""
+    n = len(hist)
+    if n < 2:
+        return [], 0
+    limit = min(match_limit, n - 1)
+    best = None
+    for end in range(n - 1):
+        if hist[end] != hist[-1]:
+            continue
+        k = 1
+        while k < min(limit, end + 1) and hist[end - k] == hist[n - 1 - k]:
+            k += 1
+        key = (k, min(count, n - 1 - end) if prefer_full else 0, end)
+        best = key if best is None or key > best else best
+    if best is None:
+        return [], 0
+    return hist[best[2] + 1:best[2] + 1 + count], best[0]
+
+
+def test_lookup_matches_its_specification_on_random_histories():
+    import random
+    rng = random.Random(11)
+    for trial in range(300):
+        alphabet = rng.choice([2, 3, 5, 20])
+        hist = [rng.randrange(alphabet) for _ in range(rng.randrange(1, 80))]
+        limit = rng.choice([1, 2, 4, 128])
+        window = rng.choice([4, 16, 1000])
+        pf = rng.random() < 0.5
+        lk = LookupDraft("r", hist[:5], history_limit=window, match_limit=limit, prefer_full_suffix=pf)
+        for i in range(5, len(hist), 7):                 # commits in pieces (window trimming, compaction)
+            lk.commit("r", hist[i:i + 7])
+        visible = hist[-window:]
+        assert lk.history == visible
+        for count in (1, 3, 15):
+            assert tuple(lk.propose_with_match("r", count)) == tuple(_lookup_spec(visible, count, limit, pf))
