@@ -436,18 +436,19 @@ __global__ void attn_combine_kernel(DecodeArgs a, const __nv_bfloat16* gate, lon
   __syncthreads();
   float L = 0.f;
   for (int s = 0; s < ns; ++s) L += cm[2 * s + 1];
-  // 2. weighted sum of the partial outputs, eight splits' loads in flight at a time
+  // 2. weighted sum of the partial outputs, 32 splits' loads in flight at a time (one round trip
+  //    up to 4,096 keys), summed in split order
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float acc = 0.f;
-    for (int s0 = 0; s0 < ns; s0 += 8) {
-      float v[8];
+    for (int s0 = 0; s0 < ns; s0 += 32) {
+      float v[32];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) {
+      for (int u = 0; u < 32; ++u) {
         const int s = s0 + u;
-        v[u] = s < ns ? __ldg(a.part_o + (((size_t)g * a.max_splits + s) * nqv + qv) * D + c) : 0.f;
+        v[u] = s < ns ? __ldcg(a.part_o + (((size_t)g * a.max_splits + s) * nqv + qv) * D + c) : 0.f;
       }
 #pragma unroll
-      for (int u = 0; u < 8; ++u)
+      for (int u = 0; u < 32; ++u)
         if (s0 + u < ns) acc += cm[2 * (s0 + u)] * v[u];
     }
     float y = acc / L;

@@ -46,6 +46,9 @@ void q38_gdn_chunk_prefill(torch::Tensor proj, torch::Tensor window, torch::Tens
                            torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w, torch::Tensor out,
                            torch::Tensor work, int64_t nk, int64_t nv, double eps);
 size_t q38_gdn_chunk_workspace_bytes(int64_t S, int64_t nv);
+void q38_markov_select(torch::Tensor logits, torch::Tensor pred, torch::Tensor succ, torch::Tensor anchor,
+                       torch::Tensor out, int64_t vocab_offset, torch::Tensor rec_val, torch::Tensor rec_idx,
+                       torch::Tensor state, std::vector<int64_t> recv_ptrs, int64_t rank, torch::Tensor err);
 void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
 void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
@@ -84,6 +87,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm", &q38_rms_norm);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);
+  m.def("markov_select", &q38_markov_select);
   m.def("peer_alloc", &q38_peer_alloc);
   m.def("ipc_handle", &q38_ipc_handle);
   m.def("ipc_open", &q38_ipc_open);

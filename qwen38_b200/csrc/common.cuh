@@ -122,6 +122,15 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
       : "memory");
 }
 
+// 1-D bulk copy global -> shared (no multicast) of `bytes` (multiple of 16, both addresses 16-byte
+// aligned), completing on `bar` with complete_tx.
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(gmem_src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 __device__ __forceinline__ uint64_t policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
@@ -284,6 +293,34 @@ inline cudaError_t launch_pdl(Kern kern, dim3 grid, dim3 block, size_t smem, cud
   return cudaLaunchKernelEx(&cfg, kern, args...);
 }
 
+// Same, as a thread-block cluster of `cluster` CTAs (no attribute when the cluster is one CTA).
+template <typename Kern, typename... Args>
+inline cudaError_t launch_pdl_cluster(Kern kern, dim3 grid, dim3 block, size_t smem, cudaStream_t st, dim3 cluster,
+                                      Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[2];
+  int n = 0;
+  if (cluster.x * cluster.y * cluster.z > 1) {
+    attr[n].id = cudaLaunchAttributeClusterDimension;
+    attr[n].val.clusterDim.x = cluster.x;
+    attr[n].val.clusterDim.y = cluster.y;
+    attr[n].val.clusterDim.z = cluster.z;
+    ++n;
+  }
+  if (pdl_enabled()) {
+    attr[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
+  cfg.attrs = attr;
+  cfg.numAttrs = n;
+  return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
 // ------------------------------------------------------------------ sampling noise
 // Counter-based Gumbel noise for sampling by Gumbel-max (argmax of logits / T + G over the
 // vocabulary draws from softmax(logits / T)).  The 64-bit mix is the SplitMix64 finaliser
@@ -299,6 +336,29 @@ __device__ __forceinline__ float gumbel_noise(unsigned long long key, unsigned l
   const unsigned long long h = mix64(key ^ mix64(index + 0x9e3779b97f4a7c15ULL));
   const float u = ((float)(h >> 40) + 0.5f) * (1.0f / 16777216.0f);     // (0, 1), 24 bits
   return -logf(-logf(u));
+}
+
+// ------------------------------------------------------------------ Markov selector scores
+// Dot product of one successor row (bf16 [R]) with pred[prev] (fp32 in shared memory), computed by
+// the 8 lanes of a row group: lane j of the group takes the 8-element chunks j, j + 8, j + 16, ...
+// with fmaf in chunk order, then the group sums with a fixed xor butterfly (4, 2, 1).  Every
+// selector kernel uses this, so they all produce the same score bits.
+__device__ __forceinline__ float markov_row_dot(const __nv_bfloat16* row, const float* pp, int R, int j) {
+  float d = 0.f;
+  for (int c = j; c * 8 < R; c += 8) {
+    const uint4 u = *reinterpret_cast<const uint4*>(row + c * 8);
+    const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float2 f = __bfloat1622float2(b[q]);
+      d = fmaf(f.x, pp[c * 8 + 2 * q], d);
+      d = fmaf(f.y, pp[c * 8 + 2 * q + 1], d);
+    }
+  }
+  d += __shfl_xor_sync(0xffffffffu, d, 4);
+  d += __shfl_xor_sync(0xffffffffu, d, 2);
+  d += __shfl_xor_sync(0xffffffffu, d, 1);
+  return d;
 }
 
 // ------------------------------------------------------------------ misc math

@@ -108,10 +108,10 @@ void clear_map_cache() {
 }
 
 // Split count for a weight of `m_tiles` row tiles and `kblocks` K blocks: a function of the weight
-// shape only (never of the token count), about two CTAs per SM.
-static int pick_splits(int m_tiles, int kblocks, int sms) {
+// shape only (never of the token count), about two CTAs per SM, at most one portable cluster.
+int pick_splits(int m_tiles, int kblocks, int sms) {
   int s = (2 * sms) / std::max(1, m_tiles);
-  s = std::max(1, std::min(s, kblocks / 4));
+  s = std::max(1, std::min(std::min(s, kblocks / 4), MAX_CLUSTER_SPLITS));
   return s;
 }
 
@@ -134,6 +134,15 @@ static Scratch scratch_of(torch::Tensor ws, torch::Tensor counters, torch::Tenso
 }
 
 static int num_sms() { return device_sms(); }
+
+static bool splitk_cluster() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("Q38_SPLITK");
+    v = (e && std::string(e) == "cluster") ? 1 : 0;
+  }
+  return v == 1;
+}
 
 // out (m, n) layout: swap -> out[n * ldo + m]; prefill -> out[m * ldo + n]
 // `w` is a tile-contiguous weight ([ceil(N/128) * ceil(K/64) * 128, 64], see tile_weight in
@@ -163,13 +172,17 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     g.M = N;
     g.N = T;
     const int m_tiles = (N + BM - 1) / BM;
-    int splits = (epi == EPI_SWIGLU || epi == EPI_ARGMAX) ? std::max(1, std::min(2 * num_sms() / m_tiles, g.kblocks / 4))
-                                                         : pick_splits(m_tiles, g.kblocks, num_sms());
+    int splits = pick_splits(m_tiles, g.kblocks, num_sms());
     int kps = (g.kblocks + splits - 1) / splits;
     splits = (g.kblocks + kps - 1) / kps;
     g.splits = splits;
     g.kps = kps;
-    if (splits > 1) {
+    // Split-K fix-up: the last-arriving CTA through global memory by default; Q38_SPLITK=cluster
+    // reduces through DSMEM inside a cluster of the tile's splits (same bits).  Measured on B200
+    // the cluster form was slower: clusters of up to 8 CTAs at two CTAs per SM no longer fit the
+    // grid into one wave once GPC boundaries are respected.  ARGMAX always uses the global form.
+    g.cluster_k = epi != EPI_ARGMAX && splitk_cluster();
+    if (splits > 1 && !g.cluster_k) {
       TORCH_CHECK((int64_t)m_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
       TORCH_CHECK(m_tiles <= sc.n_counters, "split-K counter array too small");
     }

@@ -23,6 +23,8 @@
 #include <torch/extension.h>
 #include <ATen/cuda/CUDAContext.h>
 
+#include <cooperative_groups.h>
+
 #include "common.cuh"
 
 namespace q38 {
@@ -70,6 +72,9 @@ struct GemmArgs {
   const float* samp_scale;    // EPI_ARGMAX: per token row 1/temperature (0: greedy), or nullptr
   const unsigned long long* samp_key;   // per token row noise key
   long long vocab_off;        // global vocabulary index of weight row 0 (noise index)
+  int cluster_k;              // swap mode, splits > 1: the splits of a tile form one cluster and
+                              // reduce through DSMEM (the launch sets cluster dims (1, 1, splits));
+                              // 0: partials through `ws` and the last-arriving CTA (`counters`)
 };
 
 // trace points: 0 entry, 1 setup done, 2 first stage landed, 3 last MMA issued, 4 accumulator
@@ -87,8 +92,103 @@ struct Smem {
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
-  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 1) * 8 + 16 + 1024;  // + alignment slack
+  static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 2) * 8 + 16 + 1024;  // + alignment slack
 };
+
+// Swap-mode split-K through distributed shared memory.  The `splits` CTAs of one weight tile are
+// one thread-block cluster (cluster rank = split).  Each CTA parks its fp32 accumulator tile
+// [32 tokens][128 rows] in its own (now idle) operand ring; after one cluster barrier, CTA c sums
+// every split's values for its slice of the tile's output units in split order 0, 1, .. (the
+// same additions, in the same order, as the last-arriving-CTA fix-up, so the bits do not depend on
+// the path) and runs the epilogue for that slice; a second barrier keeps each CTA's tile alive
+// until its peers have read it.  Compared with the global-memory fix-up this drops the partial
+// round trip through L2, the fence, the arrival counter and the serial tail in one CTA, and the
+// epilogue (the residual update or the NVLink push of EPI_PUSH_F32) runs on every CTA of the tile.
+// Output units: one weight row (128 per tile), or for SwiGLU one [gate, up] row pair (64 per tile).
+// A CTA whose mbarrier wait gave up contributes zeros; the error word already carries the failure.
+template <int EPI>
+__device__ __forceinline__ void swap_cluster_epilogue(const GemmArgs& g, float* tile_s, uint32_t trow, bool have,
+                                                      int m_tile, int split, int row) {
+  namespace cg = cooperative_groups;
+  cg::cluster_group cluster = cg::this_cluster();
+  {
+    uint32_t r[32];
+    if (have) {
+      tmem_ld_32x32b_x32(trow, r);
+      tmem_ld_wait();
+    }
+#pragma unroll
+    for (int j = 0; j < 32; ++j) tile_s[j * BM + row] = have ? __uint_as_float(r[j]) : 0.f;
+  }
+  cluster.sync();
+  if (threadIdx.x == 0) Q38_STAMP(5);
+  constexpr bool SW = EPI == EPI_SWIGLU;
+  constexpr int UNITS = SW ? BM / 2 : BM;
+  constexpr int EMAX = (UNITS / 2) * 32 / 128;       // elements per thread at splits >= 2
+  const int S = g.splits;
+  const int per = (UNITS + S - 1) / S;
+  const int u0 = min(UNITS, split * per), nu = min(UNITS, u0 + per) - u0;
+  const int nvalid = min(32, g.N);
+  const int nel = nu * nvalid;
+  const float* peer[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) peer[q] = q < S ? cluster.map_shared_rank(tile_s, q) : tile_s;
+  // every element's split sum first (all DSMEM loads in flight), then the memory epilogue with
+  // every global load issued before any dependent store
+  float v[EMAX];
+  int off[EMAX];
+#pragma unroll
+  for (int k = 0; k < EMAX; ++k) {
+    const int e = threadIdx.x + k * 128;
+    const int u = u0 + (e < nel ? e % nu : 0), j = e < nel ? e / nu : 0;
+    float acc = 0.f, up = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      if (q < S && e < nel) {
+        acc += peer[q][j * BM + u];
+        if constexpr (SW) up += peer[q][j * BM + u + BM / 2];
+      }
+    }
+    if constexpr (SW) {
+      v[k] = silu_f(acc) * up;
+      off[k] = e < nel ? (int)(j * g.ldo + m_tile * (BM / 2) + u) : -1;
+    } else {
+      v[k] = acc;
+      off[k] = (e < nel && m_tile * BM + u < g.M) ? (int)(j * g.ldo + m_tile * BM + u) : -1;
+    }
+  }
+  if constexpr (EPI == EPI_ADD_F32) {
+    float* o = reinterpret_cast<float*>(g.out);
+    float r[EMAX];
+#pragma unroll
+    for (int k = 0; k < EMAX; ++k) r[k] = off[k] >= 0 ? o[off[k]] : 0.f;
+#pragma unroll
+    for (int k = 0; k < EMAX; ++k)
+      if (off[k] >= 0) o[off[k]] = r[k] + v[k];
+  } else if constexpr (EPI == EPI_BF16 || SW) {
+#pragma unroll
+    for (int k = 0; k < EMAX; ++k)
+      if (off[k] >= 0) reinterpret_cast<__nv_bfloat16*>(g.out)[off[k]] = __float2bfloat16(v[k]);
+  } else if constexpr (EPI == EPI_F32) {
+#pragma unroll
+    for (int k = 0; k < EMAX; ++k)
+      if (off[k] >= 0) reinterpret_cast<float*>(g.out)[off[k]] = v[k];
+  } else if constexpr (EPI == EPI_PUSH_F32) {
+    const ArArgs& a = g.ar;
+    const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_words;
+#pragma unroll
+    for (int k = 0; k < EMAX; ++k) {
+      if (off[k] < 0) continue;
+      const int j = off[k] / (int)g.ldo;
+      const unsigned long long w =
+          ((unsigned long long)((uint32_t)a.epochs[(size_t)a.slot * AR_MAX_ROWS + j] + 1u) << 32) |
+          __float_as_uint(v[k]);
+      for (int p = 0; p < a.world; ++p)
+        st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.recv[p]) + mine + off[k], w);
+    }
+  }
+  cluster.sync();
+}
 
 template <int BN, int STAGES, int EPI, bool SWAP>
 __global__ void __launch_bounds__(128, 1)
@@ -99,7 +199,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
   uint64_t* empty_bar = full_bar + STAGES;
   uint64_t* acc_bar = empty_bar + STAGES;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 1);
+  uint64_t* fix_bar = acc_bar + 1;                // split-K fix-up: staged partials landed
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
   int* last_flag = reinterpret_cast<int*>(tmem_slot + 2);
 
@@ -211,7 +312,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const int row = warp * 32 + lane;   // TMEM lane == tile row m
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 
-  if (ok && nk > 0) {
+  bool clustered = false;
+  if constexpr (SWAP && EPI != EPI_ARGMAX) {
+    clustered = g.splits > 1 && g.cluster_k;
+    if (clustered)
+      swap_cluster_epilogue<EPI>(g, reinterpret_cast<float*>(smem), trow, ok && nk > 0, m_tile, split, row);
+  }
+  if (ok && nk > 0 && !clustered) {
     if constexpr (SWAP) {
       // Each thread owns output feature m0+row, tokens n0 .. n0+BN-1 (BN == 32).
       static_assert(BN == 32, "swap mode uses 32 token columns");
@@ -239,29 +346,58 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         do_epi = *last_flag != 0;
         if (do_epi) {
           __threadfence();
-          // Sum the partials in split order; the loads of two splits are in flight together
-          // (L2 loads: the partials were written by other CTAs of this grid).
-          const float* base = g.ws + (size_t)tile * g.splits * (BM * BN);
-#pragma unroll
-          for (int j = 0; j < 32; ++j) acc[j] = 0.f;
-          int s = 0;
-          for (; s + 1 < g.splits; s += 2) {
-            const float* p0 = base + (size_t)s * (BM * BN);
-            const float* p1 = p0 + BM * BN;
-            float x0[32], x1[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              x0[j] = __ldcg(p0 + j * BM + row);
-              x1[j] = __ldcg(p1 + j * BM + row);
+          // Sum the partials in split order (the fixing CTA's own from registers).  The other
+          // splits' 16 KB partials are requested at once: up to RING_PARTS by bulk copies into the
+          // idle operand ring (one round trip for all of them), any beyond that by direct L2 loads
+          // issued before the wait.  The partials were written by other CTAs' generic stores and
+          // published by the counter; the proxy fence orders the bulk (async-proxy) reads after.
+          constexpr int PART = BM * BN;                                  // floats per partial
+          constexpr int RING_PARTS = (STAGES * S::STAGE_BYTES) / (PART * 4);
+          const float* base = g.ws + (size_t)tile * g.splits * PART;
+          float* stage = reinterpret_cast<float*>(smem);
+          asm volatile("fence.proxy.async.global;" ::: "memory");
+          if (tid == 0) {
+            mbar_init(fix_bar, 1);
+            fence_mbar_init();
+            int k = 0;
+            const int nb = min(g.splits - 1, RING_PARTS);
+            mbar_expect_tx(fix_bar, (uint32_t)(nb * PART * 4));
+            for (int s = 0; s < g.splits && k < nb; ++s) {
+              if (s == split) continue;
+              bulk_load(stage + (size_t)k * PART, base + (size_t)s * PART, PART * 4, fix_bar);
+              ++k;
             }
-#pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] = (acc[j] + x0[j]) + x1[j];
           }
-          if (s < g.splits) {
-            const float* p0 = base + (size_t)s * (BM * BN);
+          float extra[32];                 // the one direct-loaded partial (splits - 1 > RING_PARTS)
+          int extra_s = -1;
+          if (g.splits - 1 > RING_PARTS) {
+            extra_s = g.splits - 1 == split ? g.splits - 2 : g.splits - 1;
 #pragma unroll
-            for (int j = 0; j < 32; ++j) acc[j] += __ldcg(p0 + j * BM + row);
+            for (int j = 0; j < 32; ++j) extra[j] = __ldcg(base + (size_t)extra_s * PART + j * BM + row);
           }
+          __syncthreads();                 // fix_bar initialised before anyone waits on it
+          const bool staged = mbar_wait(fix_bar, 0, g.err, kErrSplitK, abort_flag);
+          float own[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) { own[j] = acc[j]; acc[j] = 0.f; }
+          if (staged) {
+            int k = 0;
+            for (int s = 0; s < g.splits; ++s) {
+              if (s == split) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[j] += own[j];
+              } else if (s == extra_s) {
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[j] += extra[j];
+              } else {
+                const float* sp = stage + (size_t)k * PART;
+#pragma unroll
+                for (int j = 0; j < 32; ++j) acc[j] += sp[j * BM + row];
+                ++k;
+              }
+            }
+          }
+          __syncthreads();                 // the epilogue may reuse the ring the partials sat in
           if (tid == 0) g.counters[tile] = 0;
         }
       }
@@ -453,12 +589,19 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g
   constexpr int smem = Smem<BN, STAGES>::TOTAL;
   const cudaError_t attr = set_smem_once<gemm_tn_kernel<BN, STAGES, EPI, SWAP>>(smem);
   TORCH_CHECK(attr == cudaSuccess, "cudaFuncSetAttribute failed");
-  TORCH_CHECK(launch_pdl(kern, grid, dim3(128), (size_t)smem, st, ma, mb, g) == cudaSuccess, "GEMM launch failed");
+  const unsigned cz = (SWAP && g.cluster_k && g.splits > 1) ? (unsigned)g.splits : 1u;
+  TORCH_CHECK(launch_pdl_cluster(kern, grid, dim3(128), (size_t)smem, st, dim3(1, 1, cz), ma, mb, g) == cudaSuccess,
+              "GEMM launch failed");
 }
 
 constexpr int SKINNY_STAGES = 5;   // 5 x 20 KB ring: two CTAs per SM
+constexpr int MAX_CLUSTER_SPLITS = 8;   // split-K CTAs of one tile: one portable cluster
 constexpr int PREFILL_BN = 256;
 constexpr int PREFILL_STAGES = 4;  // 4 x 48 KB ring
+
+// Split-K count of the skinny GEMM for a weight shape (gemm.cu; shared by every entry point so
+// they produce the same bits).
+int pick_splits(int m_tiles, int kblocks, int sms);
 
 // epilogue-dispatched launchers, one translation unit each
 void launch_swap(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st);

@@ -117,7 +117,7 @@ extern "C" __attribute__((visibility("default"))) int q38_linear_noalloc(const v
   if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return Q38_NOALLOC_ECUDA;
   const int kblocks = (K + BK - 1) / BK;
   const int m_tiles = (N + BM - 1) / BM;
-  int splits = std::max(1, std::min((2 * sms) / std::max(1, m_tiles), kblocks / 4));
+  int splits = pick_splits(m_tiles, kblocks, sms);
   int kps = (kblocks + splits - 1) / splits;
   splits = (kblocks + kps - 1) / kps;
   if (m_tiles > kCounters) return Q38_NOALLOC_ESIZE;

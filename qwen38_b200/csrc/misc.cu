@@ -13,21 +13,76 @@
 
 namespace q38 {
 
-// One CTA per row; the row stays in registers between the sum of squares and the scaling.
+// RMSNorm rows are spread over a cluster of NORM_CPR CTAs (128 threads each): CTA c of row r owns
+// the 128-column chunks c, c + NORM_CPR, c + 2 NORM_CPR, ... of the row, so a [16, 5120] residual
+// runs on 128 CTAs instead of 16 and each CTA touches 640 columns.  The sum of squares is reduced
+// in a fixed order (per thread over its chunks, xor butterfly in the warp, the four warps in order,
+// then the cluster's CTAs in rank order through distributed shared memory), so every kernel that
+// normalises with this core - the plain norm and the all-reduce norm - produces the same bits for
+// the same row.
+constexpr int NORM_CPR = 8;
+constexpr int NORM_NT = 128;
+
+__device__ __forceinline__ void cluster_arrive_relaxed() {
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ uint32_t cluster_rank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Store `v` into CTA `rank`'s copy of the shared variable at `local`.
+__device__ __forceinline__ void st_cluster_f32(const float* local, uint32_t rank, float v) {
+  uint32_t a = smem_u32(local), ra;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(a), "r"(rank));
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(ra), "f"(v) : "memory");
+}
+
+// Row total of the per-thread partial `ss` over the whole cluster (every CTA gets the same bits).
+// `flag` is exchanged alongside (all CTAs learn the minimum); the caller has issued
+// cluster_arrive_relaxed() once at kernel start, which this matches before the first remote store.
+__device__ __forceinline__ float norm_row_total(float ss, int& flag) {
+  __shared__ float red[NORM_NT / 32];
+  __shared__ float xch[NORM_CPR];
+  __shared__ float okx[NORM_CPR];
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  cluster_wait();                                  // every CTA of the cluster has started
+  if (threadIdx.x < NORM_CPR) {
+    const float t = ((red[0] + red[1]) + red[2]) + red[3];
+    const uint32_t me = cluster_rank();
+    st_cluster_f32(&xch[me], threadIdx.x, t);
+    st_cluster_f32(&okx[me], threadIdx.x, (float)flag);
+  }
+  cluster_sync_all();
+  float tot = 0.f;
+#pragma unroll
+  for (int p = 0; p < NORM_CPR; ++p) {
+    tot += xch[p];
+    flag = min(flag, (int)okx[p]);
+  }
+  return tot;
+}
+
 template <typename TIn, int VPT>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(NORM_NT)
 rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restrict__ w, int H, float eps,
                 __nv_bfloat16* __restrict__ out, long long ldo) {
+  cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  const int r = blockIdx.x;
+  const int c = (int)cluster_rank(), r = blockIdx.y;
   const TIn* xr = x + (size_t)r * ldx;
-  __shared__ float red[32];
   float v[VPT], wv[VPT];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {             // row and weight loads share one memory round trip
-    const int i = threadIdx.x + u * blockDim.x;
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
     float f = 0.f;
     wv[u] = 0.f;
     if (i < H) {
@@ -38,30 +93,23 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
     v[u] = f;
     ss += f * f;
   }
-  ss = warp_sum(ss);
-  const int w_ = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) red[w_] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) red[31] = rsqrtf(t / H + eps);
-  }
-  __syncthreads();
-  const float inv = red[31];
+  int flag = 1;
+  const float inv = rsqrtf(norm_row_total(ss, flag) / H + eps);
   __nv_bfloat16* o = out + (size_t)r * ldo;
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {
-    const int i = threadIdx.x + u * blockDim.x;
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
     if (i < H) o[i] = __float2bfloat16(v[u] * inv * wv[u]);
   }
 }
 
-// The second half of the pushed tensor-parallel all-reduce (the GEMM half is EPI_PUSH_F32): one
-// CTA per token row reads every rank's {value, epoch} words of its row, spinning (bounded) on each
-// until this use's epoch appears, adds the W partials in rank order 0..W-1 to the fp32 residual row
-// (identical bits on every rank), writes the row back, advances the row's epoch, and - when a norm
-// weight is given - emits its RMSNorm in bf16.
+// The second half of the pushed tensor-parallel all-reduce (the GEMM half is EPI_PUSH_F32): the
+// CTAs of a row read every rank's {value, epoch} words of their chunks - all ranks' loads in flight
+// at once - and spin (bounded) on each until this use's epoch appears, add the W partials in rank
+// order 0..W-1 to the fp32 residual (identical bits on every rank), and - when a norm weight is
+// given - emit the row's RMSNorm in bf16.  The residual, the row's epoch and the output are
+// written only when every CTA of the row saw every word: a peer that never published leaves them
+// untouched (the error word records it).
 constexpr int AR_RANKS = 8;
 constexpr int AR_ROWS = 32;
 
@@ -71,86 +119,74 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 
-template <int VPT>
-__global__ void __launch_bounds__(256)
+template <int VPT, int WORLD>
+__global__ void __launch_bounds__(NORM_NT)
 rms_norm_ar_kernel(float* __restrict__ x, int H, const float* __restrict__ w, float eps,
                    __nv_bfloat16* __restrict__ out, long long ldo, const unsigned long long* __restrict__ recv,
-                   int* __restrict__ epochs, int slot, int world, long long block_words, int* err) {
+                   int* __restrict__ epochs, int slot, long long block_words, int* err) {
+  cluster_arrive_relaxed();
   pdl_wait();
   pdl_trigger();
-  const int r = blockIdx.x;
-  __shared__ int ok_s;
-  __shared__ float red[32];
-  if (threadIdx.x == 0) ok_s = 1;
+  const int c = (int)cluster_rank(), r = blockIdx.y;
   const uint32_t e = (uint32_t)epochs[(size_t)slot * AR_ROWS + r] + 1u;
-  __syncthreads();
-  const unsigned long long* base = recv + (size_t)slot * world * block_words + (size_t)r * H;
-  float psum[VPT];                         // rank-ordered sums: ((0 + p_0) + p_1) + ...
-  bool ok = true;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long* base = recv + (size_t)slot * WORLD * block_words + (size_t)r * H;
+  unsigned long long wd[WORLD][VPT];
 #pragma unroll
-  for (int u = 0; u < VPT; ++u) psum[u] = 0.f;
-#pragma unroll
-  for (int q = 0; q < AR_RANKS; ++q) {
-    if (q >= world) break;
-    unsigned long long wv4[VPT];
-#pragma unroll
-    for (int u = 0; u < VPT; ++u) {          // issue every load of this source before spinning
-      const int i = threadIdx.x + u * blockDim.x;
-      wv4[u] = i < H ? ld_relaxed_sys_u64(base + (size_t)q * block_words + i) : ((unsigned long long)e << 32);
-    }
+  for (int q = 0; q < WORLD; ++q)             // every rank's words of this thread's columns in flight
 #pragma unroll
     for (int u = 0; u < VPT; ++u) {
-      const int i = threadIdx.x + u * blockDim.x;
-      while (ok && (uint32_t)(wv4[u] >> 32) != e) {
+      const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+      wd[q][u] = i < H ? ld_relaxed_sys_u64(base + (size_t)q * block_words + i) : ((unsigned long long)e << 32);
+    }
+  int flag = 1;
+  const unsigned long long t0 = globaltimer();
+#pragma unroll
+  for (int q = 0; q < WORLD; ++q)
+#pragma unroll
+    for (int u = 0; u < VPT; ++u) {
+      const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+      while (flag && (uint32_t)(wd[q][u] >> 32) != e) {
         if (globaltimer() - t0 > kWaitLimitNs) {
-          ok = false;
+          flag = 0;
           break;
         }
-        wv4[u] = ld_relaxed_sys_u64(base + (size_t)q * block_words + i);
+        wd[q][u] = ld_relaxed_sys_u64(base + (size_t)q * block_words + i);
       }
-      if (i < H) psum[u] += __uint_as_float((uint32_t)wv4[u]);
     }
-  }
-  if (!ok) {
-    record_error(err, kErrPeer);
-    ok_s = 0;
-  }
-  __syncthreads();
-  if (!ok_s) return;                       // a peer never published: residual and epoch untouched
+  if (!flag) record_error(err, kErrPeer);
+  flag = __syncthreads_and(flag);
   float* xr = x + (size_t)r * H;
   float v[VPT], wv[VPT];
   float ss = 0.f;
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {
-    const int i = threadIdx.x + u * blockDim.x;
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+    float psum = 0.f;                          // rank-ordered: ((0 + p_0) + p_1) + ...
+#pragma unroll
+    for (int q = 0; q < WORLD; ++q) psum += __uint_as_float((uint32_t)wd[q][u]);
     float xv = 0.f;
     wv[u] = 0.f;
     if (i < H) {
       xv = xr[i];
       if (w) wv[u] = w[i];
     }
-    v[u] = xv + psum[u];
-    if (i < H) xr[i] = v[u];
+    v[u] = xv + psum;
     ss += v[u] * v[u];
   }
-  if (threadIdx.x == 0) epochs[(size_t)slot * AR_ROWS + r] = (int)e;
-  if (!out) return;
-  ss = warp_sum(ss);
-  const int w_ = threadIdx.x >> 5, l = threadIdx.x & 31;
-  if (l == 0) red[w_] = ss;
-  __syncthreads();
-  if (threadIdx.x < 32) {
-    float t = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-    t = warp_sum(t);
-    if (threadIdx.x == 0) red[31] = rsqrtf(t / H + eps);
+  const float tot = norm_row_total(ss, flag);
+  if (!flag) return;                          // some CTA of the row missed a word: nothing written
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+    if (i < H) xr[i] = v[u];
   }
-  __syncthreads();
-  const float inv = red[31];
+  if (c == 0 && threadIdx.x == 0) epochs[(size_t)slot * AR_ROWS + r] = (int)e;
+  if (!out) return;
+  const float inv = rsqrtf(tot / H + eps);
   __nv_bfloat16* o = out + (size_t)r * ldo;
 #pragma unroll
   for (int u = 0; u < VPT; ++u) {
-    const int i = threadIdx.x + u * blockDim.x;
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
     if (i < H) o[i] = __float2bfloat16(v[u] * inv * wv[u]);
   }
 }
@@ -175,7 +211,9 @@ __global__ void embed_kernel(const int64_t* __restrict__ ids, const __nv_bfloat1
   }
 }
 
-// One Markov step over a vocab tile of 256 rows: per-tile (max, argmax) of logits + bias.
+// One Markov step over a vocab tile of 256 rows: per-tile (max, argmax) of logits + bias.  The row
+// scores use markov_row_dot (common.cuh), the arithmetic of the one-launch selector (markov.cu).
+
 __global__ void __launch_bounds__(256)
 markov_step_kernel(const float* __restrict__ logits, const __nv_bfloat16* __restrict__ pred,
                    const __nv_bfloat16* __restrict__ succ, int V, int R, const int64_t* __restrict__ prev,
@@ -188,28 +226,22 @@ markov_step_kernel(const float* __restrict__ logits, const __nv_bfloat16* __rest
   const int64_t pv = *prev;
   for (int i = threadIdx.x; i < R; i += blockDim.x) pp[i] = __bfloat162float(pred[(size_t)pv * R + i]);
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, grp = threadIdx.x >> 3, j = threadIdx.x & 7;
   float best = -INFINITY;
   int bi = 0x7fffffff;
   const int v0 = blockIdx.x * 256;
-  for (int rr = warp; rr < 256; rr += 8) {
-    const int v = v0 + rr;
-    if (v >= V) break;
-    const __nv_bfloat16* srow = succ + (size_t)v * R;
-    float d = 0.f;
-    for (int k = lane * 8; k < R; k += 256) {
-      const uint4 u = *reinterpret_cast<const uint4*>(srow + k);
-      const __nv_bfloat162* b = reinterpret_cast<const __nv_bfloat162*>(&u);
+  for (int r0 = 0; r0 < 256 && v0 + r0 < V; r0 += 32) {     // uniform trip count over the CTA
+    const int v = v0 + r0 + grp;
+    const bool valid = v < V;
+    const int vr = valid ? v : v0;                              // invalid groups score a row, discard it
+    const float sc = logits[vr] + markov_row_dot(succ + (size_t)vr * R, pp, R, j);
+    if (valid && (sc > best || (sc == best && v < bi))) { best = sc; bi = v; }
+  }
 #pragma unroll
-      for (int q = 0; q < 4; ++q) {
-        const float2 f = __bfloat1622float2(b[q]);
-        d = fmaf(f.x, pp[k + 2 * q], d);
-        d = fmaf(f.y, pp[k + 2 * q + 1], d);
-      }
-    }
-    d = warp_sum(d);
-    const float sc = logits[v] + d;
-    if (sc > best || (sc == best && v < bi)) { best = sc; bi = v; }
+  for (int o = 16; o >= 8; o >>= 1) {
+    const float v2 = __shfl_xor_sync(0xffffffffu, best, o);
+    const int i2 = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (v2 > best || (v2 == best && i2 < bi)) { best = v2; bi = i2; }
   }
   if (lane == 0) { sv[warp] = best; si[warp] = bi; }
   __syncthreads();
@@ -257,29 +289,34 @@ __global__ void markov_finalize_kernel(const float* __restrict__ part_val, const
 
 }  // namespace q38
 
+// Per-row chunk count of the cluster-spread norms: VPT 128-column chunks per CTA.
+static int norm_vpt(int H) { return (((H + q38::NORM_NT - 1) / q38::NORM_NT) + q38::NORM_CPR - 1) / q38::NORM_CPR; }
+
 void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(out.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kFloat, "bf16 out, fp32 weight");
   const int R = (int)x.size(0), H = (int)x.size(1);
   if (R == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
-  TORCH_CHECK(H <= 256 * 32, "rms_norm: hidden too large");
-  const int vpt = (H + 255) / 256;
-#define Q38_NORM(VV)                                                                                        \
-  if (x.scalar_type() == at::kFloat)                                                                        \
-    q38::launch_pdl(q38::rms_norm_kernel<float, VV>, dim3(R), dim3(256), 0, st, (const float*)x.data_ptr<float>(), \
-        (long long)x.stride(0), (const float*)w.data_ptr<float>(), H, (float)eps,                          \
-        reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));                        \
-  else                                                                                                      \
-    q38::launch_pdl(q38::rms_norm_kernel<__nv_bfloat16, VV>, dim3(R), dim3(256), 0, st,                     \
-        reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0),                       \
+  const int vpt = norm_vpt(H);
+  TORCH_CHECK(vpt <= 8 && R <= 65535, "rms_norm: hidden above 8192 or too many rows");
+  const dim3 grid(q38::NORM_CPR, R), cl(q38::NORM_CPR, 1, 1);
+#define Q38_NORM(VV)                                                                                          \
+  if (x.scalar_type() == at::kFloat) {                                                                        \
+    TORCH_CHECK(q38::launch_pdl_cluster(q38::rms_norm_kernel<float, VV>, grid, dim3(q38::NORM_NT), 0, st, cl,  \
+        (const float*)x.data_ptr<float>(), (long long)x.stride(0), (const float*)w.data_ptr<float>(), H,     \
+        (float)eps, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0)) == cudaSuccess, \
+        "rms_norm launch");                                                                                    \
+  } else {                                                                                                    \
+    TORCH_CHECK(q38::launch_pdl_cluster(q38::rms_norm_kernel<__nv_bfloat16, VV>, grid, dim3(q38::NORM_NT), 0,  \
+        st, cl, reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0),               \
         (const float*)w.data_ptr<float>(), H, (float)eps, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),  \
-        (long long)out.stride(0));
+        (long long)out.stride(0)) == cudaSuccess, "rms_norm launch");                                         \
+  }
   if (vpt <= 1) { Q38_NORM(1) }
-  else if (vpt <= 4) { Q38_NORM(4) }
-  else if (vpt <= 8) { Q38_NORM(8) }
-  else if (vpt <= 20) { Q38_NORM(20) }
-  else { Q38_NORM(32) }
+  else if (vpt <= 2) { Q38_NORM(2) }
+  else if (vpt <= 5) { Q38_NORM(5) }
+  else { Q38_NORM(8) }
 #undef Q38_NORM
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
@@ -331,20 +368,36 @@ void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps
   const int R = (int)x.size(0), H = (int)x.size(1);
   TORCH_CHECK(R <= q38::AR_ROWS && (int64_t)R * H <= block_words, "residual larger than a receive block");
   TORCH_CHECK(epochs.scalar_type() == at::kInt && epochs.numel() >= (slot + 1) * q38::AR_ROWS, "epoch array too small");
-  TORCH_CHECK(H <= 256 * 20, "hidden too large");
+  const int vpt = norm_vpt(H);
+  TORCH_CHECK(vpt <= 5, "hidden above 5120 not served by the all-reduce norm");
   if (R == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
   const float* wp = w ? w->data_ptr<float>() : nullptr;
   __nv_bfloat16* op = out ? reinterpret_cast<__nv_bfloat16*>(out->data_ptr()) : nullptr;
   const long long ldo = out ? out->stride(0) : 0;
-  const int vpt = (H + 255) / 256;
-#define Q38_NORM_AR(VV)                                                                                          \
-  q38::launch_pdl(q38::rms_norm_ar_kernel<VV>, dim3(R), dim3(256), 0, st, x.data_ptr<float>(), H, wp, (float)eps,  \
-                  op, ldo, reinterpret_cast<const unsigned long long*>(recv_local), epochs.data_ptr<int>(),     \
-                  (int)slot, (int)world, (long long)block_words, err.data_ptr<int>());
-  if (vpt <= 4) { Q38_NORM_AR(4) }
-  else if (vpt <= 8) { Q38_NORM_AR(8) }
-  else { Q38_NORM_AR(20) }
-#undef Q38_NORM_AR
+  const dim3 grid(q38::NORM_CPR, R), cl(q38::NORM_CPR, 1, 1);
+  cudaError_t e = cudaErrorInvalidValue;
+#define Q38_AR(VV, WW)                                                                                         \
+  e = q38::launch_pdl_cluster(q38::rms_norm_ar_kernel<VV, WW>, grid, dim3(q38::NORM_NT), 0, st, cl,              \
+                              x.data_ptr<float>(), H, wp, (float)eps, op, ldo,                                 \
+                              reinterpret_cast<const unsigned long long*>(recv_local), epochs.data_ptr<int>(), \
+                              (int)slot, (long long)block_words, err.data_ptr<int>());
+#define Q38_AR_W(VV)                                                                                           \
+  switch (world) {                                                                                             \
+    case 1: Q38_AR(VV, 1) break;                                                                               \
+    case 2: Q38_AR(VV, 2) break;                                                                               \
+    case 4: Q38_AR(VV, 4) break;                                                                               \
+    case 8: Q38_AR(VV, 8) break;                                                                               \
+    case 3: Q38_AR(VV, 3) break;                                                                               \
+    case 5: Q38_AR(VV, 5) break;                                                                               \
+    case 6: Q38_AR(VV, 6) break;                                                                               \
+    default: Q38_AR(VV, 7) break;                                                                              \
+  }
+  if (vpt <= 1) { Q38_AR_W(1) }
+  else if (vpt <= 2) { Q38_AR_W(2) }
+  else { Q38_AR_W(5) }
+#undef Q38_AR_W
+#undef Q38_AR
+  TORCH_CHECK(e == cudaSuccess, "rms_norm_ar launch failed");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }

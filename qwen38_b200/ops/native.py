@@ -73,6 +73,7 @@ class NativeOps(TorchOps):
         self.max_keys = max_keys
         self._attn_bufs = {}
         self.rows_dev = torch.zeros(1, dtype=torch.int32, device=dev)
+        self.markov_state = torch.zeros(4 + 32, dtype=torch.int32, device=dev)   # grid barrier + epochs
         self.launches = 0
         self.chunked_prefill = True
         self._gdn_work = None
@@ -84,6 +85,7 @@ class NativeOps(TorchOps):
             names = [n for b, n in _ERR_NAMES.items() if e & b]
             self.err.zero_()
             self.counters.zero_()
+            self.markov_state[:2].zero_()          # a grid barrier that gave up may be mid-count
             raise KernelError(f"device error word {e}: {', '.join(names)}")
 
     # ------------------------------------------------------------------ GEMMs
@@ -309,7 +311,22 @@ class NativeOps(TorchOps):
 
     # ------------------------------------------------------------------ sampling
     def markov_select(self, logits, anchor, pred, succ, vocab_offset=0, comm=None):
+        """All P sequential Markov steps in one persistent launch (``csrc/markov.cu``); at TP > 1
+        each step's cross-rank argmax runs inside the launch over the peer-memory words of
+        ``comm.markov_ptrs``.  A communicator without peer memory takes the per-step kernels and
+        the communicator's argmax."""
         P = logits.shape[0]
+        if comm is None or hasattr(comm, "markov_ptrs"):
+            out = torch.empty(P, dtype=torch.int64, device=logits.device)
+            a = anchor.reshape(1)
+            if a.dtype != torch.int64:
+                a = a.long()
+            self.C.markov_select(logits if logits.stride(1) == 1 else logits.contiguous(), pred, succ, a, out,
+                                 int(vocab_offset), self.amax_val, self.amax_idx, self.markov_state,
+                                 list(comm.markov_ptrs) if comm is not None else [],
+                                 int(comm.rank) if comm is not None else 0, self.err)
+            self.launches += 1
+            return out
         prev = anchor.reshape(1).clone().long()
         out = torch.empty(P, dtype=torch.int64, device=logits.device)
         val = torch.empty(1, dtype=torch.float32, device=logits.device)

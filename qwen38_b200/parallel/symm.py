@@ -7,8 +7,9 @@ collectives with the kernels in ``csrc/comm.cu``:
 * ``reduce_slot_add(slot, residual)`` - the row-parallel GEMM already wrote this rank's fp32
   partial into ``slot`` (``slot_out``); one kernel barriers the ranks, sums the partials in rank
   order and adds into the residual.  No NCCL call, no copy.
-* ``argmax_reduce(val, idx)`` - cross-rank (value, index) argmax for the vocab-parallel LM head
-  and every Markov step.
+* ``argmax_reduce(val, idx)`` - cross-rank (value, index) argmax for the vocab-parallel LM head.
+* ``markov_ptrs`` - every rank's receive words of the fused Markov selector (``csrc/markov.cu``),
+  which exchanges each step's winner inside its one launch.
 
 * pushed all-reduce (``NativeOps.linear_push`` + ``NativeOps.rms_norm_ar``): the out-projection
   GEMM pushes each finished fp32 tile into every rank's receive area as {value, epoch} 8-byte
@@ -34,6 +35,7 @@ from .comm import TorchComm
 MAX_RANKS = 8
 AR_CTAS = 32
 PUSH_ROWS = 32            # rows of a pushed all-reduce (csrc: AR_MAX_ROWS)
+MARKOV_STEPS = 32         # Markov selector steps per launch (csrc/markov.cu MAX_STEPS)
 
 
 class SymmComm(TorchComm):
@@ -59,7 +61,9 @@ class SymmComm(TorchComm):
         self.fused_graph_slots, self.fused_eager_slots = fused_graph_slots, fused_eager_slots
         n_fused = fused_graph_slots + fused_eager_slots
         recv_bytes = n_fused * self.world * self.block_words * 8
-        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes, dev)
+        # fused Markov selector: one 64-bit word per (step, source rank)
+        markov_bytes = MARKOV_STEPS * MAX_RANKS * 8
+        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes + markov_bytes, dev)
         handle = self.C.ipc_handle(self.buf).to(self.device)
         handles = [torch.empty_like(handle) for _ in range(self.world)]
         dist.all_gather(handles, handle, group=self.group)
@@ -76,6 +80,7 @@ class SymmComm(TorchComm):
         self.data_ptrs = ptrs
         self.flag_ptrs = [p + data_bytes for p in ptrs]
         self.recv_ptrs = [p + data_bytes + flag_bytes for p in ptrs]
+        self.markov_ptrs = [p + data_bytes + flag_bytes + recv_bytes for p in ptrs]
         self.fepochs = torch.zeros(n_fused * PUSH_ROWS, dtype=torch.int32, device=self.device)
         self._next_fgraph = 0
         self._next_feager = 0

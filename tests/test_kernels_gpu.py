@@ -248,6 +248,28 @@ def test_markov_select(nops):
     assert out == ref
 
 
+@pytest.mark.parametrize("P,V,Rk", [(15, 151936, 256), (15, 18992, 256), (3, 1000, 64)])
+def test_fused_markov_equals_per_step_kernels(nops, P, V, Rk):
+    """The one-launch selector (grid barrier per step) picks exactly what the two-launch per-step
+    kernels pick (same dot-product order), call after call."""
+    g = torch.Generator(device=DEV).manual_seed(P + V)
+    logits = torch.randn(P, V, generator=g, device=DEV) * 2
+    pred = (torch.randn(V + 77, Rk, generator=g, device=DEV) * 0.3).to(torch.bfloat16)
+    succ = (torch.randn(V, Rk, generator=g, device=DEV) * 0.3).to(torch.bfloat16)
+    for anchor_id in (5, V + 70, 12345 % V):
+        anchor = torch.tensor([anchor_id], device=DEV)
+        fused = nops.markov_select(logits, anchor, pred, succ, vocab_offset=3)
+        prev = anchor.clone()
+        steps = torch.empty(P, dtype=torch.int64, device=DEV)
+        val = torch.empty(1, device=DEV)
+        for i in range(P):
+            nops.C.markov_step(logits[i].contiguous(), pred, succ, prev, steps[i:i + 1], val, nops.amax_val,
+                               nops.amax_idx, 3, True)
+        torch.cuda.synchronize()
+        nops.check()
+        assert fused.tolist() == steps.tolist()
+
+
 @pytest.mark.parametrize("T", [64, 300, 2048])
 def test_gdn_chunked_prefill_matches_reference(nops, T):
     proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T, seed=21)
@@ -266,4 +288,31 @@ def test_gdn_chunked_prefill_matches_reference(nops, T):
     out2 = nops.gdn_prefill(proj, win2, st2, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
     nops.chunked_prefill = True
     assert _rel(out, out2) < 3e-2
+    nops.check()
+
+
+@pytest.mark.parametrize("T,N,K", [(16, 5120, 17408), (16, 5120, 6144), (3, 384, 17408), (32, 1000, 640)])
+def test_cluster_splitk_bits_equal_global_fixup(nops, T, N, K):
+    """The skinny GEMM reduces split-K partials inside a thread-block cluster (DSMEM); the
+    allocation-free entry point still reduces them through global memory and the last-arriving
+    CTA.  Both add the same partials in the same split order, so the fp32 results are identical."""
+    import ctypes
+
+    from qwen38_b200.ops.build import so_path
+    from qwen38_b200.ops.noalloc import EPI_ADD_F32, EPI_F32, bind
+    fn, status = bind(so_path())
+    x, tw = _bf(T, K, seed=7), nops.prepare_weight(_bf(N, K, scale=0.02, seed=8))
+    st = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    y_cluster = nops.linear(x, tw, out_dtype=torch.float32)
+    y_global = torch.empty(T, N, device=DEV)
+    assert fn(x.data_ptr(), T, K, tw.t.data_ptr(), N, y_global.data_ptr(), N, EPI_F32, st) == 0
+    torch.cuda.synchronize()
+    assert status() == 0
+    assert torch.equal(y_cluster, y_global)
+    base = torch.randn(T, N, device=DEV)
+    r1, r2 = base.clone(), base.clone()
+    nops.linear_residual(x, tw, r1)
+    assert fn(x.data_ptr(), T, K, tw.t.data_ptr(), N, r2.data_ptr(), N, EPI_ADD_F32, st) == 0
+    torch.cuda.synchronize()
+    assert torch.equal(r1, r2)
     nops.check()
