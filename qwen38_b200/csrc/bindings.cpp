@@ -16,6 +16,7 @@ void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps
 int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
                          torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace);
 void q38_clear_map_cache();
+void q38_gdn_set_trace(c10::optional<torch::Tensor> trace);
 void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, torch::Tensor state,
                        torch::Tensor conv_w, torch::Tensor A_log, torch::Tensor dt_bias, torch::Tensor norm_w,
                        c10::optional<torch::Tensor> out, int64_t rows, c10::optional<torch::Tensor> rows_dev,
@@ -75,6 +76,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear_trace", &q38_linear_trace);
   m.def("clear_map_cache", &q38_clear_map_cache);
   m.def("gdn_recurrent", &q38_gdn_recurrent);
+  m.def("gdn_set_trace", &q38_gdn_set_trace);
   m.def("gdn_chunk_prefill", &q38_gdn_chunk_prefill);
   m.def("gdn_chunk_workspace_bytes", &q38_gdn_chunk_workspace_bytes);
   m.def("attn_prep", &q38_attn_prep);

@@ -24,7 +24,11 @@
 //
 // Each sub-block of SUB rows first stages its raw projected rows (q and k channels of the head's
 // key group, this CTA's v and z columns, for rows r0-(K-1) .. r0+SUB-1) in shared memory with
-// coalesced 4-byte loads, so the conv, the norms and the epilogue read only shared memory.
+// 16-byte asynchronous copies (4-byte ones when a row is not 16-byte aligned), so the conv, the
+// norms and the epilogue read only shared memory.  Thread c < D convolves q channel c and k
+// channel c for every row in registers and the row L2 norms come from one butterfly per row, so q
+// and k reach shared memory once, normalised.  The recurrence folds the decay into the state
+// update: S <- decay S + k (beta (v - decay S^T k))^T.
 //
 // Modes: WRITE_OUT (verify, prefill) and WRITE_STATE (commit, prefill).  The row count may come
 // from device memory (commit: the accepted prefix length, so the launch can live inside a CUDA
@@ -58,7 +62,17 @@ struct GdnArgs {
   const int* rows_dev;         // device row count (commit)
   int nk, nv, C;               // local key heads, value heads, conv channels
   float eps;
+  unsigned long long* trace;   // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
+  int vec16;                   // rows and channel groups 16-byte aligned: stage with 16-byte copies
 };
+
+// trace points: 0 entry, 1 past the PDL wait, 2 first sub-block staged, 3 conv + norms done,
+// 4 recurrence done, 5 norm statistics exchanged, 6 outputs written, 7 exit
+#define Q38_GSTAMP(k)                                                                                  \
+  do {                                                                                                 \
+    if (a.trace && threadIdx.x == 0 && (r0 == 0 || (k) >= 7))                                          \
+      a.trace[((size_t)blockIdx.y * gridDim.x + blockIdx.x) * 8 + (k)] = globaltimer();                \
+  } while (0)
 
 template <int D, int SPLIT>
 struct GdnShape {
@@ -78,7 +92,7 @@ gdn_recurrent_kernel(GdnArgs a) {
   constexpr int NPR = 8;                       // threads per row in row reductions
   const int h = blockIdx.x / SPLIT, sl = blockIdx.x % SPLIT;   // sl == rank in the cluster
   const int layer = blockIdx.y;
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int col = tid >> 2, part = tid & 3;
   const int gcol = sl * COLS + col;            // value column inside the head
   const int rep = a.nv / a.nk;
@@ -100,18 +114,17 @@ gdn_recurrent_kernel(GdnArgs a) {
   __shared__ __align__(16) float q_s[SUB][4 * QP], k_s[SUB][4 * QP];
   __shared__ float v_s[SUB][COLS];
   __shared__ float o_s[SUB][COLS];
-  __shared__ float g_s[SUB], b_s[SUB], nq_s[SUB], nk_s[SUB], rs_s[SUB];
+  __shared__ float g_s[SUB], b_s[SUB], rs_s[SUB];
+  __shared__ float ssq_s[SUB][4], ssk_s[SUB][4];   // per-warp row sums of squares of q and k
   __shared__ float ss_part[2][SPLIT][SUB];     // DSMEM targets, double-buffered by sub-block parity
 
   // conv taps are static; everything else may come from the previous kernel
-  constexpr int QK_PER = (2 * D + NT - 1) / NT;   // q/k channels per thread
-  float wqk[QK_PER][KC], wv[KC];
+  static_assert(D <= NT && D % 32 == 0, "thread c < D owns q channel c and k channel c");
+  float wq[KC], wk[KC], wv[KC];            // conv taps: this thread's q and k channels, v column
 #pragma unroll
-  for (int u = 0; u < QK_PER; ++u) {
-    const int c = tid + u * NT;
-    const int ch = c < D ? cq + c : ck + (c - D);
-#pragma unroll
-    for (int j = 0; j < KC; ++j) wqk[u][j] = (c < 2 * D) ? conv_w[(size_t)ch * KC + j] : 0.f;
+  for (int j = 0; j < KC; ++j) {
+    wq[j] = tid < D ? conv_w[(size_t)(cq + tid) * KC + j] : 0.f;
+    wk[j] = tid < D ? conv_w[(size_t)(ck + tid) * KC + j] : 0.f;
   }
 #pragma unroll
   for (int j = 0; j < KC; ++j) wv[j] = conv_w[(size_t)(cv + col) * KC + j];
@@ -119,32 +132,49 @@ gdn_recurrent_kernel(GdnArgs a) {
   // kernel this one follows began its own wait (every kernel of a step waits on its predecessor
   // before triggering its successor, except the GEMM, whose predecessor does), so it is read
   // before griddepcontrol.wait: its DRAM round trip overlaps the previous kernel's tail.
+  int r0 = 0;
+  Q38_GSTAMP(0);
   float S[RPT];
 #pragma unroll
   for (int i = 0; i < RPT; ++i) S[i] = state[(size_t)(part * RPT + i) * D + gcol];
   pdl_wait();
+  Q38_GSTAMP(1);
   pdl_trigger();
   const int rows = a.rows_dev ? *a.rows_dev : a.rows;
 
   cg::cluster_group cluster = cg::this_cluster();
   int parity = 0;
-  for (int r0 = 0; r0 < rows; r0 += SUB, parity ^= 1) {
+  for (r0 = 0; r0 < rows; r0 += SUB, parity ^= 1) {
     const int nsub = min(SUB, rows - r0);
-    // ---- 1. stage raw rows r0-(K-1) .. r0+nsub-1 (bf16 pairs; z only for rows >= 0)
-    constexpr int PAIRS = RAWW / 2;
-    for (int idx = tid; idx < (nsub + KC - 1) * PAIRS; idx += NT) {
-      const int i = idx / PAIRS, pp = idx % PAIRS;
-      const int c2 = 2 * pp;                       // staged channel
+    // ---- 1. stage raw rows r0-(K-1) .. r0+nsub-1 with 16-byte asynchronous copies (channel
+    //         groups of 8 are 16-byte aligned in proj and window); z only for rows >= 0
+    constexpr int V8 = RAWW / 8;
+    if (!a.vec16) {                               // rows not 16-byte aligned: 4-byte copies
+      constexpr int PAIRS = RAWW / 2;
+      for (int idx = tid; idx < (nsub + KC - 1) * PAIRS; idx += NT) {
+        const int i = idx / PAIRS, c2 = 2 * (idx % PAIRS);
+        const int r = r0 - (KC - 1) + i;
+        int ch;
+        if (c2 < D) ch = cq + c2;
+        else if (c2 < 2 * D) ch = ck + (c2 - D);
+        else if (c2 < 2 * D + COLS) ch = cv + (c2 - 2 * D);
+        else ch = cz + (c2 - 2 * D - COLS);
+        if (r >= 0) cp_async4(&raw[i][c2], proj + (size_t)r * a.proj_ld + ch);
+        else if (c2 < 2 * D + COLS) cp_async4(&raw[i][c2], window + (size_t)(r + KC - 1) * a.C + ch);
+        else *reinterpret_cast<uint32_t*>(&raw[i][c2]) = 0u;
+      }
+    }
+    for (int idx = tid; a.vec16 && idx < (nsub + KC - 1) * V8; idx += NT) {
+      const int i = idx / V8, c8 = (idx % V8) * 8;   // staged channel of the group
       const int r = r0 - (KC - 1) + i;
       int ch;
-      if (c2 < D) ch = cq + c2;
-      else if (c2 < 2 * D) ch = ck + (c2 - D);
-      else if (c2 < 2 * D + COLS) ch = cv + (c2 - 2 * D);
-      else ch = cz + (c2 - 2 * D - COLS);
-      // asynchronous 4-byte copies: every load of the sub-block is in flight at once
-      if (r >= 0) cp_async4(&raw[i][c2], proj + (size_t)r * a.proj_ld + ch);
-      else if (c2 < 2 * D + COLS) cp_async4(&raw[i][c2], window + (size_t)(r + KC - 1) * a.C + ch);
-      else *reinterpret_cast<uint32_t*>(&raw[i][c2]) = 0u;
+      if (c8 < D) ch = cq + c8;
+      else if (c8 < 2 * D) ch = ck + (c8 - D);
+      else if (c8 < 2 * D + COLS) ch = cv + (c8 - 2 * D);
+      else ch = cz + (c8 - 2 * D - COLS);
+      if (r >= 0) cp_async16(&raw[i][c8], proj + (size_t)r * a.proj_ld + ch);
+      else if (c8 < 2 * D + COLS) cp_async16(&raw[i][c8], window + (size_t)(r + KC - 1) * a.C + ch);
+      else *reinterpret_cast<uint4*>(&raw[i][c8]) = make_uint4(0u, 0u, 0u, 0u);
     }
     cp_async_commit();
     if (tid < nsub) {
@@ -152,82 +182,104 @@ gdn_recurrent_kernel(GdnArgs a) {
       const float av = __bfloat162float(proj[(size_t)r * a.proj_ld + ca]);
       const float bv = __bfloat162float(proj[(size_t)r * a.proj_ld + cb]);
       const float sp = (av + dtb) > 20.f ? (av + dtb) : log1pf(__expf(av + dtb));
-      g_s[tid] = A * sp;
+      g_s[tid] = __expf(A * sp);                   // the row's decay
       b_s[tid] = 1.f / (1.f + __expf(-bv));
     }
     cp_async_wait<0>();
     __syncthreads();
-    // ---- 2. conv + SiLU: q/k channels (one or more per thread, every row), v column per (col, part)
+    Q38_GSTAMP(2);
+    // ---- 2. conv + SiLU and L2 norms in registers: thread c < D owns q channel c and k channel c
+    //         for every row of the sub-block; row sums of squares by xor butterfly in the warp,
+    //         then over the warps in order
+    {
+      static_assert(KC == 4, "four conv taps");
+      float qv[SUB], kv[SUB], sq[SUB], sk[SUB];
 #pragma unroll
-    for (int u = 0; u < QK_PER; ++u) {
-      const int c = tid + u * NT;
-      if (c < 2 * D) {
-        const int cc = c < D ? c : c - D;
-        const int pi = (cc / RPT) * QP + (cc % RPT);
-        float* dst = c < D ? &q_s[0][pi] : &k_s[0][pi];
-        for (int t = 0; t < nsub; ++t) {
-          float acc = 0.f;
+      for (int t = 0; t < SUB; ++t) {
+        float aq = 0.f, ak = 0.f;
+        if (tid < D && t < nsub) {
 #pragma unroll
-          for (int j = 0; j < KC; ++j) acc += wqk[u][j] * __bfloat162float(raw[t + j][c]);
-          dst[t * 4 * QP] = silu_f(acc);
+          for (int j = 0; j < KC; ++j) {
+            aq += wq[j] * __bfloat162float(raw[t + j][tid]);
+            ak += wk[j] * __bfloat162float(raw[t + j][D + tid]);
+          }
+          aq = silu_f(aq);
+          ak = silu_f(ak);
+        }
+        qv[t] = aq;
+        kv[t] = ak;
+        sq[t] = aq * aq;
+        sk[t] = ak * ak;
+      }
+      // the rows' butterflies level by level, so the 2 x SUB independent shuffles of a level
+      // pipeline instead of running row after row
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) {
+#pragma unroll
+        for (int t = 0; t < SUB; ++t) {
+          sq[t] += __shfl_xor_sync(0xffffffffu, sq[t], o);
+          sk[t] += __shfl_xor_sync(0xffffffffu, sk[t], o);
+        }
+      }
+      if (lane == 0 && warp < D / 32) {
+#pragma unroll
+        for (int t = 0; t < SUB; ++t) { ssq_s[t][warp] = sq[t]; ssk_s[t][warp] = sk[t]; }
+      }
+      for (int t = part; t < nsub; t += 4) {
+        float acc = 0.f;
+#pragma unroll
+        for (int j = 0; j < KC; ++j) acc += wv[j] * __bfloat162float(raw[t + j][2 * D + col]);
+        v_s[t][col] = silu_f(acc);
+      }
+      __syncthreads();
+      if (tid < D) {
+        const int pi = (tid / RPT) * QP + (tid % RPT);
+#pragma unroll
+        for (int t = 0; t < SUB; ++t) {
+          if (t < nsub) {
+            float pq = 0.f, pk = 0.f;
+#pragma unroll
+            for (int w = 0; w < D / 32; ++w) { pq += ssq_s[t][w]; pk += ssk_s[t][w]; }
+            q_s[t][pi] = qv[t] * (rsqrtf(pq + 1e-6f) * rsqrtf((float)D));
+            k_s[t][pi] = kv[t] * rsqrtf(pk + 1e-6f);
+          }
         }
       }
     }
-    for (int t = part; t < nsub; t += 4) {
-      float acc = 0.f;
-#pragma unroll
-      for (int j = 0; j < KC; ++j) acc += wv[j] * __bfloat162float(raw[t + j][2 * D + col]);
-      v_s[t][col] = silu_f(acc);
-    }
     __syncthreads();
-    // ---- 3. L2 norms of q and k per row: 8 threads per row, fixed xor butterfly
-    {
-      const int t = tid / NPR, j = tid % NPR;
-      float pq = 0.f, pk = 0.f;
-#pragma unroll
-      for (int m = 0; m < D / NPR; ++m) {
-        const int c = j * (D / NPR) + m;
-        const int ci = (c / RPT) * QP + (c % RPT);
-        pq += q_s[t][ci] * q_s[t][ci];
-        pk += k_s[t][ci] * k_s[t][ci];
-      }
-#pragma unroll
-      for (int o = 1; o < NPR; o <<= 1) {
-        pq += __shfl_xor_sync(0xffffffffu, pq, o);
-        pk += __shfl_xor_sync(0xffffffffu, pk, o);
-      }
-      if (j == 0) {
-        nq_s[t] = rsqrtf(pq + 1e-6f) * rsqrtf((float)D);
-        nk_s[t] = rsqrtf(pk + 1e-6f);
-      }
-    }
-    __syncthreads();
-    for (int idx = tid; idx < nsub * 4 * QP; idx += NT) {
-      const int t = idx / (4 * QP), ci = idx % (4 * QP);
-      q_s[t][ci] *= nq_s[t];
-      k_s[t][ci] *= nk_s[t];
-    }
-    __syncthreads();
-    // ---- 4. sequential recurrence (fixed 4-way partial sums + xor butterfly over the 4 parts)
+    Q38_GSTAMP(3);
+    // ---- 3. sequential recurrence: S <- decay S + k (beta (v - decay S^T k))^T, o = S^T q, with
+    //         float4 shared-memory operands, a fixed 4-way partial-sum split and an xor butterfly
+    //         over the column's 4 threads
     for (int t = 0; t < nsub; ++t) {
-      const float decay = __expf(g_s[t]);
-      const float* kr = &k_s[t][part * QP];
-      const float* qr = &q_s[t][part * QP];
+      const float decay = g_s[t];
+      const float4* kr = reinterpret_cast<const float4*>(&k_s[t][part * QP]);
+      const float4* qr = reinterpret_cast<const float4*>(&q_s[t][part * QP]);
       float kv4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        S[i] *= decay;
-        kv4[i & 3] += S[i] * kr[i];
+      for (int i4 = 0; i4 < RPT / 4; ++i4) {
+        const float4 k4 = kr[i4];
+        kv4[0] = fmaf(S[4 * i4 + 0], k4.x, kv4[0]);
+        kv4[1] = fmaf(S[4 * i4 + 1], k4.y, kv4[1]);
+        kv4[2] = fmaf(S[4 * i4 + 2], k4.z, kv4[2]);
+        kv4[3] = fmaf(S[4 * i4 + 3], k4.w, kv4[3]);
       }
-      float kv = (kv4[0] + kv4[1]) + (kv4[2] + kv4[3]);
-      kv += __shfl_xor_sync(0xffffffffu, kv, 1);
-      kv += __shfl_xor_sync(0xffffffffu, kv, 2);
-      const float delta = (v_s[t][col] - kv) * b_s[t];
+      float kvs = (kv4[0] + kv4[1]) + (kv4[2] + kv4[3]);
+      kvs += __shfl_xor_sync(0xffffffffu, kvs, 1);
+      kvs += __shfl_xor_sync(0xffffffffu, kvs, 2);
+      const float delta = (v_s[t][col] - decay * kvs) * b_s[t];
       float o4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int i = 0; i < RPT; ++i) {
-        S[i] += kr[i] * delta;
-        o4[i & 3] += S[i] * qr[i];
+      for (int i4 = 0; i4 < RPT / 4; ++i4) {
+        const float4 k4 = kr[i4], q4 = qr[i4];
+        S[4 * i4 + 0] = fmaf(decay, S[4 * i4 + 0], k4.x * delta);
+        S[4 * i4 + 1] = fmaf(decay, S[4 * i4 + 1], k4.y * delta);
+        S[4 * i4 + 2] = fmaf(decay, S[4 * i4 + 2], k4.z * delta);
+        S[4 * i4 + 3] = fmaf(decay, S[4 * i4 + 3], k4.w * delta);
+        o4[0] = fmaf(S[4 * i4 + 0], q4.x, o4[0]);
+        o4[1] = fmaf(S[4 * i4 + 1], q4.y, o4[1]);
+        o4[2] = fmaf(S[4 * i4 + 2], q4.z, o4[2]);
+        o4[3] = fmaf(S[4 * i4 + 3], q4.w, o4[3]);
       }
       if constexpr (WRITE_OUT) {
         float o = (o4[0] + o4[1]) + (o4[2] + o4[3]);
@@ -236,6 +288,7 @@ gdn_recurrent_kernel(GdnArgs a) {
         if (part == 0) o_s[t][col] = o;
       }
     }
+    Q38_GSTAMP(4);
     if constexpr (WRITE_OUT) {
       __syncthreads();
       // ---- 5. gated RMSNorm: partial sums of squares over this CTA's columns, exchanged in the
@@ -259,6 +312,7 @@ gdn_recurrent_kernel(GdnArgs a) {
         }
       }
       cluster.sync();
+      Q38_GSTAMP(5);
       if (tid < nsub) {
         float s = 0.f;
 #pragma unroll
@@ -272,6 +326,7 @@ gdn_recurrent_kernel(GdnArgs a) {
         const float y = o_s[t][c] * rs_s[t] * norm_w[sl * COLS + c] * silu_f(z);
         a.out[(size_t)(r0 + t) * a.out_ld + (size_t)h * D + sl * COLS + c] = __float2bfloat16(y);
       }
+      Q38_GSTAMP(6);
     }
     __syncthreads();
   }
@@ -279,6 +334,7 @@ gdn_recurrent_kernel(GdnArgs a) {
 #pragma unroll
     for (int i = 0; i < RPT; ++i) state[(size_t)(part * RPT + i) * D + gcol] = S[i];
   }
+  Q38_GSTAMP(7);
 }
 
 // Conv window after consuming `rows` projected rows: the last K-1 inputs of [window ; proj].
@@ -307,7 +363,13 @@ __global__ void gdn_window_kernel(const __nv_bfloat16* __restrict__ proj, long l
 
 }  // namespace q38
 
+static unsigned long long* g_gdn_trace = nullptr;   // micro-benchmark stamps (kbench gdn --trace)
+
 // ----------------------------------------------------------------------------- bindings
+void q38_gdn_set_trace(c10::optional<torch::Tensor> trace) {
+  g_gdn_trace = trace ? reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>()) : nullptr;
+}
+
 // mode: 0 = verify (outputs, state untouched), 1 = commit (state + window, rows from rows_dev),
 //       2 = prefill (outputs + state + window)
 void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, torch::Tensor state,
@@ -343,6 +405,11 @@ void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, t
   a.nv = (int)nv;
   a.C = C;
   a.eps = (float)eps;
+  a.trace = g_gdn_trace;
+  a.vec16 = (a.proj_ld % 8 == 0 && C % 8 == 0 && (reinterpret_cast<uintptr_t>(a.proj) & 15) == 0 &&
+             (reinterpret_cast<uintptr_t>(a.window) & 15) == 0 && (!multi || (a.proj_layer_stride % 8 == 0 &&
+                                                                              a.win_layer_stride % 8 == 0)))
+                ? 1 : 0;
   TORCH_CHECK(KC == 4, "conv kernel size 4 supported");
   TORCH_CHECK(mode != 0 || out, "verify needs an output");
   TORCH_CHECK(a.proj_ld % 2 == 0 && C % 2 == 0 && (reinterpret_cast<uintptr_t>(a.proj) & 3) == 0 &&

@@ -32,7 +32,7 @@
 namespace q38 {
 namespace markov {
 
-constexpr int NT = 512;
+constexpr int NT = 1024;
 constexpr int MAX_RANKS = 8;
 constexpr int SLICE_SMEM_MAX = 160 * 1024;   // succ slice kept in shared memory up to this size
 constexpr int MAX_STEPS = 32;

@@ -162,7 +162,8 @@ def bench_gdn(a):
     ops = NativeOps()
     nk, nv, D = a.nv // 3, a.nv, 128
     C = 2 * nk * D + nv * D
-    proj = torch.randn(a.T, C + nv * D + 2 * nv, device="cuda").to(torch.bfloat16)
+    width = -(-(C + nv * D + 2 * nv) // 8) * 8          # the runtime's packed width (16-byte rows)
+    proj = torch.randn(a.T, width, device="cuda").to(torch.bfloat16)
     window = torch.randn(3, C, device="cuda").to(torch.bfloat16)
     state = torch.randn(nv, D, D, device="cuda") * 0.1
     conv_w = torch.rand(C, 4, device="cuda") - 0.5
@@ -177,8 +178,23 @@ def bench_gdn(a):
     ms = time_kernel(fn, a.iters)
     bytes_ = state.numel() * 4 + proj.numel() * 2
     hbm, tf, src = peaks()
-    return {"kernel": "gdn_verify", "T": a.T, "nv": nv, "ms": round(ms, 4), "gbs": round(bytes_ / ms / 1e6, 1),
-            f"frac_bw_of_{src}": round(bytes_ / ms / 1e6 / hbm, 3)}
+    out = {"kernel": "gdn_verify", "T": a.T, "nv": nv, "ms": round(ms, 4), "gbs": round(bytes_ / ms / 1e6, 1),
+           f"frac_bw_of_{src}": round(bytes_ / ms / 1e6 / hbm, 3)}
+    if a.trace:
+        # one launch with per-CTA stamps; phases in us from the earliest entry, median / max over CTAs
+        tr = torch.zeros(nv * 4 * 8, dtype=torch.int64, device="cuda")
+        ops.C.gdn_set_trace(tr)
+        torch.cuda.synchronize()
+        fn()
+        torch.cuda.synchronize()
+        ops.C.gdn_set_trace(None)
+        t = tr.view(-1, 8).cpu().double()
+        t0 = t[:, 0].min()
+        names = ["entry", "pdl_wait", "staged", "conv_norms", "recurrence", "cluster_sync", "written", "exit"]
+        out["trace_us"] = {n: {"median": round(float((t[:, k] - t0).median()) / 1e3, 2),
+                               "max": round(float((t[:, k] - t0).max()) / 1e3, 2)}
+                           for k, n in enumerate(names) if bool((t[:, k] > 0).all())}
+    return out
 
 
 def bench_gdn_prefill(a):
