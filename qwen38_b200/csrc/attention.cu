@@ -22,6 +22,7 @@
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 
+#include "attn_groups.cuh"
 #include "common.cuh"
 
 namespace q38 {
@@ -117,7 +118,6 @@ __global__ void attn_prep_kernel(PrepArgs a) {
 }
 
 // ------------------------------------------------------------------------------- decode
-constexpr int CH = 128;      // keys per split (fixed absolute chunks)
 constexpr int MAXW = 8;      // warps per CTA: one 16-row query tile each
 
 struct DecodeArgs {
@@ -157,25 +157,6 @@ __device__ __forceinline__ void mma_bf16_16816(float (&c)[4], uint32_t a0, uint3
 __device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
   __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
   return *reinterpret_cast<uint32_t*>(&v);
-}
-
-// Key groups: the absolute key axis is cut into 128-key chunks and the chunks into groups by a
-// fixed partition - one chunk per group for the first 64 chunks (8,192 keys), four per group up
-// to chunk 512 (65,536 keys), eight beyond - so short contexts keep many CTAs while long ones
-// write few partials.  The partition depends on key positions only, never on how many rows run.
-constexpr int G_T0 = 64, G_T1 = 512;           // tier boundaries in chunks
-__host__ __device__ __forceinline__ int groups_for(int nchunks) {
-  if (nchunks <= G_T0) return nchunks;
-  if (nchunks <= G_T1) return G_T0 + (nchunks - G_T0 + 3) / 4;
-  return G_T0 + (G_T1 - G_T0) / 4 + (nchunks - G_T1 + 7) / 8;
-}
-__host__ __device__ __forceinline__ int group_first_chunk(int grp) {
-  if (grp < G_T0) return grp;
-  if (grp < G_T0 + (G_T1 - G_T0) / 4) return G_T0 + 4 * (grp - G_T0);
-  return G_T1 + 8 * (grp - G_T0 - (G_T1 - G_T0) / 4);
-}
-__host__ __device__ __forceinline__ int group_chunks(int grp) {
-  return grp < G_T0 ? 1 : (grp < G_T0 + (G_T1 - G_T0) / 4 ? 4 : 8);
 }
 
 constexpr int DK_T = 64;       // keys per staged tile inside a group
@@ -702,11 +683,15 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 
+bool q38_attn_decode_tc(const torch::Tensor& q, const torch::Tensor& kcache, const torch::Tensor& vcache,
+                        const int* block_table, int block_size, const int* qpos, int T, int nq, int nkv, float scale,
+                        int causal, float* part_o, float* part_ml, int max_splits, int* err, cudaStream_t st);
+
 void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                             c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos,
                             double scale, int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off,
                             torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys,
-                            int64_t window) {
+                            int64_t window, c10::optional<torch::Tensor> err) {
   c10::cuda::CUDAGuard guard(q.device());
   const int T = (int)q.size(0), nq = (int)q.size(1), D = (int)q.size(2);
   const int nkv = (int)kcache.size(-2);
@@ -734,6 +719,10 @@ void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor
   const int warps = std::max(4, std::min(q38::MAXW, (nqv + 15) / 16));   // >= 4 warps to stage K/V
   const size_t smem = (size_t)(4 * q38::DK_T + warps * 16) * (D + 8) * 2;
   dim3 grid(nkv, q38::groups_for(a.max_splits));
+  // head dim 256 without a window: the tcgen05 kernel (attention_tc.cu); otherwise mma.sync
+  const bool tc = window == 0 && q38_attn_decode_tc(q, kcache, vcache, a.block_table, a.block_size, a.qpos, T, nq,
+                                                    nkv, a.scale, a.causal, a.part_o, a.part_ml, a.max_splits,
+                                                    err ? err->data_ptr<int>() : nullptr, st);
 #define Q38_DEC(DD)                                                                                         \
   {                                                                                                         \
     auto k = a.window > 0 ? q38::attn_decode_kernel<DD, true> : q38::attn_decode_kernel<DD, false>;         \
@@ -742,7 +731,8 @@ void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor
                 "cudaFuncSetAttribute failed");                                                             \
     q38::launch_pdl(k, grid, dim3(warps * 32), smem, st, a);                                               \
   }
-  if (D == 256) Q38_DEC(256)
+  if (tc) {
+  } else if (D == 256) Q38_DEC(256)
   else if (D == 128) Q38_DEC(128)
   else if (D == 64) Q38_DEC(64)
   else TORCH_CHECK(false, "head dim 64/128/256 supported");
@@ -759,9 +749,9 @@ void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor
 void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
-                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys) {
+                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys, c10::optional<torch::Tensor> err) {
   q38_attn_decode_window(q, kcache, vcache, block_table, block_size, qpos, scale, causal, gate, gate_off, out, part_o,
-                         part_ml, max_keys, 0);
+                         part_ml, max_keys, 0, err);
 }
 
 void q38_attn_prefill(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,

@@ -29,12 +29,12 @@ void q38_attn_prep(torch::Tensor proj, int64_t q_off, int64_t k_off, int64_t v_o
 void q38_attn_decode(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                      c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos, double scale,
                      int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off, torch::Tensor out,
-                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys);
+                     torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys, c10::optional<torch::Tensor> err);
 void q38_attn_decode_window(torch::Tensor q, torch::Tensor kcache, torch::Tensor vcache,
                             c10::optional<torch::Tensor> block_table, int64_t block_size, torch::Tensor qpos,
                             double scale, int64_t causal, c10::optional<torch::Tensor> gate, int64_t gate_off,
                             torch::Tensor out, torch::Tensor part_o, torch::Tensor part_ml, int64_t max_keys,
-                            int64_t window);
+                            int64_t window, c10::optional<torch::Tensor> err);
 std::vector<std::pair<int64_t, int64_t>> q38_attn_key_groups(int64_t nchunks);
 void q38_draft_conv(torch::Tensor x, torch::Tensor dyn, int64_t tap0, torch::Tensor base, int64_t group,
                     c10::optional<torch::Tensor> out, c10::optional<torch::Tensor> resid);

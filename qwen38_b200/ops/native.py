@@ -254,7 +254,7 @@ class NativeOps(TorchOps):
         out = torch.empty(T, H * D, dtype=torch.bfloat16, device=q.device)
         g = gate
         self.C.attn_decode(q, kcache, vcache, block_table, block_size, positions, D ** -0.5, int(causal), g,
-                           0, out, po, pml, self.max_keys)
+                           0, out, po, pml, self.max_keys, self.err)
         self.launches += 2
         return out
 
@@ -283,10 +283,10 @@ class NativeOps(TorchOps):
         out = torch.empty(T, H * D, dtype=torch.bfloat16, device=qkv.device)
         if window > 0:
             self.C.attn_decode_window(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
-                                      self.max_keys, int(window))
+                                      self.max_keys, int(window), self.err)
         else:
             self.C.attn_decode(q, kcache, vcache, None, 0, positions, D ** -0.5, 0, None, 0, out, po, pml,
-                               self.max_keys)
+                               self.max_keys, self.err)
         self.launches += 3
         return out
 

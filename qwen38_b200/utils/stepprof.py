@@ -5,7 +5,8 @@ tiny shape), prefills a seeded prompt, then times each phase of a block on its o
 
 * ``verify``  - the captured 16-row verify graph replayed ``--iters`` times at one position;
 * ``draft``   - the captured propose graph (drafter forward + Markov selector);
-* ``commit``  - GDN commit replay of ``--accept`` rows + drafter publication of their features.
+* ``commit``  - GDN commit replay of ``--accept`` rows + drafter publication of their features;
+* ``prefill`` - a committed prefill of the whole prompt (opt in: ``--phases prefill,...``).
 
 For every phase it reports the CUDA-event time per iteration (max over ranks) and, from a
 ``torch.profiler`` CUDA activity trace of the same loop, the device time per iteration of every
@@ -127,7 +128,8 @@ def main():
     rt = RuntimeConfig(max_context=max_ctx, prefill_chunk=min(4096, a.ctx))
     ops = NativeOps(device=dev, max_keys=max_ctx + 64)
     comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=a.comm != "nccl", fused=a.comm == "fused")
-    tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, device=dev, dtype=torch.bfloat16, ops=ops, comm=comm)
+    tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, device=dev, dtype=torch.bfloat16, ops=ops, comm=comm,
+                       max_slots=2)
     dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, max_context=max_ctx)
     taps = tuple(dcfg.taps)
 
@@ -155,6 +157,15 @@ def main():
         dr.append(state["feats"][:a.accept], dr.position)
         seq.verify_rows = (0, a.rows)                   # the next iteration commits the same stash
 
+    if "prefill" in phases:
+        # one committed prefill of the whole prompt on a second slot-free sequence each time
+        def prefill():
+            sq = tgt.new_sequence()
+            try:
+                tgt.prefill(sq, prompt, taps=taps)
+            finally:
+                tgt.release(sq)
+        out["phases"]["prefill"] = profile_loop(prefill, max(1, a.iters // 10))
     if "verify" in phases:
         out["phases"]["verify"] = profile_loop(verify, a.iters)
     if "draft" in phases:

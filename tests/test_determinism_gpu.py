@@ -81,7 +81,7 @@ def test_attention_writes_only_its_output(nops):
     pos = torch.arange(580, 580 + T, dtype=torch.int32, device="cuda")
     obuf, out = _padded((T, H * D), torch.bfloat16)
     po, pml = nops._bufs(Hkv, H // Hkv * T, D)
-    nops.C.attn_decode(q, kc, vc, bt, bs, pos, D ** -0.5, 1, None, 0, out, po, pml, nops.max_keys)
+    nops.C.attn_decode(q, kc, vc, bt, bs, pos, D ** -0.5, 1, None, 0, out, po, pml, nops.max_keys, nops.err)
     pbuf, pout = _padded((T, H * D), torch.bfloat16)
     nops.C.attn_prefill(q, kc, vc, bt, bs, pos, D ** -0.5, None, pout)
     torch.cuda.synchronize()
