@@ -196,20 +196,22 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
     const bool rv = qv < nqv;
     const int p_row = rv ? (a.causal ? a.qpos[qv % a.T] : n_keys - 1) : -1;
     float m_run = -INFINITY, l_run = 0.f;
+    // this pass's first tile: K and V (unless requested before the PDL wait); the previous pass's
+    // last P V must be done before V, P and O are reused
+    if (phase > 0) {
+      mbar_wait(obar, (uint32_t)((phase - 1) & 1), a.err, kErrMmaWait, abort_flag);
+      tc_fence_after();
+    }
+    if (tid == 0 && !(early && phase == 0)) {
+      mbar_expect_tx(kbar, TILE_TX);
+      load_tile(smem + K_OFF, &kmap, kbar, a, g, k_begin, n_keys);
+      mbar_expect_tx(vbar, TILE_TX);
+      load_tile(smem + V_OFF, &vmap, vbar, a, g, k_begin, n_keys);
+    }
     for (int kt = 0; kt < ntiles; ++kt, ++phase) {
       const int k0 = k_begin + kt * KT;
       const uint32_t par = (uint32_t)(phase & 1);
-      if (phase > 0) {                 // the previous tile's P V is done: V, P and O are free
-        mbar_wait(obar, par ^ 1u, a.err, kErrMmaWait, abort_flag);
-        tc_fence_after();
-      }
-      if (tid == 0 && !(early && phase == 0)) {
-        mbar_expect_tx(kbar, TILE_TX);
-        load_tile(smem + K_OFF, &kmap, kbar, a, g, k0, n_keys);
-        mbar_expect_tx(vbar, TILE_TX);
-        load_tile(smem + V_OFF, &vmap, vbar, a, g, k0, n_keys);
-      }
-      __syncthreads();                                  // Q staged (first tile) before the MMA
+      __syncthreads();                                  // Q staged / previous tile's P published
       if (tid == 32) {
         // ---- S = Q K^T (M = 128 queries, N = 128 keys, K = 256)
         if (mbar_wait(kbar, par, a.err, kErrTmaWait, abort_flag)) {
@@ -227,6 +229,21 @@ attn_decode_tc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_con
       __syncwarp();
       mbar_wait(sbar, par, a.err, kErrMmaWait, abort_flag);
       tc_fence_after();
+      // K is free once S is computed: the next tile's K streams in under this tile's softmax
+      if (tid == 0 && kt + 1 < ntiles) {
+        mbar_expect_tx(kbar, TILE_TX);
+        load_tile(smem + K_OFF, &kmap, kbar, a, g, k0 + KT, n_keys);
+      }
+      // V, P and O are free once the previous tile's P V is done: this tile's V streams in under
+      // the softmax
+      if (kt > 0) {
+        mbar_wait(obar, par ^ 1u, a.err, kErrMmaWait, abort_flag);
+        tc_fence_after();
+        if (tid == 0) {
+          mbar_expect_tx(vbar, TILE_TX);
+          load_tile(smem + V_OFF, &vmap, vbar, a, g, k0, n_keys);
+        }
+      }
       // ---- online softmax of this thread's query row over the tile (two passes over S in TMEM:
       //      the tile max, then p = exp(s - m) into the bf16 P operand and the row sum)
       float tmax = -INFINITY;
