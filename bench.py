@@ -274,6 +274,7 @@ def main():
                        "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
+                       "nvls_push": bool(getattr(comm, "recv_mc", 0)),
                        "mean_accepted_target": args.mean_accepted,
                        "l2": "inputs larger than L2: every step streams all weights (54 GB at TP1)"},
             "mean_accepted": round(statistics.mean(r["mean_accepted"] for r in results), 3),

@@ -9,7 +9,7 @@ void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tens
                         c10::optional<torch::Tensor> samp_key);
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
-                     int64_t block_words, torch::Tensor epochs);
+                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr);
 void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, c10::optional<torch::Tensor> out,
                      int64_t recv_local, torch::Tensor epochs, int64_t slot, int64_t world, int64_t block_words,
                      torch::Tensor err);

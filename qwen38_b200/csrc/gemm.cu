@@ -240,7 +240,7 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
 // this process; epochs: this rank's [slots][32] per-row epochs.
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
-                     int64_t block_words, torch::Tensor epochs) {
+                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.size(0) <= q38::AR_MAX_ROWS, "the pushed all-reduce serves <= 32 rows");
   TORCH_CHECK(x.size(0) * N <= block_words, "partial larger than a receive block");
@@ -252,6 +252,7 @@ void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor 
   q38::ArArgs a{};
   for (int p = 0; p < world; ++p) a.recv[p] = recv_ptrs[p];
   a.block_words = block_words;
+  a.mc = mc_ptr;
   a.rank = (int)rank;
   a.world = world;
   a.slot = (int)slot;

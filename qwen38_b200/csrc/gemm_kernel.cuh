@@ -39,6 +39,7 @@ constexpr int AR_MAX_ROWS = 32;
 
 struct ArArgs {
   long long recv[AR_MAX_RANKS];    // every rank's receive area (8-byte words), mapped into this process
+  long long mc;                    // NVLS multicast address of the receive areas (0: per-rank stores)
   long long block_words;           // words per (slot, source rank) block: [AR_MAX_ROWS][ldo]
   int rank, world, slot;
   const int* epochs;               // this rank's [slots][AR_MAX_ROWS] epochs (advanced by the reader)
@@ -47,6 +48,21 @@ struct ArArgs {
 __device__ __forceinline__ void st_relaxed_sys_u64(unsigned long long* addr, unsigned long long v) {
   asm volatile("st.relaxed.sys.global.u64 [%0], %1;" ::"l"(addr), "l"(v) : "memory");
 }
+// One 8-byte store through the NVSwitch multicast object: every rank's copy receives the word.
+__device__ __forceinline__ void multimem_st_u64(unsigned long long* mc_addr, unsigned long long v) {
+  asm volatile("multimem.st.relaxed.sys.global.u64 [%0], %1;" ::"l"(mc_addr), "l"(v) : "memory");
+}
+
+// Push of one {value, epoch} word to every rank's copy of this rank's receive block: a single
+// multicast store when the areas are bound to an NVLS multicast object, else one store per rank.
+__device__ __forceinline__ void push_word(const ArArgs& a, size_t word, unsigned long long v) {
+  if (a.mc) {
+    multimem_st_u64(reinterpret_cast<unsigned long long*>(a.mc) + word, v);
+  } else {
+    for (int p = 0; p < a.world; ++p) st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.recv[p]) + word, v);
+  }
+}
+
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
   unsigned long long v;
   asm volatile("ld.relaxed.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(addr) : "memory");
@@ -183,8 +199,7 @@ __device__ __forceinline__ void swap_cluster_epilogue(const GemmArgs& g, float* 
       const unsigned long long w =
           ((unsigned long long)((uint32_t)a.epochs[(size_t)a.slot * AR_MAX_ROWS + j] + 1u) << 32) |
           __float_as_uint(v[k]);
-      for (int p = 0; p < a.world; ++p)
-        st_relaxed_sys_u64(reinterpret_cast<unsigned long long*>(a.recv[p]) + mine + off[k], w);
+      push_word(a, mine + off[k], w);
     }
   }
   cluster.sync();
@@ -465,13 +480,22 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             for (int j = 0; j < 32; ++j)
               ep[j] = j < nvalid ? (uint32_t)a.epochs[(size_t)a.slot * AR_MAX_ROWS + n0 + j] + 1u : 0u;
             const size_t mine = (size_t)(a.slot * a.world + a.rank) * a.block_words;
-            for (int p = 0; p < a.world; ++p) {        // push: this rank's block in every rank
-              unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.recv[p]) + mine;
+            if (a.mc) {                                  // one multicast store reaches every rank
+              unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.mc) + mine;
 #pragma unroll
               for (int j = 0; j < 32; ++j)
                 if (j < nvalid)
-                  st_relaxed_sys_u64(dst + (size_t)(n0 + j) * g.ldo + m,
-                                     ((unsigned long long)ep[j] << 32) | __float_as_uint(acc[j]));
+                  multimem_st_u64(dst + (size_t)(n0 + j) * g.ldo + m,
+                                  ((unsigned long long)ep[j] << 32) | __float_as_uint(acc[j]));
+            } else {
+              for (int p = 0; p < a.world; ++p) {        // push: this rank's block in every rank
+                unsigned long long* dst = reinterpret_cast<unsigned long long*>(a.recv[p]) + mine;
+#pragma unroll
+                for (int j = 0; j < 32; ++j)
+                  if (j < nvalid)
+                    st_relaxed_sys_u64(dst + (size_t)(n0 + j) * g.ldo + m,
+                                       ((unsigned long long)ep[j] << 32) | __float_as_uint(acc[j]));
+              }
             }
           }
         } else {

@@ -103,6 +103,51 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
   }
 }
 
+// Many rows (prefill chunks): one CTA of 256 threads per row, row kept in registers between the
+// sum of squares and the scaling.  Row counts above NORM_CLUSTER_ROWS take this kernel; its
+// reduction order differs from the cluster kernel's, which only rows of decode / verify size
+// (where the all-reduce norm must reproduce the plain norm bit for bit) need.
+constexpr int NORM_CLUSTER_ROWS = 32;
+
+template <typename TIn, int VPT>
+__global__ void __launch_bounds__(256)
+rms_norm_rows_kernel(const TIn* __restrict__ x, long long ldx, const float* __restrict__ w, int H, float eps,
+                     __nv_bfloat16* __restrict__ out, long long ldo) {
+  pdl_wait();
+  pdl_trigger();
+  const int r = blockIdx.x;
+  const TIn* xr = x + (size_t)r * ldx;
+  __shared__ float red[8];
+  float v[VPT], wv[VPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = threadIdx.x + u * 256;
+    float f = 0.f;
+    wv[u] = 0.f;
+    if (i < H) {
+      if constexpr (std::is_same<TIn, float>::value) f = xr[i];
+      else f = __bfloat162float(xr[i]);
+      wv[u] = w[i];
+    }
+    v[u] = f;
+    ss += f * f;
+  }
+  ss = warp_sum(ss);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  float t = 0.f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) t += red[k];
+  const float inv = rsqrtf(t / H + eps);
+  __nv_bfloat16* o = out + (size_t)r * ldo;
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = threadIdx.x + u * 256;
+    if (i < H) o[i] = __float2bfloat16(v[u] * inv * wv[u]);
+  }
+}
+
 // The second half of the pushed tensor-parallel all-reduce (the GEMM half is EPI_PUSH_F32): the
 // CTAs of a row read every rank's {value, epoch} words of their chunks - all ranks' loads in flight
 // at once - and spin (bounded) on each until this use's epoch appears, add the W partials in rank
@@ -298,8 +343,30 @@ void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor ou
   const int R = (int)x.size(0), H = (int)x.size(1);
   if (R == 0) return;
   cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  if (R > q38::NORM_CLUSTER_ROWS) {
+    const int v2 = (H + 255) / 256;
+    TORCH_CHECK(v2 <= 32, "rms_norm: hidden above 8192");
+#define Q38_NORM_ROWS(VV)                                                                                   \
+  if (x.scalar_type() == at::kFloat) {                                                                      \
+    q38::launch_pdl(q38::rms_norm_rows_kernel<float, VV>, dim3(R), dim3(256), 0, st,                         \
+                    (const float*)x.data_ptr<float>(), (long long)x.stride(0), (const float*)w.data_ptr<float>(), \
+                    H, (float)eps, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0)); \
+  } else {                                                                                                  \
+    q38::launch_pdl(q38::rms_norm_rows_kernel<__nv_bfloat16, VV>, dim3(R), dim3(256), 0, st,                 \
+                    reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (long long)x.stride(0),             \
+                    (const float*)w.data_ptr<float>(), H, (float)eps,                                        \
+                    reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), (long long)out.stride(0));             \
+  }
+    if (v2 <= 4) { Q38_NORM_ROWS(4) }
+    else if (v2 <= 8) { Q38_NORM_ROWS(8) }
+    else if (v2 <= 20) { Q38_NORM_ROWS(20) }
+    else { Q38_NORM_ROWS(32) }
+#undef Q38_NORM_ROWS
+    C10_CUDA_KERNEL_LAUNCH_CHECK();
+    return;
+  }
   const int vpt = norm_vpt(H);
-  TORCH_CHECK(vpt <= 8 && R <= 65535, "rms_norm: hidden above 8192 or too many rows");
+  TORCH_CHECK(vpt <= 8, "rms_norm: hidden above 8192");
   const dim3 grid(q38::NORM_CPR, R), cl(q38::NORM_CPR, 1, 1);
 #define Q38_NORM(VV)                                                                                          \
   if (x.scalar_type() == at::kFloat) {                                                                        \

@@ -114,7 +114,7 @@ class NativeOps(TorchOps):
         w = self.prepare_weight(w)
         slot = comm.fused_slot()
         self.C.linear_push(x.contiguous(), w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs, comm.rank,
-                           slot, comm.block_words, comm.fepochs)
+                           slot, comm.block_words, comm.fepochs, int(getattr(comm, "recv_mc", 0) or 0))
         self.launches += 1
         return slot
 

@@ -14,7 +14,10 @@ collectives with the kernels in ``csrc/comm.cu``:
 * pushed all-reduce (``NativeOps.linear_push`` + ``NativeOps.rms_norm_ar``): the out-projection
   GEMM pushes each finished fp32 tile into every rank's receive area as {value, epoch} 8-byte
   words; the next RMSNorm of the residual spins on the words of its row until this use's epoch
-  appears, adds the rank-ordered sum and normalises (receive blocks [slot][source rank]).
+  appears, adds the rank-ordered sum and normalises (receive blocks [slot][source rank]).  When
+  the NVSwitch offers multicast (``torch.distributed._symmetric_memory`` with a multicast
+  pointer), the receive areas live in that symmetric memory and each word leaves the GPU once,
+  through the multicast address (``recv_mc``), instead of once per rank (``Q38_NVLS=0``: off).
 
 Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
 
@@ -25,6 +28,8 @@ its reads of the earlier one.  Each graph capture therefore numbers its collecti
 other barriers between them), and eager calls rotate through a separate range.
 """
 from __future__ import annotations
+
+import os
 
 import torch
 import torch.distributed as dist
@@ -41,7 +46,7 @@ MARKOV_STEPS = 32         # Markov selector steps per launch (csrc/markov.cu MAX
 class SymmComm(TorchComm):
     def __init__(self, device, hidden: int, group=None, slot_rows: int = 32, graph_slots: int = 768,
                  eager_slots: int = 64, fused_graph_slots: int = 160, fused_eager_slots: int = 32,
-                 fused: bool = True):
+                 fused: bool = True, nvls: bool | None = None):
         super().__init__(group)
         self.fused = fused          # row-parallel GEMMs push their tiles; the next norm reduces
         if self.world > MAX_RANKS:
@@ -63,7 +68,22 @@ class SymmComm(TorchComm):
         recv_bytes = n_fused * self.world * self.block_words * 8
         # fused Markov selector: one 64-bit word per (step, source rank)
         markov_bytes = MARKOV_STEPS * MAX_RANKS * 8
-        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes + markov_bytes, dev)
+        # the pushed all-reduce's receive areas in NVLS-capable symmetric memory when the switch
+        # supports multicast: a GEMM then stores each word once through the multicast address
+        self.recv_mc, self._recv_sym = 0, None
+        if nvls is None:
+            nvls = os.environ.get("Q38_NVLS", "1") != "0"
+        if nvls:
+            self._recv_sym = self._nvls_recv(recv_bytes)
+            agree = torch.tensor([1 if self._recv_sym is not None else 0], dtype=torch.int32, device=self.device)
+            dist.all_reduce(agree, op=dist.ReduceOp.MIN, group=self.group)
+            if int(agree.item()) == 0:              # every rank takes the same path
+                self._recv_sym = None
+        if self._recv_sym is not None:
+            recv_bytes_local = 0
+        else:
+            recv_bytes_local = recv_bytes
+        self.buf = self.C.peer_alloc(data_bytes + flag_bytes + recv_bytes_local + markov_bytes, dev)
         handle = self.C.ipc_handle(self.buf).to(self.device)
         handles = [torch.empty_like(handle) for _ in range(self.world)]
         dist.all_gather(handles, handle, group=self.group)
@@ -79,8 +99,12 @@ class SymmComm(TorchComm):
                 ptrs.append(ptr)
         self.data_ptrs = ptrs
         self.flag_ptrs = [p + data_bytes for p in ptrs]
-        self.recv_ptrs = [p + data_bytes + flag_bytes for p in ptrs]
-        self.markov_ptrs = [p + data_bytes + flag_bytes + recv_bytes for p in ptrs]
+        if self._recv_sym is not None:
+            self.recv_ptrs = list(self._recv_sym[1].buffer_ptrs)
+            self.recv_mc = int(self._recv_sym[1].multicast_ptr)
+        else:
+            self.recv_ptrs = [p + data_bytes + flag_bytes for p in ptrs]
+        self.markov_ptrs = [p + data_bytes + flag_bytes + recv_bytes_local for p in ptrs]
         self.fepochs = torch.zeros(n_fused * PUSH_ROWS, dtype=torch.int32, device=self.device)
         self._next_fgraph = 0
         self._next_feager = 0
@@ -90,6 +114,22 @@ class SymmComm(TorchComm):
         self._next_graph = 0
         self._next_eager = 0
         dist.barrier(group=self.group)
+
+    def _nvls_recv(self, nbytes: int):
+        """(tensor, handle) of a zeroed symmetric-memory buffer bound to an NVSwitch multicast object,
+        or None when this system or torch build offers none."""
+        try:
+            import torch.distributed._symmetric_memory as symm_mem
+            name = (self.group or dist.group.WORLD).group_name
+            t = symm_mem.empty(nbytes, dtype=torch.uint8, device=self.device)
+            h = symm_mem.rendezvous(t, name)
+            if not int(getattr(h, "multicast_ptr", 0) or 0):
+                return None
+            t.zero_()
+            torch.cuda.synchronize(self.device)
+            return t, h
+        except Exception:                     # no symmetric memory / multicast: per-rank stores
+            return None
 
     # ------------------------------------------------------------------ slots
     def begin_capture(self):

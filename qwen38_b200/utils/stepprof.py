@@ -185,7 +185,8 @@ def main():
         allr = [None] * world
         dist.all_gather_object(allr, out)
     if rank == 0:
-        summary = {"tp": world, "ctx": a.ctx, "rows": a.rows, "iters": a.iters, "phases": {}}
+        summary = {"tp": world, "ctx": a.ctx, "rows": a.rows, "iters": a.iters,
+                   "nvls_push": bool(getattr(comm, "recv_mc", 0)), "phases": {}}
         for ph in out["phases"]:
             ms = max(r["phases"][ph][0] for r in allr)
             busy = [r["phases"][ph][2] for r in allr]
