@@ -175,7 +175,7 @@ def main():
         from qwen38_b200.parallel.topology import check_topology
         topo = check_topology(world, comm=args.comm if args.ops == "native" else "nccl")
     comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm != "nccl" and args.ops == "native"),
-                     fused=(args.comm == "fused"))
+                     fused=(args.comm == "fused"), prefill_rows=args.prefill_chunk if args.comm == "fused" else 0)
     rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=args.prefill_chunk,
                        use_cuda_graphs=not args.no_graphs)
     if args.ops == "native":
@@ -275,6 +275,8 @@ def main():
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
                        "nvls_push": bool(getattr(comm, "recv_mc", 0)),
+                       "prefill_allreduce": "fused (reduce-scatter GEMM + multicast broadcast)"
+                       if getattr(comm, "_pf", None) is not None else ("nccl" if world > 1 else None),
                        "mean_accepted_target": args.mean_accepted,
                        "l2": "inputs larger than L2: every step streams all weights (54 GB at TP1)"},
             "mean_accepted": round(statistics.mean(r["mean_accepted"] for r in results), 3),

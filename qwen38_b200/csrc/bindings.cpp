@@ -7,6 +7,15 @@ void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tens
                         int64_t vocab_offset, torch::Tensor part_val, torch::Tensor part_idx, torch::Tensor ws,
                         torch::Tensor counters, torch::Tensor err, c10::optional<torch::Tensor> samp_scale,
                         c10::optional<torch::Tensor> samp_key);
+void q38_linear_rs(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
+                   torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> count_ptrs, int64_t rank,
+                   int64_t rows_cap);
+void q38_rs_reduce_bcast(int64_t recv_local, int64_t count_local, int64_t count_target, torch::Tensor x,
+                         int64_t x_mc, int64_t flag_mc, int64_t rank, int64_t world, int64_t rows_cap,
+                         int64_t slots, torch::Tensor err);
+void q38_rs_wait(int64_t flag_local, int64_t target, torch::Tensor err);
+void q38_rms_norm_wait(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out, int64_t flag_local,
+                       int64_t target, torch::Tensor err);
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
                      int64_t block_words, torch::Tensor epochs, int64_t mc_ptr);
@@ -72,6 +81,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("linear", &q38_linear);
   m.def("lm_head_argmax", &q38_lm_head_argmax);
   m.def("linear_push", &q38_linear_push);
+  m.def("linear_rs", &q38_linear_rs);
+  m.def("rs_reduce_bcast", &q38_rs_reduce_bcast);
+  m.def("rs_wait", &q38_rs_wait);
+  m.def("rms_norm_wait", &q38_rms_norm_wait);
   m.def("rms_norm_ar", &q38_rms_norm_ar);
   m.def("linear_trace", &q38_linear_trace);
   m.def("clear_map_cache", &q38_clear_map_cache);

@@ -150,7 +150,7 @@ static bool splitk_cluster() {
 void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
                    const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr,
                    const ArArgs* ar = nullptr, unsigned long long* trace = nullptr, int64_t ldo_override = -1,
-                   const SampleArgs* samp = nullptr) {
+                   const SampleArgs* samp = nullptr, const RsArgs* rs = nullptr) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
@@ -167,6 +167,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
   g.ws = sc.ws;
   g.counters = sc.counters;
   g.trace = trace;
+  TORCH_CHECK(epi != EPI_RS_F32 || (T > 32 && rs != nullptr), "the reduce-scatter epilogue serves prefill tiles");
   if (T <= 32) {
     // swap-AB streaming: M = weight rows, N = tokens
     g.M = N;
@@ -211,6 +212,13 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     g.splits = 1;
     g.kps = g.kblocks;
     if (epi == EPI_SWIGLU) TORCH_CHECK(N % PREFILL_BN == 0, "SwiGLU prefill needs N % 256 == 0");
+    if (epi == EPI_RS_F32) {
+      TORCH_CHECK(N % PREFILL_BN == 0, "reduce-scatter prefill needs N % 256 == 0");
+      const int tiles = (T + BM - 1) / BM;
+      TORCH_CHECK((int64_t)((tiles + rs->world - 1) / rs->world) * BM <= rs->rows_cap,
+                  "reduce-scatter area too small for this chunk");
+      g.rs = *rs;
+    }
     CUtensorMap ma = cached_map(x, BM, false);
     CUtensorMap mb = cached_map(w, BM, true);      // two 16 KB weight tiles per 256-row stage
     dim3 grid((T + BM - 1) / BM, (N + PREFILL_BN - 1) / PREFILL_BN, 1);
@@ -261,6 +269,29 @@ void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor 
   // no local output tensor: the epilogue writes the receive blocks, laid out [T, N] (ldo = N)
   torch::Tensor unused = x;
   q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_PUSH_F32, sc, nullptr, nullptr, nullptr, &a, nullptr, N);
+}
+
+// Prefill out-projection whose tiles go to their owning rank's reduce-scatter area (EPI_RS_F32):
+// recv_ptrs / count_ptrs are every rank's area and arrival counter, rows_cap the local rows per
+// source block.  The owner's q38_rs_reduce_bcast completes the all-reduce.
+void q38_linear_rs(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
+                   torch::Tensor err, std::vector<int64_t> recv_ptrs, std::vector<int64_t> count_ptrs, int64_t rank,
+                   int64_t rows_cap) {
+  c10::cuda::CUDAGuard guard(x.device());
+  const int world = (int)recv_ptrs.size();
+  TORCH_CHECK(world >= 1 && world <= q38::AR_MAX_RANKS && (int)count_ptrs.size() == world, "1..8 ranks");
+  q38::RsArgs r{};
+  for (int p = 0; p < world; ++p) {
+    r.recv[p] = recv_ptrs[p];
+    r.count[p] = count_ptrs[p];
+  }
+  r.rank = (int)rank;
+  r.world = world;
+  r.rows_cap = (int)rows_cap;
+  auto sc = q38::scratch_of(ws, counters, err);
+  torch::Tensor unused = x;
+  q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_RS_F32, sc, nullptr, nullptr, nullptr, nullptr, nullptr, N,
+                     nullptr, &r);
 }
 
 // Micro-benchmark entry: q38_linear with per-CTA phase stamps written to `trace` ([grid][8] int64).

@@ -29,7 +29,10 @@
 
 namespace q38 {
 
-enum Epi : int { EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_PUSH_F32 = 5 };
+enum Epi : int {
+  EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_PUSH_F32 = 5,
+  EPI_RS_F32 = 6,   // prefill tiles: fp32 partial straight into the owning rank's reduce-scatter area
+};
 
 constexpr int AR_MAX_RANKS = 8;
 
@@ -69,6 +72,16 @@ __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned 
   return v;
 }
 
+// Reduce-scatter of a prefill out-projection (EPI_RS_F32, tile mode): 128-row token tile t belongs
+// to rank t % world, which keeps its tiles at local rows (t / world) * 128 ..; a source writes its
+// fp32 tile into [source rank][local row][ldo] of the owner's area, then adds 1 to the owner's
+// arrival counter with a system-scope release (prefill_ar.cu reduces and broadcasts the rows).
+struct RsArgs {
+  long long recv[AR_MAX_RANKS];    // every rank's reduce-scatter area, mapped into this process
+  long long count[AR_MAX_RANKS];   // every rank's arrival counter (u64)
+  int rank, world, rows_cap;       // rows_cap: local rows per source block
+};
+
 constexpr int BM = 128;
 constexpr int BK = 64;
 
@@ -84,6 +97,7 @@ struct GemmArgs {
   float* amax_val;            // EPI_ARGMAX partials [m_tiles, N]
   int* amax_idx;
   ArArgs ar;                  // EPI_PUSH_F32 only
+  RsArgs rs;                  // EPI_RS_F32 only
   unsigned long long* trace;  // optional per-CTA %globaltimer stamps [grid][8] (micro-benchmarks)
   const float* samp_scale;    // EPI_ARGMAX: per token row 1/temperature (0: greedy), or nullptr
   const unsigned long long* samp_key;   // per token row noise key
@@ -573,6 +587,11 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
           } else {
             float* o = reinterpret_cast<float*>(g.out) + (size_t)m * g.ldo + nb;
+            if constexpr (EPI == EPI_RS_F32) {
+              const int owner = m_tile % g.rs.world;
+              const size_t lrow = (size_t)(m_tile / g.rs.world) * BM + row;
+              o = reinterpret_cast<float*>(g.rs.recv[owner]) + ((size_t)g.rs.rank * g.rs.rows_cap + lrow) * g.ldo + nb;
+            }
             if (full) {
 #pragma unroll
               for (int q = 0; q < 8; ++q) {
@@ -593,6 +612,17 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           }
         }
       }
+    }
+  }
+
+  if constexpr (!SWAP && EPI == EPI_RS_F32) {
+    // every thread's stores of the tile are done: one system-scope release increment of the
+    // owner's arrival counter (also after a failed wait, so the owner's wait ends; the error word
+    // carries the failure)
+    __syncthreads();
+    if (tid == 0) {
+      __threadfence_system();
+      atomicAdd_system(reinterpret_cast<unsigned long long*>(g.rs.count[m_tile % g.rs.world]), 1ull);
     }
   }
 

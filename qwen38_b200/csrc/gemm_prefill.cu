@@ -9,6 +9,7 @@ void launch_prefill(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const
     case EPI_F32: launch_gemm<PREFILL_BN, PREFILL_STAGES, EPI_F32, false>(ma, mb, g, grid, st); break;
     case EPI_ADD_F32: launch_gemm<PREFILL_BN, PREFILL_STAGES, EPI_ADD_F32, false>(ma, mb, g, grid, st); break;
     case EPI_SWIGLU: launch_gemm<PREFILL_BN, PREFILL_STAGES, EPI_SWIGLU, false>(ma, mb, g, grid, st); break;
+    case EPI_RS_F32: launch_gemm<PREFILL_BN, PREFILL_STAGES, EPI_RS_F32, false>(ma, mb, g, grid, st); break;
     default: TORCH_CHECK(false, "bad epilogue");
   }
 }

@@ -176,7 +176,8 @@ class HybridTarget:
         self.ops = ops or TorchOps()
         self.comm = comm or NullComm()
         # pushed all-reduce: out-projection GEMMs push their partial tiles to every rank; the next
-        # RMSNorm of the residual completes the reduction (``_pending`` = (residual, slot))
+        # RMSNorm of the residual completes the reduction (``_pending`` = (residual, "push", slot), or
+        # (residual, "rs", completion-flag target) for the fused prefill all-reduce)
         self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_push")
         self._pending = None
         tp, r = self.comm.world, self.comm.rank
@@ -294,6 +295,11 @@ class HybridTarget:
             self.ops.linear_residual(h, w, x)
         elif self.fused_ar and self.comm.fused_fits(*x.shape):
             self.push_row_parallel(h, w, x)
+        elif getattr(self.comm, "prefill_fits", None) is not None and self.comm.prefill_fits(x):
+            # prefill chunk: reduce-scatter GEMM + owner reduce + multicast broadcast, completed by
+            # the next norm / settle of x
+            self.settle(x)
+            self._pending = (x, "rs", self.comm.prefill_push(self.ops, h, self.ops.prepare_weight(w), x))
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):
             slot, part = self.comm.slot_out(*x.shape)          # GEMM writes into peer memory
             self.ops.linear(h, w, out=part)
@@ -308,23 +314,28 @@ class HybridTarget:
         (in the same kernel)."""
         eps = self.eps if eps is None else eps
         if self._pending is not None and self._pending[0] is x:
-            slot = self._pending[1]
+            _, kind, val = self._pending
             self._pending = None
-            return self.ops.rms_norm_ar(x, w, eps, self.dtype, self.comm, slot)
+            if kind == "rs":
+                return self.comm.prefill_norm(self.ops, x, w, eps, val)
+            return self.ops.rms_norm_ar(x, w, eps, self.dtype, self.comm, val)
         return self.ops.rms_norm(x, w, eps, self.dtype)
 
     def push_row_parallel(self, h, w, x):
         """Pushed all-reduce of a row-parallel out-projection into the residual ``x`` (any
         model's residual: the drafters use it too); completed by the next ``norm`` / ``settle``."""
         self.settle(x)
-        self._pending = (x, self.ops.linear_push(h, w, self.comm))
+        self._pending = (x, "push", self.ops.linear_push(h, w, self.comm))
 
     def settle(self, x=None):
         """Complete a pending pushed all-reduce without a norm (before ``x`` is read raw)."""
         if self._pending is not None and (x is None or self._pending[0] is x):
-            px, slot = self._pending
+            px, kind, val = self._pending
             self._pending = None
-            self.ops.rms_norm_ar(px, None, self.eps, self.dtype, self.comm, slot)
+            if kind == "rs":
+                self.comm.prefill_wait(self.ops, val)
+            else:
+                self.ops.rms_norm_ar(px, None, self.eps, self.dtype, self.comm, val)
 
     def _mlp(self, L, x):
         h = self.norm(x, L["post_norm"])
@@ -357,7 +368,11 @@ class HybridTarget:
             c1 = min(S, c0 + chunk)
             tok = tokens[c0:c1]
             pos0 = seq.pos
-            x = self.ops.embedding(tok, self.embed).float()
+            xbuf = self.comm.prefill_x(c1 - c0) if hasattr(self.comm, "prefill_x") else None
+            if xbuf is not None:          # the fused prefill all-reduce's symmetric residual
+                x = self.ops.embedding(tok, self.embed, out=xbuf)
+            else:
+                x = self.ops.embedding(tok, self.embed).float()
             positions = self.positions(pos0, tok.shape[0])
             for i, L in enumerate(self.layers):
                 h = self.norm(x, L["in_norm"])
@@ -380,8 +395,8 @@ class HybridTarget:
                     self.settle(x)
                     feats[c0:c1, tap_pos[i]] = x.to(self.dtype)
             seq.pos += tok.shape[0]
+            self.settle(x)                # the next chunk reuses the residual buffer
             if c1 == S:
-                self.settle(x)
                 nxt = self._head(x[-1:], sampling)
         return nxt, (feats.reshape(S, -1) if feats is not None else None)
 

@@ -63,7 +63,10 @@ class TorchOps:
         y = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w_eff
         return y.to(out_dtype)
 
-    def embedding(self, ids, table):
+    def embedding(self, ids, table, out=None):
+        if out is not None:
+            out.copy_(table[ids])
+            return out
         return table[ids]
 
     # ---- GDN -----------------------------------------------------------------------

@@ -167,8 +167,9 @@ class NativeOps(TorchOps):
         self.launches += 1
         return out.reshape(x.shape)
 
-    def embedding(self, ids, table):
-        out = torch.empty(ids.numel(), table.shape[1], dtype=torch.float32, device=ids.device)
+    def embedding(self, ids, table, out=None):
+        if out is None:
+            out = torch.empty(ids.numel(), table.shape[1], dtype=torch.float32, device=ids.device)
         self.C.embedding(ids.reshape(-1).long(), table, out)
         self.launches += 1
         return out

@@ -91,13 +91,15 @@ def init_distributed(backend: str | None = None, timeout_s: float = 120.0):
     return dist.get_rank(), dist.get_world_size(), int(os.environ.get("LOCAL_RANK", "0"))
 
 
-def make_comm(world: int, *, device=None, hidden: int = 0, peer: bool = False, fused: bool = True):
+def make_comm(world: int, *, device=None, hidden: int = 0, peer: bool = False, fused: bool = True,
+              prefill_rows: int = 0):
     """TP communicator: NullComm at one rank, the peer-memory kernels (``SymmComm``; with
-    ``fused`` the row-parallel GEMMs carry the all-reduce themselves) when ``peer`` is set on GPUs,
-    otherwise torch.distributed collectives."""
+    ``fused`` the row-parallel GEMMs carry the all-reduce themselves; ``prefill_rows`` sizes the
+    fused prefill all-reduce's buffers for chunks of up to that many rows) when ``peer`` is set on
+    GPUs, otherwise torch.distributed collectives."""
     if world == 1:
         return NullComm()
     if peer:
         from .symm import SymmComm
-        return SymmComm(device, hidden, fused=fused)
+        return SymmComm(device, hidden, fused=fused, prefill_rows=prefill_rows)
     return TorchComm()

@@ -19,7 +19,10 @@ collectives with the kernels in ``csrc/comm.cu``:
   pointer), the receive areas live in that symmetric memory and each word leaves the GPU once,
   through the multicast address (``recv_mc``), instead of once per rank (``Q38_NVLS=0``: off).
 
-Messages above ``slot_rows`` rows (prefill) go through NCCL (the base class).
+Prefill chunks (more than ``slot_rows`` rows) take the fused prefill all-reduce when NVSwitch
+multicast is available (``prefill_push``: a reduce-scatter GEMM epilogue, an owner-side reduce and a
+multicast broadcast of the finished residual rows, see csrc/prefill_ar.cu); otherwise NCCL (the
+base class).
 
 Slot reuse is safe when two uses of one slot are separated by another collective: a rank writes a
 slot again only after the barrier of a later call, which every peer reaches only after finishing
@@ -46,7 +49,7 @@ MARKOV_STEPS = 32         # Markov selector steps per launch (csrc/markov.cu MAX
 class SymmComm(TorchComm):
     def __init__(self, device, hidden: int, group=None, slot_rows: int = 32, graph_slots: int = 768,
                  eager_slots: int = 64, fused_graph_slots: int = 160, fused_eager_slots: int = 32,
-                 fused: bool = True, nvls: bool | None = None):
+                 fused: bool = True, nvls: bool | None = None, prefill_rows: int = 0):
         super().__init__(group)
         self.fused = fused          # row-parallel GEMMs push their tiles; the next norm reduces
         if self.world > MAX_RANKS:
@@ -113,7 +116,78 @@ class SymmComm(TorchComm):
         self.err = torch.zeros(1, dtype=torch.int32, device=self.device)
         self._next_graph = 0
         self._next_eager = 0
+        self._pf = None
+        # opt in (Q38_PREFILL_AR=1): measured slower than NCCL's all-reduce at TP2 on B200
+        if prefill_rows > PUSH_ROWS and self._recv_sym is not None and os.environ.get("Q38_PREFILL_AR", "0") == "1":
+            self._init_prefill(prefill_rows)
         dist.barrier(group=self.group)
+
+    # ------------------------------------------------------------------ prefill all-reduce
+    def _init_prefill(self, rows: int):
+        """Symmetric buffers of the fused prefill all-reduce (csrc/prefill_ar.cu): the replicated
+        fp32 residual of a chunk (every rank's copy written through the multicast address), the
+        reduce-scatter areas [source][local rows][hidden], the arrival counter and the completion
+        flag."""
+        import torch.distributed._symmetric_memory as symm_mem
+        H, W = self.hidden, self.world
+        tiles = -(-rows // 128)
+        cap = -(-tiles // W) * 128
+        x_bytes = -(-rows * H * 4 // 256) * 256
+        rs_bytes = W * cap * H * 4
+        total = x_bytes + rs_bytes + 256
+        t = symm_mem.empty(total, dtype=torch.uint8, device=self.device)
+        h = symm_mem.rendezvous(t, (self.group or dist.group.WORLD).group_name)
+        t.zero_()
+        torch.cuda.synchronize(self.device)
+        ptrs = list(h.buffer_ptrs)
+        mc = int(h.multicast_ptr)
+        self._pf = dict(
+            tensor=t, handle=h, rows=rows, cap=cap,
+            x=t[:rows * H * 4].view(torch.float32).view(rows, H),
+            recv_ptrs=[p + x_bytes for p in ptrs], count_ptrs=[p + x_bytes + rs_bytes for p in ptrs],
+            flag_local=ptrs[self.rank] + x_bytes + rs_bytes + 8, x_mc=mc, flag_mc=mc + x_bytes + rs_bytes + 8,
+            count_target=0, flag_target=0)
+
+    def prefill_fits(self, x) -> bool:
+        """True when ``x`` is this communicator's prefill residual buffer (fused path available)."""
+        pf = self._pf
+        return (pf is not None and x.shape[0] > PUSH_ROWS and x.shape[1] == self.hidden
+                and x.data_ptr() == pf["x"].data_ptr())
+
+    def prefill_x(self, rows: int):
+        """The [rows, hidden] fp32 residual view in symmetric memory, or None when the fused prefill
+        all-reduce is off or the chunk does not fit."""
+        pf = self._pf
+        if pf is None or rows <= PUSH_ROWS or rows > pf["rows"]:
+            return None
+        return pf["x"][:rows]
+
+    def prefill_push(self, ops, h, w, x) -> int:
+        """x += h @ w^T summed over ranks, launched: the reduce-scatter GEMM and this rank's
+        reduce + broadcast kernel.  Returns the completion-flag target the next reader waits for."""
+        pf = self._pf
+        T, W = x.shape[0], self.world
+        tiles = -(-T // 128)
+        slots = -(-tiles // W) * 128
+        owned = len(range(self.rank, tiles, W))
+        pf["count_target"] += W * owned * -(-w.N // 256)
+        ops.C.linear_rs(h.contiguous(), w.t, w.N, ops.ws, ops.counters, ops.err, pf["recv_ptrs"], pf["count_ptrs"],
+                        self.rank, pf["cap"])
+        ops.C.rs_reduce_bcast(pf["recv_ptrs"][self.rank], pf["count_ptrs"][self.rank], pf["count_target"], x,
+                              pf["x_mc"], pf["flag_mc"], self.rank, W, pf["cap"], slots, ops.err)
+        pf["flag_target"] += W * slots
+        ops.launches += 2
+        return pf["flag_target"]
+
+    def prefill_norm(self, ops, x, w, eps, target):
+        out = torch.empty(x.shape[0], x.shape[1], dtype=torch.bfloat16, device=x.device)
+        ops.C.rms_norm_wait(x, w, float(eps), out, self._pf["flag_local"], int(target), ops.err)
+        ops.launches += 1
+        return out
+
+    def prefill_wait(self, ops, target):
+        ops.C.rs_wait(self._pf["flag_local"], int(target), ops.err)
+        ops.launches += 1
 
     def _nvls_recv(self, nbytes: int):
         """(tensor, handle) of a zeroed symmetric-memory buffer bound to an NVSwitch multicast object,

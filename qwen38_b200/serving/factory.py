@@ -78,7 +78,8 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
         if torch.cuda.is_available():          # GPU ranks: peer access / NVLink preflight
             check_topology(rc.parallel.tp, comm=rc.parallel.comm if native else "nccl")
         comm = make_comm(rc.parallel.tp, device=device, hidden=cfg.hidden_size,
-                         peer=native and rc.parallel.comm != "nccl", fused=rc.parallel.comm == "fused")
+                         peer=native and rc.parallel.comm != "nccl", fused=rc.parallel.comm == "fused",
+                         prefill_rows=rc.runtime.prefill_chunk if rc.parallel.comm == "fused" else 0)
     slots = rc.serving.slots
     src = SafetensorsSource(ckpt) if ckpt else random_target_source(cfg, seed)
     if rc.runtime.weight_format == "mxfp8" and not _is_mxfp8_checkpoint(ckpt):

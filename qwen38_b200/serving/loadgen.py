@@ -120,7 +120,7 @@ def main():
         ops = NativeOps(device=dev, max_keys=max_ctx + 64)
     rt = RuntimeConfig(max_context=max_ctx, weight_format=a.weights)
     comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=cuda and a.comm != "nccl",
-                     fused=a.comm == "fused")
+                     fused=a.comm == "fused", prefill_rows=rt.prefill_chunk if a.comm == "fused" else 0)
     tsrc = random_target_source(cfg, a.seed)
     if a.weights == "mxfp8":
         from ..checkpoint import MXFP8Source

@@ -55,7 +55,7 @@ def main():
         ops = NativeOps(max_keys=max_ctx + 64)
     dev, dt = (torch.device("cuda", local), torch.bfloat16) if cuda else (torch.device("cpu"), torch.float32)
     comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=cuda and a.comm != "nccl",
-                     fused=a.comm == "fused")
+                     fused=a.comm == "fused", prefill_rows=chunk if a.comm == "fused" else 0)
     tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, device=dev, dtype=dt, ops=ops, comm=comm)
     dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, max_context=max_ctx)
     sr = SpecRuntime(tgt, dr, verifier_rows=dcfg.block_rows)

@@ -127,7 +127,8 @@ def main():
     max_ctx = a.ctx + a.iters * a.accept * 4 + 256
     rt = RuntimeConfig(max_context=max_ctx, prefill_chunk=min(4096, a.ctx))
     ops = NativeOps(device=dev, max_keys=max_ctx + 64)
-    comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=a.comm != "nccl", fused=a.comm == "fused")
+    comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=a.comm != "nccl", fused=a.comm == "fused",
+                     prefill_rows=rt.prefill_chunk if a.comm == "fused" else 0)
     tgt = HybridTarget(cfg, random_target_source(cfg, 0), rt, device=dev, dtype=torch.bfloat16, ops=ops, comm=comm,
                        max_slots=2)
     dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt, max_context=max_ctx)

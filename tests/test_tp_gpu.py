@@ -36,6 +36,8 @@ def _init(rank, world, rdv):
 
 
 def _worker(rank, world, rdv, q, mode):
+    if mode == "fused":
+        os.environ["Q38_PREFILL_AR"] = "1"       # also run the (opt-in) fused prefill all-reduce
     _init(rank, world, rdv)
     try:
         from qwen38_b200.checkpoint import random_drafter_source, random_target_source
@@ -51,7 +53,8 @@ def _worker(rank, world, rdv, q, mode):
         tgt = HybridTarget(cfg, random_target_source(cfg, 0), RuntimeConfig(max_context=1024, prefill_chunk=256),
                            device=f"cuda:{rank}", dtype=torch.bfloat16, ops=ops,
                            comm=make_comm(2, device=f"cuda:{rank}", hidden=cfg.hidden_size, peer=(mode != "nccl"),
-                                          fused=(mode == "fused")))
+                                          fused=(mode == "fused"), prefill_rows=256 if mode == "fused" else 0))
+        os.environ.pop("Q38_PREFILL_AR", None)
         dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), tgt)
         prompt = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(2)).tolist()
         gold = greedy_reference(tgt, prompt, 24)
@@ -156,3 +159,69 @@ def test_tp2_fused_gemm_allreduce_bits():
             assert maxdiff < 1e-3
     for (T0, _, _, a0), (T1, _, _, a1) in zip(out[0][1], out[1][1]):
         assert torch.equal(a0, a1)             # replicated residual: identical bits on both ranks
+
+
+def _prefill_worker(rank, world, rdv, q):
+    os.environ["Q38_PREFILL_AR"] = "1"           # the fused prefill all-reduce is opt in
+    _init(rank, world, rdv)
+    tgt = None
+    try:
+        from qwen38_b200.checkpoint import random_target_source
+        from qwen38_b200.config import FULL, LINEAR, ModelConfig, RuntimeConfig
+        from qwen38_b200.models.target import HybridTarget
+        from qwen38_b200.ops.native import NativeOps
+        from qwen38_b200.parallel.comm import make_comm
+        cfg = ModelConfig(num_hidden_layers=4, layer_types=[LINEAR, LINEAR, LINEAR, FULL])
+        ops = NativeOps(device=f"cuda:{rank}", max_keys=2048)
+        comm = make_comm(2, device=f"cuda:{rank}", hidden=cfg.hidden_size, peer=True, fused=True, prefill_rows=512)
+        tgt = HybridTarget(cfg, random_target_source(cfg, 0), RuntimeConfig(max_context=2048, prefill_chunk=512),
+                           device=f"cuda:{rank}", dtype=torch.bfloat16, ops=ops, comm=comm, max_slots=1)
+        prompt = torch.randint(0, cfg.vocab_size, (900,), generator=torch.Generator().manual_seed(4)).cuda()
+        fused_on = comm._pf is not None
+
+        def run():
+            seq = tgt.new_sequence()
+            nxt, feats = tgt.prefill(seq, prompt, taps=(1, 3))
+            out = (int(nxt.item()), feats.float().cpu(), tgt.rec[seq.slot].clone().cpu())
+            tgt.release(seq)
+            return out
+        a, b = run(), run()
+        saved, comm._pf = comm._pf, None            # the NCCL all-reduce path
+        c = run()
+        comm._pf = saved
+        ops.check()
+        comm.check()
+        q.put((rank, fused_on, a, b, c, None))
+    except BaseException as e:
+        q.put((rank, None, None, None, None, repr(e)))
+    finally:
+        torch.cuda.synchronize()
+        dist.destroy_process_group()
+
+
+def test_tp2_fused_prefill_allreduce():
+    """The fused prefill all-reduce (reduce-scatter GEMM + owner reduce + multicast broadcast) is
+    deterministic, leaves identical residuals (taps, GDN state) on both ranks, and agrees with the
+    NCCL all-reduce path to fp32 rounding.  Chunks of 512 and 388 rows (a ragged last tile)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    rdv = _rdv()
+    procs = [ctx.Process(target=_prefill_worker, args=(r, 2, rdv, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    try:
+        out = sorted([q.get(timeout=600) for _ in procs], key=lambda o: o[0])
+    finally:
+        for p in procs:
+            p.join(timeout=60)
+            if p.is_alive():
+                p.terminate()
+                p.join(timeout=10)
+    for rank, fused_on, a, b, c, err in out:
+        assert err is None, err
+        if not fused_on:
+            pytest.skip("no NVSwitch multicast on this system: the fused prefill all-reduce is off")
+        assert a[0] == b[0] and torch.equal(a[1], b[1]) and torch.equal(a[2], b[2])      # deterministic
+        assert ((a[1] - c[1]).norm() / c[1].norm()).item() < 2e-2                          # vs NCCL
+        assert ((a[2] - c[2]).norm() / c[2].norm()).item() < 2e-2
+    assert torch.equal(out[0][2][1], out[1][2][1])        # replicated residual: same taps on both ranks
