@@ -17,7 +17,8 @@ collectives with the kernels in ``csrc/comm.cu``:
   appears, adds the rank-ordered sum and normalises (receive blocks [slot][source rank]).  When
   the NVSwitch offers multicast (``torch.distributed._symmetric_memory`` with a multicast
   pointer), the receive areas live in that symmetric memory and each word leaves the GPU once,
-  through the multicast address (``recv_mc``), instead of once per rank (``Q38_NVLS=0``: off).
+  through the multicast address (``recv_mc``), instead of once per rank (opt in: ``Q38_NVLS=1``;
+  measured at TP8 on B200 it shortened the GEMMs but not the verify, 5.75 vs 5.65 ms per block).
 
 Prefill chunks (more than ``slot_rows`` rows) take the fused prefill all-reduce when NVSwitch
 multicast is available (``prefill_push``: a reduce-scatter GEMM epilogue, an owner-side reduce and a
@@ -74,8 +75,8 @@ class SymmComm(TorchComm):
         # the pushed all-reduce's receive areas in NVLS-capable symmetric memory when the switch
         # supports multicast: a GEMM then stores each word once through the multicast address
         self.recv_mc, self._recv_sym = 0, None
-        if nvls is None:
-            nvls = os.environ.get("Q38_NVLS", "1") != "0"
+        if nvls is None:           # opt in (Q38_NVLS=1): no gain measured at TP8 on B200
+            nvls = os.environ.get("Q38_NVLS", "0") == "1"
         if nvls:
             self._recv_sym = self._nvls_recv(recv_bytes)
             agree = torch.tensor([1 if self._recv_sym is not None else 0], dtype=torch.int32, device=self.device)

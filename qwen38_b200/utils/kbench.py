@@ -10,6 +10,7 @@ bandwidth / throughput against the measured peaks (``MEASURED_PEAKS.json`` at th
     python -m qwen38_b200.utils.kbench gdn --T 16 --nv 48
     python -m qwen38_b200.utils.kbench gdnpf --T 2048 --nv 48
     python -m qwen38_b200.utils.kbench attn --T 16 --ctx 4096
+    python -m qwen38_b200.utils.kbench markov --V 151936 --R 256 --P 15
 """
 from __future__ import annotations
 
@@ -224,6 +225,40 @@ def bench_gdn_prefill(a):
             "tflops": round(flops / ms / 1e9, 1), "us_per_row": round(ms * 1e3 / a.T, 3)}
 
 
+def bench_markov(a):
+    """The drafter's Markov selector over a vocabulary shard of ``--V`` rows, ``--P`` sequential
+    steps of rank ``--R``: the one-launch kernel against the per-step two-launch kernels."""
+    from ..ops.native import NativeOps
+    ops = NativeOps()
+    g = torch.Generator(device="cuda").manual_seed(0)
+    logits = torch.randn(a.P, a.V, generator=g, device="cuda")
+    pred = (torch.randn(a.V, a.R, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    succ = (torch.randn(a.V, a.R, generator=g, device="cuda") * 0.1).to(torch.bfloat16)
+    anchor = torch.tensor([7], device="cuda")
+    fused = lambda: ops.markov_select(logits, anchor, pred, succ)
+    if a.iters == 0:
+        fused()
+        torch.cuda.synchronize()
+        ops.check()
+        return {}
+    prev = anchor.clone()
+    steps = torch.empty(a.P, dtype=torch.int64, device="cuda")
+    val = torch.empty(1, device="cuda")
+
+    def per_step():
+        prev.copy_(anchor)
+        for i in range(a.P):
+            ops.C.markov_step(logits[i], pred, succ, prev, steps[i:i + 1], val, ops.amax_val, ops.amax_idx, 0, True)
+    ms_f = time_kernel(fused, a.iters)
+    ms_s = time_kernel(per_step, a.iters)
+    ops.check()
+    hbm, _, src = peaks()
+    bytes_step = a.V * a.R * 2 + a.V * 4
+    return {"kernel": "markov_select", "V": a.V, "R": a.R, "P": a.P, "fused_ms": round(ms_f, 4),
+            "per_step_kernels_ms": round(ms_s, 4), "fused_us_per_step": round(ms_f * 1e3 / a.P, 2),
+            f"fused_frac_bw_of_{src}": round(bytes_step * a.P / ms_f / 1e6 / hbm, 3)}
+
+
 def bench_attn(a):
     from ..ops.native import NativeOps
     ops = NativeOps(max_keys=a.ctx + 64)
@@ -250,7 +285,10 @@ def bench_attn(a):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("kind", choices=["gemm", "gdn", "gdnpf", "attn"])
+    ap.add_argument("kind", choices=["gemm", "gdn", "gdnpf", "attn", "markov"])
+    ap.add_argument("--V", type=int, default=151936)
+    ap.add_argument("--R", type=int, default=256)
+    ap.add_argument("--P", type=int, default=15)
     ap.add_argument("--T", type=int, default=16)
     ap.add_argument("--N", type=int, default=5120)
     ap.add_argument("--K", type=int, default=17408)
@@ -264,7 +302,8 @@ def main():
     ap.add_argument("--trace", action="store_true", help="GEMM: per-CTA phase stamps of one launch")
     ap.add_argument("--graph", type=int, default=0, help="GEMM: time N back-to-back launches in one CUDA graph")
     a = ap.parse_args()
-    out = {"gemm": bench_gemm, "gdn": bench_gdn, "gdnpf": bench_gdn_prefill, "attn": bench_attn}[a.kind](a)
+    out = {"gemm": bench_gemm, "gdn": bench_gdn, "gdnpf": bench_gdn_prefill, "attn": bench_attn,
+           "markov": bench_markov}[a.kind](a)
     if out:
         print(json.dumps(out))
 

@@ -38,6 +38,7 @@ def _init(rank, world, rdv):
 def _worker(rank, world, rdv, q, mode):
     if mode == "fused":
         os.environ["Q38_PREFILL_AR"] = "1"       # also run the (opt-in) fused prefill all-reduce
+        os.environ["Q38_NVLS"] = "1"             # and the (opt-in) multicast push
     _init(rank, world, rdv)
     try:
         from qwen38_b200.checkpoint import random_drafter_source, random_target_source
@@ -163,6 +164,7 @@ def test_tp2_fused_gemm_allreduce_bits():
 
 def _prefill_worker(rank, world, rdv, q):
     os.environ["Q38_PREFILL_AR"] = "1"           # the fused prefill all-reduce is opt in
+    os.environ["Q38_NVLS"] = "1"                 # (it needs the multicast receive areas)
     _init(rank, world, rdv)
     tgt = None
     try:
