@@ -60,6 +60,11 @@ void q38_markov_select(torch::Tensor logits, torch::Tensor pred, torch::Tensor s
                        torch::Tensor out, int64_t vocab_offset, torch::Tensor rec_val, torch::Tensor rec_idx,
                        torch::Tensor state, std::vector<int64_t> recv_ptrs, int64_t rank, torch::Tensor err);
 void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor out);
+void q38_rms_norm_split(torch::Tensor x, torch::Tensor parts, int64_t S, c10::optional<torch::Tensor> w, double eps,
+                        c10::optional<torch::Tensor> out);
+int64_t q38_swap_splits(int64_t N, int64_t K);
+int64_t q38_linear_split(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor parts,
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err);
 void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
                      torch::Tensor out, c10::optional<torch::Tensor> out_val, torch::Tensor part_val,
@@ -100,6 +105,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_prefill", &q38_attn_prefill);
   m.def("attn_key_groups", &q38_attn_key_groups);
   m.def("rms_norm", &q38_rms_norm);
+  m.def("rms_norm_split", &q38_rms_norm_split);
+  m.def("swap_splits", &q38_swap_splits);
+  m.def("linear_split", &q38_linear_split);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);
   m.def("markov_select", &q38_markov_select);

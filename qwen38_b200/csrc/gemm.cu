@@ -168,11 +168,14 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
   g.counters = sc.counters;
   g.trace = trace;
   TORCH_CHECK(epi != EPI_RS_F32 || (T > 32 && rs != nullptr), "the reduce-scatter epilogue serves prefill tiles");
-  if (T <= 32) {
-    // swap-AB streaming: M = weight rows, N = tokens
+  if (T <= SWAP_MAX_ROWS) {
+    // swap-AB streaming: M = weight rows, N = tokens in 32-token tiles (grid y).  Each token
+    // column's result depends on its own column and the split plan (a function of N, K and the SM
+    // count) only, so a row gets the same bits alone or packed with other requests' rows.
     g.M = N;
     g.N = T;
     const int m_tiles = (N + BM - 1) / BM;
+    const int n_tiles = (T + 31) / 32;
     int splits = pick_splits(m_tiles, g.kblocks, num_sms());
     int kps = (g.kblocks + splits - 1) / splits;
     splits = (g.kblocks + kps - 1) / kps;
@@ -182,10 +185,10 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     // reduces through DSMEM inside a cluster of the tile's splits (same bits).  Measured on B200
     // the cluster form was slower: clusters of up to 8 CTAs at two CTAs per SM no longer fit the
     // grid into one wave once GPC boundaries are respected.  ARGMAX always uses the global form.
-    g.cluster_k = epi != EPI_ARGMAX && splitk_cluster();
-    if (splits > 1 && !g.cluster_k) {
-      TORCH_CHECK((int64_t)m_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
-      TORCH_CHECK(m_tiles <= sc.n_counters, "split-K counter array too small");
+    g.cluster_k = epi != EPI_ARGMAX && epi != EPI_SPLIT_F32 && n_tiles == 1 && splitk_cluster();
+    if (splits > 1 && !g.cluster_k && epi != EPI_SPLIT_F32) {
+      TORCH_CHECK((int64_t)m_tiles * n_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
+      TORCH_CHECK(m_tiles * n_tiles <= sc.n_counters, "split-K counter array too small");
     }
     if (epi == EPI_PUSH_F32) {
       TORCH_CHECK(ar != nullptr && (int64_t)T * N <= ar->block_words, "pushed all-reduce: block too small");
@@ -203,10 +206,10 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     }
     CUtensorMap ma = cached_map(w, BM, true);      // one 16 KB weight tile per box
     CUtensorMap mb = cached_map(x, 32, false);
-    dim3 grid(m_tiles, 1, splits);
+    dim3 grid(m_tiles, n_tiles, splits);
     launch_swap(epi, ma, mb, g, grid, st);
   } else {
-    TORCH_CHECK(epi != EPI_ARGMAX && epi != EPI_PUSH_F32, "argmax / pushed all-reduce epilogues serve <= 32 rows");
+    TORCH_CHECK(epi != EPI_ARGMAX && epi != EPI_PUSH_F32, "argmax / pushed all-reduce epilogues serve <= 64 rows");
     g.M = T;
     g.N = N;
     g.splits = 1;
@@ -242,7 +245,7 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
   q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc);
 }
 
-// Row-parallel out-projection whose epilogue pushes this rank's fp32 partial [T, N] (T <= 32)
+// Row-parallel out-projection whose epilogue pushes this rank's fp32 partial [T, N] (T <= 64)
 // into every rank's receive block of `slot` as {value, epoch} words (EPI_PUSH_F32); the reduction
 // into the residual happens in q38_rms_norm_ar.  recv_ptrs: every rank's receive area mapped into
 // this process; epochs: this rank's [slots][32] per-row epochs.
@@ -250,7 +253,7 @@ void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor 
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
                      int64_t block_words, torch::Tensor epochs, int64_t mc_ptr) {
   c10::cuda::CUDAGuard guard(x.device());
-  TORCH_CHECK(x.size(0) <= q38::AR_MAX_ROWS, "the pushed all-reduce serves <= 32 rows");
+  TORCH_CHECK(x.size(0) <= q38::AR_MAX_ROWS, "the pushed all-reduce serves <= 64 rows");
   TORCH_CHECK(x.size(0) * N <= block_words, "partial larger than a receive block");
   const int world = (int)recv_ptrs.size();
   TORCH_CHECK(world >= 1 && world <= q38::AR_MAX_RANKS, "1..8 ranks");
@@ -269,6 +272,39 @@ void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor 
   // no local output tensor: the epilogue writes the receive blocks, laid out [T, N] (ldo = N)
   torch::Tensor unused = x;
   q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_PUSH_F32, sc, nullptr, nullptr, nullptr, &a, nullptr, N);
+}
+
+// Split-K slices of the swap-AB plan for an [N, K] weight (the count q38_linear would use).
+int64_t q38_swap_splits(int64_t N, int64_t K) {
+  const int m_tiles = (int)((N + q38::BM - 1) / q38::BM), kblocks = (int)((K + q38::BK - 1) / q38::BK);
+  const int s = q38::pick_splits(m_tiles, kblocks, q38::num_sms());
+  const int kps = (kblocks + s - 1) / s;
+  return (kblocks + kps - 1) / kps;
+}
+
+// Row-parallel out-projection of <= 64 rows whose split-K reduction is left to the consumer:
+// with S > 1 slices every slice stores its fp32 partial into parts ([S][T][N], contiguous from the
+// start of `parts`) and nothing else; the next RMSNorm of the residual (q38_rms_norm_split) adds the
+// slices in split order and then the residual, the same arithmetic as the in-kernel fix-up, so the
+// residual gets the same bits one launch later without the fix-up's serial tail.  With one slice
+// the GEMM adds into `residual` directly.  Returns S (1: nothing pending).
+int64_t q38_linear_split(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor parts,
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(x.device());
+  const int64_t T = x.size(0);
+  TORCH_CHECK(T >= 1 && T <= q38::SWAP_MAX_ROWS, "deferred split-K serves 1..64 rows");
+  TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous() && residual.size(0) == T &&
+                  residual.size(1) == N, "fp32 residual [T, N]");
+  auto sc = q38::scratch_of(ws, counters, err);
+  const int64_t S = q38_swap_splits(N, x.size(1));
+  if (S == 1) {
+    q38::gemm_dispatch(x, w, (int)N, residual, q38::EPI_ADD_F32, sc);
+    return 1;
+  }
+  TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.is_contiguous() && parts.numel() >= S * T * N,
+              "split partial buffer too small");
+  q38::gemm_dispatch(x, w, (int)N, parts, q38::EPI_SPLIT_F32, sc, nullptr, nullptr, nullptr, nullptr, nullptr, N);
+  return S;
 }
 
 // Prefill out-projection whose tiles go to their owning rank's reduce-scatter area (EPI_RS_F32):
@@ -304,7 +340,8 @@ int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Ten
               "traced epilogues: bf16, f32, add, swiglu");
   auto sc = q38::scratch_of(ws, counters, err);
   const int T = (int)x.size(0), K = (int)x.size(1);
-  const int64_t m_tiles = (T <= 32) ? (N + 127) / 128 : ((T + 127) / 128) * ((N + q38::PREFILL_BN - 1) / q38::PREFILL_BN);
+  const int64_t m_tiles = (T <= q38::SWAP_MAX_ROWS) ? ((N + 127) / 128) * ((T + 31) / 32)
+                                                    : ((T + 127) / 128) * ((N + q38::PREFILL_BN - 1) / q38::PREFILL_BN);
   const int64_t kb = (K + 63) / 64;
   TORCH_CHECK(trace.numel() >= m_tiles * kb * 8, "trace buffer too small");
   q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc, nullptr, nullptr, nullptr, nullptr,
@@ -319,7 +356,7 @@ void q38_lm_head_argmax(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tens
   c10::cuda::CUDAGuard guard(x.device());
   auto sc = q38::scratch_of(ws, counters, err);
   const int T = (int)x.size(0);
-  TORCH_CHECK(T <= 32, "LM-head argmax serves <= 32 rows");
+  TORCH_CHECK(T <= q38::SWAP_MAX_ROWS, "LM-head argmax serves <= 64 rows");
   const int tiles_needed = (int)((N + 127) / 128);
   TORCH_CHECK(part_val.numel() >= (int64_t)tiles_needed * T && part_idx.numel() >= (int64_t)tiles_needed * T,
               "argmax partial buffers too small");

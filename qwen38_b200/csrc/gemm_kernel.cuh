@@ -32,13 +32,16 @@ namespace q38 {
 enum Epi : int {
   EPI_BF16 = 0, EPI_F32 = 1, EPI_ADD_F32 = 2, EPI_SWIGLU = 3, EPI_ARGMAX = 4, EPI_PUSH_F32 = 5,
   EPI_RS_F32 = 6,   // prefill tiles: fp32 partial straight into the owning rank's reduce-scatter area
+  EPI_SPLIT_F32 = 7,  // swap mode: every split-K slice stores its own fp32 partial ([split][token][N] at
+                      // g.out, token stride ldo); no fix-up: the consumer adds the slices in split order
 };
 
 constexpr int AR_MAX_RANKS = 8;
 
 // Peer buffers of the pushed all-reduce.  Receive area of every rank: blocks [slot][src rank]
 // of `block_words` 8-byte words {fp32 value, epoch}, each a [tokens, ldo] partial.
-constexpr int AR_MAX_ROWS = 32;
+constexpr int SWAP_MAX_ROWS = 64;  // token rows the swap-AB (weight-streaming) GEMM serves, in 32-row tiles
+constexpr int AR_MAX_ROWS = 64;   // rows of one pushed all-reduce (a packed verify of up to 4 x 16)
 
 struct ArArgs {
   long long recv[AR_MAX_RANKS];    // every rank's receive area (8-byte words), mapped into this process
@@ -342,7 +345,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 
   bool clustered = false;
-  if constexpr (SWAP && EPI != EPI_ARGMAX) {
+  if constexpr (SWAP && EPI != EPI_ARGMAX && EPI != EPI_SPLIT_F32) {
     clustered = g.splits > 1 && g.cluster_k;
     if (clustered)
       swap_cluster_epilogue<EPI>(g, reinterpret_cast<float*>(smem), trow, ok && nk > 0, m_tile, split, row);
@@ -359,8 +362,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(r[j]);
 
       bool do_epi = true;
-      if (g.splits > 1) {
-        const int tile = m_tile;  // single n tile in swap mode
+      if (g.splits > 1 && EPI != EPI_SPLIT_F32) {
+        const int tile = n_tile * gridDim.x + m_tile;   // (feature tile, 32-token tile)
         float* part = g.ws + ((size_t)tile * g.splits + split) * (BM * BN);
 #pragma unroll
         for (int j = 0; j < 32; ++j) part[j * BM + row] = acc[j];
@@ -516,7 +519,12 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           // Fully unrolled over the 32 token columns (predicated), so acc[] stays in registers;
           // the residual accumulate issues every load before any add.
           if (m < g.M) {
-            if constexpr (EPI == EPI_ADD_F32) {
+            if constexpr (EPI == EPI_SPLIT_F32) {
+              float* __restrict__ o = reinterpret_cast<float*>(g.out) + (size_t)split * g.N * g.ldo;
+#pragma unroll
+              for (int j = 0; j < 32; ++j)
+                if (j < nvalid) o[(size_t)(n0 + j) * g.ldo + m] = acc[j];
+            } else if constexpr (EPI == EPI_ADD_F32) {
               float* __restrict__ o = reinterpret_cast<float*>(g.out);
               float r[32];
 #pragma unroll

@@ -10,6 +10,7 @@ void launch_swap(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const Ge
     case EPI_SWIGLU: launch_gemm<32, SKINNY_STAGES, EPI_SWIGLU, true>(ma, mb, g, grid, st); break;
     case EPI_ARGMAX: launch_gemm<32, SKINNY_STAGES, EPI_ARGMAX, true>(ma, mb, g, grid, st); break;
     case EPI_PUSH_F32: launch_gemm<32, SKINNY_STAGES, EPI_PUSH_F32, true>(ma, mb, g, grid, st); break;
+    case EPI_SPLIT_F32: launch_gemm<32, SKINNY_STAGES, EPI_SPLIT_F32, true>(ma, mb, g, grid, st); break;
     default: TORCH_CHECK(false, "bad epilogue");
   }
 }

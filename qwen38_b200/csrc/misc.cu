@@ -103,11 +103,70 @@ rms_norm_kernel(const TIn* __restrict__ x, long long ldx, const float* __restric
   }
 }
 
+// Deferred split-K reduction + residual add + RMSNorm (<= 64 rows, the cluster-spread layout of
+// rms_norm_kernel).  parts holds S fp32 slices [S][R][H] of a row-parallel GEMM (EPI_SPLIT_F32);
+// every element becomes x + (((0 + p_0) + p_1) + ... + p_{S-1}), the split-order sum and residual
+// add of the GEMM's own fix-up, and is written back to the residual x.  With a weight the updated
+// row is normalised into `out` with the norm core shared by rms_norm_kernel (same bits); without
+// one (w == nullptr) only the residual is completed.
+constexpr int MAX_SPLITS = 8;
+
+template <int VPT>
+__global__ void __launch_bounds__(NORM_NT)
+rms_norm_split_kernel(float* __restrict__ x, const float* __restrict__ parts, int S, const float* __restrict__ w,
+                      int H, float eps, __nv_bfloat16* __restrict__ out, long long ldo) {
+  cluster_arrive_relaxed();
+  pdl_wait();
+  pdl_trigger();
+  const int c = (int)cluster_rank(), r = blockIdx.y, R = gridDim.y;
+  float* xr = x + (size_t)r * H;
+  const size_t pstride = (size_t)R * H;
+  const float* pr = parts + (size_t)r * H;
+  float v[VPT], wv[VPT], acc[VPT];
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {               // residual and weight loads in one round trip
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+    v[u] = i < H ? xr[i] : 0.f;
+    wv[u] = (w != nullptr && i < H) ? w[i] : 0.f;
+    acc[u] = 0.f;
+  }
+#pragma unroll
+  for (int k = 0; k < MAX_SPLITS; ++k) {        // slices in split order
+    if (k < S) {
+#pragma unroll
+      for (int u = 0; u < VPT; ++u) {
+        const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+        if (i < H) acc[u] += __ldcg(pr + k * pstride + i);
+      }
+    }
+  }
+  float ss = 0.f;
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+    v[u] = v[u] + acc[u];
+    if (i < H) xr[i] = v[u];
+    ss += v[u] * v[u];
+  }
+  if (w == nullptr) {
+    cluster_wait();                             // matches the arrive above; no exchange needed
+    return;
+  }
+  int flag = 1;
+  const float inv = rsqrtf(norm_row_total(ss, flag) / H + eps);
+  __nv_bfloat16* o = out + (size_t)r * ldo;
+#pragma unroll
+  for (int u = 0; u < VPT; ++u) {
+    const int i = (u * NORM_CPR + c) * NORM_NT + threadIdx.x;
+    if (i < H) o[i] = __float2bfloat16(v[u] * inv * wv[u]);
+  }
+}
+
 // Many rows (prefill chunks): one CTA of 256 threads per row, row kept in registers between the
 // sum of squares and the scaling.  Row counts above NORM_CLUSTER_ROWS take this kernel; its
 // reduction order differs from the cluster kernel's, which only rows of decode / verify size
 // (where the all-reduce norm must reproduce the plain norm bit for bit) need.
-constexpr int NORM_CLUSTER_ROWS = 32;
+constexpr int NORM_CLUSTER_ROWS = 64;
 
 template <typename TIn, int VPT>
 __global__ void __launch_bounds__(256)
@@ -156,7 +215,7 @@ rms_norm_rows_kernel(const TIn* __restrict__ x, long long ldx, const float* __re
 // written only when every CTA of the row saw every word: a peer that never published leaves them
 // untouched (the error word records it).
 constexpr int AR_RANKS = 8;
-constexpr int AR_ROWS = 32;
+constexpr int AR_ROWS = 64;          // = AR_MAX_ROWS of the pushing GEMM (gemm_kernel.cuh)
 
 __device__ __forceinline__ unsigned long long ld_relaxed_sys_u64(const unsigned long long* addr) {
   unsigned long long v;
@@ -385,6 +444,46 @@ void q38_rms_norm(torch::Tensor x, torch::Tensor w, double eps, torch::Tensor ou
   else if (vpt <= 5) { Q38_NORM(5) }
   else { Q38_NORM(8) }
 #undef Q38_NORM
+  C10_CUDA_KERNEL_LAUNCH_CHECK();
+}
+
+// Completes a deferred split-K row-parallel GEMM (q38_linear_split) into the residual x and, with a
+// weight, normalises the updated rows into out (see rms_norm_split_kernel).
+void q38_rms_norm_split(torch::Tensor x, torch::Tensor parts, int64_t S, c10::optional<torch::Tensor> w, double eps,
+                        c10::optional<torch::Tensor> out) {
+  c10::cuda::CUDAGuard guard(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kFloat && x.is_contiguous() && x.dim() == 2, "contiguous fp32 residual");
+  const int R = (int)x.size(0), H = (int)x.size(1);
+  TORCH_CHECK(R >= 1 && R <= q38::NORM_CLUSTER_ROWS, "deferred split-K serves 1..64 rows");
+  TORCH_CHECK(S >= 1 && S <= q38::MAX_SPLITS, "1..8 split slices");
+  TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.is_contiguous() && parts.numel() >= S * R * H,
+              "split partial buffer too small");
+  TORCH_CHECK(w.has_value() == out.has_value(), "weight and output go together");
+  const float* wp = nullptr;
+  __nv_bfloat16* op = nullptr;
+  long long ldo = 0;
+  if (w.has_value()) {
+    TORCH_CHECK(w->scalar_type() == at::kFloat && w->numel() == H, "fp32 weight [H]");
+    TORCH_CHECK(out->scalar_type() == at::kBFloat16 && out->stride(1) == 1 && out->size(0) == R, "bf16 out [R, H]");
+    wp = w->data_ptr<float>();
+    op = reinterpret_cast<__nv_bfloat16*>(out->data_ptr());
+    ldo = out->stride(0);
+  }
+  const int vpt = norm_vpt(H);
+  TORCH_CHECK(vpt <= 8, "rms_norm: hidden above 8192");
+  cudaStream_t st = at::cuda::getCurrentCUDAStream();
+  const dim3 grid(q38::NORM_CPR, R), cl(q38::NORM_CPR, 1, 1);
+  cudaError_t e;
+#define Q38_NSPLIT(VV)                                                                                        \
+  e = q38::launch_pdl_cluster(q38::rms_norm_split_kernel<VV>, grid, dim3(q38::NORM_NT), 0, st, cl,            \
+                              x.data_ptr<float>(), (const float*)parts.data_ptr<float>(), (int)S, wp, H,      \
+                              (float)eps, op, ldo);
+  if (vpt <= 1) { Q38_NSPLIT(1) }
+  else if (vpt <= 2) { Q38_NSPLIT(2) }
+  else if (vpt <= 5) { Q38_NSPLIT(5) }
+  else { Q38_NSPLIT(8) }
+#undef Q38_NSPLIT
+  TORCH_CHECK(e == cudaSuccess, "rms_norm_split launch");
   C10_CUDA_KERNEL_LAUNCH_CHECK();
 }
 

@@ -141,7 +141,7 @@ class BlockDrafter:
     def _row_par_add(self, h, w, x):
         """x += h @ w^T summed over ranks."""
         if self.tp == 1:
-            self.ops.linear_residual(h, w, x)
+            self.target.local_row_parallel(h, w, x)     # completed by the next norm of x
         elif self.target.fused_ar and self.comm.fused_fits(*x.shape):
             self.target.push_row_parallel(h, w, x)      # completed by the next norm of x
         elif hasattr(self.comm, "slot_out") and self.comm.fits(*x.shape):

@@ -25,6 +25,8 @@ LM head with a cross-rank (value, index) argmax.  Layout per rank:
 """
 from __future__ import annotations
 
+import os
+
 from dataclasses import dataclass, field
 
 import torch
@@ -179,7 +181,12 @@ class HybridTarget:
         # RMSNorm of the residual completes the reduction (``_pending`` = (residual, "push", slot), or
         # (residual, "rs", completion-flag target) for the fused prefill all-reduce)
         self.fused_ar = bool(getattr(self.comm, "fused", False)) and hasattr(ops, "linear_push")
+        # single rank: out-projections of <= 64 rows leave their split-K slices for the next norm
+        # (``_pending`` = (residual, "split", slice count)); Q38_DEFER_SPLITK=0 keeps the in-GEMM fix-up
+        self.defer_splits = hasattr(self.ops, "linear_split") and os.environ.get("Q38_DEFER_SPLITK", "1") != "0"
         self._pending = None
+        # rows one verify may pack and stay on the batch-invariant kernels (None: no limit)
+        self.max_pack_rows = getattr(self.ops, "max_pack_rows", None)
         tp, r = self.comm.world, self.comm.rank
         self.tp, self.rank = tp, r
         self.widths = tp_widths(cfg, tp)
@@ -292,7 +299,7 @@ class HybridTarget:
     def _row_parallel(self, h, w, x):
         """x += h @ w^T summed over ranks (row-parallel out-projection + residual add)."""
         if self.tp == 1:
-            self.ops.linear_residual(h, w, x)
+            self.local_row_parallel(h, w, x)
         elif self.fused_ar and self.comm.fused_fits(*x.shape):
             self.push_row_parallel(h, w, x)
         elif getattr(self.comm, "prefill_fits", None) is not None and self.comm.prefill_fits(x):
@@ -309,6 +316,17 @@ class HybridTarget:
             self.comm.all_reduce_(part)
             x += part
 
+    def local_row_parallel(self, h, w, x):
+        """x += h @ w^T on one rank; for <= 32 rows the split-K slices are added by the next
+        ``norm`` / ``settle`` of x (the drafters use it too)."""
+        if self.defer_splits and x.shape[0] <= self.ops.max_pack_rows:
+            self.settle(x)
+            S = self.ops.linear_split(h, w, x)
+            if S > 1:
+                self._pending = (x, "split", S)
+        else:
+            self.ops.linear_residual(h, w, x)
+
     def norm(self, x, w, eps=None):
         """RMSNorm of the residual ``x``; completes a pending pushed all-reduce into ``x`` first
         (in the same kernel)."""
@@ -318,6 +336,8 @@ class HybridTarget:
             self._pending = None
             if kind == "rs":
                 return self.comm.prefill_norm(self.ops, x, w, eps, val)
+            if kind == "split":
+                return self.ops.rms_norm_split(x, w, eps, self.dtype, val)
             return self.ops.rms_norm_ar(x, w, eps, self.dtype, self.comm, val)
         return self.ops.rms_norm(x, w, eps, self.dtype)
 
@@ -334,6 +354,8 @@ class HybridTarget:
             self._pending = None
             if kind == "rs":
                 self.comm.prefill_wait(self.ops, val)
+            elif kind == "split":
+                self.ops.rms_norm_split(px, None, self.eps, self.dtype, val)
             else:
                 self.ops.rms_norm_ar(px, None, self.eps, self.dtype, self.comm, val)
 

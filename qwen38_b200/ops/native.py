@@ -58,6 +58,9 @@ _ERR_NAMES = {1: "TMA/mbarrier wait timeout", 2: "accumulator wait timeout", 4: 
 
 class NativeOps(TorchOps):
     name = "native"
+    # token rows the weight-streaming (swap-AB) GEMM, the cluster norms and the pushed all-reduce
+    # serve (csrc SWAP_MAX_ROWS / AR_MAX_ROWS): a packed verify of up to 4 x 16 rows stays on them
+    max_pack_rows = 64
 
     def __init__(self, device=None, max_keys: int = 1 << 17, ws_mb: int = 64):
         self.C = load()
@@ -77,6 +80,7 @@ class NativeOps(TorchOps):
         self.launches = 0
         self.chunked_prefill = True
         self._gdn_work = None
+        self._split_parts = None          # deferred split-K slices [8][64][N] fp32 (linear_split)
 
     # ------------------------------------------------------------------ errors
     def check(self):
@@ -108,7 +112,7 @@ class NativeOps(TorchOps):
         return out
 
     def linear_push(self, x, w, comm) -> int:
-        """GEMM half of the tensor-parallel all-reduce: x @ w^T (fp32, T <= 32 rows) goes straight
+        """GEMM half of the tensor-parallel all-reduce: x @ w^T (fp32, T <= 64 rows) goes straight
         from each finished tile into every rank's receive block of a fresh slot as {value, epoch}
         words; returns the slot for ``rms_norm_ar``."""
         w = self.prepare_weight(w)
@@ -132,6 +136,31 @@ class NativeOps(TorchOps):
         self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
         self.launches += 1
         return residual
+
+    def linear_split(self, x, w, residual) -> int:
+        """residual += x @ w^T for <= 64 rows with the split-K reduction deferred: each K slice of
+        the GEMM stores its fp32 partial and exits; ``rms_norm_split`` adds the slices (split order)
+        and the residual, the bits of ``linear_residual``.  Returns the slice count S; with S == 1
+        the GEMM has added into ``residual`` already and nothing is pending."""
+        w = self.prepare_weight(w)
+        T, N = residual.shape
+        need = 8 * self.max_pack_rows * N
+        if self._split_parts is None or self._split_parts.numel() < need:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("linear_split: slice buffer must be sized before graph capture")
+            self._split_parts = torch.empty(need, dtype=torch.float32, device=self.device)
+        S = int(self.C.linear_split(x.contiguous(), w.t, w.N, residual, self._split_parts, self.ws, self.counters,
+                                    self.err))
+        self.launches += 1
+        return S
+
+    def rms_norm_split(self, x, w, eps, out_dtype, S):
+        """Completes a pending ``linear_split`` of S slices into the residual ``x`` and returns
+        RMSNorm(x) * w in bf16 (``w`` None: completes the residual only)."""
+        out = None if w is None else torch.empty(x.shape[0], x.shape[1], dtype=torch.bfloat16, device=x.device)
+        self.C.rms_norm_split(x, self._split_parts, int(S), w, float(eps), out)
+        self.launches += 1
+        return out if out is None or out_dtype == torch.bfloat16 else out.to(out_dtype)
 
     def linear_swiglu(self, x, w_gu, block):
         if block != 64:

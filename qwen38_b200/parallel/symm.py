@@ -43,7 +43,7 @@ from .comm import TorchComm
 
 MAX_RANKS = 8
 AR_CTAS = 32
-PUSH_ROWS = 32            # rows of a pushed all-reduce (csrc: AR_MAX_ROWS)
+PUSH_ROWS = 64            # rows of a pushed all-reduce (csrc: AR_MAX_ROWS): a packed verify of 4 x 16
 MARKOV_STEPS = 32         # Markov selector steps per launch (csrc/markov.cu MAX_STEPS)
 
 

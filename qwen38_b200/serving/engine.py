@@ -37,8 +37,13 @@ class ServingEngine:
         self.max_running = max_running or slots
         if self.max_running > slots:
             raise ValueError("more running requests than target/drafter slots")
-        self.sched = Scheduler(self.max_running, prefill_chunk or target.rt.prefill_chunk,
-                               max_step_rows or self.max_running * verifier_rows, verifier_rows)
+        # a packed verify stays within the rows the target's kernels keep batch-invariant; more
+        # running requests than that are served in rotation
+        step_rows = max_step_rows or self.max_running * verifier_rows
+        pack = getattr(target, "max_pack_rows", None)
+        if pack:
+            step_rows = min(step_rows, max(pack, verifier_rows))
+        self.sched = Scheduler(self.max_running, prefill_chunk or target.rt.prefill_chunk, step_rows, verifier_rows)
         self.taps = tuple(drafter.dcfg.taps) if drafter is not None else ()
         self.free_dslots = list(range(slots - 1, -1, -1))
         self.requests: dict = {}

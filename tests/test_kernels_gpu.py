@@ -67,6 +67,32 @@ def test_batch_invariance_of_skinny_gemm(nops):
     nops.check()
 
 
+@pytest.mark.parametrize("T", [40, 64])
+def test_packed_rows_equal_single_request_rows(nops, T):
+    """A packed verify of up to 64 rows stays on the weight-streaming GEMM (two 32-token tiles):
+    each request's 16 rows get the bits they get alone, for the plain, residual-add and deferred
+    split-K epilogues, and the normalised rows match too."""
+    K, N = 5120, 5120
+    x, tw = _bf(T, K, seed=16), nops.prepare_weight(_bf(N, K, scale=0.02, seed=17))
+    w = torch.rand(N, device=DEV) + 0.5
+    full = nops.linear(x, tw, out_dtype=torch.float32)
+    base = torch.randn(T, N, device=DEV)
+    r_full = base.clone()
+    nops.linear_residual(x, tw, r_full)
+    r_split = base.clone()
+    S = nops.linear_split(x, tw, r_split)
+    n_split = nops.rms_norm_split(r_split, w, 1e-6, torch.bfloat16, S) if S > 1 else None
+    for o0 in range(0, T - 15, 16):
+        sl = slice(o0, o0 + 16)
+        assert torch.equal(nops.linear(x[sl], tw, out_dtype=torch.float32), full[sl])
+        r_one = base[sl].clone()
+        nops.linear_residual(x[sl], tw, r_one)
+        assert torch.equal(r_one, r_full[sl]) and torch.equal(r_one, r_split[sl])
+        if n_split is not None:
+            assert torch.equal(nops.rms_norm(r_one, w, 1e-6, torch.bfloat16), n_split[sl])
+    nops.check()
+
+
 @pytest.mark.parametrize("T", [1, 16])
 def test_lm_head_argmax(nops, T):
     V, K = 50000, 1024
@@ -316,3 +342,28 @@ def test_cluster_splitk_bits_equal_global_fixup(nops, T, N, K):
     torch.cuda.synchronize()
     assert torch.equal(r1, r2)
     nops.check()
+
+
+@pytest.mark.parametrize("T,N,K", [(16, 5120, 17408), (16, 5120, 6144), (1, 5120, 6144), (3, 384, 17408),
+                                   (32, 1000, 640)])
+def test_deferred_splitk_equals_in_gemm_fixup(nops, T, N, K):
+    """The split GEMM stores its K slices and the next norm adds them in split order, then the
+    residual: the residual and the normalised rows are bit-identical to the GEMM's own fix-up
+    followed by the plain norm, and the weight-less completion leaves the same residual."""
+    x, tw = _bf(T, K, seed=11), nops.prepare_weight(_bf(N, K, scale=0.02, seed=12))
+    w = torch.rand(N, device=DEV) + 0.5
+    base = torch.randn(T, N, device=DEV)
+    r_ref, r_def, r_set = base.clone(), base.clone(), base.clone()
+    nops.linear_residual(x, tw, r_ref)
+    n_ref = nops.rms_norm(r_ref, w, 1e-6, torch.bfloat16)
+    S = nops.linear_split(x, tw, r_def)
+    assert S == nops.C.swap_splits(N, K)
+    n_def = nops.rms_norm_split(r_def, w, 1e-6, torch.bfloat16, S) if S > 1 else nops.rms_norm(r_def, w, 1e-6,
+                                                                                             torch.bfloat16)
+    S2 = nops.linear_split(x, tw, r_set)
+    if S2 > 1:
+        assert nops.rms_norm_split(r_set, None, 1e-6, torch.bfloat16, S2) is None
+    torch.cuda.synchronize()
+    nops.check()
+    assert torch.equal(r_ref, r_def) and torch.equal(r_ref, r_set)
+    assert torch.equal(n_ref, n_def)
