@@ -45,7 +45,8 @@ def parse():
     ap.add_argument("--temperature", type=float, default=0.0,
                     help="> 0: sampled decoding (speculative, exact against the target's own sampler)")
     ap.add_argument("--weights", default="bf16", choices=["bf16", "mxfp8"],
-                    help="mxfp8: target linear weights are their MXFP8 round trip (computed in bf16)")
+                    help="mxfp8: target linear weights are MXFP8 (streamed as e4m3 + E8M0 scales by the "
+                         "verify / decode GEMMs, expanded exactly to bf16 in shared memory)")
     ap.add_argument("--drafter", default="dspark", choices=["dspark", "dflash2"],
                     help="dspark: the headline drafter; dflash2: the windowed drafter (same block rows)")
     ap.add_argument("--seed", type=int, default=0)
@@ -176,11 +177,13 @@ def main():
         topo = check_topology(world, comm=args.comm if args.ops == "native" else "nccl")
     comm = make_comm(world, device=device, hidden=cfg.hidden_size, peer=(args.comm != "nccl" and args.ops == "native"),
                      fused=(args.comm == "fused"), prefill_rows=args.prefill_chunk if args.comm == "fused" else 0)
+    # the library op set reads positions on the host inside attention, which a CUDA graph cannot
+    # capture: it runs eagerly
     rt = RuntimeConfig(max_context=args.ctx + args.new_tokens + 64, prefill_chunk=args.prefill_chunk,
-                       use_cuda_graphs=not args.no_graphs)
+                       use_cuda_graphs=not args.no_graphs and args.ops == "native")
     if args.ops == "native":
         from qwen38_b200.ops.native import NativeOps
-        ops = NativeOps(device=device, max_keys=rt.max_context + 64)
+        ops = NativeOps(device=device, max_keys=rt.max_context + 64, weight_format=args.weights)
     else:
         ops = TorchOps()
     t_load = time.time()
@@ -214,6 +217,9 @@ def main():
     torch.cuda.synchronize()
     t_gold = time.time() - t_gold
     sr = SpecRuntime(tgt, dr, verifier_rows=dcfg.block_rows)
+    # token-exactness against greedy decode rests on batch-invariant kernels; the library op set
+    # (cuBLAS) is not batch-invariant, so its speculative output is not checked against greedy
+    exact = args.ops == "native"
 
     def one(step, timed):
         sr.h2d_bytes = sr.d2h_bytes = 0
@@ -223,7 +229,7 @@ def main():
         w0 = time.perf_counter()
         res = sr.generate(prompt_host, n_out, pinned=PinnedAcceptance(gold, seed=1000 + step,
                                                                      mean_accepted=args.mean_accepted),
-                          gold_check=gold, prompt_host=prompt_host,
+                          gold_check=gold if exact else None, prompt_host=prompt_host,
                           **({"temperature": args.temperature, "seed": args.seed} if args.temperature > 0 else {}))
         torch.cuda.synchronize()
         wall = time.perf_counter() - w0
@@ -273,6 +279,8 @@ def main():
                        "drafter": args.drafter, "drafter_layers": dcfg.num_hidden_layers, "weights": args.weights, "temperature": args.temperature,
                        "parallelism": f"tp{world}",
                        "ops": args.ops, "comm": args.comm if world > 1 else None,
+                       "cuda_graphs": tgt.use_graphs, "gold_checked": exact,
+                       "deferred_splitk": bool(getattr(tgt, "defer_splits", False)) and world == 1,
                        "nvlinks": (topo or {}).get("nvlink_active_links"),
                        "nvls_push": bool(getattr(comm, "recv_mc", 0)),
                        "prefill_allreduce": "fused (reduce-scatter GEMM + multicast broadcast)"

@@ -18,7 +18,10 @@ void q38_rms_norm_wait(torch::Tensor x, torch::Tensor w, double eps, torch::Tens
                        int64_t target, torch::Tensor err);
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
-                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr);
+                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr,
+                     c10::optional<torch::Tensor> mx_scales);
+void q38_linear_mx(torch::Tensor x, torch::Tensor wq, torch::Tensor wsc, int64_t N, torch::Tensor out, int64_t epi,
+                   torch::Tensor ws, torch::Tensor counters, torch::Tensor err);
 void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps, c10::optional<torch::Tensor> out,
                      int64_t recv_local, torch::Tensor epochs, int64_t slot, int64_t world, int64_t block_words,
                      torch::Tensor err);
@@ -64,7 +67,8 @@ void q38_rms_norm_split(torch::Tensor x, torch::Tensor parts, int64_t S, c10::op
                         c10::optional<torch::Tensor> out);
 int64_t q38_swap_splits(int64_t N, int64_t K);
 int64_t q38_linear_split(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor parts,
-                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err);
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err,
+                         c10::optional<torch::Tensor> mx_scales);
 void q38_embedding(torch::Tensor ids, torch::Tensor table, torch::Tensor out);
 void q38_markov_step(torch::Tensor logits_row, torch::Tensor pred, torch::Tensor succ, torch::Tensor prev,
                      torch::Tensor out, c10::optional<torch::Tensor> out_val, torch::Tensor part_val,
@@ -108,6 +112,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rms_norm_split", &q38_rms_norm_split);
   m.def("swap_splits", &q38_swap_splits);
   m.def("linear_split", &q38_linear_split);
+  m.def("linear_mx", &q38_linear_mx);
   m.def("embedding", &q38_embedding);
   m.def("markov_step", &q38_markov_step);
   m.def("markov_select", &q38_markov_select);

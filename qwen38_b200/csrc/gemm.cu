@@ -144,15 +144,32 @@ static bool splitk_cluster() {
   return v == 1;
 }
 
+// MX weight: e4m3 bytes tiled like a bf16 weight ([tiles * 128, 64] uint8) and E8M0 scales
+// ([tiles * 128, 2] uint8), see mx_tile_weight in qwen38_b200/ops/native.py.
+struct MxW {
+  const uint8_t* q;
+  const uint8_t* s;
+};
+
+static MxW mx_of(const torch::Tensor& wq, const torch::Tensor& wsc) {
+  TORCH_CHECK(wq.scalar_type() == at::kByte && wsc.scalar_type() == at::kByte && wq.is_contiguous() &&
+                  wsc.is_contiguous() && wq.is_cuda() && wsc.is_cuda(), "MX weight: contiguous uint8 values and scales");
+  TORCH_CHECK(wsc.numel() * 32 == wq.numel(), "MX weight: one scale per 32 values");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(wq.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(wsc.data_ptr()) % 16 == 0,
+              "MX weight: 16-byte aligned storage");
+  return MxW{reinterpret_cast<const uint8_t*>(wq.data_ptr()), reinterpret_cast<const uint8_t*>(wsc.data_ptr())};
+}
+
 // out (m, n) layout: swap -> out[n * ldo + m]; prefill -> out[m * ldo + n]
 // `w` is a tile-contiguous weight ([ceil(N/128) * ceil(K/64) * 128, 64], see tile_weight in
 // qwen38_b200/ops/native.py) of logical shape [N, K].
 void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch::Tensor& out, int epi,
                    const Scratch& sc, float* amax_val = nullptr, int* amax_idx = nullptr, int* amax_tiles = nullptr,
                    const ArArgs* ar = nullptr, unsigned long long* trace = nullptr, int64_t ldo_override = -1,
-                   const SampleArgs* samp = nullptr, const RsArgs* rs = nullptr) {
+                   const SampleArgs* samp = nullptr, const RsArgs* rs = nullptr, const MxW* mx = nullptr) {
   TORCH_CHECK(x.is_cuda() && w.is_cuda() && out.is_cuda(), "CUDA tensors required");
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "bf16 operands required");
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == (mx ? at::kByte : at::kBFloat16),
+              "bf16 activations and bf16 (or MX e4m3) weights required");
   TORCH_CHECK(x.dim() == 2 && x.stride(1) == 1, "x [T, K] K-contiguous required");
   const int T = (int)x.size(0), K = (int)x.size(1);
   TORCH_CHECK(w.dim() == 2 && w.size(1) == BK && w.is_contiguous(), "tile-contiguous weight [rows, 64] required");
@@ -168,6 +185,8 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
   g.counters = sc.counters;
   g.trace = trace;
   TORCH_CHECK(epi != EPI_RS_F32 || (T > 32 && rs != nullptr), "the reduce-scatter epilogue serves prefill tiles");
+  TORCH_CHECK(mx == nullptr || (T <= SWAP_MAX_ROWS && epi != EPI_ARGMAX && epi != EPI_RS_F32),
+              "MX weights stream through the swap-mode GEMM (<= 64 rows)");
   if (T <= SWAP_MAX_ROWS) {
     // swap-AB streaming: M = weight rows, N = tokens in 32-token tiles (grid y).  Each token
     // column's result depends on its own column and the split plan (a function of N, K and the SM
@@ -185,7 +204,7 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
     // reduces through DSMEM inside a cluster of the tile's splits (same bits).  Measured on B200
     // the cluster form was slower: clusters of up to 8 CTAs at two CTAs per SM no longer fit the
     // grid into one wave once GPC boundaries are respected.  ARGMAX always uses the global form.
-    g.cluster_k = epi != EPI_ARGMAX && epi != EPI_SPLIT_F32 && n_tiles == 1 && splitk_cluster();
+    g.cluster_k = epi != EPI_ARGMAX && epi != EPI_SPLIT_F32 && n_tiles == 1 && mx == nullptr && splitk_cluster();
     if (splits > 1 && !g.cluster_k && epi != EPI_SPLIT_F32) {
       TORCH_CHECK((int64_t)m_tiles * n_tiles * splits * BM * 32 <= sc.ws_floats, "split-K workspace too small");
       TORCH_CHECK(m_tiles * n_tiles <= sc.n_counters, "split-K counter array too small");
@@ -204,10 +223,16 @@ void gemm_dispatch(const torch::Tensor& x, const torch::Tensor& w, int N, torch:
       g.amax_idx = amax_idx;
       *amax_tiles = m_tiles;
     }
-    CUtensorMap ma = cached_map(w, BM, true);      // one 16 KB weight tile per box
     CUtensorMap mb = cached_map(x, 32, false);
     dim3 grid(m_tiles, n_tiles, splits);
-    launch_swap(epi, ma, mb, g, grid, st);
+    if (mx) {
+      g.mxq = mx->q;
+      g.mxs = mx->s;
+      launch_swap_mx(epi, mb, g, grid, st);
+    } else {
+      CUtensorMap ma = cached_map(w, BM, true);    // one 16 KB weight tile per box
+      launch_swap(epi, ma, mb, g, grid, st);
+    }
   } else {
     TORCH_CHECK(epi != EPI_ARGMAX && epi != EPI_PUSH_F32, "argmax / pushed all-reduce epilogues serve <= 64 rows");
     g.M = T;
@@ -245,13 +270,30 @@ void q38_linear(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, 
   q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc);
 }
 
+// q38_linear with an MX weight (wq e4m3 bytes, wsc E8M0 scales; <= 64 rows, not argmax).
+void q38_linear_mx(torch::Tensor x, torch::Tensor wq, torch::Tensor wsc, int64_t N, torch::Tensor out, int64_t epi,
+                   torch::Tensor ws, torch::Tensor counters, torch::Tensor err) {
+  c10::cuda::CUDAGuard guard(x.device());
+  auto sc = q38::scratch_of(ws, counters, err);
+  const q38::MxW mx = q38::mx_of(wq, wsc);
+  if (epi == q38::EPI_BF16 || epi == q38::EPI_SWIGLU) {
+    TORCH_CHECK(out.scalar_type() == at::kBFloat16, "bf16 output required");
+  } else {
+    TORCH_CHECK(out.scalar_type() == at::kFloat, "fp32 output required");
+  }
+  TORCH_CHECK(out.stride(1) == 1, "row-contiguous output required");
+  q38::gemm_dispatch(x, wq, (int)N, out, (int)epi, sc, nullptr, nullptr, nullptr, nullptr, nullptr, -1, nullptr,
+                     nullptr, &mx);
+}
+
 // Row-parallel out-projection whose epilogue pushes this rank's fp32 partial [T, N] (T <= 64)
 // into every rank's receive block of `slot` as {value, epoch} words (EPI_PUSH_F32); the reduction
 // into the residual happens in q38_rms_norm_ar.  recv_ptrs: every rank's receive area mapped into
 // this process; epochs: this rank's [slots][32] per-row epochs.
 void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws, torch::Tensor counters,
                      torch::Tensor err, std::vector<int64_t> recv_ptrs, int64_t rank, int64_t slot,
-                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr) {
+                     int64_t block_words, torch::Tensor epochs, int64_t mc_ptr,
+                     c10::optional<torch::Tensor> mx_scales) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(x.size(0) <= q38::AR_MAX_ROWS, "the pushed all-reduce serves <= 64 rows");
   TORCH_CHECK(x.size(0) * N <= block_words, "partial larger than a receive block");
@@ -271,7 +313,10 @@ void q38_linear_push(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor 
   auto sc = q38::scratch_of(ws, counters, err);
   // no local output tensor: the epilogue writes the receive blocks, laid out [T, N] (ldo = N)
   torch::Tensor unused = x;
-  q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_PUSH_F32, sc, nullptr, nullptr, nullptr, &a, nullptr, N);
+  q38::MxW mx{};
+  if (mx_scales) mx = q38::mx_of(w, *mx_scales);
+  q38::gemm_dispatch(x, w, (int)N, unused, q38::EPI_PUSH_F32, sc, nullptr, nullptr, nullptr, &a, nullptr, N, nullptr,
+                     nullptr, mx_scales ? &mx : nullptr);
 }
 
 // Split-K slices of the swap-AB plan for an [N, K] weight (the count q38_linear would use).
@@ -289,21 +334,30 @@ int64_t q38_swap_splits(int64_t N, int64_t K) {
 // residual gets the same bits one launch later without the fix-up's serial tail.  With one slice
 // the GEMM adds into `residual` directly.  Returns S (1: nothing pending).
 int64_t q38_linear_split(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor residual, torch::Tensor parts,
-                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err) {
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err,
+                         c10::optional<torch::Tensor> mx_scales) {
   c10::cuda::CUDAGuard guard(x.device());
   const int64_t T = x.size(0);
   TORCH_CHECK(T >= 1 && T <= q38::SWAP_MAX_ROWS, "deferred split-K serves 1..64 rows");
   TORCH_CHECK(residual.scalar_type() == at::kFloat && residual.is_contiguous() && residual.size(0) == T &&
                   residual.size(1) == N, "fp32 residual [T, N]");
   auto sc = q38::scratch_of(ws, counters, err);
+  q38::MxW mxw{};
+  const q38::MxW* mx = nullptr;
+  if (mx_scales) {
+    mxw = q38::mx_of(w, *mx_scales);
+    mx = &mxw;
+  }
   const int64_t S = q38_swap_splits(N, x.size(1));
   if (S == 1) {
-    q38::gemm_dispatch(x, w, (int)N, residual, q38::EPI_ADD_F32, sc);
+    q38::gemm_dispatch(x, w, (int)N, residual, q38::EPI_ADD_F32, sc, nullptr, nullptr, nullptr, nullptr, nullptr, -1,
+                       nullptr, nullptr, mx);
     return 1;
   }
   TORCH_CHECK(parts.scalar_type() == at::kFloat && parts.is_contiguous() && parts.numel() >= S * T * N,
               "split partial buffer too small");
-  q38::gemm_dispatch(x, w, (int)N, parts, q38::EPI_SPLIT_F32, sc, nullptr, nullptr, nullptr, nullptr, nullptr, N);
+  q38::gemm_dispatch(x, w, (int)N, parts, q38::EPI_SPLIT_F32, sc, nullptr, nullptr, nullptr, nullptr, nullptr, N,
+                     nullptr, nullptr, mx);
   return S;
 }
 

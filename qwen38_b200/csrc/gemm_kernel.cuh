@@ -108,6 +108,9 @@ struct GemmArgs {
   int cluster_k;              // swap mode, splits > 1: the splits of a tile form one cluster and
                               // reduce through DSMEM (the launch sets cluster dims (1, 1, splits));
                               // 0: partials through `ws` and the last-arriving CTA (`counters`)
+  const uint8_t* mxq;         // MX weights (swap mode): e4m3 bytes, tile (t, kb) = [128 rows][64] at
+                              // ((t * kblocks + kb) * 8192)
+  const uint8_t* mxs;         // their E8M0 scales, tile (t, kb) = [128 rows][2] at ((t * kblocks + kb) * 256)
 };
 
 // trace points: 0 entry, 1 setup done, 2 first stage landed, 3 last MMA issued, 4 accumulator
@@ -124,9 +127,63 @@ struct Smem {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int BAR_OFF = STAGES * STAGE_BYTES;
+  static constexpr int NST = STAGES;                // operand ring slots
+  static constexpr int RS = 0;                      // MX load ring slots (none)
+  static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
+  static constexpr int BAR_OFF = RING_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 2) * 8 + 16 + 1024;  // + alignment slack
 };
+
+// MX (block-scaled e4m3 weight) swap-mode layout.  A load ring of RS slots {activation tile (the
+// MMA's B operand, written swizzled by TMA), 8 KB of e4m3 weight bytes, 256 B of E8M0 scales} that
+// one barrier covers, and an operand ring of NST bf16 weight tiles in the 128-byte-swizzled K-major
+// layout the MMA reads, written by two converter warps.  A load slot is free once the converters
+// and the MMA are both done with it; the producer never waits for a conversion, so RS stages of
+// weight bytes stay in flight.  The whole region is also the split-K fix-up's staging area.
+struct SmemMx {
+  static constexpr int A_BYTES = BM * BK * 2;       // one bf16 weight tile (operand ring slot)
+  static constexpr int B_BYTES = 32 * BK * 2;       // one activation tile
+  static constexpr int RAW_Q = BM * BK;             // e4m3 bytes of one weight tile
+  static constexpr int RAW_S = BM * (BK / 32);      // its scales
+  static constexpr int RSLOT = 13 * 1024;           // B | q | scales, 1024-aligned slots
+  static constexpr int NST = 3;
+  static constexpr int RS = 4;
+  static constexpr int STAGE_BYTES = A_BYTES;
+  static constexpr int R_OFF = NST * A_BYTES;
+  static constexpr int RING_BYTES = R_OFF + RS * RSLOT;
+  static constexpr int BAR_OFF = RING_BYTES;
+  static constexpr int TOTAL = BAR_OFF + (2 * NST + 2 * RS + 2) * 8 + 16 + 1024;
+  static_assert(B_BYTES + RAW_Q + RAW_S <= RSLOT, "load slot too small");
+};
+
+// Four e4m3 bytes -> four bf16 values times 2^-120 (two bf16x2 words), exact for every finite e4m3
+// including subnormals: the e4m3 sign moves to bit 15 and its 7 exponent+mantissa bits to bits
+// 10..4, so the bf16 exponent field equals the e4m3 one and the bf16 bias (127) is 120 above the
+// e4m3 bias (7).  The multiply by a power of two m2 (bf16x2) restores the block scale.
+__device__ __forceinline__ void e4m3x4_to_bf16x4_scaled(uint32_t w, uint32_t m2, uint32_t& lo, uint32_t& hi) {
+  const uint32_t t0 = __byte_perm(w, 0u, 0x1404u);  // [0, b0, 0, b1]
+  const uint32_t t1 = __byte_perm(w, 0u, 0x3424u);  // [0, b2, 0, b3]
+  const uint32_t f0 = (t0 & 0x80008000u) | ((t0 >> 4) & 0x07F007F0u);
+  const uint32_t f1 = (t1 & 0x80008000u) | ((t1 >> 4) & 0x07F007F0u);
+  // exact products (a power-of-two factor, no rounding; bf16 arithmetic keeps subnormal inputs)
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(lo) : "r"(f0), "r"(m2));
+  asm("mul.rn.bf16x2 %0, %1, %2;" : "=r"(hi) : "r"(f1), "r"(m2));
+}
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+// AND of `pred` over the `n` threads of named barrier `id` (every one of them calls it).
+__device__ __forceinline__ bool named_bar_and(int id, int n, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(n)
+      : "memory");
+  return r != 0;
+}
 
 // Swap-mode split-K through distributed shared memory.  The `splits` CTAs of one weight tile are
 // one thread-block cluster (cluster rank = split).  Each CTA parks its fp32 accumulator tile
@@ -222,15 +279,19 @@ __device__ __forceinline__ void swap_cluster_epilogue(const GemmArgs& g, float* 
   cluster.sync();
 }
 
-template <int BN, int STAGES, int EPI, bool SWAP>
+template <int BN, int STAGES, int EPI, bool SWAP, bool MX = false>
 __global__ void __launch_bounds__(128, 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs g) {
-  using S = Smem<BN, STAGES>;
+  static_assert(!MX || (SWAP && BN == 32), "MX weights stream through the swap-mode kernel");
+  using S = typename std::conditional<MX, SmemMx, Smem<BN, STAGES>>::type;
+  constexpr int NST = S::NST;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
-  uint64_t* empty_bar = full_bar + STAGES;
-  uint64_t* acc_bar = empty_bar + STAGES;
+  uint64_t* empty_bar = full_bar + NST;
+  uint64_t* rfull_bar = empty_bar + NST;         // MX load ring: activation, weight bytes, scales landed
+  uint64_t* rempty_bar = rfull_bar + S::RS;      // MX load ring: converted and consumed by the MMA
+  uint64_t* acc_bar = rempty_bar + S::RS;
   uint64_t* fix_bar = acc_bar + 1;                // split-K fix-up: staged partials landed
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_bar + 2);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
@@ -246,11 +307,15 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   constexpr int TMEM_COLS = BN < 32 ? 32 : BN;
 
   if (tid == 0) {
-    tma_prefetch_desc(&map_a);
+    if constexpr (!MX) tma_prefetch_desc(&map_a);
     tma_prefetch_desc(&map_b);
-    for (int s = 0; s < STAGES; ++s) {
-      mbar_init(&full_bar[s], 1);
+    for (int s = 0; s < NST; ++s) {
+      mbar_init(&full_bar[s], 1);                // MX: the converters' arrival
       mbar_init(&empty_bar[s], 1);
+    }
+    for (int s = 0; s < S::RS; ++s) {
+      mbar_init(&rfull_bar[s], 1);
+      mbar_init(&rempty_bar[s], 2);              // the converters and the MMA's commit
     }
     mbar_init(acc_bar, 1);
     *abort_flag = 0;
@@ -294,33 +359,106 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       if constexpr (SWAP) tma_load_2d_hint(sa + S::A_BYTES, &map_b, &full_bar[stage], kb * BK, n0, pol_x);
       else tma_load_2d_hint(sa, &map_a, &full_bar[stage], kb * BK, m0, pol_x);
     };
-    const int pre = nk < STAGES ? nk : STAGES;
-    for (int i = 0; i < pre; ++i) {
-      mbar_expect_tx(&full_bar[i], S::STAGE_BYTES);
-      load_w(i, kb0 + i);
-    }
-    pdl_wait();
-    for (int i = 0; i < pre; ++i) load_x(i, kb0 + i);
-    for (int i = pre; i < nk; ++i) {
-      const int s = i % STAGES;
-      if (!mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
-      mbar_expect_tx(&full_bar[s], S::STAGE_BYTES);
-      load_w(s, kb0 + i);
-      load_x(s, kb0 + i);
+    if constexpr (!MX) {
+      const int pre = nk < STAGES ? nk : STAGES;
+      for (int i = 0; i < pre; ++i) {
+        mbar_expect_tx(&full_bar[i], S::STAGE_BYTES);
+        load_w(i, kb0 + i);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_x(i, kb0 + i);
+      for (int i = pre; i < nk; ++i) {
+        const int s = i % STAGES;
+        if (!mbar_wait(&empty_bar[s], ((i / STAGES) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
+        mbar_expect_tx(&full_bar[s], S::STAGE_BYTES);
+        load_w(s, kb0 + i);
+        load_x(s, kb0 + i);
+      }
+    } else {
+      // MX: K block kb0 + i goes to load slot i % RS: its e4m3 tile and scales by two bulk copies
+      // (static: the first RS are requested before the PDL wait) and its activation tile by TMA.
+      const uint8_t* wq = g.mxq + (size_t)m_tile * g.kblocks * S::RAW_Q;
+      const uint8_t* wsc = g.mxs + (size_t)m_tile * g.kblocks * S::RAW_S;
+      auto load_q = [&](int i) {
+        const int r = i % S::RS;
+        uint8_t* slot = smem + S::R_OFF + r * S::RSLOT;
+        mbar_expect_tx(&rfull_bar[r], S::B_BYTES + S::RAW_Q + S::RAW_S);
+        bulk_load_hint(slot + S::B_BYTES, wq + (size_t)(kb0 + i) * S::RAW_Q, S::RAW_Q, &rfull_bar[r], pol_w);
+        bulk_load_hint(slot + S::B_BYTES + S::RAW_Q, wsc + (size_t)(kb0 + i) * S::RAW_S, S::RAW_S, &rfull_bar[r],
+                       pol_w);
+      };
+      auto load_act = [&](int i) {
+        const int r = i % S::RS;
+        tma_load_2d_hint(smem + S::R_OFF + r * S::RSLOT, &map_b, &rfull_bar[r], (kb0 + i) * BK, n0, pol_x);
+      };
+      const int pre = nk < S::RS ? nk : S::RS;
+      for (int i = 0; i < pre; ++i) load_q(i);
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) load_act(i);
+      for (int i = pre; i < nk; ++i) {
+        if (!mbar_wait(&rempty_bar[i % S::RS], ((i / S::RS) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
+        load_q(i);
+        load_act(i);
+      }
     }
   } else {
+    if constexpr (MX) {
+      if (warp >= 2) {
+        // ---------------- MX converters (warps 2-3): e4m3 x 2^(scale - 127) -> bf16, written into
+        // the operand slot in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
+        // c ^ (r % 8)).  Every value is exact (an e4m3 value times a power of two fits bf16), so the
+        // MMA sees exactly the dequantised weight.  The weight is static: conversion starts before
+        // the PDL wait.
+        const int ct = tid - 64;
+        for (int i = 0; i < nk; ++i) {
+          const int r = i % S::RS, s = i % NST;
+          bool ok = mbar_wait(&rfull_bar[r], (i / S::RS) & 1, g.err, kErrTmaWait, abort_flag);
+          if (ok && i >= NST) ok = mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, g.err, kErrTmaWait, abort_flag);
+          if (!named_bar_and(1, 64, ok)) break;      // all converter threads leave together
+          const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
+          uint8_t* a_tile = smem + s * S::A_BYTES;
+#pragma unroll
+          for (int q = 0; q < (BM * BK) / (16 * 64); ++q) {
+            const int chunk = ct + 64 * q;            // 16-byte chunk of the raw tile: row, quarter
+            const int row = chunk >> 2, c16 = chunk & 3;
+            const uint4 v = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
+            const uint32_t e = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
+            const uint32_t m = (e + 120u) << 7;        // bf16 2^(e - 127 + 120)
+            const uint32_t m2 = m | (m << 16);
+            uint32_t o[8];
+            e4m3x4_to_bf16x4_scaled(v.x, m2, o[0], o[1]);
+            e4m3x4_to_bf16x4_scaled(v.y, m2, o[2], o[3]);
+            e4m3x4_to_bf16x4_scaled(v.z, m2, o[4], o[5]);
+            e4m3x4_to_bf16x4_scaled(v.w, m2, o[6], o[7]);
+            uint8_t* rowp = a_tile + row * 128;
+            const int sw = row & 7;
+            *reinterpret_cast<uint4*>(rowp + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+            *reinterpret_cast<uint4*>(rowp + (((2 * c16 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
+          }
+          asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
+          named_bar_sync(1, 64);
+          if (ct == 0) {
+            mbar_arrive(&full_bar[s]);
+            mbar_arrive(&rempty_bar[r]);
+          }
+        }
+      }
+    }
     pdl_wait();     // nothing upstream is read or written before this point
   }
   if (tid == 32) {
     // ---------------- MMA issuer (single thread)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
     for (int i = 0; i < nk; ++i) {
-      const int s = i % STAGES;
-      if (!mbar_wait(&full_bar[s], (i / STAGES) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      const int s = i % NST;
+      if (!mbar_wait(&full_bar[s], (i / NST) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      if constexpr (MX) {            // the activation tile of this K block (landed before the conversion)
+        if (!mbar_wait(&rfull_bar[i % S::RS], (i / S::RS) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      }
       if (i == 0) Q38_STAMP(2);
       tc_fence_after();
       const uint32_t sa = smem_u32(smem + s * S::STAGE_BYTES);
-      const uint32_t sb = sa + S::A_BYTES;
+      const uint32_t sb = MX ? smem_u32(smem + S::R_OFF + (i % S::RS) * S::RSLOT) : sa + S::A_BYTES;
       const uint64_t da = smem_desc_sw128(sa), db = smem_desc_sw128(sb);
 #pragma unroll
       for (int k = 0; k < BK / 16; ++k) {
@@ -328,6 +466,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         umma_bf16(tmem, da + (uint64_t)(2 * k), db + (uint64_t)(2 * k), idesc, (i > 0 || k > 0) ? 1u : 0u);
       }
       umma_commit(&empty_bar[s]);
+      if constexpr (MX) umma_commit(&rempty_bar[i % S::RS]);
     }
     Q38_STAMP(3);
     umma_commit(acc_bar);
@@ -345,7 +484,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   const uint32_t trow = tmem + ((uint32_t)(warp * 32) << 16);
 
   bool clustered = false;
-  if constexpr (SWAP && EPI != EPI_ARGMAX && EPI != EPI_SPLIT_F32) {
+  if constexpr (SWAP && !MX && EPI != EPI_ARGMAX && EPI != EPI_SPLIT_F32) {
     clustered = g.splits > 1 && g.cluster_k;
     if (clustered)
       swap_cluster_epilogue<EPI>(g, reinterpret_cast<float*>(smem), trow, ok && nk > 0, m_tile, split, row);
@@ -384,7 +523,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           // issued before the wait.  The partials were written by other CTAs' generic stores and
           // published by the counter; the proxy fence orders the bulk (async-proxy) reads after.
           constexpr int PART = BM * BN;                                  // floats per partial
-          constexpr int RING_PARTS = (STAGES * S::STAGE_BYTES) / (PART * 4);
+          constexpr int RING_PARTS = S::RING_BYTES / (PART * 4);
           const float* base = g.ws + (size_t)tile * g.splits * PART;
           float* stage = reinterpret_cast<float*>(smem);
           asm volatile("fence.proxy.async.global;" ::: "memory");
@@ -645,13 +784,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (tid == 0) Q38_STAMP(7);
 }
 
-template <int BN, int STAGES, int EPI, bool SWAP>
+template <int BN, int STAGES, int EPI, bool SWAP, bool MX = false>
 void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st) {
-  auto kern = gemm_tn_kernel<BN, STAGES, EPI, SWAP>;
-  constexpr int smem = Smem<BN, STAGES>::TOTAL;
-  const cudaError_t attr = set_smem_once<gemm_tn_kernel<BN, STAGES, EPI, SWAP>>(smem);
+  auto kern = gemm_tn_kernel<BN, STAGES, EPI, SWAP, MX>;
+  constexpr int smem = std::conditional<MX, SmemMx, Smem<BN, STAGES>>::type::TOTAL;
+  const cudaError_t attr = set_smem_once<gemm_tn_kernel<BN, STAGES, EPI, SWAP, MX>>(smem);
   TORCH_CHECK(attr == cudaSuccess, "cudaFuncSetAttribute failed");
-  const unsigned cz = (SWAP && g.cluster_k && g.splits > 1) ? (unsigned)g.splits : 1u;
+  const unsigned cz = (SWAP && !MX && g.cluster_k && g.splits > 1) ? (unsigned)g.splits : 1u;
   TORCH_CHECK(launch_pdl_cluster(kern, grid, dim3(128), (size_t)smem, st, dim3(1, 1, cz), ma, mb, g) == cudaSuccess,
               "GEMM launch failed");
 }
@@ -667,6 +806,8 @@ int pick_splits(int m_tiles, int kblocks, int sms);
 
 // epilogue-dispatched launchers, one translation unit each
 void launch_swap(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st);
+// MX-weight swap GEMM (g.mxq / g.mxs set; mb: the activation map)
+void launch_swap_mx(int epi, const CUtensorMap& mb, const GemmArgs& g, dim3 grid, cudaStream_t st);
 void launch_prefill(int epi, const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g, dim3 grid,
                     cudaStream_t st);
 

@@ -47,6 +47,43 @@ def tile_weight(w: torch.Tensor) -> TiledWeight:
     return TiledWeight(t, N, K)
 
 
+class MXWeight:
+    """An MXFP8 GEMM weight of logical shape [N, K] (e4m3 values, one E8M0 scale per 32 elements of
+    a row) for the weight-streaming GEMM, stored like a TiledWeight: tile (n // 128, k // 64) is one
+    contiguous 8 KB block of e4m3 bytes ``q`` and one 256-byte block of scales ``s`` ([128 rows][2]).
+    ``t`` is the exact bf16 expansion in TiledWeight layout, read by the prefill-tile GEMMs (which
+    are compute-bound and take bf16 operands); the <= 64-row GEMMs stream ``q`` and ``s``."""
+    __slots__ = ("q", "s", "t", "N", "K")
+
+    def __init__(self, q, s, t, N, K):
+        self.q, self.s, self.t, self.N, self.K = q, s, t, N, K
+
+    @property
+    def shape(self):
+        return (self.N, self.K)
+
+
+def mx_tile_weight(w: torch.Tensor, bf16: TiledWeight | None = None):
+    """MXWeight of ``w`` when its values are exactly an MXFP8 tensor with the OCP scale choice
+    (so storing it as MXFP8 loses nothing), else None.  Scales above 2^7 are refused (the kernel's
+    bf16 rescale factor 2^(scale + 120) must stay a normal bf16)."""
+    from ..checkpoint import dequant_mxfp8, quant_mxfp8
+    N, K = w.shape
+    wf = w.float()
+    q, se = quant_mxfp8(wf)
+    if int(se.max()) > 134 or not torch.equal(dequant_mxfp8(q, se), wf):
+        return None
+    NT, KB = -(-N // 128), -(-K // 64)
+    qb = torch.zeros(NT * 128, KB * 64, dtype=torch.uint8, device=w.device)
+    qb[:N, :K] = q.view(torch.uint8)
+    sb = torch.zeros(NT * 128, KB * 2, dtype=torch.uint8, device=w.device)
+    sb[:N, :se.shape[1]] = se
+    qt = qb.reshape(NT, 128, KB, 64).permute(0, 2, 1, 3).contiguous().view(NT * KB * 128, 64)
+    st = sb.reshape(NT, 128, KB, 2).permute(0, 2, 1, 3).contiguous().view(NT * KB * 128, 2)
+    t = (bf16 or tile_weight(w.to(torch.bfloat16).contiguous())).t
+    return MXWeight(qt, st, t, N, K)
+
+
 def untile_weight(tw: TiledWeight) -> torch.Tensor:
     NT, KB = -(-tw.N // 128), -(-tw.K // 64)
     return tw.t.view(NT, KB, 128, 64).permute(0, 2, 1, 3).reshape(NT * 128, KB * 64)[:tw.N, :tw.K]
@@ -62,7 +99,12 @@ class NativeOps(TorchOps):
     # serve (csrc SWAP_MAX_ROWS / AR_MAX_ROWS): a packed verify of up to 4 x 16 rows stays on them
     max_pack_rows = 64
 
-    def __init__(self, device=None, max_keys: int = 1 << 17, ws_mb: int = 64):
+    def __init__(self, device=None, max_keys: int = 1 << 17, ws_mb: int = 64, weight_format: str = "bf16"):
+        if weight_format not in ("bf16", "mxfp8"):
+            raise ValueError("weight_format must be bf16 or mxfp8")
+        # mxfp8: every GEMM weight whose values are exactly MXFP8 is kept as MXFP8 and streamed at
+        # one byte per element by the <= 64-row GEMMs
+        self.weight_format = weight_format
         self.C = load()
         if not torch.cuda.is_available():
             raise RuntimeError("NativeOps needs a CUDA device")
@@ -94,7 +136,18 @@ class NativeOps(TorchOps):
 
     # ------------------------------------------------------------------ GEMMs
     def prepare_weight(self, w):
-        return w if isinstance(w, TiledWeight) else tile_weight(w.to(torch.bfloat16).contiguous())
+        if isinstance(w, (TiledWeight, MXWeight)):
+            return w
+        if self.weight_format == "mxfp8" and w.dim() == 2:
+            mw = mx_tile_weight(w)
+            if mw is not None:
+                return mw
+        return tile_weight(w.to(torch.bfloat16).contiguous())
+
+    @staticmethod
+    def _mx(w, T):
+        """True when this GEMM streams the MX bytes of ``w`` (an MXWeight, <= 64 rows)."""
+        return isinstance(w, MXWeight) and T <= NativeOps.max_pack_rows
 
     def linear(self, x, w, out_dtype=None, out=None):
         w = self.prepare_weight(w)
@@ -103,11 +156,15 @@ class NativeOps(TorchOps):
         if out_dtype == torch.float32 or (out is not None and out.dtype == torch.float32):
             if out is None:
                 out = torch.empty(T, N, dtype=torch.float32, device=x.device)
-            self.C.linear(x, w.t, N, out, EPI_F32, self.ws, self.counters, self.err)
+            epi = EPI_F32
         else:
             if out is None:
                 out = torch.empty(T, N, dtype=torch.bfloat16, device=x.device)
-            self.C.linear(x, w.t, N, out, EPI_BF16, self.ws, self.counters, self.err)
+            epi = EPI_BF16
+        if self._mx(w, T):
+            self.C.linear_mx(x, w.q, w.s, N, out, epi, self.ws, self.counters, self.err)
+        else:
+            self.C.linear(x, w.t, N, out, epi, self.ws, self.counters, self.err)
         self.launches += 1
         return out
 
@@ -117,8 +174,10 @@ class NativeOps(TorchOps):
         words; returns the slot for ``rms_norm_ar``."""
         w = self.prepare_weight(w)
         slot = comm.fused_slot()
-        self.C.linear_push(x.contiguous(), w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs, comm.rank,
-                           slot, comm.block_words, comm.fepochs, int(getattr(comm, "recv_mc", 0) or 0))
+        mx = self._mx(w, x.shape[0])
+        self.C.linear_push(x.contiguous(), w.q if mx else w.t, w.N, self.ws, self.counters, self.err, comm.recv_ptrs,
+                           comm.rank, slot, comm.block_words, comm.fepochs, int(getattr(comm, "recv_mc", 0) or 0),
+                           w.s if mx else None)
         self.launches += 1
         return slot
 
@@ -133,7 +192,10 @@ class NativeOps(TorchOps):
 
     def linear_residual(self, x, w, residual):
         w = self.prepare_weight(w)
-        self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
+        if self._mx(w, x.shape[0]):
+            self.C.linear_mx(x.contiguous(), w.q, w.s, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
+        else:
+            self.C.linear(x.contiguous(), w.t, w.N, residual, EPI_ADD_F32, self.ws, self.counters, self.err)
         self.launches += 1
         return residual
 
@@ -149,8 +211,9 @@ class NativeOps(TorchOps):
             if torch.cuda.is_current_stream_capturing():
                 raise RuntimeError("linear_split: slice buffer must be sized before graph capture")
             self._split_parts = torch.empty(need, dtype=torch.float32, device=self.device)
-        S = int(self.C.linear_split(x.contiguous(), w.t, w.N, residual, self._split_parts, self.ws, self.counters,
-                                    self.err))
+        mx = self._mx(w, T)
+        S = int(self.C.linear_split(x.contiguous(), w.q if mx else w.t, w.N, residual, self._split_parts, self.ws,
+                                    self.counters, self.err, w.s if mx else None))
         self.launches += 1
         return S
 
@@ -168,7 +231,10 @@ class NativeOps(TorchOps):
         w_gu = self.prepare_weight(w_gu)
         x = x.contiguous()
         out = torch.empty(x.shape[0], w_gu.N // 2, dtype=torch.bfloat16, device=x.device)
-        self.C.linear(x, w_gu.t, w_gu.N, out, EPI_SWIGLU, self.ws, self.counters, self.err)
+        if self._mx(w_gu, x.shape[0]):
+            self.C.linear_mx(x, w_gu.q, w_gu.s, w_gu.N, out, EPI_SWIGLU, self.ws, self.counters, self.err)
+        else:
+            self.C.linear(x, w_gu.t, w_gu.N, out, EPI_SWIGLU, self.ws, self.counters, self.err)
         self.launches += 1
         return out
 

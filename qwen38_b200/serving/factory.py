@@ -71,7 +71,7 @@ def build_engine(rc: RunConfig, *, device=None, seed: int = 0, comm=None):
     ops = None
     if native:
         from ..ops.native import NativeOps
-        ops = NativeOps(device=device, max_keys=rc.runtime.max_context + 64)
+        ops = NativeOps(device=device, max_keys=rc.runtime.max_context + 64, weight_format=rc.runtime.weight_format)
     if comm is None and rc.parallel.tp > 1:
         from ..parallel.comm import make_comm
         from ..parallel.topology import check_topology

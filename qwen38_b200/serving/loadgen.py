@@ -117,7 +117,7 @@ def main():
     max_ctx = a.prompt_len + a.new_tokens + 64
     if cuda:
         from ..ops.native import NativeOps
-        ops = NativeOps(device=dev, max_keys=max_ctx + 64)
+        ops = NativeOps(device=dev, max_keys=max_ctx + 64, weight_format=a.weights)
     rt = RuntimeConfig(max_context=max_ctx, weight_format=a.weights)
     comm = make_comm(world, device=dev, hidden=cfg.hidden_size, peer=cuda and a.comm != "nccl",
                      fused=a.comm == "fused", prefill_rows=rt.prefill_chunk if a.comm == "fused" else 0)

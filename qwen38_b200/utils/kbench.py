@@ -52,11 +52,16 @@ def time_kernel(fn, iters=20, warmup=3, flush=True):
 
 
 def bench_gemm(a):
-    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU, NativeOps
-    ops = NativeOps()
+    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU, MXWeight, NativeOps
+    ops = NativeOps(weight_format="mxfp8" if a.mx else "bf16")
     x = torch.randn(a.T, a.K, device="cuda").to(torch.bfloat16)
     w_plain = (torch.randn(a.N, a.K, device="cuda") * 0.02).to(torch.bfloat16)
+    if a.mx:                                     # an MXFP8 weight: its exact bf16 expansion
+        from ..checkpoint import dequant_mxfp8, quant_mxfp8
+        w_plain = dequant_mxfp8(*quant_mxfp8(w_plain.float())).to(torch.bfloat16)
     w = ops.prepare_weight(w_plain)              # tile-contiguous storage, done once at load time
+    if a.mx and not isinstance(w, MXWeight):
+        raise SystemExit("weight did not convert to MXFP8")
     if a.epi == "swiglu":
         fn = lambda: ops.linear_swiglu(x, w, 64)
     elif a.epi == "add":
@@ -73,18 +78,26 @@ def bench_gemm(a):
     ops.check()
     hbm, tf, src = peaks()
     flops = 2.0 * a.T * a.N * a.K
-    bytes_ = a.N * a.K * 2 + a.T * a.K * 2 + a.T * a.N * (2 if a.epi != "add" else 8)
-    out = {"kernel": "gemm", "T": a.T, "N": a.N, "K": a.K, "epi": a.epi, "ms": round(ms, 4),
+    wb = a.N * a.K * (1 + 1 / 32) if a.mx else a.N * a.K * 2
+    bytes_ = wb + a.T * a.K * 2 + a.T * a.N * (2 if a.epi != "add" else 8)
+    out = {"kernel": "gemm_mx" if a.mx else "gemm", "T": a.T, "N": a.N, "K": a.K, "epi": a.epi, "ms": round(ms, 4),
            "tflops": round(flops / ms / 1e9, 1), "gbs": round(bytes_ / ms / 1e6, 1)}
     out[f"frac_bw_of_{src}"] = round(bytes_ / ms / 1e6 / hbm, 3)
     out[f"frac_tc_of_{src}"] = round(flops / ms / 1e9 / tf, 3)
     if a.graph:
         out.update(gemm_graph(ops, x, w_plain, a))
-    if a.trace:
+    if a.trace and not a.mx:
         out["trace"] = gemm_trace(ops, x, w, a.epi)
     if a.compare:
         ref = lambda: x @ w_plain.t()
         out["cublas_ms"] = round(time_kernel(ref, a.iters), 4)
+    if a.mx:                                     # the same GEMM over the bf16 weight: same bits
+        bops = NativeOps()
+        wb16 = bops.prepare_weight(w_plain)
+        y_mx = ops.linear(x, w, out_dtype=torch.float32)
+        y_bf = bops.linear(x, wb16, out_dtype=torch.float32)
+        out["bits_equal_bf16_weight"] = bool(torch.equal(y_mx, y_bf))
+        out["bf16_weight_ms"] = round(time_kernel(lambda: bops.linear(x, wb16), a.iters), 4)
     return out
 
 
@@ -92,7 +105,7 @@ def gemm_graph(ops, x, w_plain, a):
     """Per-GEMM time when ``a.graph`` launches run back to back inside one CUDA graph (the verify
     setting: no host launch gaps), cycling over enough weight copies that no launch reads a
     weight another left in L2."""
-    wbytes = w_plain.numel() * 2
+    wbytes = int(w_plain.numel() * ((1 + 1 / 32) if a.mx else 2))
     copies = max(1, -(-3 * 126 * 2 ** 20 // wbytes))
     ws = [ops.prepare_weight(w_plain.clone()) for _ in range(copies)]
     if a.epi == "swiglu":
@@ -300,6 +313,7 @@ def main():
     ap.add_argument("--iters", type=int, default=20)
     ap.add_argument("--compare", action="store_true", help="also time torch/cuBLAS for the same GEMM")
     ap.add_argument("--trace", action="store_true", help="GEMM: per-CTA phase stamps of one launch")
+    ap.add_argument("--mx", action="store_true", help="GEMM: MXFP8 weight (e4m3 + E8M0 scales) streamed by the MX kernel")
     ap.add_argument("--graph", type=int, default=0, help="GEMM: time N back-to-back launches in one CUDA graph")
     a = ap.parse_args()
     out = {"gemm": bench_gemm, "gdn": bench_gdn, "gdnpf": bench_gdn_prefill, "attn": bench_attn,

@@ -367,3 +367,64 @@ def test_deferred_splitk_equals_in_gemm_fixup(nops, T, N, K):
     nops.check()
     assert torch.equal(r_ref, r_def) and torch.equal(r_ref, r_set)
     assert torch.equal(n_ref, n_def)
+
+
+@pytest.fixture(scope="module")
+def mxops():
+    return NativeOps(weight_format="mxfp8")
+
+
+def _mx_bf(N, K, seed):
+    """An MXFP8 weight (its exact bf16 expansion) with every finite e4m3 byte pattern planted in row 0
+    (31 per 32-element block, the block's last element 448 so its scale stays the OCP choice)."""
+    from qwen38_b200.checkpoint import dequant_mxfp8, quant_mxfp8
+    w = torch.randn(N, K, generator=torch.Generator(device=DEV).manual_seed(seed), device=DEV) * 0.02
+    q, se = quant_mxfp8(w)
+    b = torch.arange(256, device=DEV, dtype=torch.int32)
+    b = b[(b & 0x7F) != 0x7F].to(torch.uint8)
+    row = q.view(torch.uint8)[0]
+    for blk in range(min(K // 32, -(-b.numel() // 31))):
+        part = b[blk * 31:(blk + 1) * 31]
+        row[blk * 32:blk * 32 + part.numel()] = part
+        row[blk * 32 + 31] = 0x7E
+    return dequant_mxfp8(q, se).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("T", [1, 16, 40, 64])
+@pytest.mark.parametrize("N,K", [(5120, 17408), (2064, 5120), (1000, 640), (384, 6144)])
+def test_mx_gemm_bits_equal_bf16_weight(nops, mxops, T, N, K):
+    """The MXFP8 weight-streaming GEMM expands each e4m3 tile to the exact bf16 weight in shared
+    memory and shares the bf16 kernel's MMA order, split-K plan and epilogues: every epilogue's
+    output has the same bits as the bf16 GEMM over the dequantised weight."""
+    from qwen38_b200.ops.native import MXWeight
+    wb = _mx_bf(N, K, 21)
+    mw, tw = mxops.prepare_weight(wb), nops.prepare_weight(wb)
+    assert isinstance(mw, MXWeight)
+    x = _bf(T, K, seed=22)
+    assert torch.equal(mxops.linear(x, mw, out_dtype=torch.float32), nops.linear(x, tw, out_dtype=torch.float32))
+    assert torch.equal(mxops.linear(x, mw), nops.linear(x, tw))
+    base = torch.randn(T, N, device=DEV)
+    r_mx, r_bf = base.clone(), base.clone()
+    mxops.linear_residual(x, mw, r_mx)
+    nops.linear_residual(x, tw, r_bf)
+    assert torch.equal(r_mx, r_bf)
+    r_mx, r_bf = base.clone(), base.clone()
+    S = mxops.linear_split(x, mw, r_mx)
+    assert S == nops.linear_split(x, tw, r_bf)
+    if S > 1:
+        mxops.rms_norm_split(r_mx, None, 1e-6, torch.bfloat16, S)
+        nops.rms_norm_split(r_bf, None, 1e-6, torch.bfloat16, S)
+    assert torch.equal(r_mx, r_bf)
+    if N % 128 == 0:
+        assert torch.equal(mxops.linear_swiglu(x, mw, 64), nops.linear_swiglu(x, tw, 64))
+    torch.cuda.synchronize()
+    mxops.check()
+    nops.check()
+
+
+def test_mx_prefill_rows_use_the_bf16_expansion(nops, mxops):
+    wb = _mx_bf(1024, 2048, 23)
+    mw, tw = mxops.prepare_weight(wb), nops.prepare_weight(wb)
+    x = _bf(300, 2048, seed=24)
+    assert torch.equal(mxops.linear(x, mw, out_dtype=torch.float32), nops.linear(x, tw, out_dtype=torch.float32))
+    mxops.check()

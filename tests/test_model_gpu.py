@@ -112,3 +112,29 @@ def test_native_serving_packed_verify_matches_single_stream(nops):
         assert r.output == g
     assert eng.steps["decode"] < sum(len(g) for g in golds)
     nops.check()
+
+
+def test_mxfp8_weights_stream_and_match_the_bf16_expansion(nops):
+    """BASELINE config 5's weight format on the runtime: the target's linear weights are MXFP8
+    (``MXFP8Source``); with ``weight_format="mxfp8"`` the verify / decode GEMMs stream them as e4m3
+    + E8M0 bytes, and every prediction equals the bf16 kernels' over the same (exactly expanded)
+    weights, speculative output included."""
+    from qwen38_b200.checkpoint import MXFP8Source
+    from qwen38_b200.ops.native import MXWeight
+    cfg, dcfg = tiny_model_config(), tiny_drafter_config()
+    rt = RuntimeConfig(max_context=1024, prefill_chunk=64, gdn_chunk=16)
+    src = MXFP8Source(random_target_source(cfg, 0))
+    mx = NativeOps(weight_format="mxfp8")
+    t_mx = HybridTarget(cfg, src, rt, device="cuda", dtype=torch.bfloat16, ops=mx)
+    t_bf = HybridTarget(cfg, src, rt, device="cuda", dtype=torch.bfloat16, ops=nops)
+    n_mx = sum(isinstance(w, MXWeight) for L in t_mx.layers for w in L.values())
+    assert n_mx >= 2 * cfg.num_hidden_layers
+    prompt = torch.randint(0, cfg.vocab_size, (100,), generator=torch.Generator().manual_seed(9)).tolist()
+    gold = greedy_reference(t_bf, prompt, 24)
+    assert greedy_reference(t_mx, prompt, 24) == gold
+    dr = BlockDrafter(dcfg, random_drafter_source(dcfg, cfg.vocab_size, 1), t_mx)
+    res = SpecRuntime(t_mx, dr, verifier_rows=8).generate(prompt, 24, gold_check=gold,
+                                                          pinned=PinnedAcceptance(gold, seed=2, mean_accepted=4))
+    assert res["tokens"] == gold
+    mx.check()
+    nops.check()
