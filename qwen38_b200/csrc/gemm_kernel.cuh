@@ -129,6 +129,7 @@ struct Smem {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int NST = STAGES;                // operand ring slots
   static constexpr int RS = 0;                      // MX load ring slots (none)
+  static constexpr int R_OFF = 0, RSLOT = 0;       // (MX load ring only)
   static constexpr int RING_BYTES = STAGES * STAGE_BYTES;
   static constexpr int BAR_OFF = RING_BYTES;
   static constexpr int TOTAL = BAR_OFF + (2 * STAGES + 2) * 8 + 16 + 1024;  // + alignment slack

@@ -428,3 +428,24 @@ def test_mx_prefill_rows_use_the_bf16_expansion(nops, mxops):
     x = _bf(300, 2048, seed=24)
     assert torch.equal(mxops.linear(x, mw, out_dtype=torch.float32), nops.linear(x, tw, out_dtype=torch.float32))
     mxops.check()
+
+
+def test_gdn_chunked_prefill_state_error_does_not_compound(nops):
+    """The bench's prefill shape (48 value heads, 16 key heads, 4,096 rows = 64 chunks): the carried
+    fp32 state after 1,024 and after 4,096 rows, against the fp32 reference.  The chunked kernel's
+    bf16 operands give a bounded per-chunk error; this pins that it does not grow with the number
+    of chunks the state is carried through (max over heads of the per-head relative error)."""
+    errs = {}
+    for T in (1024, 4096):
+        proj, window, state, conv_w, A_log, dt, norm_w, dims = _gdn_case(T, nk=16, nv=48, seed=31)
+        ref_st = state.clone()
+        TorchOps().gdn_prefill(proj.float(), window.float().clone(), ref_st, conv_w, A_log, dt, norm_w, 1e-6, dims,
+                               64, torch.float32)
+        st = state.clone()
+        nops.chunked_prefill = True
+        nops.gdn_prefill(proj, window.clone(), st, conv_w, A_log, dt, norm_w, 1e-6, dims, 64, torch.bfloat16)
+        per_head = ((st - ref_st).flatten(1).norm(dim=1) / ref_st.flatten(1).norm(dim=1)).max().item()
+        errs[T] = per_head
+    nops.check()
+    assert errs[4096] < 2e-2, errs
+    assert errs[4096] < 1.5 * errs[1024] + 2e-3, errs
