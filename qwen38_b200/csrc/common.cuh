@@ -124,6 +124,12 @@ __device__ __forceinline__ void tma_load_2d_hint(void* smem_dst, const CUtensorM
 
 // 1-D bulk copy global -> shared (no multicast) of `bytes` (multiple of 16, both addresses 16-byte
 // aligned), completing on `bar` with complete_tx.
+// Bulk prefetch of global memory into L2 (no shared memory, no completion): lets a producer run
+// far ahead of its shared-memory ring.  Address 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_prefetch_l2(const void* gmem_src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem_src), "r"(bytes) : "memory");
+}
+
 // Same, with an L2 cache-policy hint.
 __device__ __forceinline__ void bulk_load_hint(void* smem_dst, const void* gmem_src, uint32_t bytes, uint64_t* bar,
                                                uint64_t policy) {

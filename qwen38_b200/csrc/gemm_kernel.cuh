@@ -149,6 +149,7 @@ struct SmemMx {
   static constexpr int RSLOT = 13 * 1024;           // B | q | scales, 1024-aligned slots
   static constexpr int NST = 3;
   static constexpr int RS = 4;
+  static constexpr int PF = 12;                     // stages prefetched into L2 beyond the load ring
   static constexpr int STAGE_BYTES = A_BYTES;
   static constexpr int R_OFF = NST * A_BYTES;
   static constexpr int RING_BYTES = R_OFF + RS * RSLOT;
@@ -392,14 +393,24 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         const int r = i % S::RS;
         tma_load_2d_hint(smem + S::R_OFF + r * S::RSLOT, &map_b, &rfull_bar[r], (kb0 + i) * BK, n0, pol_x);
       };
+      // Weight bytes also go to L2 PF stages ahead of the ring, so the ring's copies find them there:
+      // the ring holds 4 x 8 KB of weight, too few bytes in flight to cover HBM latency by itself.
+      auto prefetch = [&](int i) {
+        if (i < nk) {
+          bulk_prefetch_l2(wq + (size_t)(kb0 + i) * S::RAW_Q, S::RAW_Q);
+          bulk_prefetch_l2(wsc + (size_t)(kb0 + i) * S::RAW_S, S::RAW_S);
+        }
+      };
       const int pre = nk < S::RS ? nk : S::RS;
       for (int i = 0; i < pre; ++i) load_q(i);
+      for (int i = pre; i < pre + S::PF; ++i) prefetch(i);
       pdl_wait();
       for (int i = 0; i < pre; ++i) load_act(i);
       for (int i = pre; i < nk; ++i) {
         if (!mbar_wait(&rempty_bar[i % S::RS], ((i / S::RS) - 1) & 1, g.err, kErrTmaWait, abort_flag)) break;
         load_q(i);
         load_act(i);
+        prefetch(i + S::PF);
       }
     }
   } else {
