@@ -429,19 +429,28 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           if (!named_bar_and(1, 64, ok)) break;      // all converter threads leave together
           const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
           uint8_t* a_tile = smem + s * S::A_BYTES;
+          // Thread ct handles the 16-byte chunks ct, ct + 64, ... (row = chunk / 4, quarter = chunk % 4):
+          // every load is issued before any conversion or store, so the eight chunks' shared-memory
+          // latencies overlap (one converter warp per scheduler has no other warps to hide them).
+          constexpr int CH = (BM * BK) / (16 * 64);
+          uint4 v[CH];
+          uint32_t e[CH];
 #pragma unroll
-          for (int q = 0; q < (BM * BK) / (16 * 64); ++q) {
-            const int chunk = ct + 64 * q;            // 16-byte chunk of the raw tile: row, quarter
-            const int row = chunk >> 2, c16 = chunk & 3;
-            const uint4 v = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
-            const uint32_t e = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
-            const uint32_t m = (e + 120u) << 7;        // bf16 2^(e - 127 + 120)
+          for (int q = 0; q < CH; ++q) {
+            const int chunk = ct + 64 * q, row = chunk >> 2, c16 = chunk & 3;
+            v[q] = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
+            e[q] = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
+          }
+#pragma unroll
+          for (int q = 0; q < CH; ++q) {
+            const int chunk = ct + 64 * q, row = chunk >> 2, c16 = chunk & 3;
+            const uint32_t m = (e[q] + 120u) << 7;     // bf16 2^(e - 127 + 120)
             const uint32_t m2 = m | (m << 16);
             uint32_t o[8];
-            e4m3x4_to_bf16x4_scaled(v.x, m2, o[0], o[1]);
-            e4m3x4_to_bf16x4_scaled(v.y, m2, o[2], o[3]);
-            e4m3x4_to_bf16x4_scaled(v.z, m2, o[4], o[5]);
-            e4m3x4_to_bf16x4_scaled(v.w, m2, o[6], o[7]);
+            e4m3x4_to_bf16x4_scaled(v[q].x, m2, o[0], o[1]);
+            e4m3x4_to_bf16x4_scaled(v[q].y, m2, o[2], o[3]);
+            e4m3x4_to_bf16x4_scaled(v[q].z, m2, o[4], o[5]);
+            e4m3x4_to_bf16x4_scaled(v[q].w, m2, o[6], o[7]);
             uint8_t* rowp = a_tile + row * 128;
             const int sw = row & 7;
             *reinterpret_cast<uint4*>(rowp + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
