@@ -26,7 +26,8 @@ void q38_rms_norm_ar(torch::Tensor x, c10::optional<torch::Tensor> w, double eps
                      int64_t recv_local, torch::Tensor epochs, int64_t slot, int64_t world, int64_t block_words,
                      torch::Tensor err);
 int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
-                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace);
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace,
+                         c10::optional<torch::Tensor> mx_scales);
 void q38_clear_map_cache();
 void q38_gdn_set_trace(c10::optional<torch::Tensor> trace);
 void q38_gdn_recurrent(int64_t mode, torch::Tensor proj, torch::Tensor window, torch::Tensor state,

@@ -387,7 +387,8 @@ void q38_linear_rs(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor ws
 // Micro-benchmark entry: q38_linear with per-CTA phase stamps written to `trace` ([grid][8] int64).
 // Returns the grid size.
 int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Tensor out, int64_t epi,
-                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace) {
+                         torch::Tensor ws, torch::Tensor counters, torch::Tensor err, torch::Tensor trace,
+                         c10::optional<torch::Tensor> mx_scales) {
   c10::cuda::CUDAGuard guard(x.device());
   TORCH_CHECK(trace.scalar_type() == at::kLong && trace.is_contiguous(), "int64 trace buffer");
   TORCH_CHECK(epi == q38::EPI_BF16 || epi == q38::EPI_F32 || epi == q38::EPI_ADD_F32 || epi == q38::EPI_SWIGLU,
@@ -397,9 +398,13 @@ int64_t q38_linear_trace(torch::Tensor x, torch::Tensor w, int64_t N, torch::Ten
   const int64_t m_tiles = (T <= q38::SWAP_MAX_ROWS) ? ((N + 127) / 128) * ((T + 31) / 32)
                                                     : ((T + 127) / 128) * ((N + q38::PREFILL_BN - 1) / q38::PREFILL_BN);
   const int64_t kb = (K + 63) / 64;
-  TORCH_CHECK(trace.numel() >= m_tiles * kb * 8, "trace buffer too small");
+  // MX: 4 more words per CTA after the stamps (converter / MMA wait and work cycles)
+  TORCH_CHECK(trace.numel() >= m_tiles * kb * (mx_scales ? 12 : 8), "trace buffer too small");
+  q38::MxW mx{};
+  if (mx_scales) mx = q38::mx_of(w, *mx_scales);
   q38::gemm_dispatch(x, w, (int)N, out, (int)epi, sc, nullptr, nullptr, nullptr, nullptr,
-                     reinterpret_cast<unsigned long long*>(trace.data_ptr<int64_t>()));
+                     reinterpret_cast<unsigned long long*>(trace.data_ptr<int64_t>()), -1, nullptr, nullptr,
+                     mx_scales ? &mx : nullptr);
   return m_tiles;
 }
 

@@ -422,10 +422,16 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
         // MMA sees exactly the dequantised weight.  The weight is static: conversion starts before
         // the PDL wait.
         const int ct = tid - 64;
+        long long c_raw = 0, c_empty = 0, c_work = 0;   // cycle totals (micro-benchmark trace only)
         for (int i = 0; i < nk; ++i) {
           const int r = i % S::RS, s = i % NST;
+          const long long t0 = clock64();
           bool ok = mbar_wait(&rfull_bar[r], (i / S::RS) & 1, g.err, kErrTmaWait, abort_flag);
+          const long long t1 = clock64();
           if (ok && i >= NST) ok = mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, g.err, kErrTmaWait, abort_flag);
+          const long long t2 = clock64();
+          c_raw += t1 - t0;
+          c_empty += t2 - t1;
           if (!named_bar_and(1, 64, ok)) break;      // all converter threads leave together
           const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
           uint8_t* a_tile = smem + s * S::A_BYTES;
@@ -462,6 +468,16 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             mbar_arrive(&full_bar[s]);
             mbar_arrive(&rempty_bar[r]);
           }
+          c_work += clock64() - t2;
+        }
+        if (g.trace && ct == 0) {
+          // after the [grid][8] stamps: per CTA {converter cycles waiting for the load, waiting for
+          // a free operand slot, converting; MMA thread cycles waiting for a converted tile}
+          unsigned long long* mt = g.trace + (size_t)gridDim.x * gridDim.y * gridDim.z * 8 +
+                                   ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4;
+          mt[0] = (unsigned long long)c_raw;
+          mt[1] = (unsigned long long)c_empty;
+          mt[2] = (unsigned long long)c_work;
         }
       }
     }
@@ -470,9 +486,12 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   if (tid == 32) {
     // ---------------- MMA issuer (single thread)
     constexpr uint32_t idesc = idesc_bf16_f32(BM, BN);
+    long long c_full = 0;
     for (int i = 0; i < nk; ++i) {
       const int s = i % NST;
+      const long long tw = MX ? clock64() : 0;
       if (!mbar_wait(&full_bar[s], (i / NST) & 1, g.err, kErrTmaWait, abort_flag)) break;
+      if constexpr (MX) c_full += clock64() - tw;
       if constexpr (MX) {            // the activation tile of this K block (landed before the conversion)
         if (!mbar_wait(&rfull_bar[i % S::RS], (i / S::RS) & 1, g.err, kErrTmaWait, abort_flag)) break;
       }
@@ -488,6 +507,12 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
       }
       umma_commit(&empty_bar[s]);
       if constexpr (MX) umma_commit(&rempty_bar[i % S::RS]);
+    }
+    if constexpr (MX) {
+      if (g.trace)
+        g.trace[(size_t)gridDim.x * gridDim.y * gridDim.z * 8 +
+                ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4 + 3] =
+            (unsigned long long)c_full;
     }
     Q38_STAMP(3);
     umma_commit(acc_bar);

@@ -86,7 +86,7 @@ def bench_gemm(a):
     out[f"frac_tc_of_{src}"] = round(flops / ms / 1e9 / tf, 3)
     if a.graph:
         out.update(gemm_graph(ops, x, w_plain, a))
-    if a.trace and not a.mx:
+    if a.trace:
         out["trace"] = gemm_trace(ops, x, w, a.epi)
     if a.compare:
         ref = lambda: x @ w_plain.t()
@@ -143,8 +143,9 @@ def gemm_graph(ops, x, w_plain, a):
 def gemm_trace(ops, x, w, epi):
     """One launch with per-CTA %globaltimer stamps: where a GEMM's time goes (launch skew, setup,
     first TMA round trip, streaming, epilogue, split-K fix-up) in microseconds."""
-    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU
+    from ..ops.native import EPI_ADD_F32, EPI_BF16, EPI_SWIGLU, MXWeight
     T = x.shape[0]
+    mx = isinstance(w, MXWeight)
     code = {"bf16": EPI_BF16, "add": EPI_ADD_F32, "swiglu": EPI_SWIGLU}[epi]
     N = w.N
     if epi == "swiglu":
@@ -154,13 +155,24 @@ def gemm_trace(ops, x, w, epi):
     else:
         out = torch.empty(T, N, dtype=torch.bfloat16, device="cuda")
     kb = -(-x.shape[1] // 64)
-    tiles = -(-N // 128) if T <= 32 else -(-T // 128) * -(-N // 256)
-    tr = torch.zeros(tiles * kb * 8, dtype=torch.int64, device="cuda")
+    tiles = -(-N // 128) * -(-T // 32) if T <= 64 else -(-T // 128) * -(-N // 256)
+    tr = torch.zeros(tiles * kb * (12 if mx else 8), dtype=torch.int64, device="cuda")
     torch.empty(64 << 20, dtype=torch.float32, device="cuda").zero_()     # cold L2
     torch.cuda.synchronize()
-    ops.C.linear_trace(x, w.t, N, out, code, ops.ws, ops.counters, ops.err, tr)
+    grid = ops.C.linear_trace(x, w.q if mx else w.t, N, out, code, ops.ws, ops.counters, ops.err, tr,
+                              w.s if mx else None)
     torch.cuda.synchronize()
-    t = tr.view(-1, 8).cpu()
+    t8 = tr.cpu()
+    ctas = grid * ops.C.swap_splits(N, x.shape[1]) if T <= 64 else grid
+    extra = {}
+    if mx:
+        # per CTA cycle totals after the stamps: converter waiting for loads / for a free operand
+        # slot / converting, MMA thread waiting for converted tiles (medians over the CTAs)
+        c = t8[ctas * 8:ctas * 12].view(-1, 4).double()
+        med = lambda v: int(float(v.median()))
+        extra = {"mx_cycles_med": {"conv_wait_load": med(c[:, 0]), "conv_wait_slot": med(c[:, 1]),
+                                   "conv_work": med(c[:, 2]), "mma_wait_tile": med(c[:, 3])}}
+    t = t8[:ctas * 8].view(-1, 8)
     t = t[t[:, 0] > 0].double()
     t0 = t[:, 0].min()
     q = lambda v: [round(float(v.quantile(p)) / 1e3, 2) for p in (0.0, 0.5, 1.0)]
@@ -168,7 +180,8 @@ def gemm_trace(ops, x, w, epi):
             "start_skew_us[min,med,max]": q(t[:, 0] - t0), "setup_us": q(t[:, 1] - t[:, 0]),
             "first_stage_us": q(t[:, 2] - t[:, 1]), "stream_us": q(t[:, 3] - t[:, 2]),
             "mma_drain_us": q(t[:, 4] - t[:, 3]), "epilogue_us": q(t[:, 6] - t[:, 4]),
-            "teardown_us": q(t[:, 7] - t[:, 6]), "last_stream_end_us": round(float(t[:, 3].max() - t0) / 1e3, 2)}
+            "teardown_us": q(t[:, 7] - t[:, 6]), "last_stream_end_us": round(float(t[:, 3].max() - t0) / 1e3, 2),
+            **extra}
 
 
 def bench_gdn(a):
