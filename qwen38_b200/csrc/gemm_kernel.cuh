@@ -430,8 +430,8 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const long long t1 = clock64();
           if (ok && i >= NST) ok = mbar_wait(&empty_bar[s], ((i / NST) - 1) & 1, g.err, kErrTmaWait, abort_flag);
           const long long t2 = clock64();
-          c_raw += t1 - t0;
-          c_empty += t2 - t1;
+          c_raw += t2 - t0;
+          (void)t1;
           if (!named_bar_and(1, 64, ok)) break;      // all converter threads leave together
           const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
           uint8_t* a_tile = smem + s * S::A_BYTES;
@@ -462,22 +462,25 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             *reinterpret_cast<uint4*>(rowp + (((2 * c16) ^ sw) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
             *reinterpret_cast<uint4*>(rowp + (((2 * c16 + 1) ^ sw) << 4)) = make_uint4(o[4], o[5], o[6], o[7]);
           }
+          const long long t3 = clock64();
+          c_work += t3 - t2;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
           named_bar_sync(1, 64);
           if (ct == 0) {
             mbar_arrive(&full_bar[s]);
             mbar_arrive(&rempty_bar[r]);
           }
-          c_work += clock64() - t2;
+          c_empty += clock64() - t3;
         }
         if (g.trace && ct == 0) {
-          // after the [grid][8] stamps: per CTA {converter cycles waiting for the load, waiting for
-          // a free operand slot, converting; MMA thread cycles waiting for a converted tile}
+          // after the [grid][8] stamps: per CTA {converter cycles waiting for the load and a free
+          // operand slot, converting (loads, expansion, stores), publishing (proxy fence, barrier,
+          // arrivals); MMA thread cycles waiting for a converted tile}
           unsigned long long* mt = g.trace + (size_t)gridDim.x * gridDim.y * gridDim.z * 8 +
                                    ((size_t)(blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x) * 4;
           mt[0] = (unsigned long long)c_raw;
-          mt[1] = (unsigned long long)c_empty;
-          mt[2] = (unsigned long long)c_work;
+          mt[1] = (unsigned long long)c_work;
+          mt[2] = (unsigned long long)c_empty;
         }
       }
     }

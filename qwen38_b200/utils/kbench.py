@@ -166,12 +166,12 @@ def gemm_trace(ops, x, w, epi):
     ctas = grid * ops.C.swap_splits(N, x.shape[1]) if T <= 64 else grid
     extra = {}
     if mx:
-        # per CTA cycle totals after the stamps: converter waiting for loads / for a free operand
-        # slot / converting, MMA thread waiting for converted tiles (medians over the CTAs)
+        # per CTA cycle totals after the stamps: converter waiting (load, free slot) / converting /
+        # publishing (proxy fence, barrier, arrivals), MMA thread waiting for tiles (medians)
         c = t8[ctas * 8:ctas * 12].view(-1, 4).double()
         med = lambda v: int(float(v.median()))
-        extra = {"mx_cycles_med": {"conv_wait_load": med(c[:, 0]), "conv_wait_slot": med(c[:, 1]),
-                                   "conv_work": med(c[:, 2]), "mma_wait_tile": med(c[:, 3])}}
+        extra = {"mx_cycles_med": {"conv_wait": med(c[:, 0]), "conv_convert": med(c[:, 1]),
+                                   "conv_publish": med(c[:, 2]), "mma_wait_tile": med(c[:, 3])}}
     t = t8[:ctas * 8].view(-1, 8)
     t = t[t[:, 0] > 0].double()
     t0 = t[:, 0].min()
