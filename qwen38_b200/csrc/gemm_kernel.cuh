@@ -282,11 +282,16 @@ __device__ __forceinline__ void swap_cluster_epilogue(const GemmArgs& g, float* 
 }
 
 template <int BN, int STAGES, int EPI, bool SWAP, bool MX = false>
-__global__ void __launch_bounds__(128, 1)
+__global__ void __launch_bounds__(MX ? 256 : 128, MX ? 2 : 1)
 gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant__ CUtensorMap map_b, GemmArgs g) {
   static_assert(!MX || (SWAP && BN == 32), "MX weights stream through the swap-mode kernel");
   using S = typename std::conditional<MX, SmemMx, Smem<BN, STAGES>>::type;
   constexpr int NST = S::NST;
+  // CTA barrier of the epilogue threads: in the MX kernel warps 4-7 (converters) have left by then
+  auto cta_sync = [] {
+    if constexpr (MX) named_bar_sync(2, 128);
+    else __syncthreads();
+  };
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint64_t* full_bar = reinterpret_cast<uint64_t*>(smem + S::BAR_OFF);
@@ -415,13 +420,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
   } else {
     if constexpr (MX) {
-      if (warp >= 2) {
-        // ---------------- MX converters (warps 2-3): e4m3 x 2^(scale - 127) -> bf16, written into
+      if (warp >= 4) {
+        // ---------------- MX converters (warps 4-7, which exist only in the MX kernel and leave
+        // after the main loop: every later barrier names the 128 threads of warps 0-3): e4m3 x 2^(scale - 127) -> bf16, written into
         // the operand slot in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
         // c ^ (r % 8)).  Every value is exact (an e4m3 value times a power of two fits bf16), so the
         // MMA sees exactly the dequantised weight.  The weight is static: conversion starts before
         // the PDL wait.
-        const int ct = tid - 64;
+        const int ct = tid - 128;
         long long c_raw = 0, c_empty = 0, c_work = 0;   // cycle totals (micro-benchmark trace only)
         for (int i = 0; i < nk; ++i) {
           const int r = i % S::RS, s = i % NST;
@@ -432,24 +438,24 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const long long t2 = clock64();
           c_raw += t2 - t0;
           (void)t1;
-          if (!named_bar_and(1, 64, ok)) break;      // all converter threads leave together
+          if (!named_bar_and(1, 128, ok)) break;     // all converter threads leave together
           const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
           uint8_t* a_tile = smem + s * S::A_BYTES;
           // Thread ct handles the 16-byte chunks ct, ct + 64, ... (row = chunk / 4, quarter = chunk % 4):
           // every load is issued before any conversion or store, so the eight chunks' shared-memory
           // latencies overlap (one converter warp per scheduler has no other warps to hide them).
-          constexpr int CH = (BM * BK) / (16 * 64);
+          constexpr int CH = (BM * BK) / (16 * 128);
           uint4 v[CH];
           uint32_t e[CH];
 #pragma unroll
           for (int q = 0; q < CH; ++q) {
-            const int chunk = ct + 64 * q, row = chunk >> 2, c16 = chunk & 3;
+            const int chunk = ct + 128 * q, row = chunk >> 2, c16 = chunk & 3;
             v[q] = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
             e[q] = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
           }
 #pragma unroll
           for (int q = 0; q < CH; ++q) {
-            const int chunk = ct + 64 * q, row = chunk >> 2, c16 = chunk & 3;
+            const int chunk = ct + 128 * q, row = chunk >> 2, c16 = chunk & 3;
             const uint32_t m = (e[q] + 120u) << 7;     // bf16 2^(e - 127 + 120)
             const uint32_t m2 = m | (m << 16);
             uint32_t o[8];
@@ -465,7 +471,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const long long t3 = clock64();
           c_work += t3 - t2;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
-          named_bar_sync(1, 64);
+          named_bar_sync(1, 128);
           if (ct == 0) {
             mbar_arrive(&full_bar[s]);
             mbar_arrive(&rempty_bar[r]);
@@ -482,6 +488,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           mt[1] = (unsigned long long)c_work;
           mt[2] = (unsigned long long)c_empty;
         }
+        return;                                   // the epilogue belongs to warps 0-3
       }
     }
     pdl_wait();     // nothing upstream is read or written before this point
@@ -525,7 +532,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   __syncwarp();
   mbar_wait(acc_bar, 0, g.err, kErrMmaWait, abort_flag);
   tc_fence_after();
-  __syncthreads();
+  cta_sync();
   if (tid == 0) Q38_STAMP(4);
   const bool ok = (*abort_flag == 0);   // CTA-uniform after the barrier
 
@@ -556,13 +563,13 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
         for (int j = 0; j < 32; ++j) part[j * BM + row] = acc[j];
         __threadfence();
-        __syncthreads();
+        cta_sync();
         if (tid == 0) {
           const int prev = atomicAdd(&g.counters[tile], 1);
           *last_flag = (prev == g.splits - 1);
           Q38_STAMP(5);
         }
-        __syncthreads();
+        cta_sync();
         do_epi = *last_flag != 0;
         if (do_epi) {
           __threadfence();
@@ -595,7 +602,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 32; ++j) extra[j] = __ldcg(base + (size_t)extra_s * PART + j * BM + row);
           }
-          __syncthreads();                 // fix_bar initialised before anyone waits on it
+          cta_sync();                 // fix_bar initialised before anyone waits on it
           const bool staged = mbar_wait(fix_bar, 0, g.err, kErrSplitK, abort_flag);
           float own[32];
 #pragma unroll
@@ -617,7 +624,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
               }
             }
           }
-          __syncthreads();                 // the epilogue may reuse the ring the partials sat in
+          cta_sync();                 // the epilogue may reuse the ring the partials sat in
           if (tid == 0) g.counters[tile] = 0;
         }
       }
@@ -631,7 +638,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
 #pragma unroll
             for (int j = 0; j < 32; ++j) up_s[j * 64 + (row - 64)] = acc[j];
           }
-          __syncthreads();
+          cta_sync();
           if (row < 64) {
             __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(g.out);
             const int f = m_tile * 64 + row;
@@ -664,7 +671,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
             }
             if (lane == 0) { sv[warp * 32 + j] = v; si[warp * 32 + j] = idx; }
           }
-          __syncthreads();
+          cta_sync();
           if (tid < nvalid) {
             float v = sv[tid];
             int idx = si[tid];
@@ -815,7 +822,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     // every thread's stores of the tile are done: one system-scope release increment of the
     // owner's arrival counter (also after a failed wait, so the owner's wait ends; the error word
     // carries the failure)
-    __syncthreads();
+    cta_sync();
     if (tid == 0) {
       __threadfence_system();
       atomicAdd_system(reinterpret_cast<unsigned long long*>(g.rs.count[m_tile % g.rs.world]), 1ull);
@@ -825,7 +832,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
   // ---------------- teardown
   if (tid == 0) Q38_STAMP(6);
   tc_fence_before();
-  __syncthreads();
+  cta_sync();
   if (warp == 0) {
     tc_fence_after();
     tmem_dealloc(tmem, TMEM_COLS);
@@ -840,7 +847,8 @@ void launch_gemm(const CUtensorMap& ma, const CUtensorMap& mb, const GemmArgs& g
   const cudaError_t attr = set_smem_once<gemm_tn_kernel<BN, STAGES, EPI, SWAP, MX>>(smem);
   TORCH_CHECK(attr == cudaSuccess, "cudaFuncSetAttribute failed");
   const unsigned cz = (SWAP && !MX && g.cluster_k && g.splits > 1) ? (unsigned)g.splits : 1u;
-  TORCH_CHECK(launch_pdl_cluster(kern, grid, dim3(128), (size_t)smem, st, dim3(1, 1, cz), ma, mb, g) == cudaSuccess,
+  TORCH_CHECK(launch_pdl_cluster(kern, grid, dim3(MX ? 256 : 128), (size_t)smem, st, dim3(1, 1, cz), ma, mb, g) ==
+                  cudaSuccess,
               "GEMM launch failed");
 }
 
