@@ -147,8 +147,8 @@ struct SmemMx {
   static constexpr int RAW_Q = BM * BK;             // e4m3 bytes of one weight tile
   static constexpr int RAW_S = BM * (BK / 32);      // its scales
   static constexpr int RSLOT = 13 * 1024;           // B | q | scales, 1024-aligned slots
-  static constexpr int NST = 2;
-  static constexpr int RS = 5;
+  static constexpr int NST = 3;
+  static constexpr int RS = 4;
   static constexpr int PF = 12;                     // stages prefetched into L2 beyond the load ring
   static constexpr int STAGE_BYTES = A_BYTES;
   static constexpr int R_OFF = NST * A_BYTES;
@@ -420,15 +420,14 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
     }
   } else {
     if constexpr (MX) {
-      if (warp >= 2) {
-        // ---------------- MX converters (warps 2-7; warps 4-7 exist only in the MX kernel and leave
+      if (warp >= 4) {
+        // ---------------- MX converters (warps 4-7, which exist only in the MX kernel and leave
         // after the main loop: every later barrier names the 128 threads of warps 0-3): e4m3 x 2^(scale - 127) -> bf16, written into
         // the operand slot in the 128-byte-swizzled K-major layout (16-byte chunk c of row r at
         // c ^ (r % 8)).  Every value is exact (an e4m3 value times a power of two fits bf16), so the
         // MMA sees exactly the dequantised weight.  The weight is static: conversion starts before
         // the PDL wait.
-        constexpr int NCV = 192;                  // converter threads
-        const int ct = tid - 64;
+        const int ct = tid - 128;
         long long c_raw = 0, c_empty = 0, c_work = 0;   // cycle totals (micro-benchmark trace only)
         for (int i = 0; i < nk; ++i) {
           const int r = i % S::RS, s = i % NST;
@@ -439,27 +438,24 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const long long t2 = clock64();
           c_raw += t2 - t0;
           (void)t1;
-          if (!named_bar_and(1, NCV, ok)) break;     // all converter threads leave together
+          if (!named_bar_and(1, 128, ok)) break;     // all converter threads leave together
           const uint8_t* raw = smem + S::R_OFF + r * S::RSLOT + S::B_BYTES;
           uint8_t* a_tile = smem + s * S::A_BYTES;
-          // Thread ct handles the 16-byte chunks ct, ct + NCV, .. (row = chunk / 4, quarter = chunk % 4);
-          // all of its loads are issued before any conversion or store, so their latencies overlap.
-          constexpr int NCH = (BM * BK) / 16;       // 16-byte chunks per tile
-          constexpr int CH = (NCH + NCV - 1) / NCV;
+          // Thread ct handles the 16-byte chunks ct, ct + 64, ... (row = chunk / 4, quarter = chunk % 4):
+          // every load is issued before any conversion or store, so the eight chunks' shared-memory
+          // latencies overlap (one converter warp per scheduler has no other warps to hide them).
+          constexpr int CH = (BM * BK) / (16 * 128);
           uint4 v[CH];
           uint32_t e[CH];
 #pragma unroll
           for (int q = 0; q < CH; ++q) {
-            const int chunk = ct + NCV * q, row = chunk >> 2, c16 = chunk & 3;
-            if (chunk < NCH) {
-              v[q] = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
-              e[q] = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
-            }
+            const int chunk = ct + 128 * q, row = chunk >> 2, c16 = chunk & 3;
+            v[q] = *reinterpret_cast<const uint4*>(raw + row * BK + c16 * 16);
+            e[q] = raw[S::RAW_Q + row * (BK / 32) + (c16 >> 1)];   // scale of this 32-group
           }
 #pragma unroll
           for (int q = 0; q < CH; ++q) {
-            const int chunk = ct + NCV * q, row = chunk >> 2, c16 = chunk & 3;
-            if (chunk >= NCH) break;
+            const int chunk = ct + 128 * q, row = chunk >> 2, c16 = chunk & 3;
             const uint32_t m = (e[q] + 120u) << 7;     // bf16 2^(e - 127 + 120)
             const uint32_t m2 = m | (m << 16);
             uint32_t o[8];
@@ -475,7 +471,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           const long long t3 = clock64();
           c_work += t3 - t2;
           asm volatile("fence.proxy.async.shared::cta;" ::: "memory");   // generic writes -> tensor core reads
-          named_bar_sync(1, NCV);
+          named_bar_sync(1, 128);
           if (ct == 0) {
             mbar_arrive(&full_bar[s]);
             mbar_arrive(&rempty_bar[r]);
@@ -492,7 +488,7 @@ gemm_tn_kernel(const __grid_constant__ CUtensorMap map_a, const __grid_constant_
           mt[1] = (unsigned long long)c_work;
           mt[2] = (unsigned long long)c_empty;
         }
-        if (warp >= 4) return;                    // the epilogue belongs to warps 0-3
+        return;                                   // the epilogue belongs to warps 0-3
       }
     }
     pdl_wait();     // nothing upstream is read or written before this point
