@@ -260,6 +260,12 @@ def main():
     if world > 1:
         dist.all_reduce(times, op=dist.ReduceOp.MAX)
     pp_ms, tg_ms, wall_s = times.tolist()
+    # per-step spread (each step's TG time is the max over ranks, like the totals)
+    step_tg = torch.tensor([r["tg_ms"] for r in results], dtype=torch.float64, device=device)
+    if world > 1:
+        dist.all_reduce(step_tg, op=dist.ReduceOp.MAX)
+    step_tok_s = sorted(r["committed"] / (ms / 1e3) for r, ms in zip(results, step_tg.tolist()))
+    step_verify = sorted(r["verify_ms_per_block"] for r in results)
     committed = sum(r["committed"] for r in results)
     prompt_toks = sum(r["prompt_tokens"] for r in results)
     tg = committed / (tg_ms / 1e3)
@@ -291,6 +297,11 @@ def main():
             "block_ms": {k: round(statistics.mean(r[k + "_ms_per_block"] for r in results), 3)
                          for k in ("draft", "verify", "commit")},
             "tokens_per_block": round(statistics.mean(r["tokens_per_block"] for r in results), 3),
+            "step_spread": {"tg_tok_s": [round(step_tok_s[0], 1), round(statistics.median(step_tok_s), 1),
+                                         round(step_tok_s[-1], 1)],
+                            "verify_ms_per_block": [round(step_verify[0], 3), round(statistics.median(step_verify), 3),
+                                                    round(step_verify[-1], 3)],
+                            "order": "min, median, max over the timed steps"},
             "clocks": clocks,
             "provenance": {k: v for k, v in _provenance().items() if k in ("sources_sha256", "extension_sha256",
                                                                                  "device", "driver", "torch")},
