@@ -14,6 +14,7 @@ if not torch.cuda.is_available():
     pytest.skip("needs a CUDA device", allow_module_level=True)
 
 from qwen38_b200.ops.native import NativeOps, untile_weight  # noqa: E402
+from qwen38_b200.parallel.symm import PUSH_ROWS  # noqa: E402
 
 ERR_PEER = 8
 
@@ -23,10 +24,10 @@ class _Areas:
 
     def __init__(self, world, hidden, slots=4):
         self.world, self.rank, self.hidden = world, 0, hidden
-        self.block_words = 32 * hidden
+        self.block_words = PUSH_ROWS * hidden
         self.recv = torch.zeros(slots * world * self.block_words, dtype=torch.int64, device="cuda")
         self.recv_ptrs = [self.recv.data_ptr()] * world
-        self.fepochs = torch.zeros(slots * 32, dtype=torch.int32, device="cuda")
+        self.fepochs = torch.zeros(slots * PUSH_ROWS, dtype=torch.int32, device="cuda")
         self.slots, self._n = slots, 0
 
     def fused_slot(self):
@@ -40,7 +41,7 @@ def ops():
     return NativeOps()
 
 
-@pytest.mark.parametrize("T,N,K", [(1, 5120, 3072), (16, 5120, 8704), (32, 5120, 6144), (7, 1024, 640)])
+@pytest.mark.parametrize("T,N,K", [(1, 5120, 3072), (16, 5120, 8704), (32, 5120, 6144), (7, 1024, 640), (64, 5120, 6144)])
 def test_one_rank_equals_residual_epilogue_and_plain_norm(ops, T, N, K):
     g = torch.Generator(device="cuda").manual_seed(T * 7 + K)
     x = torch.randn(T, K, generator=g, device="cuda").to(torch.bfloat16)
