@@ -115,7 +115,7 @@ def test_native_serving_packed_verify_matches_single_stream(nops):
 
 
 def test_mxfp8_weights_stream_and_match_the_bf16_expansion(nops):
-    """BASELINE config 5's weight format on the runtime: the target's linear weights are MXFP8
+    """The multi-user benchmark's weight format on the runtime: the target's linear weights are MXFP8
     (``MXFP8Source``); with ``weight_format="mxfp8"`` the verify / decode GEMMs stream them as e4m3
     + E8M0 bytes, and every prediction equals the bf16 kernels' over the same (exactly expanded)
     weights, speculative output included."""
