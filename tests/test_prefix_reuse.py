@@ -128,3 +128,12 @@ def test_prefix_reuse_tp2_gloo():
     for rank, reused, exact_tokens, exact_state in out:
         assert reused == 128, reused
         assert exact_tokens and exact_state
+
+
+def test_prefix_bench_tool_is_token_exact_and_reuses():
+    """The prefix-reuse benchmark tool on the tiny shape (CPU): request B restores request A's
+    boundary checkpoint, prefills only its new suffix and stays token-exact against greedy."""
+    from qwen38_b200.utils.prefixbench import parse, run
+    out = run(parse(["--model", "tiny", "--ctx", "256", "--reuse", "128", "--new-tokens", "16"]))
+    assert out["token_exact"] and out["reused_prefix"] == 128
+    assert out["registry"]["hits"] == 1 and out["registry"]["captures"] >= 1
