@@ -688,3 +688,21 @@ def test_streaming_completion_echo():
         assert lp["token_ids"][:3] == [97, 98, 99] and lp["token_logprobs"][0] is None
         assert len(lp["token_logprobs"]) == 3 + 3 and all(v is not None for v in lp["token_logprobs"][1:])
     app.state.loop.close()
+
+
+def test_packed_verify_rows_capped_by_the_targets_batch_invariant_rows(tiny):
+    """A target whose kernels keep at most ``max_pack_rows`` rows batch-invariant gets packed verifies
+    of at most that many rows; the other running requests rotate into the next packs and every
+    request still equals its single-stream greedy output."""
+    tgt, dr = _setup(tiny)
+    tgt.max_pack_rows = 8                       # two 4-row blocks per packed verify
+    prompts = [_prompt(11, 80), _prompt(12, 60), _prompt(13, 90)]
+    golds = [greedy_reference(tgt, p, 12) for p in prompts]
+    eng = ServingEngine(tgt, dr, verifier_rows=4)
+    assert eng.sched.max_step_rows == 8
+    reqs = [eng.add_request(p, 12, pinned=PinnedAcceptance(g, seed=i, mean_accepted=1))
+            for i, (p, g) in enumerate(zip(prompts, golds))]
+    eng.run()
+    for r, g in zip(reqs, golds):
+        assert r.state == FINISHED, r.error
+        assert r.output == g
